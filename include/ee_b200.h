@@ -1,0 +1,184 @@
+/*
+ * ee_b200.h - C ABI of the B200 (sm_100a) entropy-gated mixed-precision engine.
+ *
+ * Library: libee_b200.so (built in-tree by triton-kernels-optimization_b200/build.py).
+ *
+ * Conventions
+ *  - Every compute entry point takes a CUDA stream as `void* stream` (a cudaStream_t;
+ *    NULL = the legacy default stream) and only enqueues work on it: the call returns
+ *    before the GPU is done.  Nothing here synchronises the device.
+ *  - All buffers are device pointers owned by the caller; nothing allocates device
+ *    memory.  Matrices are row-major with an explicit leading dimension in ELEMENTS.
+ *  - Returns EE_OK (0) or a negative EE_ERR_* status; ee_last_error() gives the text
+ *    of the last failure on the calling thread.  Nothing is enqueued when a call
+ *    returns an error.
+ *  - fp16 buffers are passed as `void*` (IEEE binary16), e4m3 buffers as uint8_t
+ *    (OCP FP8 E4M3FN bytes).
+ *  - Entry points are thread-safe; calls on different streams may run concurrently
+ *    when they use different output and workspace buffers.
+ *
+ * Reference surface each entry point replaces ("EE/" = the reference's
+ * entropy-engine/ directory):
+ *   EE/python/kernels.py:264-312  fused_softmax_entropy_kernel -> ee_softmax_entropy
+ *   EE/python/kernels.py:416-453  fused_softmax_entropy        -> ee_fused_softmax_entropy_4d
+ *   EE/python/dispatch.py:55-82   PipelinedEntropyDispatcher   -> ee_route_batch_max, ee_route
+ *   EE/python/dispatch.py:43-48   quantize_weights_int8        -> ee_quantize_weights_int8
+ *   EE/python/kernels.py:330-351  triton_int8_gemm             -> ee_linear_int8
+ *   EE/python/kernels.py:354-373  triton_fp8_gemm              -> ee_linear_fp8
+ *   EE/python/kernels.py:380-409  triton_fp16_gemm             -> ee_gemm_fp16
+ *   EE/csrc/engine.cpp:106-166    CubinEngine::forward         -> ee_gemm_int8
+ *   EE/python/dispatch.py:126-140 EntropyDispatchedLinear      -> ee_gated_linear
+ */
+#ifndef EE_B200_H_
+#define EE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define EE_API __attribute__((visibility("default")))
+#else
+#define EE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EE_ABI_VERSION 1
+
+#define EE_OK 0
+#define EE_ERR_INVALID (-1)     /* bad argument (null pointer, negative or zero size, bad flag) */
+#define EE_ERR_MISALIGNED (-2)  /* pointer / leading dimension misses the required alignment */
+#define EE_ERR_UNSUPPORTED (-3) /* shape outside what the kernels support (see each entry) */
+#define EE_ERR_CUDA (-4)        /* a CUDA runtime / driver call failed (text in ee_last_error) */
+#define EE_ERR_DEVICE (-5)      /* a kernel reported an error word (see ee_device_check) */
+
+/* Precision buckets = route ids = the reference's PrecisionTier values. */
+#define EE_INT8 0
+#define EE_FP8 1
+#define EE_FP16 2
+
+EE_API int ee_abi_version(void);
+EE_API const char* ee_last_error(void);
+
+/* Reads and clears the current device's error word (set by a kernel whose bounded
+ * wait gave up).  Synchronous.  EE_OK if clear, EE_ERR_DEVICE otherwise; *value
+ * (nullable) receives the word. */
+EE_API int ee_device_check(int* value);
+
+/* ---------------------------------------------------------------- softmax + entropy
+ * Per row r of the fp16 matrix x [rows, n] (row stride ld):
+ *   p = softmax(x[r]), H[r] = -sum p log p   (fp32 math)
+ * causal != 0 masks column j of row r when j > r % S (the reference's query_pos).
+ * probs (fp16 [rows, n], stride ldp) is written when non-NULL (masked entries = 0).
+ * route (int8 [rows]) is written when non-NULL: H < tau_low -> EE_INT8,
+ * H < tau_high -> EE_FP8, else EE_FP16 (strict comparisons).
+ * Any n >= 1; the fast path wants n % 8 == 0, ld % 8 == 0 and 16-byte aligned rows.
+ * Replaces EE/python/kernels.py:264-312. */
+EE_API int ee_softmax_entropy(const void* x, int64_t rows, int64_t n, int64_t ld, int causal, int64_t S, void* probs,
+                       int64_t ldp, float* H, int8_t* route, double tau_low, double tau_high, void* stream);
+
+/* The reference's 4-D surface: logits [B, Hh, S, S] contiguous fp16 ->
+ * probs [B, Hh, S, S] fp16 (nullable), row_entropy [B*Hh*S] fp32 (caller scratch,
+ * required), batch_entropy [B] = mean of row_entropy over (Hh, S).
+ * Replaces EE/python/kernels.py:416-453. */
+EE_API int ee_fused_softmax_entropy_4d(const void* logits, int64_t B, int64_t Hh, int64_t S, int causal, void* probs,
+                                float* row_entropy, float* batch_entropy, void* stream);
+
+/* ---------------------------------------------------------------- routing
+ * route[i] = dual-threshold tier of H[i]                (per-row granularity) */
+EE_API int ee_route(const float* H, int64_t rows, double tau_low, double tau_high, int8_t* route, void* stream);
+/* The reference dispatcher's granularity: tier of max(H[0..n)).  max_out (fp32[1])
+ * and tier_out (int8[1]) are device pointers (either may be NULL; both may point to
+ * mapped pinned host memory).  Replaces EE/python/dispatch.py:63-82. */
+EE_API int ee_route_batch_max(const float* H, int64_t n, double tau_low, double tau_high, float* max_out, int8_t* tier_out,
+                       void* stream);
+
+/* ---------------------------------------------------------------- weights (offline)
+ * Per-output-channel INT8 quantisation of W fp16 [N, K] (nn.Linear layout, row
+ * stride ldw):  s[n] = max(amax_k |W[n,k]| / 127, 1e-8),
+ * q = clamp(round_half_even(W / s), -127, 127).
+ * div_mode 0 evaluates amax/127 as amax * fp32(1/127) (what torch does on CUDA),
+ * 1 as an IEEE division (what torch does on CPU).
+ * w_kn: int8 [K, N] (the reference's returned layout), w_nk: int8 [N, K]; either may
+ * be NULL.  Replaces EE/python/dispatch.py:43-48. */
+EE_API int ee_quantize_weights_int8(const void* W, int64_t N, int64_t K, int64_t ldw, int8_t* w_kn, int8_t* w_nk,
+                             float* scale, int div_mode, void* stream);
+
+/* From the reference's weight format (int8 [K, N] + fp32 scale [N]) build the
+ * K-major [N, K] operand packs of the three buckets (each nullable):
+ *   w_i8_nk   = q,   w_e4m3_nk = e4m3(fp16(q)),   w_f16_nk = fp16(fp16(q) * fp16(s)).
+ * These equal, bit for bit, the operands the reference's Triton kernels build per
+ * tile (EE/python/kernels.py:166, :233). */
+EE_API int ee_pack_weights(const int8_t* w_kn, const float* scale, int64_t K, int64_t N, int8_t* w_i8_nk,
+                    uint8_t* w_e4m3_nk, void* w_f16_nk, void* stream);
+
+/* ---------------------------------------------------------------- activations
+ * Per-row symmetric quantisation of A fp16 [M, K] (row stride lda, K % 8 == 0):
+ *   INT8: s = fp16(amax/127), q = trunc(A / s)               (EE/python/kernels.py:336-338)
+ *   e4m3: s = fp16(amax/448), q = e4m3(fp16(A * fp16(1/s)))  (EE/python/kernels.py:361, :144-160)
+ * q: [M, K] contiguous, scale: fp32 [M]. */
+EE_API int ee_quant_rows_int8(const void* A, int64_t M, int64_t K, int64_t lda, int8_t* q, float* scale, void* stream);
+EE_API int ee_quant_rows_e4m3(const void* A, int64_t M, int64_t K, int64_t lda, uint8_t* q, float* scale, void* stream);
+
+/* ---------------------------------------------------------------- tcgen05 GEMMs
+ * Y fp16 [M, N] (row stride ldy) = A [M, K] . W_nk [N, K]^T with the bucket's
+ * epilogue.  Requirements: K % 16 == 0, N % 8 == 0, ldy % 8 == 0, every matrix and
+ * scale pointer 16-byte aligned; M, N, K < 2^31.  M == 0 is a no-op.
+ *   ee_gemm_int8 : y = fp16((fp32(acc_i32) * a_scale[m]) * w_scale[n])
+ *                  (EE/python/kernels.py:52-110, EE/csrc/engine.cpp:106-166)
+ *   ee_gemm_fp8  : y = fp16((acc_f32 * a_scale[m]) * w_scale[n])  (EE/python/kernels.py:120-180)
+ *   ee_gemm_fp16 : y = fp16(acc_f32)                              (EE/python/kernels.py:194-246)
+ * The *_acc variants store the raw accumulators (int32 / fp32 [M, N], ldy = N) for
+ * verification. */
+EE_API int ee_gemm_int8(const int8_t* A, const float* a_scale, const int8_t* W_nk, const float* w_scale, void* Y,
+                 int64_t M, int64_t N, int64_t K, int64_t ldy, void* stream);
+EE_API int ee_gemm_fp8(const uint8_t* A, const float* a_scale, const uint8_t* W_nk, const float* w_scale, void* Y,
+                int64_t M, int64_t N, int64_t K, int64_t ldy, void* stream);
+EE_API int ee_gemm_fp16(const void* A, const void* W_nk, void* Y, int64_t M, int64_t N, int64_t K, int64_t ldy,
+                 void* stream);
+EE_API int ee_gemm_int8_acc(const int8_t* A, const int8_t* W_nk, int32_t* acc, int64_t M, int64_t N, int64_t K,
+                     void* stream);
+EE_API int ee_gemm_fp8_acc(const uint8_t* A, const uint8_t* W_nk, float* acc, int64_t M, int64_t N, int64_t K,
+                    void* stream);
+EE_API int ee_gemm_fp16_acc(const void* A, const void* W_nk, float* acc, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* fp16 activations in, quantisation fused in front of the GEMM (the reference's
+ * launchers).  Workspace: ee_linear_workspace_bytes(M, K) bytes, 256-byte aligned.
+ * Replace EE/python/kernels.py:330-351 (INT8) and :354-373 (FP8). */
+EE_API size_t ee_linear_workspace_bytes(int64_t M, int64_t K);
+EE_API int ee_linear_int8(const void* A, int64_t lda, const int8_t* W_nk, const float* w_scale, void* Y, int64_t M,
+                   int64_t N, int64_t K, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+EE_API int ee_linear_fp8(const void* A, int64_t lda, const uint8_t* W_e4m3_nk, const float* w_scale, void* Y, int64_t M,
+                  int64_t N, int64_t K, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- entropy-gated linear
+ * The on-device dispatcher: per-row routing of A's rows by the entropy of the
+ * matching logits rows, per-row quantisation into three compacted buckets, one
+ * persistent tcgen05 GEMM over all buckets, results scattered back in row order:
+ *   Y[i] = gemm_{route[i]}(A, W)[i].
+ * Workspace: ee_gated_workspace_bytes(M, K) bytes, 256-byte aligned, one per
+ * concurrently running call.  After ee_gate_rows the workspace holds the routing of
+ * M rows; any number of ee_gated_gemm calls (one per projection that shares the
+ * routing, with its own A of M rows and width K) may follow on the same stream.
+ * ee_gated_linear = ee_gate_rows + ee_gated_gemm.
+ * H (fp32 [M]) and route (int8 [M]) are outputs; NULL keeps them in the workspace.
+ * bucket_counts (int32 [3], device, nullable) receives the rows per bucket. */
+EE_API size_t ee_gated_workspace_bytes(int64_t M, int64_t K);
+EE_API int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high, float* H,
+                 int8_t* route, int32_t* bucket_counts, void* workspace, size_t workspace_bytes, void* stream);
+EE_API int ee_gated_gemm(const void* A, int64_t lda, int64_t M, int64_t K, const int8_t* W_i8_nk,
+                  const uint8_t* W_e4m3_nk, const void* W_f16_nk, const float* w_scale, int64_t N, void* Y,
+                  int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+EE_API int ee_gated_linear(const void* logits, int64_t n, int64_t ld_logits, const void* A, int64_t lda, int64_t M,
+                    int64_t K, const int8_t* W_i8_nk, const uint8_t* W_e4m3_nk, const void* W_f16_nk,
+                    const float* w_scale, int64_t N, double tau_low, double tau_high, float* H, int8_t* route,
+                    int32_t* bucket_counts, void* Y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EE_B200_H_ */

@@ -1,0 +1,41 @@
+"""Entropy-gated mixed-precision engine for B200 (sm_100a).
+
+Drop-in for the hot path of IqtedarU/triton-kernels-optimization (entropy-engine):
+the reference's operator names (``triton_int8_gemm``, ``triton_fp8_gemm``,
+``triton_fp16_gemm``, ``fused_softmax_entropy``, ``quantize_weights_int8``,
+``PrecisionTier``, ``PipelinedEntropyDispatcher``, ``EntropyDispatchedLinear``,
+``CubinEngine``) backed by hand-written tcgen05 / TMA kernels behind the C ABI of
+``libee_b200.so`` (include/ee_b200.h).  The package directory name contains dashes,
+so it is imported through ``__graft_entry__.load_package()`` (module name
+``tko_b200``).
+"""
+from . import _lib
+from .dispatch import (
+    EntropyDispatchedLinear,
+    EntropyRouter,
+    PipelinedEntropyDispatcher,
+    PrecisionTier,
+    gated_linear,
+    tier_of,
+)
+from .kernels import (
+    WeightPack,
+    fused_softmax_entropy,
+    gemm_accumulators,
+    gemm_int8_prequant,
+    pack_for,
+    quant_rows_e4m3,
+    quant_rows_int8,
+    quantize_weights_int8,
+    softmax_entropy_rows,
+    triton_fp8_gemm,
+    triton_fp16_gemm,
+    triton_int8_gemm,
+)
+
+LIB_PATH = _lib.LIB_PATH
+
+
+def load_library():
+    """Load libee_b200.so (raises ImportError when it has not been built)."""
+    return _lib.load()

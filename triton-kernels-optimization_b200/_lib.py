@@ -1,0 +1,98 @@
+"""ctypes binding of libee_b200.so (include/ee_b200.h).
+
+Every wrapper raises RuntimeError carrying ee_last_error() when a call returns a
+non-zero status, which is how the reference's TORCH_CHECK / CUDA_DRIVER_CHECK
+failures surface in Python (EE/csrc/engine.cpp:13-21, :112-124).  There is no
+fallback: when the library is missing the import fails loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_double, c_int, c_int8, c_int32, c_int64, c_size_t, c_uint8, c_void_p
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG_DIR, "libee_b200.so")
+
+EE_OK = 0
+STATUS_NAMES = {
+    -1: "EE_ERR_INVALID",
+    -2: "EE_ERR_MISALIGNED",
+    -3: "EE_ERR_UNSUPPORTED",
+    -4: "EE_ERR_CUDA",
+    -5: "EE_ERR_DEVICE",
+}
+
+_P = c_void_p  # every device pointer crosses as an untyped address
+# name -> (restype, argtypes): the exact declarations of include/ee_b200.h
+SIGNATURES = {
+    "ee_abi_version": (c_int, []),
+    "ee_last_error": (c_char_p, []),
+    "ee_device_check": (c_int, [POINTER(c_int)]),
+    "ee_softmax_entropy": (c_int, [_P, c_int64, c_int64, c_int64, c_int, c_int64, _P, c_int64, _P, _P, c_double,
+                                   c_double, _P]),
+    "ee_fused_softmax_entropy_4d": (c_int, [_P, c_int64, c_int64, c_int64, c_int, _P, _P, _P, _P]),
+    "ee_route": (c_int, [_P, c_int64, c_double, c_double, _P, _P]),
+    "ee_route_batch_max": (c_int, [_P, c_int64, c_double, c_double, _P, _P, _P]),
+    "ee_quantize_weights_int8": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, _P, c_int, _P]),
+    "ee_pack_weights": (c_int, [_P, _P, c_int64, c_int64, _P, _P, _P, _P]),
+    "ee_quant_rows_int8": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, _P]),
+    "ee_quant_rows_e4m3": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, _P]),
+    "ee_gemm_int8": (c_int, [_P, _P, _P, _P, _P, c_int64, c_int64, c_int64, c_int64, _P]),
+    "ee_gemm_fp8": (c_int, [_P, _P, _P, _P, _P, c_int64, c_int64, c_int64, c_int64, _P]),
+    "ee_gemm_fp16": (c_int, [_P, _P, _P, c_int64, c_int64, c_int64, c_int64, _P]),
+    "ee_gemm_int8_acc": (c_int, [_P, _P, _P, c_int64, c_int64, c_int64, _P]),
+    "ee_gemm_fp8_acc": (c_int, [_P, _P, _P, c_int64, c_int64, c_int64, _P]),
+    "ee_gemm_fp16_acc": (c_int, [_P, _P, _P, c_int64, c_int64, c_int64, _P]),
+    "ee_linear_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "ee_linear_int8": (c_int, [_P, c_int64, _P, _P, _P, c_int64, c_int64, c_int64, c_int64, _P, c_size_t, _P]),
+    "ee_linear_fp8": (c_int, [_P, c_int64, _P, _P, _P, c_int64, c_int64, c_int64, c_int64, _P, c_size_t, _P]),
+    "ee_gated_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "ee_gate_rows": (c_int, [_P, c_int64, c_int64, c_int64, c_double, c_double, _P, _P, _P, _P, c_size_t, _P]),
+    "ee_gated_gemm": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, _P, _P, c_int64, _P, c_int64, _P, c_size_t,
+                              _P]),
+    "ee_gated_linear": (c_int, [_P, c_int64, c_int64, _P, c_int64, c_int64, c_int64, _P, _P, _P, _P, c_int64,
+                                c_double, c_double, _P, _P, _P, _P, c_int64, _P, c_size_t, _P]),
+}
+
+_lib = None
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the library once and attach the declared signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(
+            f"{path} is missing: build it with `python triton-kernels-optimization_b200/build.py` "
+            "(there is no CPU fallback)")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    msg = load().ee_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(status: int, what: str) -> None:
+    if status != EE_OK:
+        raise RuntimeError(f"{what}: {STATUS_NAMES.get(status, status)}: {last_error()}")
+
+
+def call(name: str, *args) -> None:
+    """Invoke an int-returning entry point and raise on a non-zero status."""
+    check(getattr(load(), name)(*args), name)
+
+
+def device_check() -> int:
+    """Read and clear the current device's error word; raise if it was set."""
+    v = c_int(0)
+    check(load().ee_device_check(ctypes.byref(v)), "ee_device_check")
+    return v.value

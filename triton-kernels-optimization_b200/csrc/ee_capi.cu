@@ -1,0 +1,525 @@
+// ee_capi.cu - the extern "C" boundary (include/ee_b200.h): argument validation,
+// status codes, workspace layout, TMA tensor-map encoding and kernel sequencing.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/ee_b200.h"
+#include "ee_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(EE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int check_launch(int st, const char* what) {
+  if (st == 0) return EE_OK;
+  cudaError_t e = cudaGetLastError();
+  return fail(EE_ERR_CUDA, "%s launch failed: %s", what, cudaGetErrorString(e));
+}
+
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+constexpr int64_t kMaxDim = (int64_t(1) << 31) - 1;
+
+// ---------------------------------------------------------------- driver entry point
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D K-major operand map: rows x K elements, 128-byte swizzled boxes of
+// {128 bytes of K} x box_rows.
+int encode_kmajor(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int64_t ld_elems, int elem_bytes,
+                  int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(EE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (no CUDA driver?)");
+  const CUtensorMapDataType dt = elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_elems) * elem_bytes};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / elem_bytes), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(EE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return EE_OK;
+}
+
+int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cache[dev & 63] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cache[dev & 63] = v;
+  }
+  return cache[dev & 63];
+}
+
+// ---------------------------------------------------------------- GEMM plumbing
+struct GemmOperands {
+  const void* a8 = nullptr;   // uint8 [M_cap, K] (INT8 / FP8 buckets)
+  const void* a16 = nullptr;  // fp16  [M_cap, K] (FP16 bucket)
+  int64_t ld8 = 0, ld16 = 0;
+  const void* w[3] = {nullptr, nullptr, nullptr};  // [N, K] per bucket
+};
+
+int check_gemm_shape(int64_t M, int64_t N, int64_t K, int64_t ldy) {
+  if (M < 0 || N <= 0 || K <= 0) return fail(EE_ERR_INVALID, "bad GEMM shape M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (M > kMaxDim || N > kMaxDim || K > kMaxDim) return fail(EE_ERR_UNSUPPORTED, "GEMM dimension >= 2^31");
+  if (K % 16 != 0) return fail(EE_ERR_UNSUPPORTED, "K=%lld must be a multiple of 16", (long long)K);
+  if (N % 8 != 0) return fail(EE_ERR_UNSUPPORTED, "N=%lld must be a multiple of 8", (long long)N);
+  if (ldy < N || ldy % 8 != 0) return fail(EE_ERR_MISALIGNED, "ldy=%lld must be >= N and a multiple of 8", (long long)ldy);
+  return EE_OK;
+}
+
+// Encodes the maps for the operands present and launches the persistent kernel.
+// Unused slots get a copy of a valid map (they are never dereferenced).
+int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cudaStream_t s) {
+  ee::GemmMaps maps;
+  std::memset(&maps, 0, sizeof(maps));
+  const CUtensorMap* any = nullptr;
+  int st;
+  if (op.a8) {
+    if ((st = encode_kmajor(&maps.a8, op.a8, args.M_cap, args.K, op.ld8, 1, ee::kBM)) != EE_OK) return st;
+    any = &maps.a8;
+  }
+  if (op.a16) {
+    if ((st = encode_kmajor(&maps.a16, op.a16, args.M_cap, args.K, op.ld16, 2, ee::kBM)) != EE_OK) return st;
+    any = any ? any : &maps.a16;
+  }
+  for (int b = 0; b < 3; ++b) {
+    if (op.w[b]) {
+      const int eb = (b == ee::kFP16) ? 2 : 1;
+      if ((st = encode_kmajor(&maps.w[b], op.w[b], args.N, args.K, args.K, eb, ee::kBN)) != EE_OK) return st;
+    }
+  }
+  if (any == nullptr) return fail(EE_ERR_INVALID, "GEMM without an A operand");
+  if (!op.a8) maps.a8 = *any;
+  if (!op.a16) maps.a16 = *any;
+  for (int b = 0; b < 3; ++b)
+    if (!op.w[b]) maps.w[b] = op.w[0] ? maps.w[0] : (op.w[1] ? maps.w[1] : maps.w[2]);
+
+  const int64_t ntn = (args.N + ee::kBN - 1) / ee::kBN;
+  int64_t tiles;
+  if (dynamic_counts) {
+    tiles = ((args.M_cap + ee::kBM - 1) / ee::kBM + 2) * ntn;  // bucket boundaries add <= 2 row tiles
+  } else {
+    tiles = 0;
+    for (int b = 0; b < 3; ++b) tiles += ((args.counts[b] + ee::kBM - 1) / ee::kBM) * ntn;
+  }
+  const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
+  return check_launch(ee::launch_gated_gemm(maps, args, grid, s), "gated_gemm_kernel");
+}
+
+ee::GemmArgs base_args(int64_t M_cap, int64_t N, int64_t K, void* Y, int64_t ldy, int out_mode) {
+  ee::GemmArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.M_cap = static_cast<int>(M_cap);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.Y = Y;
+  a.ldy = ldy;
+  a.out_mode = out_mode;
+  return a;
+}
+
+// ---------------------------------------------------------------- workspaces
+struct LinearWs {
+  float* sa;
+  uint8_t* q;
+};
+size_t linear_ws_bytes(int64_t M, int64_t K) { return align256(sizeof(float) * M) + align256(size_t(M) * K); }
+LinearWs linear_ws(void* ws, int64_t M) {
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  LinearWs w;
+  w.sa = reinterpret_cast<float*>(p);
+  w.q = p + align256(sizeof(float) * M);
+  return w;
+}
+
+struct GatedWs {
+  uint32_t* ticket;
+  int32_t* counts;
+  int32_t* perm;
+  int32_t* slot;
+  int8_t* route;
+  float* H;
+  float* sa;
+  uint8_t* buf8;
+  void* buf16;
+};
+size_t gated_ws_bytes(int64_t M, int64_t K) {
+  return 256 + 2 * align256(sizeof(int32_t) * M) + align256(M) + 2 * align256(sizeof(float) * M) +
+         align256(size_t(M) * K) + align256(size_t(M) * K * 2);
+}
+GatedWs gated_ws(void* ws, int64_t M, int64_t K) {
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  GatedWs w;
+  w.ticket = reinterpret_cast<uint32_t*>(p);
+  w.counts = reinterpret_cast<int32_t*>(p + 16);
+  p += 256;
+  w.perm = reinterpret_cast<int32_t*>(p);
+  p += align256(sizeof(int32_t) * M);
+  w.slot = reinterpret_cast<int32_t*>(p);
+  p += align256(sizeof(int32_t) * M);
+  w.route = reinterpret_cast<int8_t*>(p);
+  p += align256(M);
+  w.H = reinterpret_cast<float*>(p);
+  p += align256(sizeof(float) * M);
+  w.sa = reinterpret_cast<float*>(p);
+  p += align256(sizeof(float) * M);
+  w.buf8 = p;
+  p += align256(size_t(M) * K);
+  w.buf16 = p;
+  return w;
+}
+
+int check_ws(const void* ws, size_t have, size_t need) {
+  if (ws == nullptr) return fail(EE_ERR_INVALID, "workspace is NULL");
+  if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return fail(EE_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  if (have < need) return fail(EE_ERR_INVALID, "workspace too small: %zu < %zu bytes", have, need);
+  return EE_OK;
+}
+
+int pack_rows(const void* A, int64_t lda, int64_t M, int64_t K, const int8_t* route, int fixed_bucket,
+              const int32_t* slot, float* sa, uint8_t* buf8, int64_t ld8, void* buf16, int64_t ld16, cudaStream_t s) {
+  ee::PackArgs p;
+  p.A = A;
+  p.lda = lda;
+  p.M = M;
+  p.K = static_cast<int>(K);
+  p.route = route;
+  p.fixed_bucket = fixed_bucket;
+  p.slot = slot;
+  p.sa = sa;
+  p.buf8 = buf8;
+  p.ld8 = ld8;
+  p.buf16 = buf16;
+  p.ld16 = ld16;
+  return check_launch(ee::launch_pack_rows(p, s), "pack_rows");
+}
+
+int check_rows_input(const void* A, int64_t M, int64_t K, int64_t lda) {
+  if (A == nullptr) return fail(EE_ERR_INVALID, "A is NULL");
+  if (M < 0 || K <= 0 || M > kMaxDim || K > kMaxDim) return fail(EE_ERR_INVALID, "bad shape M=%lld K=%lld", (long long)M, (long long)K);
+  if (K % 8 != 0 || lda < K || lda % 8 != 0 || !al16(A))
+    return fail(EE_ERR_MISALIGNED, "A needs K %% 8 == 0, lda %% 8 == 0 (lda >= K) and a 16-byte aligned base");
+  return EE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ee_abi_version(void) { return EE_ABI_VERSION; }
+
+const char* ee_last_error(void) { return g_last_error.c_str(); }
+
+int ee_device_check(int* value) {
+  int v = 0;
+  if (ee::read_and_clear_device_error(&v) != 0) return fail(EE_ERR_CUDA, "reading the device error word failed");
+  if (value) *value = v;
+  if (v != 0) return fail(EE_ERR_DEVICE, "device error word 0x%x (a bounded wait in a kernel gave up)", v);
+  return EE_OK;
+}
+
+// ------------------------------------------------------------------ softmax + entropy
+int ee_softmax_entropy(const void* x, int64_t rows, int64_t n, int64_t ld, int causal, int64_t S, void* probs,
+                       int64_t ldp, float* H, int8_t* route, double tau_low, double tau_high, void* stream) {
+  if (rows < 0 || rows > kMaxDim) return fail(EE_ERR_INVALID, "bad rows=%lld", (long long)rows);
+  if (rows == 0) return EE_OK;
+  if (x == nullptr || H == nullptr) return fail(EE_ERR_INVALID, "x and H are required");
+  if (n <= 0 || n > kMaxDim || ld < n) return fail(EE_ERR_INVALID, "bad n=%lld / ld=%lld", (long long)n, (long long)ld);
+  if (probs != nullptr && ldp < n) return fail(EE_ERR_INVALID, "ldp=%lld < n", (long long)ldp);
+  if (causal && S <= 0) return fail(EE_ERR_INVALID, "causal masking needs S >= 1");
+  if ((reinterpret_cast<uintptr_t>(x) & 1u) || (probs && (reinterpret_cast<uintptr_t>(probs) & 1u)) ||
+      (reinterpret_cast<uintptr_t>(H) & 3u))
+    return fail(EE_ERR_MISALIGNED, "x/probs must be 2-byte and H 4-byte aligned");
+  ee::SoftmaxArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.x = x;
+  a.ldx = ld;
+  a.rows = rows;
+  a.n = static_cast<int>(n);
+  a.causal = causal ? 1 : 0;
+  a.S = causal ? S : 1;
+  a.probs = probs;
+  a.ldp = ldp;
+  a.H = H;
+  a.route = route;
+  a.tau_low = tau_low;
+  a.tau_high = tau_high;
+  return check_launch(ee::launch_softmax_entropy(a, as_stream(stream)), "softmax_entropy");
+}
+
+int ee_fused_softmax_entropy_4d(const void* logits, int64_t B, int64_t Hh, int64_t S, int causal, void* probs,
+                                float* row_entropy, float* batch_entropy, void* stream) {
+  if (B < 0 || Hh < 0 || S < 0) return fail(EE_ERR_INVALID, "negative shape");
+  if (B == 0 || Hh == 0 || S == 0) return EE_OK;
+  if (row_entropy == nullptr || batch_entropy == nullptr)
+    return fail(EE_ERR_INVALID, "row_entropy and batch_entropy are required");
+  const int64_t rows = B * Hh * S;
+  int st = ee_softmax_entropy(logits, rows, S, S, causal, S, probs, S, row_entropy, nullptr, 0.f, 0.f, stream);
+  if (st != EE_OK) return st;
+  return check_launch(ee::launch_batch_mean(row_entropy, B, Hh * S, batch_entropy, as_stream(stream)), "batch_mean");
+}
+
+// ------------------------------------------------------------------ routing
+int ee_route(const float* H, int64_t rows, double tau_low, double tau_high, int8_t* route, void* stream) {
+  if (rows < 0) return fail(EE_ERR_INVALID, "rows < 0");
+  if (rows == 0) return EE_OK;
+  if (H == nullptr || route == nullptr) return fail(EE_ERR_INVALID, "H and route are required");
+  return check_launch(ee::launch_route(H, rows, tau_low, tau_high, route, as_stream(stream)), "route");
+}
+
+int ee_route_batch_max(const float* H, int64_t n, double tau_low, double tau_high, float* max_out, int8_t* tier_out,
+                       void* stream) {
+  if (H == nullptr || n <= 0) return fail(EE_ERR_INVALID, "H is required and n must be >= 1");
+  return check_launch(ee::launch_batch_max_route(H, n, tau_low, tau_high, max_out, tier_out, as_stream(stream)),
+                      "batch_max_route");
+}
+
+// ------------------------------------------------------------------ weights
+int ee_quantize_weights_int8(const void* W, int64_t N, int64_t K, int64_t ldw, int8_t* w_kn, int8_t* w_nk,
+                             float* scale, int div_mode, void* stream) {
+  if (W == nullptr || scale == nullptr) return fail(EE_ERR_INVALID, "W and scale are required");
+  if (N <= 0 || K <= 0 || ldw < K || N > kMaxDim || K > kMaxDim) return fail(EE_ERR_INVALID, "bad shape");
+  if (div_mode != 0 && div_mode != 1) return fail(EE_ERR_INVALID, "div_mode must be 0 or 1");
+  return check_launch(ee::launch_quantize_weights(W, ldw, N, K, w_kn, w_nk, scale, div_mode, as_stream(stream)),
+                      "quantize_weights");
+}
+
+int ee_pack_weights(const int8_t* w_kn, const float* scale, int64_t K, int64_t N, int8_t* w_i8_nk,
+                    uint8_t* w_e4m3_nk, void* w_f16_nk, void* stream) {
+  if (w_kn == nullptr) return fail(EE_ERR_INVALID, "w_kn is required");
+  if (w_f16_nk != nullptr && scale == nullptr) return fail(EE_ERR_INVALID, "the fp16 pack needs the scale");
+  if (K <= 0 || N <= 0 || K > kMaxDim || N > kMaxDim) return fail(EE_ERR_INVALID, "bad shape");
+  return check_launch(ee::launch_pack_weights(w_kn, scale, K, N, w_i8_nk, w_e4m3_nk, w_f16_nk, as_stream(stream)),
+                      "pack_weights");
+}
+
+// ------------------------------------------------------------------ activations
+int ee_quant_rows_int8(const void* A, int64_t M, int64_t K, int64_t lda, int8_t* q, float* scale, void* stream) {
+  int st = check_rows_input(A, M, K, lda);
+  if (st != EE_OK) return st;
+  if (M == 0) return EE_OK;
+  if (q == nullptr || scale == nullptr || !al16(q)) return fail(EE_ERR_INVALID, "q (16-byte aligned) and scale are required");
+  return pack_rows(A, lda, M, K, nullptr, ee::kINT8, nullptr, scale, reinterpret_cast<uint8_t*>(q), K, nullptr, 0,
+                   as_stream(stream));
+}
+
+int ee_quant_rows_e4m3(const void* A, int64_t M, int64_t K, int64_t lda, uint8_t* q, float* scale, void* stream) {
+  int st = check_rows_input(A, M, K, lda);
+  if (st != EE_OK) return st;
+  if (M == 0) return EE_OK;
+  if (q == nullptr || scale == nullptr || !al16(q)) return fail(EE_ERR_INVALID, "q (16-byte aligned) and scale are required");
+  return pack_rows(A, lda, M, K, nullptr, ee::kFP8, nullptr, scale, q, K, nullptr, 0, as_stream(stream));
+}
+
+// ------------------------------------------------------------------ GEMMs
+static int gemm_single(int bucket, const void* A, const float* a_scale, const void* W, const float* w_scale, void* Y,
+                       int64_t M, int64_t N, int64_t K, int64_t ldy, int out_mode, void* stream) {
+  int st = check_gemm_shape(M, N, K, ldy);
+  if (st != EE_OK) return st;
+  if (M == 0) return EE_OK;
+  if (A == nullptr || W == nullptr || Y == nullptr) return fail(EE_ERR_INVALID, "A, W and Y are required");
+  if (!al16(A) || !al16(W) || !al16(Y)) return fail(EE_ERR_MISALIGNED, "A, W and Y must be 16-byte aligned");
+  if (bucket != ee::kFP16 && out_mode == 0) {
+    if (a_scale == nullptr || w_scale == nullptr) return fail(EE_ERR_INVALID, "scales are required");
+    if (!al16(w_scale)) return fail(EE_ERR_MISALIGNED, "w_scale must be 16-byte aligned");
+  }
+  GemmOperands op;
+  if (bucket == ee::kFP16) {
+    op.a16 = A;
+    op.ld16 = K;
+  } else {
+    op.a8 = A;
+    op.ld8 = K;
+  }
+  op.w[bucket] = W;
+  ee::GemmArgs args = base_args(M, N, K, Y, ldy, out_mode);
+  args.counts[bucket] = static_cast<int>(M);
+  args.sa = a_scale;
+  args.sb = w_scale;
+  return run_gemm(op, args, false, as_stream(stream));
+}
+
+int ee_gemm_int8(const int8_t* A, const float* a_scale, const int8_t* W_nk, const float* w_scale, void* Y,
+                 int64_t M, int64_t N, int64_t K, int64_t ldy, void* stream) {
+  return gemm_single(ee::kINT8, A, a_scale, W_nk, w_scale, Y, M, N, K, ldy, 0, stream);
+}
+int ee_gemm_fp8(const uint8_t* A, const float* a_scale, const uint8_t* W_nk, const float* w_scale, void* Y,
+                int64_t M, int64_t N, int64_t K, int64_t ldy, void* stream) {
+  return gemm_single(ee::kFP8, A, a_scale, W_nk, w_scale, Y, M, N, K, ldy, 0, stream);
+}
+int ee_gemm_fp16(const void* A, const void* W_nk, void* Y, int64_t M, int64_t N, int64_t K, int64_t ldy,
+                 void* stream) {
+  return gemm_single(ee::kFP16, A, nullptr, W_nk, nullptr, Y, M, N, K, ldy, 0, stream);
+}
+int ee_gemm_int8_acc(const int8_t* A, const int8_t* W_nk, int32_t* acc, int64_t M, int64_t N, int64_t K,
+                     void* stream) {
+  return gemm_single(ee::kINT8, A, nullptr, W_nk, nullptr, acc, M, N, K, N, 1, stream);
+}
+int ee_gemm_fp8_acc(const uint8_t* A, const uint8_t* W_nk, float* acc, int64_t M, int64_t N, int64_t K,
+                    void* stream) {
+  return gemm_single(ee::kFP8, A, nullptr, W_nk, nullptr, acc, M, N, K, N, 1, stream);
+}
+int ee_gemm_fp16_acc(const void* A, const void* W_nk, float* acc, int64_t M, int64_t N, int64_t K, void* stream) {
+  return gemm_single(ee::kFP16, A, nullptr, W_nk, nullptr, acc, M, N, K, N, 1, stream);
+}
+
+size_t ee_linear_workspace_bytes(int64_t M, int64_t K) {
+  if (M < 0 || K < 0) return 0;
+  return linear_ws_bytes(M, K);
+}
+
+static int linear_8bit(int bucket, const void* A, int64_t lda, const void* W, const float* w_scale, void* Y,
+                       int64_t M, int64_t N, int64_t K, int64_t ldy, void* ws, size_t ws_bytes, void* stream) {
+  int st = check_gemm_shape(M, N, K, ldy);
+  if (st != EE_OK) return st;
+  if ((st = check_rows_input(A, M, K, lda)) != EE_OK) return st;
+  if (M == 0) return EE_OK;
+  if ((st = check_ws(ws, ws_bytes, linear_ws_bytes(M, K))) != EE_OK) return st;
+  if (W == nullptr || w_scale == nullptr || Y == nullptr) return fail(EE_ERR_INVALID, "W, w_scale and Y are required");
+  if (!al16(W) || !al16(Y) || !al16(w_scale)) return fail(EE_ERR_MISALIGNED, "W, w_scale and Y must be 16-byte aligned");
+  LinearWs w = linear_ws(ws, M);
+  if ((st = pack_rows(A, lda, M, K, nullptr, bucket, nullptr, w.sa, w.q, K, nullptr, 0, as_stream(stream))) != EE_OK)
+    return st;
+  return gemm_single(bucket, w.q, w.sa, W, w_scale, Y, M, N, K, ldy, 0, stream);
+}
+
+int ee_linear_int8(const void* A, int64_t lda, const int8_t* W_nk, const float* w_scale, void* Y, int64_t M,
+                   int64_t N, int64_t K, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+  return linear_8bit(ee::kINT8, A, lda, W_nk, w_scale, Y, M, N, K, ldy, workspace, workspace_bytes, stream);
+}
+int ee_linear_fp8(const void* A, int64_t lda, const uint8_t* W_e4m3_nk, const float* w_scale, void* Y, int64_t M,
+                  int64_t N, int64_t K, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+  return linear_8bit(ee::kFP8, A, lda, W_e4m3_nk, w_scale, Y, M, N, K, ldy, workspace, workspace_bytes, stream);
+}
+
+// ------------------------------------------------------------------ entropy-gated linear
+size_t ee_gated_workspace_bytes(int64_t M, int64_t K) {
+  if (M < 0 || K < 0) return 0;
+  return gated_ws_bytes(M, K);
+}
+
+int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high, float* H,
+                 int8_t* route, int32_t* bucket_counts, void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 0 || M > kMaxDim) return fail(EE_ERR_INVALID, "bad M=%lld", (long long)M);
+  int st = check_ws(workspace, workspace_bytes, gated_ws_bytes(M, 0));
+  if (st != EE_OK) return st;
+  if (logits == nullptr) return fail(EE_ERR_INVALID, "logits is NULL");
+  if (n <= 0 || ld < n || n > kMaxDim) return fail(EE_ERR_INVALID, "bad n=%lld / ld=%lld", (long long)n, (long long)ld);
+  if (reinterpret_cast<uintptr_t>(logits) & 1u) return fail(EE_ERR_MISALIGNED, "logits must be 2-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  GatedWs w = gated_ws(workspace, M, 0);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, 32, s);  // ticket + counts
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+  if (M > 0) {
+    ee::SoftmaxArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.x = logits;
+    a.ldx = ld;
+    a.rows = M;
+    a.n = static_cast<int>(n);
+    a.S = 1;
+    a.H = w.H;
+    a.route = w.route;
+    a.tau_low = tau_low;
+    a.tau_high = tau_high;
+    a.perm = w.perm;
+    a.slot = w.slot;
+    a.counts = w.counts;
+    a.ticket = w.ticket;
+    if ((st = check_launch(ee::launch_softmax_entropy(a, s), "softmax_entropy")) != EE_OK) return st;
+  }
+  if (H && M > 0 && (e = cudaMemcpyAsync(H, w.H, sizeof(float) * M, cudaMemcpyDeviceToDevice, s)) != cudaSuccess)
+    return cuda_fail(e, "cudaMemcpyAsync(H)");
+  if (route && M > 0 && (e = cudaMemcpyAsync(route, w.route, M, cudaMemcpyDeviceToDevice, s)) != cudaSuccess)
+    return cuda_fail(e, "cudaMemcpyAsync(route)");
+  if (bucket_counts &&
+      (e = cudaMemcpyAsync(bucket_counts, w.counts, 3 * sizeof(int32_t), cudaMemcpyDeviceToDevice, s)) != cudaSuccess)
+    return cuda_fail(e, "cudaMemcpyAsync(counts)");
+  return EE_OK;
+}
+
+int ee_gated_gemm(const void* A, int64_t lda, int64_t M, int64_t K, const int8_t* W_i8_nk,
+                  const uint8_t* W_e4m3_nk, const void* W_f16_nk, const float* w_scale, int64_t N, void* Y,
+                  int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_gemm_shape(M, N, K, ldy);
+  if (st != EE_OK) return st;
+  if ((st = check_rows_input(A, M, K, lda)) != EE_OK) return st;
+  if ((st = check_ws(workspace, workspace_bytes, gated_ws_bytes(M, K))) != EE_OK) return st;
+  if (M == 0) return EE_OK;
+  if (!W_i8_nk || !W_e4m3_nk || !W_f16_nk || !w_scale || !Y) return fail(EE_ERR_INVALID, "all three weight packs, w_scale and Y are required");
+  if (!al16(W_i8_nk) || !al16(W_e4m3_nk) || !al16(W_f16_nk) || !al16(w_scale) || !al16(Y))
+    return fail(EE_ERR_MISALIGNED, "weights, w_scale and Y must be 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  GatedWs w = gated_ws(workspace, M, K);
+  if ((st = pack_rows(A, lda, M, K, w.route, 0, w.slot, w.sa, w.buf8, K, w.buf16, K, s)) != EE_OK) return st;
+  GemmOperands op;
+  op.a8 = w.buf8;
+  op.ld8 = K;
+  op.a16 = w.buf16;
+  op.ld16 = K;
+  op.w[ee::kINT8] = W_i8_nk;
+  op.w[ee::kFP8] = W_e4m3_nk;
+  op.w[ee::kFP16] = W_f16_nk;
+  ee::GemmArgs args = base_args(M, N, K, Y, ldy, 0);
+  args.dyn_counts = w.counts;
+  args.perm = w.perm;
+  args.sa = w.sa;
+  args.sb = w_scale;
+  return run_gemm(op, args, true, s);
+}
+
+int ee_gated_linear(const void* logits, int64_t n, int64_t ld_logits, const void* A, int64_t lda, int64_t M,
+                    int64_t K, const int8_t* W_i8_nk, const uint8_t* W_e4m3_nk, const void* W_f16_nk,
+                    const float* w_scale, int64_t N, double tau_low, double tau_high, float* H, int8_t* route,
+                    int32_t* bucket_counts, void* Y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  int st = check_gemm_shape(M, N, K, ldy);
+  if (st != EE_OK) return st;
+  if ((st = check_ws(workspace, workspace_bytes, gated_ws_bytes(M, K))) != EE_OK) return st;
+  if ((st = ee_gate_rows(logits, M, n, ld_logits, tau_low, tau_high, H, route, bucket_counts, workspace,
+                         workspace_bytes, stream)) != EE_OK)
+    return st;
+  return ee_gated_gemm(A, lda, M, K, W_i8_nk, W_e4m3_nk, W_f16_nk, w_scale, N, Y, ldy, workspace, workspace_bytes,
+                       stream);
+}
+
+}  // extern "C"

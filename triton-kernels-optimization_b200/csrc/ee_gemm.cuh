@@ -1,0 +1,338 @@
+// ee_gemm.cuh - persistent, warp-specialised tcgen05 GEMM over the three precision
+// buckets of the gated linear layer.  Included once, by ee_kernels.cu.
+//
+//   Y[perm[p], :] = epilogue_b( A_b[p, :] . W_b[:, :]^T )   for every position p of bucket b
+//
+// bucket INT8 : tcgen05.mma kind::i8     int8 x int8  -> int32 TMEM accumulator,
+//               y = fp16((fp32(acc) * sa[p]) * sb[n])
+// bucket FP8  : tcgen05.mma kind::f8f6f4 e4m3 x e4m3 -> fp32 accumulator,
+//               y = fp16((acc * sa[p]) * sb[n])
+// bucket FP16 : tcgen05.mma kind::f16    f16 x f16   -> fp32 accumulator, y = fp16(acc)
+//
+// Tiles are 128 x 256 (UMMA M x N, one CTA), K staged 128 bytes at a time (128 int8 /
+// e4m3 or 64 fp16 elements) through a 4-deep TMA ring with 128-byte swizzle.
+// Warp roles: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 2..5
+// epilogue (TMEM -> registers -> dequant -> scattered fp16 row stores).  The 512 TMEM
+// columns hold two 256-column accumulators so the epilogue of one tile overlaps the
+// MMAs of the next.  Tile order: FP16 tiles first (twice the tensor time of 8-bit),
+// then FP8, then INT8; inside a bucket the row tile varies fastest, so CTAs that run
+// together share a weight tile.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "ee_internal.h"
+#include "ee_ptx.cuh"
+
+namespace ee {
+
+__device__ int g_device_error;  // sticky error word, read back by read_and_clear_device_error
+
+constexpr int kAStageBytes = kBM * kBKBytes;  // 16 KB
+constexpr int kBStageBytes = kBN * kBKBytes;  // 32 KB
+constexpr int kStageBytes = kAStageBytes + kBStageBytes;
+constexpr int kGemmThreads = 192;
+constexpr int kTmemCols = 2 * kBN;  // two accumulators
+constexpr int kBarrierBytes = 256;
+constexpr size_t kGemmSmem = 1024 /*alignment slack*/ + size_t(kStages) * kStageBytes + kBarrierBytes;
+
+struct TileGeo {
+  int cnt[3], off[3], mtiles[3], tiles[3];
+  int ntn, total;
+};
+
+__device__ __forceinline__ TileGeo make_geo(const GemmArgs& a) {
+  TileGeo g;
+  if (a.dyn_counts != nullptr) {
+#pragma unroll
+    for (int b = 0; b < 3; ++b) g.cnt[b] = *(const volatile int32_t*)(a.dyn_counts + b);
+  } else {
+#pragma unroll
+    for (int b = 0; b < 3; ++b) g.cnt[b] = a.counts[b];
+  }
+  g.off[0] = 0;
+  g.off[1] = g.cnt[0];
+  g.off[2] = g.cnt[0] + g.cnt[1];
+  g.ntn = (a.N + kBN - 1) / kBN;
+  g.total = 0;
+#pragma unroll
+  for (int b = 0; b < 3; ++b) {
+    g.mtiles[b] = (g.cnt[b] + kBM - 1) / kBM;
+    g.tiles[b] = g.mtiles[b] * g.ntn;
+    g.total += g.tiles[b];
+  }
+  return g;
+}
+
+// tile index -> bucket, first position (row of A), first output column
+__device__ __forceinline__ int decode_tile(const TileGeo& g, int t, int& pos0, int& n0) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const int b = 2 - i;
+    if (t < g.tiles[b]) {
+      const int mt = t % g.mtiles[b];
+      const int nt = t / g.mtiles[b];
+      pos0 = g.off[b] + mt * kBM;
+      n0 = nt * kBN;
+      return b;
+    }
+    t -= g.tiles[b];
+  }
+  pos0 = 0;
+  n0 = 0;
+  return 0;
+}
+
+__device__ __forceinline__ int kblocks_of(int b, int K) {
+  const int per = (b == kFP16) ? (kBKBytes / 2) : kBKBytes;  // elements per stage
+  return (K + per - 1) / per;
+}
+
+// issue the 4 UMMAs (each K = 32 bytes) of one stage
+template <int KIND>
+__device__ __forceinline__ void mma_stage(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr, bool first) {
+  constexpr uint32_t idesc = (KIND == kKindI8)   ? make_idesc(2u, 1u, kBM, kBN)   // s32 <- s8 x s8
+                             : (KIND == kKindF8) ? make_idesc(1u, 0u, kBM, kBN)   // f32 <- e4m3 x e4m3
+                                                 : make_idesc(1u, 0u, kBM, kBN);  // f32 <- f16 x f16
+  const uint64_t da = sdesc_k_sw128(a_addr);
+  const uint64_t db = sdesc_k_sw128(b_addr);
+#pragma unroll
+  for (int k = 0; k < kBKBytes / 32; ++k) {
+    // advancing the start address by 32 bytes = 2 in the descriptor's 16-byte units
+    tc_mma<KIND>(d_tmem, da + 2u * k, db + 2u * k, idesc, (first && k == 0) ? 0u : 1u);
+  }
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gated_gemm_kernel(const __grid_constant__ CUtensorMap tm_a8, const __grid_constant__ CUtensorMap tm_a16,
+                      const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
+                      const __grid_constant__ CUtensorMap tm_w2, const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages * kAStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kStages * kBStageBytes);
+  uint64_t* full = bars;                  // [kStages] TMA -> MMA
+  uint64_t* empty = bars + kStages;       // [kStages] MMA -> TMA
+  uint64_t* acc_full = bars + 2 * kStages;     // [2] MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;          // [2] epilogue -> MMA
+  uint64_t* drain = acc_empty + 2;             // MMA drain on abort
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const TileGeo geo = make_geo(args);
+  if (static_cast<int>(blockIdx.x) >= geo.total) return;  // uniform for the whole CTA
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);  // one arrive per epilogue warp
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a8);
+    tma_prefetch_desc(&tm_a16);
+    tma_prefetch_desc(&tm_w0);
+    tma_prefetch_desc(&tm_w1);
+    tma_prefetch_desc(&tm_w2);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int K = args.K;
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    uint32_t stage = 0, phase = 0;
+    uint32_t issued_mask = 0, issued_parity = 0;  // per stage: load in flight, its phase parity
+    bool failed = false;
+    for (int t = blockIdx.x; t < geo.total && !failed; t += gridDim.x) {
+      int pos0, n0;
+      const int b = decode_tile(geo, t, pos0, n0);
+      const int nkb = kblocks_of(b, K);
+      const int kstep = (b == kFP16) ? kBKBytes / 2 : kBKBytes;
+      const CUtensorMap* ta = (b == kFP16) ? &tm_a16 : &tm_a8;
+      const CUtensorMap* tw = (b == kINT8) ? &tm_w0 : (b == kFP8 ? &tm_w1 : &tm_w2);
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+          failed = true;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[stage], kStageBytes);
+          tma_load_2d(sA + stage * kAStageBytes, ta, &full[stage], kb * kstep, pos0);
+          tma_load_2d(sB + stage * kBStageBytes, tw, &full[stage], kb * kstep, n0);
+        }
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        __syncwarp();
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (failed) {
+      if (lane == 0) {
+        atomicOr(&g_device_error, kErrWaitTimeout);
+        *abort_flag = 1;
+      }
+      // let the copies already issued land before the shared memory goes away
+      for (int s = 0; s < kStages; ++s)
+        if (issued_mask & (1u << s)) (void)mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    uint32_t stage = 0, phase = 0, ab = 0, aphase = 0;
+    bool failed = false;
+    for (int t = blockIdx.x; t < geo.total && !failed; t += gridDim.x) {
+      int pos0, n0;
+      const int b = decode_tile(geo, t, pos0, n0);
+      const int nkb = kblocks_of(b, K);
+      if (!mbar_wait(&acc_empty[ab], aphase ^ 1u, abort_flag)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + ab * kBN;
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_addr = smem_u32(sA + stage * kAStageBytes);
+          const uint32_t b_addr = smem_u32(sB + stage * kBStageBytes);
+          if (b == kINT8)
+            mma_stage<kKindI8>(d_tmem, a_addr, b_addr, kb == 0);
+          else if (b == kFP8)
+            mma_stage<kKindF8>(d_tmem, a_addr, b_addr, kb == 0);
+          else
+            mma_stage<kKindF16>(d_tmem, a_addr, b_addr, kb == 0);
+          tc_commit(&empty[stage]);  // frees the stage once these MMAs have read it
+        }
+        __syncwarp();
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (failed) break;
+      if (lane == 0) tc_commit(&acc_full[ab]);
+      __syncwarp();
+      ab ^= 1u;
+      if (ab == 0) aphase ^= 1u;
+    }
+    if (failed) {
+      if (lane == 0) {
+        atomicOr(&g_device_error, kErrWaitTimeout);
+        *abort_flag = 1;
+        tc_commit(drain);  // completes once every MMA issued so far has finished
+      }
+      __syncwarp();
+      (void)mbar_wait(drain, 0u, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5)
+    const int quarter = warp & 3;  // TMEM lanes this warp may access: 32*quarter ..
+    uint32_t ab = 0, aphase = 0;
+    for (int t = blockIdx.x; t < geo.total; t += gridDim.x) {
+      int pos0, n0;
+      const int b = decode_tile(geo, t, pos0, n0);
+      if (!mbar_wait(&acc_full[ab], aphase, abort_flag)) {
+        if (lane == 0) {
+          atomicOr(&g_device_error, kErrWaitTimeout);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      tc_fence_after();
+      const int pos = pos0 + quarter * 32 + lane;
+      const bool valid = pos < geo.off[b] + geo.cnt[b];
+      const int64_t orow = valid ? (args.perm ? static_cast<int64_t>(args.perm[pos]) : static_cast<int64_t>(pos)) : 0;
+      const float sa = (valid && b != kFP16 && args.out_mode == 0) ? args.sa[pos] : 1.f;
+      const uint32_t taddr = tmem_base + ab * kBN + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
+        tmem_ld32(taddr + c * 32, r);
+        tmem_ld_wait(r);
+        const int nc = n0 + c * 32;
+        if (!valid || nc >= args.N) continue;
+        if (args.out_mode == 1) {
+          uint32_t* y = static_cast<uint32_t*>(args.Y) + orow * args.ldy + nc;
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            if (nc + 4 * g < args.N) *reinterpret_cast<uint4*>(y + 4 * g) = make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
+          continue;
+        }
+        float f[32];
+        if (b == kFP16) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+        } else {
+          float sbv[32];
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            if (nc + 4 * g < args.N) {
+              const float4 q = __ldg(reinterpret_cast<const float4*>(args.sb + nc + 4 * g));
+              sbv[4 * g] = q.x;
+              sbv[4 * g + 1] = q.y;
+              sbv[4 * g + 2] = q.z;
+              sbv[4 * g + 3] = q.w;
+            } else {
+              sbv[4 * g] = sbv[4 * g + 1] = sbv[4 * g + 2] = sbv[4 * g + 3] = 0.f;
+            }
+          }
+          if (b == kINT8) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j])), sa), sbv[j]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__fmul_rn(__uint_as_float(r[j]), sa), sbv[j]);
+          }
+        }
+        __half* y = static_cast<__half*>(args.Y) + orow * args.ldy + nc;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          if (nc + 8 * g < args.N) {
+            uint4 u;
+            __half2* h2 = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) h2[k] = __floats2half2_rn(f[8 * g + 2 * k], f[8 * g + 2 * k + 1]);
+            *reinterpret_cast<uint4*>(y + 8 * g) = u;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+      ab ^= 1u;
+      if (ab == 0) aphase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+}  // namespace ee

@@ -1,0 +1,98 @@
+// ee_internal.h - declarations shared by the device translation unit (ee_kernels.cu)
+// and the C-ABI translation unit (ee_capi.cu).  Not part of the public interface.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace ee {
+
+// Precision buckets (route ids); the numbering is the reference's PrecisionTier.
+enum Bucket : int { kINT8 = 0, kFP8 = 1, kFP16 = 2 };
+
+// Device error word bits (read back by ee_device_check).
+enum DeviceError : int {
+  kErrWaitTimeout = 1,  // an mbarrier wait in the GEMM gave up
+  kErrTmem = 2,         // tensor-memory allocation returned an unusable address
+};
+
+// ----------------------------------------------------------------- row kernels
+struct SoftmaxArgs {
+  const void* x;      // fp16 [rows, n] with row stride ldx (elements)
+  int64_t ldx;
+  int64_t rows;
+  int n;
+  int causal;         // mask column j of row r when j > r % S
+  int64_t S;
+  void* probs;        // fp16 [rows, n] with row stride ldp, nullable
+  int64_t ldp;
+  float* H;           // fp32 [rows], required
+  int8_t* route;      // int8 [rows], nullable
+  double tau_low, tau_high;  // compared in double, like the reference's Python floats
+  // compaction (all nullable together): rows grouped by route, stable in row order
+  int32_t* perm;      // [rows] position -> row
+  int32_t* slot;      // [rows] row -> position
+  int32_t* counts;    // [4] rows per bucket (INT8, FP8, FP16) + spare
+  uint32_t* ticket;   // zero-initialised counter; left at zero by the kernel
+};
+int launch_softmax_entropy(const SoftmaxArgs& a, cudaStream_t s);
+
+struct PackArgs {
+  const void* A;      // fp16 [M, K], row stride lda (elements)
+  int64_t lda;
+  int64_t M;
+  int K;
+  const int8_t* route;  // nullable: every row goes to fixed_bucket
+  int fixed_bucket;
+  const int32_t* slot;  // nullable: position = row
+  float* sa;            // [positions] per-row activation scale (8-bit buckets)
+  uint8_t* buf8;        // [positions, K] int8 / e4m3 rows, row stride ld8 bytes
+  int64_t ld8;
+  void* buf16;          // [positions, K] fp16 rows, row stride ld16 elements, nullable if unused
+  int64_t ld16;
+};
+int launch_pack_rows(const PackArgs& a, cudaStream_t s);
+
+// per-output-channel INT8 weight quantisation of W fp16 [N, K]
+// div_mode 0: scale = amax * fp32(1/127) (torch on CUDA); 1: scale = amax / 127 (torch on CPU)
+int launch_quantize_weights(const void* W, int64_t ldw, int64_t N, int64_t K, int8_t* w_kn, int8_t* w_nk,
+                            float* scale, int div_mode, cudaStream_t s);
+// [K, N] int8 + scale[N] -> K-major packs for the three buckets
+int launch_pack_weights(const int8_t* w_kn, const float* scale, int64_t K, int64_t N, int8_t* w_i8,
+                        uint8_t* w_e4m3, void* w_f16, cudaStream_t s);
+int launch_batch_mean(const float* H, int64_t B, int64_t per_batch, float* out, cudaStream_t s);
+int launch_batch_max_route(const float* H, int64_t n, double tl, double th, float* max_out, int8_t* tier_out,
+                           cudaStream_t s);
+int launch_route(const float* H, int64_t rows, double tl, double th, int8_t* route, cudaStream_t s);
+
+// ----------------------------------------------------------------- gated GEMM
+constexpr int kBM = 128;          // rows per tile (UMMA M)
+constexpr int kBN = 256;          // columns per tile (UMMA N)
+constexpr int kBKBytes = 128;     // bytes of K per pipeline stage (one 128B swizzle row)
+constexpr int kStages = 4;
+
+struct GemmArgs {
+  int M_cap;               // positions covered by the A tensor maps
+  int N, K;
+  const int32_t* dyn_counts;  // device [3] rows per bucket, or null to use counts[]
+  int counts[3];
+  const int32_t* perm;     // position -> output row, nullable (identity)
+  const float* sa;         // [M_cap] activation scale per position (INT8 / FP8 buckets)
+  const float* sb;         // [N] weight scale per output channel (INT8 / FP8 buckets)
+  void* Y;                 // fp16 [rows, N] (out_mode 0) or 32-bit [rows, N] (out_mode 1)
+  int64_t ldy;             // elements
+  int out_mode;            // 0: dequantised fp16, 1: raw accumulators (int32 / fp32)
+};
+struct GemmMaps {
+  CUtensorMap a8;          // uint8 [M_cap, K], box {128, 128}
+  CUtensorMap a16;         // fp16  [M_cap, K], box {64, 128}
+  CUtensorMap w[3];        // bucket weights [N, K] K-major, box {128 B, 256}
+};
+int launch_gated_gemm(const GemmMaps& maps, const GemmArgs& args, int grid, cudaStream_t s);
+size_t gemm_smem_bytes();
+
+// device error word
+int read_and_clear_device_error(int* value);
+
+}  // namespace ee

@@ -1,0 +1,130 @@
+// ee_kernels.cu - the single device translation unit: every kernel of the engine and
+// the C++ launchers the C-ABI layer (ee_capi.cu) calls.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "ee_gemm.cuh"
+#include "ee_internal.h"
+#include "ee_rows.cuh"
+
+namespace ee {
+
+namespace {
+inline int status_of(cudaError_t e) { return e == cudaSuccess ? 0 : -4; }
+
+inline unsigned grid_of(int64_t rows, int per_block) {
+  return static_cast<unsigned>((rows + per_block - 1) / per_block);
+}
+
+template <int TPR, int NV>
+int run_softmax_vec(const SoftmaxArgs& a, cudaStream_t s) {
+  softmax_entropy_vec_kernel<TPR, NV><<<grid_of(a.rows, 256 / TPR), 256, 0, s>>>(a);
+  return status_of(cudaGetLastError());
+}
+
+template <int TPR, int NV>
+int run_pack_vec(const PackArgs& a, cudaStream_t s) {
+  pack_rows_vec_kernel<TPR, NV><<<grid_of(a.M, 256 / TPR), 256, 0, s>>>(a);
+  return status_of(cudaGetLastError());
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+}  // namespace
+
+int launch_softmax_entropy(const SoftmaxArgs& a, cudaStream_t s) {
+  if (a.rows <= 0) return 0;
+  const bool vec = (a.n % 8 == 0) && (a.ldx % 8 == 0) && aligned16(a.x) &&
+                   (a.probs == nullptr || ((a.ldp % 8 == 0) && aligned16(a.probs)));
+  if (vec) {
+    const int n = a.n;
+    if (n <= 256) return run_softmax_vec<32, 1>(a, s);
+    if (n <= 512) return run_softmax_vec<32, 2>(a, s);
+    if (n <= 1024) return run_softmax_vec<32, 4>(a, s);
+    if (n <= 2048) return run_softmax_vec<128, 2>(a, s);
+    if (n <= 4096) return run_softmax_vec<256, 2>(a, s);
+    if (n <= 8192) return run_softmax_vec<256, 4>(a, s);
+    if (n <= 16384) return run_softmax_vec<256, 8>(a, s);
+  }
+  softmax_entropy_loop_kernel<<<static_cast<unsigned>(a.rows), 256, 0, s>>>(a);
+  return status_of(cudaGetLastError());
+}
+
+int launch_pack_rows(const PackArgs& a, cudaStream_t s) {
+  if (a.M <= 0) return 0;
+  const int K = a.K;
+  if (K <= 1024) return run_pack_vec<32, 4>(a, s);
+  if (K <= 2048) return run_pack_vec<64, 4>(a, s);
+  if (K <= 4096) return run_pack_vec<128, 4>(a, s);
+  if (K <= 8192) return run_pack_vec<256, 4>(a, s);
+  if (K <= 16384) return run_pack_vec<256, 8>(a, s);
+  pack_rows_loop_kernel<<<static_cast<unsigned>(a.M), 256, 0, s>>>(a);
+  return status_of(cudaGetLastError());
+}
+
+int launch_quantize_weights(const void* W, int64_t ldw, int64_t N, int64_t K, int8_t* w_kn, int8_t* w_nk,
+                            float* scale, int div_mode, cudaStream_t s) {
+  if (N <= 0) return 0;
+  quantize_weights_kernel<<<static_cast<unsigned>(N), 256, 0, s>>>(static_cast<const __half*>(W), ldw, N, K, w_kn,
+                                                                   w_nk, scale, div_mode);
+  return status_of(cudaGetLastError());
+}
+
+int launch_pack_weights(const int8_t* w_kn, const float* scale, int64_t K, int64_t N, int8_t* w_i8,
+                        uint8_t* w_e4m3, void* w_f16, cudaStream_t s) {
+  if (K <= 0 || N <= 0) return 0;
+  dim3 grid(static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>((N + 31) / 32));
+  pack_weights_kernel<<<grid, 256, 0, s>>>(w_kn, scale, K, N, w_i8, w_e4m3, static_cast<__half*>(w_f16));
+  return status_of(cudaGetLastError());
+}
+
+int launch_batch_mean(const float* H, int64_t B, int64_t per_batch, float* out, cudaStream_t s) {
+  if (B <= 0) return 0;
+  batch_mean_kernel<<<static_cast<unsigned>(B), 256, 0, s>>>(H, per_batch, out);
+  return status_of(cudaGetLastError());
+}
+
+int launch_batch_max_route(const float* H, int64_t n, double tl, double th, float* max_out, int8_t* tier_out,
+                           cudaStream_t s) {
+  batch_max_route_kernel<<<1, 256, 0, s>>>(H, n, tl, th, max_out, tier_out);
+  return status_of(cudaGetLastError());
+}
+
+int launch_route(const float* H, int64_t rows, double tl, double th, int8_t* route, cudaStream_t s) {
+  if (rows <= 0) return 0;
+  route_kernel<<<grid_of(rows, 256), 256, 0, s>>>(H, rows, tl, th, route);
+  return status_of(cudaGetLastError());
+}
+
+size_t gemm_smem_bytes() { return kGemmSmem; }
+
+int launch_gated_gemm(const GemmMaps& m, const GemmArgs& args, int grid, cudaStream_t s) {
+  static std::once_flag attr_once[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -4;
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once[dev & 63], [&] {
+    attr_err = cudaFuncSetAttribute(gated_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kGemmSmem));
+  });
+  if (attr_err != cudaSuccess) return -4;
+  if (grid <= 0) return 0;
+  gated_gemm_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(m.a8, m.a16, m.w[0], m.w[1], m.w[2], args);
+  return status_of(cudaGetLastError());
+}
+
+int read_and_clear_device_error(int* value) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
+  if (e != cudaSuccess) return -4;
+  if (v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    if (e != cudaSuccess) return -4;
+  }
+  *value = v;
+  return 0;
+}
+
+}  // namespace ee

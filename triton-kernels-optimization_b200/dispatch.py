@@ -1,0 +1,256 @@
+"""The reference's dispatch surface (EE/python/dispatch.py) on the B200 engine.
+
+* ``PrecisionTier`` / ``quantize_weights_int8`` -- same ids and weight format.
+* ``PipelinedEntropyDispatcher`` -- the reference's batch-max dual-threshold rule
+  (dispatch.py:55-97); the max and the tier are computed on the device and reach
+  the host through pinned memory guarded by an event, not ``.item()`` on a device
+  tensor.
+* ``EntropyDispatchedLinear`` -- drop-in nn.Linear replacement (dispatch.py:103-143):
+  ``forward(x, tier)`` runs the whole tensor in one precision as the reference does;
+  ``forward_gated(x, router)`` routes every row by its own entropy on the device.
+* ``EntropyRouter`` -- the on-device dispatcher: softmax + entropy + per-row route +
+  stable bucket compaction in one kernel, reusable by every linear that shares the
+  rows (``gated_linear``).
+"""
+from __future__ import annotations
+
+from enum import IntEnum
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+from ._lib import call
+from .kernels import (
+    WeightPack,
+    _check_act,
+    _ptr,
+    _require,
+    _stream,
+    quantize_weights_int8,
+    triton_fp16_gemm,
+    triton_fp8_gemm,
+    triton_int8_gemm,
+)
+
+__all__ = [
+    "PrecisionTier",
+    "quantize_weights_int8",
+    "PipelinedEntropyDispatcher",
+    "EntropyDispatchedLinear",
+    "EntropyRouter",
+    "gated_linear",
+]
+
+
+class PrecisionTier(IntEnum):
+    """Precision tiers ordered by compute throughput (EE/python/dispatch.py:32-36)."""
+    INT8 = 0
+    FP8 = 1
+    FP16 = 2
+
+
+def tier_of(value: float, tau_low: float, tau_high: float) -> PrecisionTier:
+    """Dual-threshold rule with strict comparisons (EE/python/dispatch.py:74-79)."""
+    if value < tau_low:
+        return PrecisionTier.INT8
+    if value < tau_high:
+        return PrecisionTier.FP8
+    return PrecisionTier.FP16
+
+
+class PipelinedEntropyDispatcher:
+    """Batch-max dual-threshold dispatcher (EE/python/dispatch.py:55-97).
+
+    ``submit_entropy`` enqueues, on the current stream, one kernel that takes the max
+    of the batch's entropies, then an asynchronous copy of that max into pinned host
+    memory, and records an event.  ``get_tier`` waits for that event only (not for the
+    whole device) and applies the rule on the host in double precision, exactly as the
+    reference compares its Python float.  Before any submission it returns FP16.
+    """
+
+    def __init__(self, tau_low: float = 2.0, tau_high: float = 3.5):
+        self.tau_low = tau_low
+        self.tau_high = tau_high
+        self._pinned = torch.empty(1, dtype=torch.float32, pin_memory=torch.cuda.is_available())
+        self._dev: Optional[torch.Tensor] = None
+        self._event: Optional[torch.cuda.Event] = None
+        self._has_value = False
+        self.tier_counts = {PrecisionTier.INT8: 0, PrecisionTier.FP8: 0, PrecisionTier.FP16: 0}
+
+    def submit_entropy(self, entropy_batch: torch.Tensor) -> None:
+        h = entropy_batch.detach()
+        if h.dtype != torch.float32:
+            h = h.float()
+        h = h.contiguous().reshape(-1)
+        _require(h.is_cuda and h.numel() > 0, "entropy_batch must be a non-empty CUDA tensor")
+        if self._dev is None or self._dev.device != h.device:
+            self._dev = torch.empty(2, dtype=torch.float32, device=h.device)
+        with torch.cuda.device(h.device):
+            call("ee_route_batch_max", h.data_ptr(), h.numel(), float(self.tau_low), float(self.tau_high),
+                 self._dev.data_ptr(), None, _stream())
+            self._pinned.copy_(self._dev[:1], non_blocking=True)
+            self._event = torch.cuda.Event()
+            self._event.record()
+        self._has_value = True
+
+    def get_tier(self) -> PrecisionTier:
+        if not self._has_value:
+            return PrecisionTier.FP16
+        self._event.synchronize()
+        tier = tier_of(float(self._pinned[0]), self.tau_low, self.tau_high)
+        self.tier_counts[tier] += 1
+        return tier
+
+    def reset_stats(self) -> None:
+        self._has_value = False
+        self.tier_counts = {t: 0 for t in PrecisionTier}
+
+    def get_stats(self) -> dict:
+        total = sum(self.tier_counts.values())
+        return {
+            tier.name: {"count": self.tier_counts[tier], "pct": self.tier_counts[tier] / max(total, 1) * 100}
+            for tier in PrecisionTier
+        }
+
+
+class EntropyRouter:
+    """On-device per-row dispatcher.
+
+    ``route(logits)`` launches one kernel over the fp16 logits [M, n]: per-row softmax
+    entropy, dual-threshold route id and the stable compaction of the rows into the
+    INT8 / FP8 / FP16 buckets, all kept in a device workspace.  Every
+    ``gated_linear(A, pack)`` that follows on the same stream reuses that routing for
+    its own activations (A rows correspond to logits rows).  No host round trip.
+    """
+
+    def __init__(self, tau_low: float = 0.41, tau_high: float = 1.68):
+        self.tau_low = float(tau_low)
+        self.tau_high = float(tau_high)
+        self.M = 0
+        self._ws: Optional[torch.Tensor] = None
+        self._ws_k = 0
+        self.H: Optional[torch.Tensor] = None
+        self.route_ids: Optional[torch.Tensor] = None
+        self.counts: Optional[torch.Tensor] = None
+
+    def _ensure_ws(self, M: int, K: int, device) -> None:
+        K = max(K, self._ws_k)
+        need = _lib.load().ee_gated_workspace_bytes(M, K)
+        if self._ws is None or self._ws.numel() < need or self._ws.device != device:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=device)
+        self._ws_k = K
+
+    def reserve(self, M: int, K: int, device) -> None:
+        """Pre-size the workspace for M rows and activations up to width K."""
+        self._ensure_ws(M, K, torch.device(device))
+
+    def route(self, logits: torch.Tensor) -> torch.Tensor:
+        _require(logits.is_cuda and logits.dim() == 2 and logits.dtype == torch.float16,
+                 "logits must be a CUDA fp16 [M, n] tensor")
+        if logits.stride(1) != 1:
+            logits = logits.contiguous()
+        M, n = logits.shape
+        dev = logits.device
+        self._ensure_ws(M, self._ws_k, dev)
+        self.M = M
+        if self.H is None or self.H.numel() != M or self.H.device != dev:
+            self.H = torch.empty(M, dtype=torch.float32, device=dev)
+            self.route_ids = torch.empty(M, dtype=torch.int8, device=dev)
+            self.counts = torch.empty(3, dtype=torch.int32, device=dev)
+        with torch.cuda.device(dev):
+            call("ee_gate_rows", logits.data_ptr(), M, n, logits.stride(0), self.tau_low, self.tau_high,
+                 self.H.data_ptr(), self.route_ids.data_ptr(), self.counts.data_ptr(), self._ws.data_ptr(),
+                 self._ws.numel(), _stream())
+        return self.route_ids
+
+    def gated_linear(self, a: torch.Tensor, pack: WeightPack, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        a = _check_act(a)
+        M, K = a.shape
+        _require(M == self.M, f"routed {self.M} rows but A has {M}")
+        _require(K == pack.K, f"K mismatch: a is [{M},{K}], weight is [{pack.K},{pack.N}]")
+        need = _lib.load().ee_gated_workspace_bytes(M, K)
+        _require(self._ws is not None and self._ws.numel() >= need,
+                 "workspace too small for this K: call reserve(M, K, device) before route()")
+        y = out if out is not None else torch.empty(M, pack.N, dtype=torch.float16, device=a.device)
+        with torch.cuda.device(a.device):
+            call("ee_gated_gemm", a.data_ptr(), a.stride(0), M, K, pack.w_i8.data_ptr(), pack.w_e4m3.data_ptr(),
+                 pack.w_f16.data_ptr(), pack.scale.data_ptr(), pack.N, y.data_ptr(), y.stride(0),
+                 self._ws.data_ptr(), self._ws.numel(), _stream())
+        return y
+
+
+def gated_linear(logits: torch.Tensor, a: torch.Tensor, pack: WeightPack, tau_low: float = 0.41,
+                 tau_high: float = 1.68):
+    """Entropy-gated linear in one call: returns (Y fp16 [M, N], H fp32 [M],
+    route int8 [M], bucket counts int32 [3])."""
+    r = EntropyRouter(tau_low, tau_high)
+    r.reserve(a.shape[0], a.shape[1], a.device)
+    r.route(logits)
+    y = r.gated_linear(a, pack)
+    return y, r.H, r.route_ids, r.counts
+
+
+class EntropyDispatchedLinear(nn.Module):
+    """nn.Linear stand-in with three precision tiers (EE/python/dispatch.py:103-143).
+
+    Holds the reference's buffers (``weight_int8`` [K, N], ``weight_scale`` [N]) plus
+    the K-major operand packs the sm_100a kernels read.
+    """
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = False):
+        super().__init__()
+        self.in_features = in_features
+        self.out_features = out_features
+        self.register_buffer("weight_int8", None)
+        self.register_buffer("weight_scale", None)
+        if bias:
+            self.register_buffer("bias", None)
+        else:
+            self.bias = None
+        self.pack: Optional[WeightPack] = None
+
+    @classmethod
+    def from_linear(cls, linear: nn.Linear) -> "EntropyDispatchedLinear":
+        has_bias = linear.bias is not None
+        layer = cls(linear.in_features, linear.out_features, bias=has_bias)
+        w_int8, w_scale = quantize_weights_int8(linear.weight)
+        layer.weight_int8 = w_int8
+        layer.weight_scale = w_scale
+        layer.pack = WeightPack(w_int8, w_scale)
+        if has_bias:
+            layer.bias = linear.bias.detach().to(torch.float16)
+        return layer
+
+    def _pack(self) -> WeightPack:
+        if self.pack is None or self.pack.w_i8.device != self.weight_int8.device:
+            self.pack = WeightPack(self.weight_int8, self.weight_scale)
+        return self.pack
+
+    def forward(self, x: torch.Tensor, tier: PrecisionTier = PrecisionTier.FP16) -> torch.Tensor:
+        orig_shape = x.shape
+        x_2d = x.reshape(-1, self.in_features).contiguous().to(torch.float16)
+        p = self._pack()
+        if tier == PrecisionTier.INT8:
+            out = triton_int8_gemm(x_2d, p)
+        elif tier == PrecisionTier.FP8:
+            out = triton_fp8_gemm(x_2d, p)
+        else:
+            out = triton_fp16_gemm(x_2d, p)
+        if self.bias is not None:
+            out = out + self.bias.unsqueeze(0)
+        return out.reshape(orig_shape[:-1] + (self.out_features,))
+
+    def forward_gated(self, x: torch.Tensor, router: EntropyRouter) -> torch.Tensor:
+        """Per-row routed forward: row i of x runs in the precision the router chose
+        for row i (route the logits first with ``router.route``)."""
+        orig_shape = x.shape
+        x_2d = x.reshape(-1, self.in_features).contiguous().to(torch.float16)
+        out = router.gated_linear(x_2d, self._pack())
+        if self.bias is not None:
+            out = out + self.bias.unsqueeze(0)
+        return out.reshape(orig_shape[:-1] + (self.out_features,))
+
+    def extra_repr(self):
+        return f"in={self.in_features}, out={self.out_features}, bias={self.bias is not None}"
