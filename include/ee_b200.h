@@ -171,6 +171,20 @@ EE_API int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, do
 EE_API int ee_gated_gemm(const void* A, int64_t lda, int64_t M, int64_t K, const int8_t* W_i8_nk,
                   const uint8_t* W_e4m3_nk, const void* W_f16_nk, const float* w_scale, int64_t N, void* Y,
                   int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+/* The two halves of ee_gated_gemm, for callers that time or schedule them apart:
+ * ee_gated_pack quantises / copies A's rows into the workspace's bucket buffers
+ * (per the routing left there by ee_gate_rows); ee_gated_gemm_packed runs the
+ * persistent tcgen05 GEMM over the packed buckets and scatters Y. */
+EE_API int ee_gated_pack(const void* A, int64_t lda, int64_t M, int64_t K, void* workspace, size_t workspace_bytes,
+                         void* stream);
+EE_API int ee_gated_gemm_packed(int64_t M, int64_t K, const int8_t* W_i8_nk, const uint8_t* W_e4m3_nk,
+                                const void* W_f16_nk, const float* w_scale, int64_t N, void* Y, int64_t ldy,
+                                void* workspace, size_t workspace_bytes, void* stream);
+/* Byte offsets, inside a gated workspace for (M, K), of: [0] bucket counts int32[3],
+ * [1] perm int32[M] (position -> row), [2] slot int32[M] (row -> position),
+ * [3] route int8[M], [4] H fp32[M], [5] activation scales fp32[M], [6] 8-bit rows
+ * [M, K], [7] fp16 rows [M, K].  Lets a caller read the routing in place. */
+EE_API int ee_gated_workspace_layout(int64_t M, int64_t K, int64_t* offsets);
 EE_API int ee_gated_linear(const void* logits, int64_t n, int64_t ld_logits, const void* A, int64_t lda, int64_t M,
                     int64_t K, const int8_t* W_i8_nk, const uint8_t* W_e4m3_nk, const void* W_f16_nk,
                     const float* w_scale, int64_t N, double tau_low, double tau_high, float* H, int8_t* route,

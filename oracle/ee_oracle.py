@@ -162,18 +162,27 @@ def quantize_weights_int8(W: np.ndarray, div_mode: str = "cuda"):
     return np.ascontiguousarray(q), s
 
 
-def _row_scale_f16(a: np.ndarray, denom: float) -> np.ndarray:
+def _row_scale_f16(a: np.ndarray, denom: float, div_mode: str = "cuda") -> np.ndarray:
     """fp16(amax_k |a| / denom) clamped in fp16 (a no-op: the clamp bounds 1e-8 and
     1e-12 round below the smallest fp16 subnormal), widened to fp32
-    (EE/python/kernels.py:336, :361)."""
+    (EE/python/kernels.py:336, :361).  torch evaluates the division by the Python
+    scalar on CUDA as amax * fp32(1/denom) (``div_mode='cuda'``, the reference's
+    deployment) and on CPU as an IEEE division (``div_mode='cpu'``); for denom 448 the
+    two differ when the fp16 result is subnormal."""
     amax = np.abs(np.asarray(a, dtype=np.float16)).max(axis=1).astype(np.float32)
-    return (amax / np.float32(denom)).astype(np.float16).astype(np.float32)
+    if div_mode == "cuda":
+        q = amax * (np.float32(1.0) / np.float32(denom))
+    elif div_mode == "cpu":
+        q = amax / np.float32(denom)
+    else:
+        raise ValueError(div_mode)
+    return q.astype(np.float32).astype(np.float16).astype(np.float32)
 
 
-def quant_rows_int8(a: np.ndarray):
+def quant_rows_int8(a: np.ndarray, div_mode: str = "cuda"):
     """EE/python/kernels.py:336-338: s = fp32(fp16(amax/127)), q = trunc(fp32(a) / s)
     (IEEE division, conversion truncates toward zero).  Returns (int8 [M, K], s [M])."""
-    s = _row_scale_f16(a, 127.0)
+    s = _row_scale_f16(a, 127.0, div_mode)
     with np.errstate(divide="ignore", invalid="ignore"):
         qf = np.asarray(a, dtype=np.float16).astype(np.float32) / s[:, None]
     qf = np.where(np.isnan(qf), 0.0, qf)
@@ -181,14 +190,15 @@ def quant_rows_int8(a: np.ndarray):
     return q, s
 
 
-def quant_rows_e4m3(a: np.ndarray):
+def quant_rows_e4m3(a: np.ndarray, div_mode: str = "cuda"):
     """EE/python/kernels.py:361 (scale) and :144, :157-160 (in-kernel conversion):
     s = fp32(fp16(amax/448)), inv = fp16(1/s), a8 = e4m3(fp16(a * inv)).
     Returns (e4m3 codes [M, K], s [M])."""
-    s = _row_scale_f16(a, 448.0)
+    s = _row_scale_f16(a, 448.0, div_mode)
     with np.errstate(divide="ignore"):
         inv = (np.float32(1.0) / s).astype(np.float16)
-    prod = (np.asarray(a, dtype=np.float16) * inv[:, None]).astype(np.float16)
+    with np.errstate(invalid="ignore"):
+        prod = (np.asarray(a, dtype=np.float16) * inv[:, None]).astype(np.float16)
     return f16_to_e4m3(prod), s
 
 
@@ -217,10 +227,10 @@ def weight_f16(w_kn: np.ndarray, s_w: np.ndarray) -> np.ndarray:
     return (qh * np.asarray(s_w, np.float32).astype(np.float16)[None, :]).astype(np.float16)
 
 
-def gemm_fp8(a: np.ndarray, w_kn: np.ndarray, s_w: np.ndarray):
+def gemm_fp8(a: np.ndarray, w_kn: np.ndarray, s_w: np.ndarray, div_mode: str = "cuda"):
     """Full reference FP8 path (EE/python/kernels.py:354-373, :120-180):
     y = fp16((acc * s_a[m]) * s_w[n]), acc = e4m3(a) . e4m3(w)."""
-    a8, s_a = quant_rows_e4m3(a)
+    a8, s_a = quant_rows_e4m3(a, div_mode)
     acc = e4m3_to_f64(a8) @ e4m3_to_f64(weight_e4m3(w_kn))
     return ((acc.astype(np.float32) * s_a[:, None]) * np.asarray(s_w, np.float32)[None, :]).astype(np.float16)
 
@@ -231,14 +241,14 @@ def gemm_fp16(a: np.ndarray, w_kn: np.ndarray, s_w: np.ndarray):
     return acc.astype(np.float32).astype(np.float16)
 
 
-def linear_by_tier(a: np.ndarray, w_kn: np.ndarray, s_w: np.ndarray, tier: int):
+def linear_by_tier(a: np.ndarray, w_kn: np.ndarray, s_w: np.ndarray, tier: int, div_mode: str = "cuda"):
     """EntropyDispatchedLinear.forward for one tier on the whole tensor
     (EE/python/dispatch.py:126-140, bias omitted)."""
     if tier == INT8:
-        q, s = quant_rows_int8(a)
+        q, s = quant_rows_int8(a, div_mode)
         return gemm_int8(q, s, w_kn, s_w)
     if tier == FP8:
-        return gemm_fp8(a, w_kn, s_w)
+        return gemm_fp8(a, w_kn, s_w, div_mode)
     return gemm_fp16(a, w_kn, s_w)
 
 

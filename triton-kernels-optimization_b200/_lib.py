@@ -51,6 +51,9 @@ SIGNATURES = {
     "ee_gate_rows": (c_int, [_P, c_int64, c_int64, c_int64, c_double, c_double, _P, _P, _P, _P, c_size_t, _P]),
     "ee_gated_gemm": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, _P, _P, c_int64, _P, c_int64, _P, c_size_t,
                               _P]),
+    "ee_gated_pack": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_size_t, _P]),
+    "ee_gated_gemm_packed": (c_int, [c_int64, c_int64, _P, _P, _P, _P, c_int64, _P, c_int64, _P, c_size_t, _P]),
+    "ee_gated_workspace_layout": (c_int, [c_int64, c_int64, POINTER(c_int64)]),
     "ee_gated_linear": (c_int, [_P, c_int64, c_int64, _P, c_int64, c_int64, c_int64, _P, _P, _P, _P, c_int64,
                                 c_double, c_double, _P, _P, _P, _P, c_int64, _P, c_size_t, _P]),
 }

@@ -477,20 +477,44 @@ int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double ta
   return EE_OK;
 }
 
-int ee_gated_gemm(const void* A, int64_t lda, int64_t M, int64_t K, const int8_t* W_i8_nk,
-                  const uint8_t* W_e4m3_nk, const void* W_f16_nk, const float* w_scale, int64_t N, void* Y,
-                  int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
-  int st = check_gemm_shape(M, N, K, ldy);
+int ee_gated_workspace_layout(int64_t M, int64_t K, int64_t* offsets) {
+  if (M < 0 || K < 0 || offsets == nullptr) return fail(EE_ERR_INVALID, "bad arguments");
+  char* base = nullptr;
+  GatedWs w = gated_ws(base, M, K);
+  offsets[0] = reinterpret_cast<char*>(w.counts) - base;
+  offsets[1] = reinterpret_cast<char*>(w.perm) - base;
+  offsets[2] = reinterpret_cast<char*>(w.slot) - base;
+  offsets[3] = reinterpret_cast<char*>(w.route) - base;
+  offsets[4] = reinterpret_cast<char*>(w.H) - base;
+  offsets[5] = reinterpret_cast<char*>(w.sa) - base;
+  offsets[6] = reinterpret_cast<char*>(w.buf8) - base;
+  offsets[7] = reinterpret_cast<char*>(w.buf16) - base;
+  return EE_OK;
+}
+
+int ee_gated_pack(const void* A, int64_t lda, int64_t M, int64_t K, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+  int st = check_rows_input(A, M, K, lda);
   if (st != EE_OK) return st;
-  if ((st = check_rows_input(A, M, K, lda)) != EE_OK) return st;
+  if (K % 16 != 0) return fail(EE_ERR_UNSUPPORTED, "K=%lld must be a multiple of 16", (long long)K);
   if ((st = check_ws(workspace, workspace_bytes, gated_ws_bytes(M, K))) != EE_OK) return st;
   if (M == 0) return EE_OK;
-  if (!W_i8_nk || !W_e4m3_nk || !W_f16_nk || !w_scale || !Y) return fail(EE_ERR_INVALID, "all three weight packs, w_scale and Y are required");
+  GatedWs w = gated_ws(workspace, M, K);
+  return pack_rows(A, lda, M, K, w.route, 0, w.slot, w.sa, w.buf8, K, w.buf16, K, as_stream(stream));
+}
+
+int ee_gated_gemm_packed(int64_t M, int64_t K, const int8_t* W_i8_nk, const uint8_t* W_e4m3_nk,
+                         const void* W_f16_nk, const float* w_scale, int64_t N, void* Y, int64_t ldy,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_gemm_shape(M, N, K, ldy);
+  if (st != EE_OK) return st;
+  if ((st = check_ws(workspace, workspace_bytes, gated_ws_bytes(M, K))) != EE_OK) return st;
+  if (M == 0) return EE_OK;
+  if (!W_i8_nk || !W_e4m3_nk || !W_f16_nk || !w_scale || !Y)
+    return fail(EE_ERR_INVALID, "all three weight packs, w_scale and Y are required");
   if (!al16(W_i8_nk) || !al16(W_e4m3_nk) || !al16(W_f16_nk) || !al16(w_scale) || !al16(Y))
     return fail(EE_ERR_MISALIGNED, "weights, w_scale and Y must be 16-byte aligned");
-  cudaStream_t s = as_stream(stream);
   GatedWs w = gated_ws(workspace, M, K);
-  if ((st = pack_rows(A, lda, M, K, w.route, 0, w.slot, w.sa, w.buf8, K, w.buf16, K, s)) != EE_OK) return st;
   GemmOperands op;
   op.a8 = w.buf8;
   op.ld8 = K;
@@ -504,7 +528,17 @@ int ee_gated_gemm(const void* A, int64_t lda, int64_t M, int64_t K, const int8_t
   args.perm = w.perm;
   args.sa = w.sa;
   args.sb = w_scale;
-  return run_gemm(op, args, true, s);
+  return run_gemm(op, args, true, as_stream(stream));
+}
+
+int ee_gated_gemm(const void* A, int64_t lda, int64_t M, int64_t K, const int8_t* W_i8_nk,
+                  const uint8_t* W_e4m3_nk, const void* W_f16_nk, const float* w_scale, int64_t N, void* Y,
+                  int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_gemm_shape(M, N, K, ldy);
+  if (st != EE_OK) return st;
+  if ((st = ee_gated_pack(A, lda, M, K, workspace, workspace_bytes, stream)) != EE_OK) return st;
+  return ee_gated_gemm_packed(M, K, W_i8_nk, W_e4m3_nk, W_f16_nk, w_scale, N, Y, ldy, workspace, workspace_bytes,
+                              stream);
 }
 
 int ee_gated_linear(const void* logits, int64_t n, int64_t ld_logits, const void* A, int64_t lda, int64_t M,

@@ -358,16 +358,20 @@ struct RowScale {
 };
 
 // Scale of one row from its fp16 abs-max (exact in fp32):
-//   INT8: s = fp16(amax / 127)       FP8: s = fp16(amax / 448), inv = fp16(1 / s)
-// The fp16 clamp to 1e-8 / 1e-12 of the reference is a no-op in fp16 (both bounds
-// round below the smallest fp16 subnormal), so s is the rounded quotient itself.
+//   INT8: s = fp16(amax * fp32(1/127))
+//   FP8:  s = fp16(amax * fp32(1/448)),  inv = fp16(1 / s)
+// torch evaluates the reference's `amax / 127.0` / `amax / 448.0` on CUDA as a
+// multiplication by the fp32 reciprocal (for 448 that differs from a true division
+// when the fp16 result is subnormal).  The fp16 clamp to 1e-8 / 1e-12 of the
+// reference is a no-op in fp16 (both bounds round below the smallest fp16
+// subnormal), so s is the rounded product itself.
 __device__ __forceinline__ RowScale row_scale(float amax, int bucket) {
   RowScale r;
   if (bucket == kINT8) {
-    r.s = __half2float(__float2half_rn(__fdiv_rn(amax, 127.f)));
+    r.s = __half2float(__float2half_rn(__fmul_rn(amax, 1.0f / 127.0f)));
     r.inv = __float2half_rn(0.f);
   } else {
-    r.s = __half2float(__float2half_rn(__fdiv_rn(amax, 448.f)));
+    r.s = __half2float(__float2half_rn(__fmul_rn(amax, 1.0f / 448.0f)));
     r.inv = __float2half_rn(div_full(1.f, r.s));
   }
   return r;

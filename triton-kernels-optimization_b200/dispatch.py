@@ -14,6 +14,7 @@
 """
 from __future__ import annotations
 
+import ctypes
 from enum import IntEnum
 from typing import Optional
 
@@ -122,7 +123,9 @@ class EntropyRouter:
     entropy, dual-threshold route id and the stable compaction of the rows into the
     INT8 / FP8 / FP16 buckets, all kept in a device workspace.  Every
     ``gated_linear(A, pack)`` that follows on the same stream reuses that routing for
-    its own activations (A rows correspond to logits rows).  No host round trip.
+    its own activations (row i of A belongs to row i of the logits).  There is no host
+    round trip; ``H``, ``route_ids``, ``counts`` and ``perm`` are views into the
+    workspace, valid until the next ``route``.
     """
 
     def __init__(self, tau_low: float = 0.41, tau_high: float = 1.68):
@@ -130,21 +133,29 @@ class EntropyRouter:
         self.tau_high = float(tau_high)
         self.M = 0
         self._ws: Optional[torch.Tensor] = None
-        self._ws_k = 0
+        self._ws_k = 16
         self.H: Optional[torch.Tensor] = None
         self.route_ids: Optional[torch.Tensor] = None
         self.counts: Optional[torch.Tensor] = None
-
-    def _ensure_ws(self, M: int, K: int, device) -> None:
-        K = max(K, self._ws_k)
-        need = _lib.load().ee_gated_workspace_bytes(M, K)
-        if self._ws is None or self._ws.numel() < need or self._ws.device != device:
-            self._ws = torch.empty(need, dtype=torch.uint8, device=device)
-        self._ws_k = K
+        self.perm: Optional[torch.Tensor] = None
 
     def reserve(self, M: int, K: int, device) -> None:
-        """Pre-size the workspace for M rows and activations up to width K."""
-        self._ensure_ws(M, K, torch.device(device))
+        """Size the workspace for M rows and activations up to width K."""
+        self._ws_k = max(self._ws_k, int(K))
+        need = _lib.load().ee_gated_workspace_bytes(M, self._ws_k)
+        device = torch.device(device)
+        if self._ws is None or self._ws.numel() < need or self._ws.device != device:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=device)
+            self.H = None  # views of the old workspace are stale
+
+    def _views(self, M: int) -> None:
+        off = (ctypes.c_int64 * 8)()
+        call("ee_gated_workspace_layout", M, 0, off)
+        ws = self._ws
+        self.counts = ws[off[0]:off[0] + 12].view(torch.int32)
+        self.perm = ws[off[1]:off[1] + 4 * M].view(torch.int32)
+        self.route_ids = ws[off[3]:off[3] + M].view(torch.int8)
+        self.H = ws[off[4]:off[4] + 4 * M].view(torch.float32)
 
     def route(self, logits: torch.Tensor) -> torch.Tensor:
         _require(logits.is_cuda and logits.dim() == 2 and logits.dtype == torch.float16,
@@ -152,44 +163,59 @@ class EntropyRouter:
         if logits.stride(1) != 1:
             logits = logits.contiguous()
         M, n = logits.shape
-        dev = logits.device
-        self._ensure_ws(M, self._ws_k, dev)
+        self.reserve(M, self._ws_k, logits.device)
+        if M != self.M or self.H is None:
+            self._views(M)
         self.M = M
-        if self.H is None or self.H.numel() != M or self.H.device != dev:
-            self.H = torch.empty(M, dtype=torch.float32, device=dev)
-            self.route_ids = torch.empty(M, dtype=torch.int8, device=dev)
-            self.counts = torch.empty(3, dtype=torch.int32, device=dev)
-        with torch.cuda.device(dev):
-            call("ee_gate_rows", logits.data_ptr(), M, n, logits.stride(0), self.tau_low, self.tau_high,
-                 self.H.data_ptr(), self.route_ids.data_ptr(), self.counts.data_ptr(), self._ws.data_ptr(),
-                 self._ws.numel(), _stream())
+        with torch.cuda.device(logits.device):
+            call("ee_gate_rows", logits.data_ptr(), M, n, logits.stride(0), self.tau_low, self.tau_high, None, None,
+                 None, self._ws.data_ptr(), self._ws.numel(), _stream())
         return self.route_ids
 
-    def gated_linear(self, a: torch.Tensor, pack: WeightPack, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def _check(self, a: torch.Tensor, pack: WeightPack):
         a = _check_act(a)
         M, K = a.shape
         _require(M == self.M, f"routed {self.M} rows but A has {M}")
         _require(K == pack.K, f"K mismatch: a is [{M},{K}], weight is [{pack.K},{pack.N}]")
-        need = _lib.load().ee_gated_workspace_bytes(M, K)
-        _require(self._ws is not None and self._ws.numel() >= need,
+        _require(self._ws is not None and self._ws.numel() >= _lib.load().ee_gated_workspace_bytes(M, K),
                  "workspace too small for this K: call reserve(M, K, device) before route()")
-        y = out if out is not None else torch.empty(M, pack.N, dtype=torch.float16, device=a.device)
+        return a
+
+    def pack_rows(self, a: torch.Tensor) -> None:
+        """Quantise / copy A's rows into the bucket buffers (first half of gated_linear)."""
+        a = _check_act(a)
+        M, K = a.shape
+        _require(M == self.M, f"routed {self.M} rows but A has {M}")
         with torch.cuda.device(a.device):
-            call("ee_gated_gemm", a.data_ptr(), a.stride(0), M, K, pack.w_i8.data_ptr(), pack.w_e4m3.data_ptr(),
-                 pack.w_f16.data_ptr(), pack.scale.data_ptr(), pack.N, y.data_ptr(), y.stride(0),
-                 self._ws.data_ptr(), self._ws.numel(), _stream())
+            call("ee_gated_pack", a.data_ptr(), a.stride(0), M, K, self._ws.data_ptr(), self._ws.numel(), _stream())
+        self._packed_k = K
+
+    def gemm_packed(self, pack: WeightPack, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Bucketed tcgen05 GEMM over the rows packed by ``pack_rows`` (second half)."""
+        M, K = self.M, pack.K
+        _require(getattr(self, "_packed_k", None) == K, "pack_rows(A) with A of width K must come first")
+        y = out if out is not None else torch.empty(M, pack.N, dtype=torch.float16, device=self._ws.device)
+        with torch.cuda.device(y.device):
+            call("ee_gated_gemm_packed", M, K, pack.w_i8.data_ptr(), pack.w_e4m3.data_ptr(), pack.w_f16.data_ptr(),
+                 pack.scale.data_ptr(), pack.N, y.data_ptr(), y.stride(0), self._ws.data_ptr(), self._ws.numel(),
+                 _stream())
         return y
+
+    def gated_linear(self, a: torch.Tensor, pack: WeightPack, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        a = self._check(a, pack)
+        self.pack_rows(a)
+        return self.gemm_packed(pack, out)
 
 
 def gated_linear(logits: torch.Tensor, a: torch.Tensor, pack: WeightPack, tau_low: float = 0.41,
                  tau_high: float = 1.68):
     """Entropy-gated linear in one call: returns (Y fp16 [M, N], H fp32 [M],
-    route int8 [M], bucket counts int32 [3])."""
+    route int8 [M], bucket counts int32 [3]) -- the last three are copies."""
     r = EntropyRouter(tau_low, tau_high)
     r.reserve(a.shape[0], a.shape[1], a.device)
     r.route(logits)
     y = r.gated_linear(a, pack)
-    return y, r.H, r.route_ids, r.counts
+    return y, r.H.clone(), r.route_ids.clone(), r.counts.clone()
 
 
 class EntropyDispatchedLinear(nn.Module):
