@@ -153,6 +153,24 @@ EE_API int ee_linear_int8(const void* A, int64_t lda, const int8_t* W_nk, const 
 EE_API int ee_linear_fp8(const void* A, int64_t lda, const uint8_t* W_e4m3_nk, const float* w_scale, void* Y, int64_t M,
                   int64_t N, int64_t K, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of ee_linear_int8 (this entry point has no counterpart in
+ * the reference).  Same inputs, output and result; instead of a caller-provided
+ * workspace it keeps the quantised activations and their scales in a fixed block of
+ * device memory compiled into this library (16 MiB + 64 KiB per device, held until
+ * the process exits).  It is for callers that cannot hand out device memory: e.g. a
+ * serving process that reserves all of the GPU's memory for its own pool at start-up
+ * and forbids any further allocation, or a plug-in hosted by another runtime that owns
+ * the allocator and gives the plug-in no way to borrow from it.
+ * Limits: M <= 16384 rows and M * K <= 2^24; larger calls return EE_ERR_UNSUPPORTED
+ * (use ee_linear_int8 then).  The first call on a device looks up the block's device
+ * address (cudaGetSymbolAddress, once per device); make that first call before any
+ * stream capture begins.  All calls share the one block and each call overwrites what
+ * the previous left there (nothing in it needs to start at zero): calls that can
+ * overlap on the GPU -- on different streams, or from different threads -- race on it
+ * and must be serialised by the caller. */
+EE_API int ee_linear_int8_noalloc(const void* A, int64_t lda, const int8_t* W_nk, const float* w_scale, void* Y,
+                                  int64_t M, int64_t N, int64_t K, int64_t ldy, void* stream);
+
 /* ---------------------------------------------------------------- entropy-gated linear
  * The on-device dispatcher: per-row routing of A's rows by the entropy of the
  * matching logits rows, per-row quantisation into three compacted buckets, one

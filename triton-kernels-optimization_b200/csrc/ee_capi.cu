@@ -431,6 +431,69 @@ int ee_linear_fp8(const void* A, int64_t lda, const uint8_t* W_e4m3_nk, const fl
   return linear_8bit(ee::kFP8, A, lda, W_e4m3_nk, w_scale, Y, M, N, K, ldy, workspace, workspace_bytes, stream);
 }
 
+}  // extern "C"
+
+// ------------------------------------------------------------------ allocation-free INT8 linear
+// Scratch of ee_linear_int8_noalloc: a fixed block of device memory that lives in this
+// library's own module, so the entry point never asks for memory at call time.  It
+// holds the per-row activation scales (first 64 KiB, up to 16384 rows) followed by
+// the quantised int8 activations (up to 16 MiB, i.e. M * K <= 2^24).  Every device
+// that loads the library keeps this 16 MiB + 64 KiB block until the process exits.
+static constexpr int64_t kNoAllocMaxRows = 16384;
+static constexpr int64_t kNoAllocMaxQuantBytes = int64_t(1) << 24;
+static constexpr size_t kNoAllocScaleBytes = size_t(kNoAllocMaxRows) * sizeof(float);
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScaleBytes + kNoAllocMaxQuantBytes];
+
+namespace {
+// Device address of g_noalloc_scratch, looked up once per device.  In host code the
+// symbol g_noalloc_scratch is only a host-side handle: its device address has to come
+// from cudaGetSymbolAddress with that device current.
+struct NoAllocSlot {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  void* ptr = nullptr;
+};
+NoAllocSlot g_noalloc_slots[64];
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(EE_ERR_UNSUPPORTED, "device ordinal %d >= 64", dev);
+  NoAllocSlot& slot = g_noalloc_slots[dev];
+  std::call_once(slot.once, [&slot] { slot.err = cudaGetSymbolAddress(&slot.ptr, g_noalloc_scratch); });
+  if (slot.err != cudaSuccess) return cuda_fail(slot.err, "cudaGetSymbolAddress(g_noalloc_scratch)");
+  *out = slot.ptr;
+  return EE_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int ee_linear_int8_noalloc(const void* A, int64_t lda, const int8_t* W_nk, const float* w_scale, void* Y, int64_t M,
+                           int64_t N, int64_t K, int64_t ldy, void* stream) {
+  int st = check_gemm_shape(M, N, K, ldy);
+  if (st != EE_OK) return st;
+  if ((st = check_rows_input(A, M, K, lda)) != EE_OK) return st;
+  if (M > kNoAllocMaxRows || M * K > kNoAllocMaxQuantBytes)
+    return fail(EE_ERR_UNSUPPORTED,
+                "ee_linear_int8_noalloc: M=%lld, K=%lld exceeds its fixed scratch (M <= %lld rows and "
+                "M*K <= %lld bytes); use ee_linear_int8 with a caller-owned workspace",
+                (long long)M, (long long)K, (long long)kNoAllocMaxRows, (long long)kNoAllocMaxQuantBytes);
+  if (M == 0) return EE_OK;
+  if (W_nk == nullptr || w_scale == nullptr || Y == nullptr) return fail(EE_ERR_INVALID, "W, w_scale and Y are required");
+  if (!al16(W_nk) || !al16(Y) || !al16(w_scale)) return fail(EE_ERR_MISALIGNED, "W, w_scale and Y must be 16-byte aligned");
+  void* scratch = nullptr;
+  if ((st = noalloc_scratch(&scratch)) != EE_OK) return st;
+  // Both regions are fully rewritten for rows [0, M) before the GEMM reads them, and
+  // the GEMM's tensor map ends at row M, so nothing has to start at zero.
+  float* sa = static_cast<float*>(scratch);
+  uint8_t* q = static_cast<uint8_t*>(scratch) + kNoAllocScaleBytes;
+  if ((st = pack_rows(A, lda, M, K, nullptr, ee::kINT8, nullptr, sa, q, K, nullptr, 0, as_stream(stream))) != EE_OK)
+    return st;
+  return gemm_single(ee::kINT8, q, sa, W_nk, w_scale, Y, M, N, K, ldy, 0, stream);
+}
+
 // ------------------------------------------------------------------ entropy-gated linear
 size_t ee_gated_workspace_bytes(int64_t M, int64_t K) {
   if (M < 0 || K < 0) return 0;
