@@ -1,0 +1,123 @@
+"""The C ABI without a GPU: the library loads, exports every entry point that
+include/ee_b200.h declares, and rejects bad arguments with the documented status
+codes before touching the device.  CPU only."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "ee_b200.h")
+
+EE_ERR_INVALID, EE_ERR_MISALIGNED, EE_ERR_UNSUPPORTED = -1, -2, -3
+
+
+def _declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"EE_API\s+[\w\s\*]+?\b(ee_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib(pkg):
+    return pkg.load_library()
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert "ee_gated_linear" in names and "ee_softmax_entropy" in names
+    assert len(names) >= 25
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    out = subprocess.run(["nm", "-D", "--defined-only", pkg.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r"\bT (ee_\w+)", out))
+    missing = [n for n in _declared() if n not in exported]
+    assert not missing, missing
+    # nothing else leaks out of the library's C interface
+    assert exported == set(_declared()), sorted(exported - set(_declared()))
+
+
+def test_ctypes_signatures_cover_the_header(pkg):
+    from importlib import import_module
+
+    sigs = import_module("tko_b200._lib").SIGNATURES
+    assert set(sigs) == set(_declared())
+
+
+def test_library_has_no_gpu_driver_dependency(pkg):
+    out = subprocess.run(["ldd", pkg.LIB_PATH], capture_output=True, text=True).stdout
+    assert "libcuda.so" not in out and "libcudart" not in out
+
+
+def test_abi_version(lib):
+    assert lib.ee_abi_version() == 1
+
+
+def _msg(pkg):
+    return pkg._lib.last_error()
+
+
+def test_gemm_argument_checks(pkg, lib):
+    p = ctypes.c_void_p(256)
+    # K not a multiple of 16
+    assert lib.ee_gemm_int8(p, p, p, p, p, 128, 256, 100, 256, None) == EE_ERR_UNSUPPORTED
+    assert "multiple of 16" in _msg(pkg)
+    # N not a multiple of 8
+    assert lib.ee_gemm_fp16(p, p, p, 128, 250, 128, 250, None) == EE_ERR_UNSUPPORTED
+    # ldy smaller than N
+    assert lib.ee_gemm_fp8(p, p, p, p, p, 128, 256, 128, 128, None) == EE_ERR_MISALIGNED
+    # negative M
+    assert lib.ee_gemm_int8(p, p, p, p, p, -1, 256, 128, 256, None) == EE_ERR_INVALID
+    # misaligned operand
+    assert lib.ee_gemm_fp16(ctypes.c_void_p(258), p, p, 128, 256, 128, 256, None) == EE_ERR_MISALIGNED
+    # M == 0 is a no-op
+    assert lib.ee_gemm_int8(p, p, p, p, p, 0, 256, 128, 256, None) == 0
+
+
+def test_workspace_checks(pkg, lib):
+    p = ctypes.c_void_p(256)
+    need = lib.ee_gated_workspace_bytes(1024, 4096)
+    assert need >= 1024 * 4096 * 3
+    st = lib.ee_gated_gemm(p, 4096, 1024, 4096, p, p, p, p, 4096, p, 4096, p, need - 1, None)
+    assert st == EE_ERR_INVALID and "too small" in _msg(pkg)
+    st = lib.ee_gated_gemm(p, 4096, 1024, 4096, p, p, p, p, 4096, p, 4096, ctypes.c_void_p(272), need, None)
+    assert st == EE_ERR_MISALIGNED
+    assert lib.ee_linear_workspace_bytes(-1, 5) == 0
+
+
+def test_workspace_layout_offsets(pkg, lib):
+    off = (ctypes.c_int64 * 8)()
+    assert lib.ee_gated_workspace_layout(1000, 512, off) == 0
+    offs = list(off)
+    assert offs == sorted(offs) and all(o % 256 == 0 for o in offs[1:]) and offs[0] % 16 == 0
+    assert offs[7] - offs[6] >= 1000 * 512
+
+
+def test_softmax_argument_checks(pkg, lib):
+    p = ctypes.c_void_p(256)
+    assert lib.ee_softmax_entropy(p, 4, 0, 0, 0, 1, None, 0, p, None, 0.0, 0.0, None) == EE_ERR_INVALID
+    assert lib.ee_softmax_entropy(p, 4, 8, 8, 1, 0, None, 8, p, None, 0.0, 0.0, None) == EE_ERR_INVALID
+    assert lib.ee_softmax_entropy(None, 4, 8, 8, 0, 1, None, 8, p, None, 0.0, 0.0, None) == EE_ERR_INVALID
+    assert lib.ee_softmax_entropy(p, 0, 8, 8, 0, 1, None, 8, p, None, 0.0, 0.0, None) == 0
+
+
+def test_errors_raise_runtime_error_in_python(pkg):
+    from importlib import import_module
+
+    _lib = import_module("tko_b200._lib")
+    with pytest.raises(RuntimeError, match="EE_ERR_UNSUPPORTED"):
+        _lib.call("ee_gemm_int8", 256, 256, 256, 256, 256, 128, 256, 100, 256, None)
+
+
+def test_calls_without_a_device_fail_cleanly(pkg, lib):
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is visible")
+    # valid arguments reach the CUDA runtime, which reports the missing device
+    p = ctypes.c_void_p(256)
+    st = lib.ee_gemm_fp16(p, p, p, 128, 256, 128, 256, None)
+    assert st == -4

@@ -1,0 +1,102 @@
+"""Multi-rank host logic on CPU (gloo, world size 2): row partitioning of the gated
+path, gathering of the ranks' results, and host-side failure detection of a rank
+that never reaches a step.  No GPU."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import ee_oracle as orc
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _sharding():
+    import sys
+
+    if ROOT not in sys.path:
+        sys.path.insert(0, ROOT)
+    import __graft_entry__ as g
+
+    g.load_package()
+    from importlib import import_module
+
+    return import_module("tko_b200.sharding")
+
+
+def test_row_shard_covers_rows_exactly():
+    sh = _sharding()
+    for total in (0, 1, 7, 4096, 4097):
+        for world in (1, 2, 3, 8):
+            spans = [sh.row_shard(total, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == total
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            sizes = [b - a for a, b in spans]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        sh.row_shard(10, 2, 2)
+
+
+def _worker_gated(rank, world, port, inp, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    sh = _sharding()
+    M = inp["A"].shape[0]
+    a, b = sh.row_shard(M, world, rank)
+    w_kn, w_s = orc.quantize_weights_int8(inp["W"])
+    res = orc.gated_linear(inp["logits"][a:b], inp["A"][a:b], w_kn, w_s, 0.41, 1.68)
+    y = torch.from_numpy(res["Y"].view(np.int16).astype(np.int32))  # gloo has no int16
+    r = torch.from_numpy(res["route"].astype(np.int64))
+    y_all = sh.gather_rows(y, world)
+    r_all = sh.gather_rows(r, world)
+    if rank == 0:
+        np.savez(out_path, Y=y_all.numpy(), route=r_all.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_row_sharded_gated_linear_equals_single_rank(tmp_path):
+    inp = orc.make_gating_inputs(M=37, n=256, K=128, N=64, seed=7)
+    out = str(tmp_path / "gathered.npz")
+    mp.start_processes(_worker_gated, args=(2, _free_port(), inp, out), nprocs=2, start_method="spawn")
+    got = np.load(out)
+    w_kn, w_s = orc.quantize_weights_int8(inp["W"])
+    ref = orc.gated_linear(inp["logits"], inp["A"], w_kn, w_s, 0.41, 1.68)
+    assert np.array_equal(got["route"], ref["route"].astype(np.int64))
+    assert np.array_equal(got["Y"], ref["Y"].view(np.int16).astype(np.int32))
+
+
+def _worker_liveness(rank, world, port, result_path):
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+    sh = _sharding()
+    store = dist.distributed_c10d._get_default_store()
+    sh.check_peers(store, world, rank, "step0", timeout_s=5.0)  # everyone is alive
+    if rank == 1:
+        return  # this rank "dies" between steps: it never reaches step1
+    try:
+        sh.check_peers(store, world, rank, "step1", timeout_s=1.0)
+        msg = "no error"
+    except sh.PeerTimeout as exc:
+        msg = str(exc)
+    with open(result_path, "w") as f:
+        f.write(msg)
+
+
+def test_missing_rank_is_detected_on_the_host(tmp_path):
+    out = str(tmp_path / "liveness.txt")
+    mp.start_processes(_worker_liveness, args=(2, _free_port(), out), nprocs=2, start_method="spawn")
+    msg = open(out).read()
+    assert "ranks [1] did not reach 'step1'" in msg

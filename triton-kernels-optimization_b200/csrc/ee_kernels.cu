@@ -20,13 +20,13 @@ inline unsigned grid_of(int64_t rows, int per_block) {
 
 template <int TPR, int NV>
 int run_softmax_vec(const SoftmaxArgs& a, cudaStream_t s) {
-  softmax_entropy_vec_kernel<TPR, NV><<<grid_of(a.rows, 256 / TPR), 256, 0, s>>>(a);
+  softmax_entropy_vec_kernel<TPR, NV><<<grid_of(a.rows, kRowThreads / TPR), kRowThreads, 0, s>>>(a);
   return status_of(cudaGetLastError());
 }
 
 template <int TPR, int NV>
 int run_pack_vec(const PackArgs& a, cudaStream_t s) {
-  pack_rows_vec_kernel<TPR, NV><<<grid_of(a.M, 256 / TPR), 256, 0, s>>>(a);
+  pack_rows_vec_kernel<TPR, NV><<<grid_of(a.M, kRowThreads / TPR), kRowThreads, 0, s>>>(a);
   return status_of(cudaGetLastError());
 }
 
@@ -39,13 +39,15 @@ int launch_softmax_entropy(const SoftmaxArgs& a, cudaStream_t s) {
                    (a.probs == nullptr || ((a.ldp % 8 == 0) && aligned16(a.probs)));
   if (vec) {
     const int n = a.n;
+    // one warp per row up to 4096 columns (no block-level synchronisation), then 2 / 4
+    // warps per row; 16 x 16-byte loads in flight per thread at the larger widths
     if (n <= 256) return run_softmax_vec<32, 1>(a, s);
     if (n <= 512) return run_softmax_vec<32, 2>(a, s);
     if (n <= 1024) return run_softmax_vec<32, 4>(a, s);
-    if (n <= 2048) return run_softmax_vec<128, 2>(a, s);
-    if (n <= 4096) return run_softmax_vec<256, 2>(a, s);
-    if (n <= 8192) return run_softmax_vec<256, 4>(a, s);
-    if (n <= 16384) return run_softmax_vec<256, 8>(a, s);
+    if (n <= 2048) return run_softmax_vec<32, 8>(a, s);
+    if (n <= 4096) return run_softmax_vec<32, 16>(a, s);
+    if (n <= 8192) return run_softmax_vec<64, 16>(a, s);
+    if (n <= 16384) return run_softmax_vec<128, 16>(a, s);
   }
   softmax_entropy_loop_kernel<<<static_cast<unsigned>(a.rows), 256, 0, s>>>(a);
   return status_of(cudaGetLastError());
@@ -54,11 +56,12 @@ int launch_softmax_entropy(const SoftmaxArgs& a, cudaStream_t s) {
 int launch_pack_rows(const PackArgs& a, cudaStream_t s) {
   if (a.M <= 0) return 0;
   const int K = a.K;
+  if (K <= 512) return run_pack_vec<32, 2>(a, s);
   if (K <= 1024) return run_pack_vec<32, 4>(a, s);
-  if (K <= 2048) return run_pack_vec<64, 4>(a, s);
-  if (K <= 4096) return run_pack_vec<128, 4>(a, s);
-  if (K <= 8192) return run_pack_vec<256, 4>(a, s);
-  if (K <= 16384) return run_pack_vec<256, 8>(a, s);
+  if (K <= 2048) return run_pack_vec<32, 8>(a, s);
+  if (K <= 4096) return run_pack_vec<32, 16>(a, s);
+  if (K <= 8192) return run_pack_vec<64, 16>(a, s);
+  if (K <= 16384) return run_pack_vec<128, 16>(a, s);
   pack_rows_loop_kernel<<<static_cast<unsigned>(a.M), 256, 0, s>>>(a);
   return status_of(cudaGetLastError());
 }

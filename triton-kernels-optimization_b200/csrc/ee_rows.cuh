@@ -97,11 +97,13 @@ __device__ __forceinline__ int8_t route_of(float h, double tl, double th) {
 // ----------------------------------------------------------------------------------
 // stable bucket compaction, run by the last block of a softmax launch to finish
 // (threadfence-reduction pattern).  Positions: bucket INT8 rows first, then FP8, then
-// FP16, each group in increasing row order.
+// FP16, each group in increasing row order.  NT = threads per block (128 or 256).
 // ----------------------------------------------------------------------------------
+template <int NT>
 __device__ void compact_routes_last_block(const SoftmaxArgs& a) {
+  constexpr int PER_LANE = NT / 32;  // scan entries per lane of the scanning warp
   __shared__ int s_last;
-  __shared__ int s_scan[3][256];
+  __shared__ int s_scan[3][NT];
   __shared__ int s_tot[3];
   __threadfence();
   __syncthreads();
@@ -116,7 +118,7 @@ __device__ void compact_routes_last_block(const SoftmaxArgs& a) {
   const int64_t M = a.rows;
   const int tid = threadIdx.x;
   // contiguous chunk per thread, a multiple of 16 routes so it can be read as uint4
-  const int64_t per = ((M + 255) / 256 + 15) / 16 * 16;
+  const int64_t per = ((M + NT - 1) / NT + 15) / 16 * 16;
   const int64_t r0 = tid * per;
   const int64_t r1 = r0 + per < M ? r0 + per : M;
   int cnt[3] = {0, 0, 0};
@@ -140,15 +142,15 @@ __device__ void compact_routes_last_block(const SoftmaxArgs& a) {
   s_scan[1][tid] = cnt[1];
   s_scan[2][tid] = cnt[2];
   __syncthreads();
-  // exclusive scan of each bucket's 256 counts by one warp (8 entries per lane)
+  // exclusive scan of each bucket's NT counts by one warp (PER_LANE entries per lane)
   const int warp = tid >> 5, lane = tid & 31;
   if (warp < 3) {
-    int v[8];
+    int v[PER_LANE];
     int run = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < PER_LANE; ++i) {
       v[i] = run;
-      run += s_scan[warp][lane * 8 + i];
+      run += s_scan[warp][lane * PER_LANE + i];
     }
     int incl = run;
 #pragma unroll
@@ -158,7 +160,7 @@ __device__ void compact_routes_last_block(const SoftmaxArgs& a) {
     }
     const int excl = incl - run;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) s_scan[warp][lane * 8 + i] = v[i] + excl;
+    for (int i = 0; i < PER_LANE; ++i) s_scan[warp][lane * PER_LANE + i] = v[i] + excl;
     if (lane == 31) s_tot[warp] = incl;
   }
   __syncthreads();
@@ -179,63 +181,71 @@ __device__ void compact_routes_last_block(const SoftmaxArgs& a) {
   }
 }
 
+// 8 fp16 of a 16-byte vector -> floats, entries at or beyond `lim` -> -inf
+__device__ __forceinline__ void unpack8_masked(const uint4& u, int e0, int lim, float (&f)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 p = __half22float2(h[k]);
+    f[2 * k] = (e0 + 2 * k < lim) ? p.x : kNegInf;
+    f[2 * k + 1] = (e0 + 2 * k + 1 < lim) ? p.y : kNegInf;
+  }
+}
+
 // ----------------------------------------------------------------------------------
-// softmax + entropy, register-resident rows.  256 threads per block, TPR threads per
-// row, NV 16-byte vectors (8 fp16) per thread: rows up to TPR*NV*8 columns.
-// Requires n % 8 == 0, ldx % 8 == 0, 16-byte aligned base (and the same for probs).
+// softmax + entropy, register-resident rows.  128 threads per block, TPR threads per
+// row (32: one warp per row, shuffles only), NV 16-byte vectors (8 fp16) per thread
+// kept as raw fp16 in registers: rows up to TPR*NV*8 columns.  Requires n % 8 == 0,
+// ldx % 8 == 0 and a 16-byte aligned base (and the same for probs).
 // ----------------------------------------------------------------------------------
+constexpr int kRowThreads = 128;
+
 template <int TPR, int NV>
-__global__ void __launch_bounds__(256) softmax_entropy_vec_kernel(const SoftmaxArgs a) {
-  constexpr int RPB = 256 / TPR;
+__global__ void __launch_bounds__(kRowThreads) softmax_entropy_vec_kernel(const SoftmaxArgs a) {
+  constexpr int RPB = kRowThreads / TPR;
   __shared__ float red[3 * 8];
   const int g = threadIdx.x / TPR, lt = threadIdx.x % TPR;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * RPB + g;
   const bool ok = row < a.rows;
   const int n = a.n;
-  int lim = n;
+  int lim = ok ? n : 0;
   if (a.causal && ok) {
     const int64_t q = row % a.S;
     lim = q + 1 < n ? static_cast<int>(q + 1) : n;
   }
-  float v[NV * 8];
+  uint4 u[NV];
   const __half* xr = static_cast<const __half*>(a.x) + (ok ? row : 0) * a.ldx;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int e0 = (lt + i * TPR) * 8;
-    if (ok && e0 < n) {
-      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(xr + e0));
-      const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float2 f = __half22float2(h[k]);
-        v[i * 8 + 2 * k] = (e0 + 2 * k < lim) ? f.x : kNegInf;
-        v[i * 8 + 2 * k + 1] = (e0 + 2 * k + 1 < lim) ? f.y : kNegInf;
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 8; ++k) v[i * 8 + k] = kNegInf;
-    }
+    u[i] = (e0 < lim) ? __ldcs(reinterpret_cast<const uint4*>(xr + e0)) : make_uint4(0u, 0u, 0u, 0u);
   }
   float m = kNegInf;
 #pragma unroll
-  for (int k = 0; k < NV * 8; ++k) m = fmaxf(m, v[k]);
+  for (int i = 0; i < NV; ++i) {
+    float f[8];
+    unpack8_masked(u[i], (lt + i * TPR) * 8, lim, f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m = fmaxf(m, f[k]);
+  }
   m = group_max<TPR>(m, red);
 
   float z = 0.f, c = 0.f, t = 0.f;
 #pragma unroll
-  for (int k = 0; k < NV * 8; ++k) {
-    const float xk = v[k];
-    if (xk == m) {
-      c += 1.f;
-      v[k] = 1.f;
-    } else if (xk > kNegInf) {
-      const float d = xk - m;
-      const float e = __expf(d);
-      z += e;
-      t += e * d;
-      v[k] = e;
-    } else {
-      v[k] = 0.f;
+  for (int i = 0; i < NV; ++i) {
+    float f[8];
+    unpack8_masked(u[i], (lt + i * TPR) * 8, lim, f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float xk = f[k];
+      if (xk == m) {
+        c += 1.f;
+      } else if (xk > kNegInf) {
+        const float d = xk - m;
+        const float e = __expf(d);
+        z += e;
+        t += e * d;
+      }
     }
   }
   group_sum3<TPR>(z, c, t, red);
@@ -251,15 +261,21 @@ __global__ void __launch_bounds__(256) softmax_entropy_vec_kernel(const SoftmaxA
     for (int i = 0; i < NV; ++i) {
       const int e0 = (lt + i * TPR) * 8;
       if (e0 < n) {
-        uint4 u;
-        __half2* h2 = reinterpret_cast<__half2*>(&u);
+        float f[8];
+        unpack8_masked(u[i], e0, lim, f);
+        uint4 o;
+        __half2* h2 = reinterpret_cast<__half2*>(&o);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) h2[k] = __floats2half2_rn(v[i * 8 + 2 * k] * inv, v[i * 8 + 2 * k + 1] * inv);
-        __stcs(reinterpret_cast<uint4*>(pr + e0), u);
+        for (int k = 0; k < 4; ++k) {
+          const float p0 = (f[2 * k] > kNegInf) ? __expf(f[2 * k] - m) * inv : 0.f;
+          const float p1 = (f[2 * k + 1] > kNegInf) ? __expf(f[2 * k + 1] - m) * inv : 0.f;
+          h2[k] = __floats2half2_rn(p0, p1);
+        }
+        __stcs(reinterpret_cast<uint4*>(pr + e0), o);
       }
     }
   }
-  if (a.perm != nullptr) compact_routes_last_block(a);
+  if (a.perm != nullptr) compact_routes_last_block<kRowThreads>(a);
 }
 
 // Online softmax statistics (see entropy_from_stats) for the streaming path.
@@ -346,7 +362,7 @@ __global__ void __launch_bounds__(256) softmax_entropy_loop_kernel(const Softmax
       pr[j] = __float2half_rn(e * inv);
     }
   }
-  if (a.perm != nullptr) compact_routes_last_block(a);
+  if (a.perm != nullptr) compact_routes_last_block<256>(a);
 }
 
 // ----------------------------------------------------------------------------------
@@ -415,29 +431,28 @@ __device__ __forceinline__ float absmax8(const uint4& u, float m) {
 }
 
 template <int TPR, int NV>
-__global__ void __launch_bounds__(256) pack_rows_vec_kernel(const PackArgs a) {
-  constexpr int RPB = 256 / TPR;
+__global__ void __launch_bounds__(kRowThreads) pack_rows_vec_kernel(const PackArgs a) {
+  constexpr int RPB = kRowThreads / TPR;
   __shared__ float red[8];
   const int g = threadIdx.x / TPR, lt = threadIdx.x % TPR;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * RPB + g;
   const bool ok = row < a.M;
-  const int K = a.K;
+  const int K = ok ? a.K : 0;
   const int b = ok ? (a.route ? static_cast<int>(a.route[row]) : a.fixed_bucket) : kFP16;
   const int64_t pos = ok ? (a.slot ? static_cast<int64_t>(a.slot[row]) : row) : 0;
   const __half* ar = static_cast<const __half*>(a.A) + (ok ? row : 0) * a.lda;
   uint4 u[NV];
-  float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int e0 = (lt + i * TPR) * 8;
-    if (ok && e0 < K) {
-      u[i] = __ldcs(reinterpret_cast<const uint4*>(ar + e0));
-      amax = absmax8(u[i], amax);
-    } else {
-      u[i] = make_uint4(0u, 0u, 0u, 0u);
-    }
+    u[i] = (e0 < K) ? __ldcs(reinterpret_cast<const uint4*>(ar + e0)) : make_uint4(0u, 0u, 0u, 0u);
   }
-  amax = group_max<TPR>(amax, red);
+  float amax = 0.f;
+  if (b != kFP16) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) amax = absmax8(u[i], amax);
+  }
+  amax = group_max<TPR>(amax, red);  // reached by every thread (may hold __syncthreads)
   if (!ok) return;
   if (b == kFP16) {
     __half* dst = static_cast<__half*>(a.buf16) + pos * a.ld16;
@@ -450,10 +465,18 @@ __global__ void __launch_bounds__(256) pack_rows_vec_kernel(const PackArgs a) {
   }
   const RowScale rs = row_scale(amax, b);
   uint8_t* dst = a.buf8 + pos * a.ld8;
+  if (b == kINT8) {
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int e0 = (lt + i * TPR) * 8;
-    if (e0 < K) *reinterpret_cast<uint2*>(dst + e0) = (b == kINT8) ? quant8_int8(u[i], rs.s) : quant8_e4m3(u[i], rs.inv);
+    for (int i = 0; i < NV; ++i) {
+      const int e0 = (lt + i * TPR) * 8;
+      if (e0 < K) *reinterpret_cast<uint2*>(dst + e0) = quant8_int8(u[i], rs.s);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int e0 = (lt + i * TPR) * 8;
+      if (e0 < K) *reinterpret_cast<uint2*>(dst + e0) = quant8_e4m3(u[i], rs.inv);
+    }
   }
   if (lt == 0) a.sa[pos] = rs.s;
 }
