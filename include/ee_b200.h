@@ -209,6 +209,47 @@ EE_API int ee_gated_linear(const void* logits, int64_t n, int64_t ld_logits, con
                     int32_t* bucket_counts, void* Y, int64_t ldy, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/* ---------------------------------------------------------------- gated layer loop (engine)
+ * The reference runs its layer loop in Python with a host synchronisation per layer
+ * (EE/python/dispatch.py:192-203, EE/python/quality_eval.py:133-141) and launches
+ * one cubin at a time from C++ (EE/csrc/engine.cpp:64-200).  The engine takes a fixed
+ * description of L gated layers -- per layer the routing logits and P projections,
+ * every buffer at a fixed device address owned by the caller -- and enqueues the
+ * whole loop with no host round trip: eagerly (ee_engine_run) or as a CUDA graph
+ * recorded once and replayed (ee_engine_capture / ee_engine_launch).  Layers run in
+ * order on one stream and share one workspace (ee_engine_workspace_bytes). */
+typedef struct ee_engine ee_engine;
+
+typedef struct ee_projection {
+  int64_t K, N;
+  const void* A;           /* fp16 [rows, K] input, row stride lda */
+  int64_t lda;
+  const int8_t* w_i8_nk;   /* the three packs of ee_pack_weights and the weight scale */
+  const uint8_t* w_e4m3_nk;
+  const void* w_f16_nk;
+  const float* w_scale;
+  void* Y;                 /* fp16 [rows, N] output, row stride ldy */
+  int64_t ldy;
+} ee_projection;
+
+typedef struct ee_gated_layer {
+  const void* logits;      /* fp16 [rows, n_logits], row stride ld_logits: routes this layer's rows */
+  int64_t n_logits, ld_logits;
+  int32_t n_proj;
+  const ee_projection* proj;
+} ee_gated_layer;
+
+EE_API size_t ee_engine_workspace_bytes(int64_t rows, int32_t n_layers, const ee_gated_layer* layers);
+/* Copies the descriptions; the buffers they point to must outlive the engine. */
+EE_API int ee_engine_create(int64_t rows, double tau_low, double tau_high, int32_t n_layers,
+                            const ee_gated_layer* layers, void* workspace, size_t workspace_bytes, ee_engine** out);
+EE_API int ee_engine_run(ee_engine* engine, void* stream);
+/* Records the loop into a CUDA graph; stream must be a created (non-default) stream. */
+EE_API int ee_engine_capture(ee_engine* engine, void* stream);
+/* Replays the recorded graph (records it first if needed). */
+EE_API int ee_engine_launch(ee_engine* engine, void* stream);
+EE_API int ee_engine_destroy(ee_engine* engine);
+
 #ifdef __cplusplus
 }
 #endif

@@ -18,6 +18,7 @@ from .dispatch import (
     gated_linear,
     tier_of,
 )
+from .engine import CubinEngine, GatedLayerEngine
 from .kernels import (
     WeightPack,
     fused_softmax_entropy,

@@ -174,6 +174,7 @@ LinearWs linear_ws(void* ws, int64_t M) {
 struct GatedWs {
   uint32_t* ticket;
   int32_t* counts;
+  uint32_t* sched;  // GEMM tile scheduler words (zeroed by ee_gate_rows, left zero by the GEMM)
   int32_t* perm;
   int32_t* slot;
   int8_t* route;
@@ -191,6 +192,7 @@ GatedWs gated_ws(void* ws, int64_t M, int64_t K) {
   GatedWs w;
   w.ticket = reinterpret_cast<uint32_t*>(p);
   w.counts = reinterpret_cast<int32_t*>(p + 16);
+  w.sched = reinterpret_cast<uint32_t*>(p + 64);
   p += 256;
   w.perm = reinterpret_cast<int32_t*>(p);
   p += align256(sizeof(int32_t) * M);
@@ -242,6 +244,10 @@ int check_rows_input(const void* A, int64_t M, int64_t K, int64_t lda) {
 }
 
 }  // namespace
+
+namespace ee {
+void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+}  // namespace ee
 
 extern "C" {
 
@@ -510,7 +516,7 @@ int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double ta
   if (reinterpret_cast<uintptr_t>(logits) & 1u) return fail(EE_ERR_MISALIGNED, "logits must be 2-byte aligned");
   cudaStream_t s = as_stream(stream);
   GatedWs w = gated_ws(workspace, M, 0);
-  cudaError_t e = cudaMemsetAsync(workspace, 0, 32, s);  // ticket + counts
+  cudaError_t e = cudaMemsetAsync(workspace, 0, 128, s);  // ticket, counts, GEMM tile scheduler
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
   if (M > 0) {
     ee::SoftmaxArgs a;
@@ -591,6 +597,7 @@ int ee_gated_gemm_packed(int64_t M, int64_t K, const int8_t* W_i8_nk, const uint
   args.perm = w.perm;
   args.sa = w.sa;
   args.sb = w_scale;
+  args.sched = w.sched;
   return run_gemm(op, args, true, as_stream(stream));
 }
 

@@ -105,6 +105,74 @@ __device__ __forceinline__ void mma_stage(uint32_t d_tmem, uint32_t a_addr, uint
   }
 }
 
+// ---------------------------------------------------------------------------------
+// tile feed.  Static mode: tiles blockIdx.x, blockIdx.x + gridDim.x, ...  Dynamic mode
+// (args.sched != nullptr): the producer warp claims the next tile from a global counter
+// and publishes it through a ring of kTileRing shared-memory slots; the MMA warp and the
+// four epilogue warps read the same sequence from the ring.  Claiming in tile order
+// (FP16 tiles first) gives longest-first list scheduling across the SMs.
+// ---------------------------------------------------------------------------------
+constexpr int kTileRing = 4;
+constexpr uint32_t kRingConsumers = 5;  // MMA warp + 4 epilogue warps
+
+struct Feed {
+  uint32_t slot, phase;
+  int next;  // static mode
+};
+
+// producer side; returns the tile (>= total: no more work) or -1 if a wait gave up
+__device__ __forceinline__ int feed_produce(Feed& f, bool dyn, int* ring, uint64_t* ring_full, uint64_t* ring_empty,
+                                            uint32_t* counter, int lane, const volatile int* abort) {
+  if (!dyn) {
+    const int t = f.next;
+    f.next += gridDim.x;
+    return t;
+  }
+  if (!mbar_wait(&ring_empty[f.slot], f.phase ^ 1u, abort)) return -1;
+  int t = 0;
+  if (lane == 0) {
+    t = static_cast<int>(atomicAdd(counter, 1u));
+    ring[f.slot] = t;
+    mbar_arrive(&ring_full[f.slot]);
+  }
+  t = __shfl_sync(0xffffffffu, t, 0);
+  if (++f.slot == kTileRing) {
+    f.slot = 0;
+    f.phase ^= 1u;
+  }
+  return t;
+}
+
+// consumer side (whole warp); lane 0 releases the slot
+__device__ __forceinline__ int feed_consume(Feed& f, bool dyn, const int* ring, uint64_t* ring_full,
+                                            uint64_t* ring_empty, int lane, const volatile int* abort) {
+  if (!dyn) {
+    const int t = f.next;
+    f.next += gridDim.x;
+    return t;
+  }
+  if (!mbar_wait(&ring_full[f.slot], f.phase, abort)) return -1;
+  const int t = *reinterpret_cast<const volatile int*>(&ring[f.slot]);
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&ring_empty[f.slot]);
+  if (++f.slot == kTileRing) {
+    f.slot = 0;
+    f.phase ^= 1u;
+  }
+  return t;
+}
+
+// the last CTA to leave resets the scheduler words for the next launch
+__device__ __forceinline__ void feed_retire(const GemmArgs& args) {
+  if (args.sched == nullptr || threadIdx.x != 0) return;
+  __threadfence();
+  const uint32_t prev = atomicAdd(&args.sched[1], 1u);
+  if (prev == gridDim.x - 1) {
+    atomicExch(&args.sched[0], 0u);
+    atomicExch(&args.sched[1], 0u);
+  }
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gated_gemm_kernel(const __grid_constant__ CUtensorMap tm_a8, const __grid_constant__ CUtensorMap tm_a16,
                       const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
@@ -114,17 +182,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * kAStageBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kStages * kBStageBytes);
-  uint64_t* full = bars;                  // [kStages] TMA -> MMA
-  uint64_t* empty = bars + kStages;       // [kStages] MMA -> TMA
-  uint64_t* acc_full = bars + 2 * kStages;     // [2] MMA -> epilogue
-  uint64_t* acc_empty = acc_full + 2;          // [2] epilogue -> MMA
-  uint64_t* drain = acc_empty + 2;             // MMA drain on abort
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* full = bars;                         // [kStages] TMA -> MMA
+  uint64_t* empty = bars + kStages;              // [kStages] MMA -> TMA
+  uint64_t* acc_full = bars + 2 * kStages;       // [2] MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;            // [2] epilogue -> MMA
+  uint64_t* drain = acc_empty + 2;               // MMA drain on abort
+  uint64_t* ring_full = drain + 1;               // [kTileRing] producer -> consumers
+  uint64_t* ring_empty = ring_full + kTileRing;  // [kTileRing] consumers -> producer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring_empty + kTileRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* ring = const_cast<int*>(abort_flag + 1);  // [kTileRing] tile indices
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const TileGeo geo = make_geo(args);
-  if (static_cast<int>(blockIdx.x) >= geo.total) return;  // uniform for the whole CTA
+  const bool dyn = args.sched != nullptr;
+  if (static_cast<int>(blockIdx.x) >= geo.total) {  // uniform for the whole CTA
+    feed_retire(args);
+    return;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -136,6 +211,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&acc_empty[i], 4);  // one arrive per epilogue warp
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < kTileRing; ++i) {
+      mbar_init(&ring_full[i], 1);
+      mbar_init(&ring_empty[i], kRingConsumers);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -156,12 +235,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int K = args.K;
+  Feed feed{0u, 0u, static_cast<int>(blockIdx.x)};
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     uint32_t stage = 0, phase = 0;
     uint32_t issued_mask = 0, issued_parity = 0;  // per stage: load in flight, its phase parity
     bool failed = false;
-    for (int t = blockIdx.x; t < geo.total && !failed; t += gridDim.x) {
+    for (;;) {
+      const int t = feed_produce(feed, dyn, ring, ring_full, ring_empty, args.sched, lane, abort_flag);
+      if (t < 0) {
+        failed = true;
+        break;
+      }
+      if (t >= geo.total) break;
       int pos0, n0;
       const int b = decode_tile(geo, t, pos0, n0);
       const int nkb = kblocks_of(b, K);
@@ -186,6 +272,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           phase ^= 1u;
         }
       }
+      if (failed) break;
     }
     if (failed) {
       if (lane == 0) {
@@ -200,7 +287,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     uint32_t stage = 0, phase = 0, ab = 0, aphase = 0;
     bool failed = false;
-    for (int t = blockIdx.x; t < geo.total && !failed; t += gridDim.x) {
+    for (;;) {
+      const int t = feed_consume(feed, dyn, ring, ring_full, ring_empty, lane, abort_flag);
+      if (t < 0) {
+        failed = true;
+        break;
+      }
+      if (t >= geo.total) break;
       int pos0, n0;
       const int b = decode_tile(geo, t, pos0, n0);
       const int nkb = kblocks_of(b, K);
@@ -252,10 +345,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------------ epilogue (warps 2..5)
     const int quarter = warp & 3;  // TMEM lanes this warp may access: 32*quarter ..
     uint32_t ab = 0, aphase = 0;
-    for (int t = blockIdx.x; t < geo.total; t += gridDim.x) {
-      int pos0, n0;
-      const int b = decode_tile(geo, t, pos0, n0);
-      if (!mbar_wait(&acc_full[ab], aphase, abort_flag)) {
+    for (;;) {
+      const int t = feed_consume(feed, dyn, ring, ring_full, ring_empty, lane, abort_flag);
+      bool failed = t < 0;
+      if (!failed && t >= geo.total) break;
+      int pos0 = 0, n0 = 0;
+      const int b = failed ? 0 : decode_tile(geo, t, pos0, n0);
+      if (!failed && !mbar_wait(&acc_full[ab], aphase, abort_flag)) failed = true;
+      if (failed) {
         if (lane == 0) {
           atomicOr(&g_device_error, kErrWaitTimeout);
           *abort_flag = 1;
@@ -333,6 +430,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+  feed_retire(args);
 }
 
 }  // namespace ee

@@ -83,6 +83,8 @@ struct GemmArgs {
   void* Y;                 // fp16 [rows, N] (out_mode 0) or 32-bit [rows, N] (out_mode 1)
   int64_t ldy;             // elements
   int out_mode;            // 0: dequantised fp16, 1: raw accumulators (int32 / fp32)
+  uint32_t* sched;         // nullable: [0] next tile, [1] CTAs done -- zero at launch, left zero;
+                           // null = static round-robin tile order
 };
 struct GemmMaps {
   CUtensorMap a8;          // uint8 [M_cap, K], box {128, 128}
@@ -94,5 +96,12 @@ size_t gemm_smem_bytes();
 
 // device error word
 int read_and_clear_device_error(int* value);
+
+// one-time per-device set-up of kernel attributes (safe to call repeatedly); lets a
+// caller finish it before a stream capture starts
+int prepare_device();
+
+// sets the text ee_last_error() returns on the calling thread
+void set_last_error(const char* msg);
 
 }  // namespace ee

@@ -39,14 +39,14 @@ int launch_softmax_entropy(const SoftmaxArgs& a, cudaStream_t s) {
                    (a.probs == nullptr || ((a.ldp % 8 == 0) && aligned16(a.probs)));
   if (vec) {
     const int n = a.n;
-    // one warp per row up to 4096 columns (no block-level synchronisation), then 2 / 4
-    // warps per row; 16 x 16-byte loads in flight per thread at the larger widths
+    // one warp per row up to 2048 columns (no block-level synchronisation), then 2 / 4
+    // warps per row so every thread keeps at most 8 vectors (64 fp16) in registers
     if (n <= 256) return run_softmax_vec<32, 1>(a, s);
     if (n <= 512) return run_softmax_vec<32, 2>(a, s);
     if (n <= 1024) return run_softmax_vec<32, 4>(a, s);
     if (n <= 2048) return run_softmax_vec<32, 8>(a, s);
-    if (n <= 4096) return run_softmax_vec<32, 16>(a, s);
-    if (n <= 8192) return run_softmax_vec<64, 16>(a, s);
+    if (n <= 4096) return run_softmax_vec<64, 8>(a, s);
+    if (n <= 8192) return run_softmax_vec<128, 8>(a, s);
     if (n <= 16384) return run_softmax_vec<128, 16>(a, s);
   }
   softmax_entropy_loop_kernel<<<static_cast<unsigned>(a.rows), 256, 0, s>>>(a);
@@ -59,8 +59,8 @@ int launch_pack_rows(const PackArgs& a, cudaStream_t s) {
   if (K <= 512) return run_pack_vec<32, 2>(a, s);
   if (K <= 1024) return run_pack_vec<32, 4>(a, s);
   if (K <= 2048) return run_pack_vec<32, 8>(a, s);
-  if (K <= 4096) return run_pack_vec<32, 16>(a, s);
-  if (K <= 8192) return run_pack_vec<64, 16>(a, s);
+  if (K <= 4096) return run_pack_vec<64, 8>(a, s);
+  if (K <= 8192) return run_pack_vec<128, 8>(a, s);
   if (K <= 16384) return run_pack_vec<128, 16>(a, s);
   pack_rows_loop_kernel<<<static_cast<unsigned>(a.M), 256, 0, s>>>(a);
   return status_of(cudaGetLastError());
@@ -102,16 +102,20 @@ int launch_route(const float* H, int64_t rows, double tl, double th, int8_t* rou
 
 size_t gemm_smem_bytes() { return kGemmSmem; }
 
-int launch_gated_gemm(const GemmMaps& m, const GemmArgs& args, int grid, cudaStream_t s) {
+int prepare_device() {
   static std::once_flag attr_once[64];
+  static cudaError_t attr_err[64];
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return -4;
-  cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once[dev & 63], [&] {
-    attr_err = cudaFuncSetAttribute(gated_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(kGemmSmem));
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -4;
+  std::call_once(attr_once[dev], [dev] {
+    attr_err[dev] = cudaFuncSetAttribute(gated_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kGemmSmem));
   });
-  if (attr_err != cudaSuccess) return -4;
+  return attr_err[dev] == cudaSuccess ? 0 : -4;
+}
+
+int launch_gated_gemm(const GemmMaps& m, const GemmArgs& args, int grid, cudaStream_t s) {
+  if (prepare_device() != 0) return -4;
   if (grid <= 0) return 0;
   gated_gemm_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(m.a8, m.a16, m.w[0], m.w[1], m.w[2], args);
   return status_of(cudaGetLastError());
