@@ -356,8 +356,16 @@ def main(argv=None) -> int:
     counts = router.counts.cpu().tolist()
     mix = {"INT8": counts[0], "FP8": counts[1], "FP16": counts[2]}
 
+    # the timed step is the C++ engine's CUDA graph of the same launches (one host call)
+    engine = pkg.GatedLayerEngine([(logits, [(acts[p], packs[p], ys[p]) for p in range(n_proj)])], *TAU)
+    engine.capture()
+    for _ in range(max(args.warmup, 3)):
+        flush()
+        engine.launch()
+    torch.cuda.synchronize()
+
     E = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
-    evs = [[E() for _ in range(2 + 2 * n_proj)] for _ in range(args.steps)]
+    step_evs = [(E(), E()) for _ in range(args.steps)]
     sampler = ClockSampler(range(world)) if rank == 0 else None
     barrier()
     torch.cuda.synchronize()
@@ -366,20 +374,32 @@ def main(argv=None) -> int:
         time.sleep(0.3)
     for k in range(args.steps):
         flush()  # between steps, outside the step's events
-        step(evs[k])
+        step_evs[k][0].record()
+        engine.launch()
+        step_evs[k][1].record()
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop() if sampler else None
     pkg._lib.device_check()
-
-    step_ms = [ev[0].elapsed_time(ev[-1]) for ev in evs]
-    gate_ms = [ev[0].elapsed_time(ev[1]) for ev in evs]
-    gemm_ms = [[ev[2 + 2 * p].elapsed_time(ev[3 + 2 * p]) for p in range(n_proj)] for ev in evs]
-    total_ms = sum(step_ms)
+    total_ms = sum(a.elapsed_time(b) for a, b in step_evs)
     if world > 1:
         t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
+
+    # per-kernel breakdown: eager launches bracketed by events; a GPU-side sleep before
+    # each step lets the host enqueue the whole step first, so no launch latency leaks in
+    n_instr = min(args.steps, 50)
+    evs = [[E() for _ in range(2 + 2 * n_proj)] for _ in range(n_instr)]
+    for k in range(n_instr):
+        flush()
+        torch.cuda._sleep(4_000_000)
+        step(evs[k])
+    torch.cuda.synchronize()
+    gate_ms = [ev[0].elapsed_time(ev[1]) for ev in evs]
+    pack_ms = [[ev[1 + 2 * p if p == 0 else 3 + 2 * (p - 1)].elapsed_time(ev[2 + 2 * p]) for p in range(n_proj)]
+               for ev in evs]
+    gemm_ms = [[ev[2 + 2 * p].elapsed_time(ev[3 + 2 * p]) for p in range(n_proj)] for ev in evs]
 
     # ------------------------------------------------------------------ e2e (public API, host buffers)
     e2e = None
@@ -433,14 +453,14 @@ def main(argv=None) -> int:
         f_tot = sum(f_b)
         peak_eff = f_tot / sum(f / p for f, p in zip(f_b, p_b))
         gemm_total_ms = sum(sum(x) for x in gemm_ms)
-        achieved = f_tot * args.steps / (gemm_total_ms / 1e3) / 1e12
+        achieved = f_tot * n_instr / (gemm_total_ms / 1e3) / 1e12
         traffic = None
         tpath = os.path.join(ROOT, "profiles", "gemm_traffic.json")
         if os.path.exists(tpath):
             with open(tpath) as f:
                 traffic = json.load(f).get("dram_bytes_per_launch")
         gate_bytes = 2.0 * M * N_LOGIT + 4 * M + M
-        gate_gbs = gate_bytes * args.steps / (sum(gate_ms) / 1e3) / 1e9
+        gate_gbs = gate_bytes * n_instr / (sum(gate_ms) / 1e3) / 1e9
         value = world * step_flops(M) * args.steps / (total_ms / 1e3) / 1e12
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -453,8 +473,14 @@ def main(argv=None) -> int:
                                 "bytes_per_launch": gate_bytes,
                                 "note": "route kernel incl. compaction; algorithmic bytes 2Mn + 4M + M"},
             "per_projection_tflops": {
-                name: 2.0 * M * K * N * args.steps / (sum(g[p] for g in gemm_ms) / 1e3) / 1e12
+                name: 2.0 * M * K * N * n_instr / (sum(g[p] for g in gemm_ms) / 1e3) / 1e12
                 for p, (name, K, N) in enumerate(PROJECTIONS)},
+            "per_kernel_us": {
+                "softmax_entropy_route": 1e3 * sum(gate_ms) / n_instr,
+                **{f"pack_{name}": 1e3 * sum(x[p] for x in pack_ms) / n_instr for p, (name, _, _) in enumerate(PROJECTIONS)},
+                **{f"gemm_{name}": 1e3 * sum(x[p] for x in gemm_ms) / n_instr for p, (name, _, _) in enumerate(PROJECTIONS)},
+                "note": f"eager launches, {n_instr} steps, events around each kernel"},
+            "timing": "value / ms_per_step: CUDA-graph replays of the step (GatedLayerEngine), events around each replay",
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_eff, "unit": "TFLOP/s",
                          "frac": achieved / peak_eff, "traffic": traffic,
                          "kernel": "gated_gemm_kernel (3 launches per step, one per projection)",

@@ -62,6 +62,12 @@ extern "C" {
 EE_API int ee_abi_version(void);
 EE_API const char* ee_last_error(void);
 
+/* GEMM tiling policy for every later call in the process (no counterpart in the
+ * reference): 0 = automatic (CTA-pair 256 x 256 tiles when a call has more than 128
+ * rows, else single-CTA 128 x 256 tiles), 1 = always single-CTA, 2 = always CTA pairs.
+ * Results are identical under every policy. */
+EE_API int ee_set_gemm_policy(int policy);
+
 /* Reads and clears the current device's error word (set by a kernel whose bounded
  * wait gave up).  Synchronous.  EE_OK if clear, EE_ERR_DEVICE otherwise; *value
  * (nullable) receives the word. */

@@ -1,0 +1,54 @@
+"""Both GEMM kernels -- single-CTA 128 x 256 tiles and CTA-pair (tcgen05 cta_group::2)
+256 x 256 tiles -- forced through ee_set_gemm_policy: exact int32 accumulators, fp32
+accumulators, and the gated linear per bucket against the reference formulas."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from test_gpu_gated import _inputs, _ref_fp8, _ref_fp16, _ref_int8, _relf  # noqa: E402
+
+
+@pytest.fixture(params=[1, 2], ids=["single_cta", "cta_pair"])
+def policy(request, pkg, cuda):
+    lib = pkg.load_library()
+    assert lib.ee_set_gemm_policy(request.param) == 0
+    yield request.param
+    assert lib.ee_set_gemm_policy(0) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (300, 264, 1040), (1024, 4096, 4096), (257, 512, 2048)])
+def test_accumulators(pkg, cuda, policy, M, N, K):
+    g = torch.Generator().manual_seed(M + N + K + policy)
+    a = torch.randint(-128, 128, (M, K), generator=g, dtype=torch.int32).to(torch.int8).to(cuda)
+    w = torch.randint(-128, 128, (N, K), generator=g, dtype=torch.int32).to(torch.int8).to(cuda)
+    acc = pkg.gemm_accumulators("int8", a, w)
+    assert torch.equal(acc.to(torch.int64), (a.double() @ w.double().T).round().to(torch.int64))
+    a16 = torch.randn(M, K, generator=g).half().to(cuda)
+    w16 = (torch.randn(N, K, generator=g) * 0.02).half().to(cuda)
+    acc = pkg.gemm_accumulators("fp16", a16, w16)
+    ref = a16.double() @ w16.double().T
+    assert ((acc.double() - ref).norm() / ref.norm()) < 1e-5
+    a8 = a16.to(torch.float8_e4m3fn).view(torch.uint8)
+    w8 = (w16 * 40).to(torch.float8_e4m3fn).view(torch.uint8)
+    acc = pkg.gemm_accumulators("fp8", a8, w8)
+    ref = a8.view(torch.float8_e4m3fn).double() @ w8.view(torch.float8_e4m3fn).double().T
+    assert ((acc.double() - ref).norm() / ref.norm()) < 1e-5
+    torch.cuda.synchronize()
+    assert pkg._lib.device_check() == 0
+
+
+@pytest.mark.parametrize("M,n,K,N", [(1024, 4096, 4096, 4096), (333, 256, 1024, 264), (4096, 4096, 1024, 1536)])
+def test_gated_linear(pkg, cuda, policy, M, n, K, N):
+    logits, a, w = _inputs(M, n, K, N, 5 * M + n + policy, cuda)
+    p = pkg.WeightPack(*pkg.quantize_weights_int8(w))
+    y, H, route, counts = pkg.gated_linear(logits, a, p, 0.41, 1.68)
+    torch.cuda.synchronize()
+    assert pkg._lib.device_check() == 0
+    rows = [torch.nonzero(route == b).flatten() for b in range(3)]
+    if rows[0].numel():
+        assert torch.equal(y[rows[0]].view(torch.int16), _ref_int8(a[rows[0]], p).view(torch.int16))
+    if rows[1].numel():
+        assert _relf(y[rows[1]], _ref_fp8(a[rows[1]], p)) < 1e-2
+    if rows[2].numel():
+        assert _relf(y[rows[2]], _ref_fp16(a[rows[2]], p)) < 1e-2

@@ -5,6 +5,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -106,9 +107,15 @@ int check_gemm_shape(int64_t M, int64_t N, int64_t K, int64_t ldy) {
   return EE_OK;
 }
 
-// Encodes the maps for the operands present and launches the persistent kernel.
-// Unused slots get a copy of a valid map (they are never dereferenced).
+std::atomic<int> g_gemm_policy{0};  // 0 auto, 1 single-CTA tiles, 2 CTA-pair tiles
+
+// Encodes the maps for the operands present and launches the persistent kernel: the
+// CTA-pair kernel (256-row tiles) when the problem has more than 128 rows, else the
+// single-CTA kernel.  Unused slots get a copy of a valid map (never dereferenced).
 int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cudaStream_t s) {
+  const int policy = g_gemm_policy.load(std::memory_order_relaxed);
+  const bool pair = policy == 2 || (policy == 0 && args.M_cap > ee::kBM);
+  const int wbox = pair ? ee::kBN / 2 : ee::kBN;
   ee::GemmMaps maps;
   std::memset(&maps, 0, sizeof(maps));
   const CUtensorMap* any = nullptr;
@@ -124,7 +131,7 @@ int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cud
   for (int b = 0; b < 3; ++b) {
     if (op.w[b]) {
       const int eb = (b == ee::kFP16) ? 2 : 1;
-      if ((st = encode_kmajor(&maps.w[b], op.w[b], args.N, args.K, args.K, eb, ee::kBN)) != EE_OK) return st;
+      if ((st = encode_kmajor(&maps.w[b], op.w[b], args.N, args.K, args.K, eb, wbox)) != EE_OK) return st;
     }
   }
   if (any == nullptr) return fail(EE_ERR_INVALID, "GEMM without an A operand");
@@ -134,12 +141,18 @@ int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cud
     if (!op.w[b]) maps.w[b] = op.w[0] ? maps.w[0] : (op.w[1] ? maps.w[1] : maps.w[2]);
 
   const int64_t ntn = (args.N + ee::kBN - 1) / ee::kBN;
+  const int64_t bm = pair ? ee::kPairTileRows : ee::kBM;
   int64_t tiles;
   if (dynamic_counts) {
-    tiles = ((args.M_cap + ee::kBM - 1) / ee::kBM + 2) * ntn;  // bucket boundaries add <= 2 row tiles
+    tiles = ((args.M_cap + bm - 1) / bm + 2) * ntn;  // bucket boundaries add <= 2 row tiles
   } else {
     tiles = 0;
-    for (int b = 0; b < 3; ++b) tiles += ((args.counts[b] + ee::kBM - 1) / ee::kBM) * ntn;
+    for (int b = 0; b < 3; ++b) tiles += ((args.counts[b] + bm - 1) / bm) * ntn;
+  }
+  if (pair) {
+    const int64_t max_pairs = num_sms() / 2;
+    const int pairs = static_cast<int>(tiles < max_pairs ? tiles : max_pairs);
+    return check_launch(ee::launch_gated_gemm_pair(maps, args, pairs, s), "gated_gemm_pair_kernel");
   }
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
   return check_launch(ee::launch_gated_gemm(maps, args, grid, s), "gated_gemm_kernel");
@@ -236,7 +249,7 @@ int pack_rows(const void* A, int64_t lda, int64_t M, int64_t K, const int8_t* ro
 }
 
 int check_rows_input(const void* A, int64_t M, int64_t K, int64_t lda) {
-  if (A == nullptr) return fail(EE_ERR_INVALID, "A is NULL");
+  if (A == nullptr && M != 0) return fail(EE_ERR_INVALID, "A is NULL");  // M == 0: an empty batch, no pointers needed
   if (M < 0 || K <= 0 || M > kMaxDim || K > kMaxDim) return fail(EE_ERR_INVALID, "bad shape M=%lld K=%lld", (long long)M, (long long)K);
   if (K % 8 != 0 || lda < K || lda % 8 != 0 || !al16(A))
     return fail(EE_ERR_MISALIGNED, "A needs K %% 8 == 0, lda %% 8 == 0 (lda >= K) and a 16-byte aligned base");
@@ -252,6 +265,12 @@ void set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
 extern "C" {
 
 int ee_abi_version(void) { return EE_ABI_VERSION; }
+
+int ee_set_gemm_policy(int policy) {
+  if (policy < 0 || policy > 2) return fail(EE_ERR_INVALID, "policy must be 0 (auto), 1 (single-CTA) or 2 (CTA pair)");
+  g_gemm_policy.store(policy, std::memory_order_relaxed);
+  return EE_OK;
+}
 
 const char* ee_last_error(void) { return g_last_error.c_str(); }
 

@@ -43,7 +43,7 @@ struct TileGeo {
   int ntn, total;
 };
 
-__device__ __forceinline__ TileGeo make_geo(const GemmArgs& a) {
+__device__ __forceinline__ TileGeo make_geo(const GemmArgs& a, int bm) {
   TileGeo g;
   if (a.dyn_counts != nullptr) {
 #pragma unroll
@@ -59,27 +59,29 @@ __device__ __forceinline__ TileGeo make_geo(const GemmArgs& a) {
   g.total = 0;
 #pragma unroll
   for (int b = 0; b < 3; ++b) {
-    g.mtiles[b] = (g.cnt[b] + kBM - 1) / kBM;
+    g.mtiles[b] = (g.cnt[b] + bm - 1) / bm;
     g.tiles[b] = g.mtiles[b] * g.ntn;
     g.total += g.tiles[b];
   }
   return g;
 }
 
-// tile index -> bucket, first position (row of A), first output column
-__device__ __forceinline__ int decode_tile(const TileGeo& g, int t, int& pos0, int& n0) {
-#pragma unroll
-  for (int i = 0; i < 3; ++i) {
-    const int b = 2 - i;
-    if (t < g.tiles[b]) {
-      const int mt = t % g.mtiles[b];
-      const int nt = t / g.mtiles[b];
-      pos0 = g.off[b] + mt * kBM;
-      n0 = nt * kBN;
-      return b;
-    }
-    t -= g.tiles[b];
-  }
+// tile index -> bucket, first position (row of A), first output column.  Tiles run
+// FP16 first (the longest K loops), then FP8, then INT8; m fastest inside a bucket.
+// Written out per bucket: a loop with an early return here kept TileGeo on the stack.
+__device__ __forceinline__ int decode_in(const TileGeo& g, int b, int t, int bm, int& pos0, int& n0) {
+  const int mt = t % g.mtiles[b];
+  const int nt = t / g.mtiles[b];
+  pos0 = g.off[b] + mt * bm;
+  n0 = nt * kBN;
+  return b;
+}
+__device__ __forceinline__ int decode_tile(const TileGeo& g, int t, int bm, int& pos0, int& n0) {
+  if (t < g.tiles[2]) return decode_in(g, 2, t, bm, pos0, n0);
+  t -= g.tiles[2];
+  if (t < g.tiles[1]) return decode_in(g, 1, t, bm, pos0, n0);
+  t -= g.tiles[1];
+  if (t < g.tiles[0]) return decode_in(g, 0, t, bm, pos0, n0);
   pos0 = 0;
   n0 = 0;
   return 0;
@@ -102,6 +104,72 @@ __device__ __forceinline__ void mma_stage(uint32_t d_tmem, uint32_t a_addr, uint
   for (int k = 0; k < kBKBytes / 32; ++k) {
     // advancing the start address by 32 bytes = 2 in the descriptor's 16-byte units
     tc_mma<KIND>(d_tmem, da + 2u * k, db + 2u * k, idesc, (first && k == 0) ? 0u : 1u);
+  }
+}
+
+// Drains one 32-lane quarter of a 128 x 256 accumulator from TMEM (taddr: its lanes,
+// first column), applies the bucket's epilogue and stores the valid rows.  `pos` is
+// this thread's row position; the whole warp must call it (tcgen05.ld is .sync.aligned).
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const TileGeo& geo, int b, int pos, int n0,
+                                              uint32_t taddr) {
+  // end of bucket b's positions, by selects: a runtime index into TileGeo would move
+  // the whole struct to the stack
+  const int end = (b == 0) ? geo.cnt[0] : (b == 1) ? geo.off[1] + geo.cnt[1] : geo.off[2] + geo.cnt[2];
+  const bool valid = pos < end;
+  const int64_t orow = valid ? (args.perm ? static_cast<int64_t>(args.perm[pos]) : static_cast<int64_t>(pos)) : 0;
+  const float sa = (valid && b != kFP16 && args.out_mode == 0) ? args.sa[pos] : 1.f;
+#pragma unroll 1
+  for (int c = 0; c < kBN / 32; ++c) {
+    uint32_t r[32];
+    __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
+    tmem_ld32(taddr + c * 32, r);
+    tmem_ld_wait(r);
+    const int nc = n0 + c * 32;
+    if (!valid || nc >= args.N) continue;
+    if (args.out_mode == 1) {
+      uint32_t* y = static_cast<uint32_t*>(args.Y) + orow * args.ldy + nc;
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        if (nc + 4 * g < args.N) *reinterpret_cast<uint4*>(y + 4 * g) = make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
+      continue;
+    }
+    float f[32];
+    if (b == kFP16) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+    } else {
+      float sbv[32];
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        if (nc + 4 * g < args.N) {
+          const float4 q = __ldg(reinterpret_cast<const float4*>(args.sb + nc + 4 * g));
+          sbv[4 * g] = q.x;
+          sbv[4 * g + 1] = q.y;
+          sbv[4 * g + 2] = q.z;
+          sbv[4 * g + 3] = q.w;
+        } else {
+          sbv[4 * g] = sbv[4 * g + 1] = sbv[4 * g + 2] = sbv[4 * g + 3] = 0.f;
+        }
+      }
+      if (b == kINT8) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j])), sa), sbv[j]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__fmul_rn(__uint_as_float(r[j]), sa), sbv[j]);
+      }
+    }
+    __half* y = static_cast<__half*>(args.Y) + orow * args.ldy + nc;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      if (nc + 8 * g < args.N) {
+        uint4 u;
+        __half2* h2 = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) h2[k] = __floats2half2_rn(f[8 * g + 2 * k], f[8 * g + 2 * k + 1]);
+        *reinterpret_cast<uint4*>(y + 8 * g) = u;
+      }
+    }
   }
 }
 
@@ -194,7 +262,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int* ring = const_cast<int*>(abort_flag + 1);  // [kTileRing] tile indices
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const TileGeo geo = make_geo(args);
+  const TileGeo geo = make_geo(args, kBM);
   const bool dyn = args.sched != nullptr;
   if (static_cast<int>(blockIdx.x) >= geo.total) {  // uniform for the whole CTA
     feed_retire(args);
@@ -249,7 +317,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (t >= geo.total) break;
       int pos0, n0;
-      const int b = decode_tile(geo, t, pos0, n0);
+      const int b = decode_tile(geo, t, kBM, pos0, n0);
       const int nkb = kblocks_of(b, K);
       const int kstep = (b == kFP16) ? kBKBytes / 2 : kBKBytes;
       const CUtensorMap* ta = (b == kFP16) ? &tm_a16 : &tm_a8;
@@ -295,7 +363,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (t >= geo.total) break;
       int pos0, n0;
-      const int b = decode_tile(geo, t, pos0, n0);
+      const int b = decode_tile(geo, t, kBM, pos0, n0);
       const int nkb = kblocks_of(b, K);
       if (!mbar_wait(&acc_empty[ab], aphase ^ 1u, abort_flag)) {
         failed = true;
@@ -350,7 +418,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool failed = t < 0;
       if (!failed && t >= geo.total) break;
       int pos0 = 0, n0 = 0;
-      const int b = failed ? 0 : decode_tile(geo, t, pos0, n0);
+      const int b = failed ? 0 : decode_tile(geo, t, kBM, pos0, n0);
       if (!failed && !mbar_wait(&acc_full[ab], aphase, abort_flag)) failed = true;
       if (failed) {
         if (lane == 0) {
@@ -360,64 +428,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      const int pos = pos0 + quarter * 32 + lane;
-      const bool valid = pos < geo.off[b] + geo.cnt[b];
-      const int64_t orow = valid ? (args.perm ? static_cast<int64_t>(args.perm[pos]) : static_cast<int64_t>(pos)) : 0;
-      const float sa = (valid && b != kFP16 && args.out_mode == 0) ? args.sa[pos] : 1.f;
-      const uint32_t taddr = tmem_base + ab * kBN + (static_cast<uint32_t>(quarter * 32) << 16);
-#pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
-        tmem_ld32(taddr + c * 32, r);
-        tmem_ld_wait(r);
-        const int nc = n0 + c * 32;
-        if (!valid || nc >= args.N) continue;
-        if (args.out_mode == 1) {
-          uint32_t* y = static_cast<uint32_t*>(args.Y) + orow * args.ldy + nc;
-#pragma unroll
-          for (int g = 0; g < 8; ++g)
-            if (nc + 4 * g < args.N) *reinterpret_cast<uint4*>(y + 4 * g) = make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
-          continue;
-        }
-        float f[32];
-        if (b == kFP16) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
-        } else {
-          float sbv[32];
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            if (nc + 4 * g < args.N) {
-              const float4 q = __ldg(reinterpret_cast<const float4*>(args.sb + nc + 4 * g));
-              sbv[4 * g] = q.x;
-              sbv[4 * g + 1] = q.y;
-              sbv[4 * g + 2] = q.z;
-              sbv[4 * g + 3] = q.w;
-            } else {
-              sbv[4 * g] = sbv[4 * g + 1] = sbv[4 * g + 2] = sbv[4 * g + 3] = 0.f;
-            }
-          }
-          if (b == kINT8) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j])), sa), sbv[j]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__fmul_rn(__uint_as_float(r[j]), sa), sbv[j]);
-          }
-        }
-        __half* y = static_cast<__half*>(args.Y) + orow * args.ldy + nc;
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          if (nc + 8 * g < args.N) {
-            uint4 u;
-            __half2* h2 = reinterpret_cast<__half2*>(&u);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) h2[k] = __floats2half2_rn(f[8 * g + 2 * k], f[8 * g + 2 * k + 1]);
-            *reinterpret_cast<uint4*>(y + 8 * g) = u;
-          }
-        }
-      }
+      epilogue_tile(args, geo, b, pos0 + quarter * 32 + lane, n0,
+                    tmem_base + ab * kBN + (static_cast<uint32_t>(quarter * 32) << 16));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
@@ -431,6 +443,325 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
   feed_retire(args);
+}
+
+// ---------------------------------------------------------------------------------
+// CTA-pair variant (tcgen05 cta_group::2).  A cluster of two CTAs on neighbouring SMs
+// computes a 256 x 256 tile: each CTA stages 128 rows of A and 128 rows of B (half of
+// the tile's output columns) per 128-byte K stage, the leader CTA issues M=256 x N=256
+// UMMAs that read both CTAs' stages, and each CTA's TMEM holds its own 128 x 256 half
+// of the accumulator.  Per FLOP every CTA moves a third less operand data than the
+// single-CTA 128 x 256 tile, and the smaller stages allow a 6-deep ring.
+//   full[s]      leader only: both CTAs' TMA bytes of stage s (leader arms 64 KB)
+//   empty[s]     both CTAs: the leader's commit frees stage s in both (multicast commit)
+//   acc_full[i]  both CTAs: accumulator i is complete (multicast commit)
+//   acc_empty[i] leader only: 8 arrivals, the four epilogue warps of each CTA
+// Tiles are dealt statically (pair p takes p, p + pairs, ...) or, when the call carries
+// scheduler words, claimed dynamically by each pair's leader (pair_feed_publish).
+// ---------------------------------------------------------------------------------
+
+// tile feed of a CTA pair: static (pair p: p, p + pairs, ...) or dynamic -- the leader's
+// producer claims a tile and publishes it into the tile ring of both CTAs (its own by a
+// local store, the peer's through distributed shared memory, each followed by an arrive
+// on that CTA's ring_full); the five consumers of each CTA (MMA issuer or the peer's
+// producer, four epilogue warps) release the slot on the leader's ring_empty.
+struct PairFeed {
+  uint32_t slot, phase;
+  int next;
+};
+
+__device__ __forceinline__ int pair_feed_publish(PairFeed& f, bool dyn, int* ring, uint64_t* ring_full,
+                                                 uint64_t* ring_empty, uint32_t* counter, int npairs, int lane,
+                                                 const volatile int* abort) {
+  if (!dyn) {
+    const int t = f.next;
+    f.next += npairs;
+    return t;
+  }
+  if (!mbar_wait<true>(&ring_empty[f.slot], f.phase ^ 1u, abort)) return -1;
+  int t = 0;
+  if (lane == 0) {
+    t = static_cast<int>(atomicAdd(counter, 1u));
+    ring[f.slot] = t;
+    mbar_arrive(&ring_full[f.slot]);
+    st_shared_cluster_u32(map_to_cta(smem_u32(&ring[f.slot]), 1), static_cast<uint32_t>(t));
+    mbar_arrive_cluster(map_to_cta(smem_u32(&ring_full[f.slot]), 1));
+  }
+  t = __shfl_sync(0xffffffffu, t, 0);
+  if (++f.slot == kTileRing) {
+    f.slot = 0;
+    f.phase ^= 1u;
+  }
+  return t;
+}
+
+__device__ __forceinline__ int pair_feed_consume(PairFeed& f, bool dyn, const int* ring, uint64_t* ring_full,
+                                                 uint64_t* ring_empty, int npairs, int lane,
+                                                 const volatile int* abort) {
+  if (!dyn) {
+    const int t = f.next;
+    f.next += npairs;
+    return t;
+  }
+  if (!mbar_wait<true>(&ring_full[f.slot], f.phase, abort)) return -1;
+  const int t = *reinterpret_cast<const volatile int*>(&ring[f.slot]);
+  __syncwarp();
+  if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_u32(&ring_empty[f.slot]), 0));
+  if (++f.slot == kTileRing) {
+    f.slot = 0;
+    f.phase ^= 1u;
+  }
+  return t;
+}
+
+// leader CTAs count themselves out; the last one resets the scheduler words
+__device__ __forceinline__ void feed_retire_pair(const GemmArgs& args, int npairs) {
+  if (args.sched == nullptr || threadIdx.x != 0) return;
+  __threadfence();
+  const uint32_t prev = atomicAdd(&args.sched[1], 1u);
+  if (prev == static_cast<uint32_t>(npairs) - 1) {
+    atomicExch(&args.sched[0], 0u);
+    atomicExch(&args.sched[1], 0u);
+  }
+}
+
+constexpr int kPairRows = 256;
+constexpr int kStagesPair = 6;
+constexpr int kHalfStageBytes = 128 * kBKBytes;  // 16 KB: one operand half of one CTA
+constexpr int kStageBytesPair = 2 * kHalfStageBytes;
+constexpr size_t kGemmSmemPair = 1024 + size_t(kStagesPair) * kStageBytesPair + kBarrierBytes;
+
+template <int KIND>
+__device__ __forceinline__ void mma_stage_pair(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr, bool first) {
+  constexpr uint32_t idesc = (KIND == kKindI8)   ? make_idesc(2u, 1u, kPairRows, kBN)
+                             : (KIND == kKindF8) ? make_idesc(1u, 0u, kPairRows, kBN)
+                                                 : make_idesc(1u, 0u, kPairRows, kBN);
+  const uint64_t da = sdesc_k_sw128(a_addr);
+  const uint64_t db = sdesc_k_sw128(b_addr);
+#pragma unroll
+  for (int k = 0; k < kBKBytes / 32; ++k)
+    tc_mma_pair<KIND>(d_tmem, da + 2u * k, db + 2u * k, idesc, (first && k == 0) ? 0u : 1u);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gated_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a8, const __grid_constant__ CUtensorMap tm_a16,
+                           const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
+                           const __grid_constant__ CUtensorMap tm_w2, const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStagesPair * kHalfStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kStagesPair * kHalfStageBytes);
+  uint64_t* full = bars;                        // [kStagesPair]
+  uint64_t* empty = bars + kStagesPair;         // [kStagesPair]
+  uint64_t* acc_full = bars + 2 * kStagesPair;  // [2]
+  uint64_t* acc_empty = acc_full + 2;           // [2]
+  uint64_t* drain = acc_empty + 2;
+  uint64_t* ring_full = drain + 1;               // [kTileRing] both CTAs: tile published
+  uint64_t* ring_empty = ring_full + kTileRing;  // [kTileRing] leader: 10 consumers released the slot
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring_empty + kTileRing);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* ring = const_cast<int*>(abort_flag + 1);  // [kTileRing]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  const TileGeo geo = make_geo(args, kPairRows);
+  const bool dyn = args.sched != nullptr;
+  if (pair >= geo.total) {  // the same decision in both CTAs of the pair
+    if (leader) feed_retire_pair(args, npairs);
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStagesPair; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);  // 4 epilogue warps x 2 CTAs
+    }
+    mbar_init(drain, 1);
+    for (int i = 0; i < kTileRing; ++i) {
+      mbar_init(&ring_full[i], 1);
+      mbar_init(&ring_empty[i], 2 * kRingConsumers);  // MMA / producer + 4 epilogue warps, x 2 CTAs
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a8);
+    tma_prefetch_desc(&tm_a16);
+    tma_prefetch_desc(&tm_w0);
+    tma_prefetch_desc(&tm_w1);
+    tma_prefetch_desc(&tm_w2);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int K = args.K;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    uint32_t stage = 0, phase = 0;
+    uint32_t issued_mask = 0, issued_parity = 0;
+    bool failed = false;
+    PairFeed feed{0u, 0u, pair};
+    for (;;) {
+      const int t = leader ? pair_feed_publish(feed, dyn, ring, ring_full, ring_empty, args.sched, npairs, lane, abort_flag)
+                           : pair_feed_consume(feed, dyn, ring, ring_full, ring_empty, npairs, lane, abort_flag);
+      if (t < 0) {
+        failed = true;
+        break;
+      }
+      if (t >= geo.total) break;
+      int pos0, n0;
+      const int b = decode_tile(geo, t, kPairRows, pos0, n0);
+      const int nkb = kblocks_of(b, K);
+      const int kstep = (b == kFP16) ? kBKBytes / 2 : kBKBytes;
+      const CUtensorMap* ta = (b == kFP16) ? &tm_a16 : &tm_a8;
+      const CUtensorMap* tw = (b == kINT8) ? &tm_w0 : (b == kFP8 ? &tm_w1 : &tm_w2);
+      const int arow = pos0 + static_cast<int>(rank) * 128;
+      const int brow = n0 + static_cast<int>(rank) * (kBN / 2);
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+          failed = true;
+          break;
+        }
+        if (lane == 0) {
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytesPair);
+          const uint32_t bar = map_to_cta(smem_u32(&full[stage]), 0);
+          tma_load_2d_pair(sA + stage * kHalfStageBytes, ta, bar, kb * kstep, arow);
+          tma_load_2d_pair(sB + stage * kHalfStageBytes, tw, bar, kb * kstep, brow);
+        }
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        __syncwarp();
+        if (++stage == kStagesPair) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (failed) break;
+    }
+    if (failed) {
+      if (lane == 0) {
+        atomicOr(&g_device_error, kErrWaitTimeout);
+        *abort_flag = 1;
+      }
+      if (leader)
+        for (int s = 0; s < kStagesPair; ++s)
+          if (issued_mask & (1u << s)) (void)mbar_wait(&full[s], (issued_parity >> s) & 1u, nullptr);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA)
+    if (leader) {
+      uint32_t stage = 0, phase = 0, ab = 0, aphase = 0;
+      bool failed = false;
+      PairFeed feed{0u, 0u, pair};
+      for (;;) {
+        const int t = pair_feed_consume(feed, dyn, ring, ring_full, ring_empty, npairs, lane, abort_flag);
+        if (t < 0) {
+          failed = true;
+          break;
+        }
+        if (t >= geo.total) break;
+        int pos0, n0;
+        const int b = decode_tile(geo, t, kPairRows, pos0, n0);
+        const int nkb = kblocks_of(b, K);
+        if (!mbar_wait<true>(&acc_empty[ab], aphase ^ 1u, abort_flag)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + ab * kBN;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            failed = true;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t a_addr = smem_u32(sA + stage * kHalfStageBytes);
+            const uint32_t b_addr = smem_u32(sB + stage * kHalfStageBytes);
+            if (b == kINT8)
+              mma_stage_pair<kKindI8>(d_tmem, a_addr, b_addr, kb == 0);
+            else if (b == kFP8)
+              mma_stage_pair<kKindF8>(d_tmem, a_addr, b_addr, kb == 0);
+            else
+              mma_stage_pair<kKindF16>(d_tmem, a_addr, b_addr, kb == 0);
+            tc_commit_pair_both(&empty[stage], 0x3);
+          }
+          __syncwarp();
+          if (++stage == kStagesPair) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (failed) break;
+        if (lane == 0) tc_commit_pair_both(&acc_full[ab], 0x3);
+        __syncwarp();
+        ab ^= 1u;
+        if (ab == 0) aphase ^= 1u;
+      }
+      if (failed) {
+        if (lane == 0) {
+          atomicOr(&g_device_error, kErrWaitTimeout);
+          *abort_flag = 1;
+          tc_commit_pair_local(drain);
+        }
+        __syncwarp();
+        (void)mbar_wait(drain, 0u, nullptr);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    uint32_t ab = 0, aphase = 0;
+    const uint32_t leader_acc_empty0 = map_to_cta(smem_u32(&acc_empty[0]), 0);
+    PairFeed feed{0u, 0u, pair};
+    for (;;) {
+      const int t = pair_feed_consume(feed, dyn, ring, ring_full, ring_empty, npairs, lane, abort_flag);
+      if (t < 0) {
+        if (lane == 0) {
+          atomicOr(&g_device_error, kErrWaitTimeout);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      if (t >= geo.total) break;
+      int pos0, n0;
+      const int b = decode_tile(geo, t, kPairRows, pos0, n0);
+      if (!mbar_wait(&acc_full[ab], aphase, abort_flag)) {
+        if (lane == 0) {
+          atomicOr(&g_device_error, kErrWaitTimeout);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      tc_fence_after();
+      epilogue_tile(args, geo, b, pos0 + static_cast<int>(rank) * 128 + quarter * 32 + lane, n0,
+                    tmem_base + ab * kBN + (static_cast<uint32_t>(quarter * 32) << 16));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(leader_acc_empty0 + ab * static_cast<uint32_t>(sizeof(uint64_t)));
+      ab ^= 1u;
+      if (ab == 0) aphase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal it or read its stages
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
+  if (leader) feed_retire_pair(args, npairs);
 }
 
 }  // namespace ee

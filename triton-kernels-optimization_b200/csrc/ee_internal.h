@@ -92,6 +92,9 @@ struct GemmMaps {
   CUtensorMap w[3];        // bucket weights [N, K] K-major, box {128 B, 256}
 };
 int launch_gated_gemm(const GemmMaps& maps, const GemmArgs& args, int grid, cudaStream_t s);
+// CTA-pair kernel: 256-row tiles; grid = 2 x pairs; the A / W maps use 128-row boxes
+int launch_gated_gemm_pair(const GemmMaps& maps, const GemmArgs& args, int pairs, cudaStream_t s);
+constexpr int kPairTileRows = 256;
 size_t gemm_smem_bytes();
 
 // device error word

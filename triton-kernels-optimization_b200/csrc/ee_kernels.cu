@@ -20,7 +20,11 @@ inline unsigned grid_of(int64_t rows, int per_block) {
 
 template <int TPR, int NV>
 int run_softmax_vec(const SoftmaxArgs& a, cudaStream_t s) {
-  softmax_entropy_vec_kernel<TPR, NV><<<grid_of(a.rows, kRowThreads / TPR), kRowThreads, 0, s>>>(a);
+  const unsigned grid = grid_of(a.rows, kRowThreads / TPR);
+  if (a.causal || a.probs != nullptr)
+    softmax_entropy_vec_kernel<TPR, NV, true><<<grid, kRowThreads, 0, s>>>(a);
+  else
+    softmax_entropy_vec_kernel<TPR, NV, false><<<grid, kRowThreads, 0, s>>>(a);
   return status_of(cudaGetLastError());
 }
 
@@ -33,21 +37,34 @@ int run_pack_vec(const PackArgs& a, cudaStream_t s) {
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 }  // namespace
 
+int sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cache[dev] = v;
+  }
+  return cache[dev];
+}
+
 int launch_softmax_entropy(const SoftmaxArgs& a, cudaStream_t s) {
   if (a.rows <= 0) return 0;
   const bool vec = (a.n % 8 == 0) && (a.ldx % 8 == 0) && aligned16(a.x) &&
                    (a.probs == nullptr || ((a.ldp % 8 == 0) && aligned16(a.probs)));
   if (vec) {
+    // one warp per row up to 1024 columns (no block-level synchronisation), then 2 / 4 / 8
+    // warps per row so every thread keeps at most 8 vectors (64 fp16) in registers (a
+    // sweep of these shapes on B200: 2 warps x 8 vectors was fastest at 4096 columns)
     const int n = a.n;
-    // one warp per row up to 2048 columns (no block-level synchronisation), then 2 / 4
-    // warps per row so every thread keeps at most 8 vectors (64 fp16) in registers
     if (n <= 256) return run_softmax_vec<32, 1>(a, s);
     if (n <= 512) return run_softmax_vec<32, 2>(a, s);
     if (n <= 1024) return run_softmax_vec<32, 4>(a, s);
-    if (n <= 2048) return run_softmax_vec<32, 8>(a, s);
+    if (n <= 2048) return run_softmax_vec<64, 4>(a, s);
     if (n <= 4096) return run_softmax_vec<64, 8>(a, s);
     if (n <= 8192) return run_softmax_vec<128, 8>(a, s);
-    if (n <= 16384) return run_softmax_vec<128, 16>(a, s);
+    if (n <= 16384) return run_softmax_vec<256, 8>(a, s);
   }
   softmax_entropy_loop_kernel<<<static_cast<unsigned>(a.rows), 256, 0, s>>>(a);
   return status_of(cudaGetLastError());
@@ -56,12 +73,13 @@ int launch_softmax_entropy(const SoftmaxArgs& a, cudaStream_t s) {
 int launch_pack_rows(const PackArgs& a, cudaStream_t s) {
   if (a.M <= 0) return 0;
   const int K = a.K;
+
   if (K <= 512) return run_pack_vec<32, 2>(a, s);
   if (K <= 1024) return run_pack_vec<32, 4>(a, s);
-  if (K <= 2048) return run_pack_vec<32, 8>(a, s);
+  if (K <= 2048) return run_pack_vec<64, 4>(a, s);
   if (K <= 4096) return run_pack_vec<64, 8>(a, s);
   if (K <= 8192) return run_pack_vec<128, 8>(a, s);
-  if (K <= 16384) return run_pack_vec<128, 16>(a, s);
+  if (K <= 16384) return run_pack_vec<256, 8>(a, s);
   pack_rows_loop_kernel<<<static_cast<unsigned>(a.M), 256, 0, s>>>(a);
   return status_of(cudaGetLastError());
 }
@@ -110,8 +128,18 @@ int prepare_device() {
   std::call_once(attr_once[dev], [dev] {
     attr_err[dev] = cudaFuncSetAttribute(gated_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kGemmSmem));
+    if (attr_err[dev] == cudaSuccess)
+      attr_err[dev] = cudaFuncSetAttribute(gated_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(kGemmSmemPair));
   });
   return attr_err[dev] == cudaSuccess ? 0 : -4;
+}
+
+int launch_gated_gemm_pair(const GemmMaps& m, const GemmArgs& args, int pairs, cudaStream_t s) {
+  if (prepare_device() != 0) return -4;
+  if (pairs <= 0) return 0;
+  gated_gemm_pair_kernel<<<2 * pairs, kGemmThreads, kGemmSmemPair, s>>>(m.a8, m.a16, m.w[0], m.w[1], m.w[2], args);
+  return status_of(cudaGetLastError());
 }
 
 int launch_gated_gemm(const GemmMaps& m, const GemmArgs& args, int grid, cudaStream_t s) {

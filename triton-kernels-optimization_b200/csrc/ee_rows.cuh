@@ -99,8 +99,11 @@ __device__ __forceinline__ int8_t route_of(float h, double tl, double th) {
 // (threadfence-reduction pattern).  Positions: bucket INT8 rows first, then FP8, then
 // FP16, each group in increasing row order.  NT = threads per block (128 or 256).
 // ----------------------------------------------------------------------------------
+// Scalar arguments, never a reference to the kernel's parameter struct: a reference
+// would make every caller keep a copy of that struct on its stack.
 template <int NT>
-__device__ void compact_routes_last_block(const SoftmaxArgs& a) {
+__device__ __noinline__ void compact_routes_last_block(const int8_t* route, int64_t M, int32_t* perm,
+                                                       int32_t* slot, int32_t* counts, unsigned* ticket) {
   constexpr int PER_LANE = NT / 32;  // scan entries per lane of the scanning warp
   __shared__ int s_last;
   __shared__ int s_scan[3][NT];
@@ -108,14 +111,13 @@ __device__ void compact_routes_last_block(const SoftmaxArgs& a) {
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(a.ticket, 1u);
+    const unsigned prev = atomicAdd(ticket, 1u);
     s_last = (prev == gridDim.x - 1) ? 1 : 0;
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
 
-  const int64_t M = a.rows;
   const int tid = threadIdx.x;
   // contiguous chunk per thread, a multiple of 16 routes so it can be read as uint4
   const int64_t per = ((M + NT - 1) / NT + 15) / 16 * 16;
@@ -124,7 +126,7 @@ __device__ void compact_routes_last_block(const SoftmaxArgs& a) {
   int cnt[3] = {0, 0, 0};
   for (int64_t r = r0; r < r1; r += 16) {
     if (r + 16 <= r1) {
-      const uint4 u = __ldcg(reinterpret_cast<const uint4*>(a.route + r));
+      const uint4 u = __ldcg(reinterpret_cast<const uint4*>(route + r));
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -135,7 +137,12 @@ __device__ void compact_routes_last_block(const SoftmaxArgs& a) {
         cnt[0] += 4 - ones - twos;
       }
     } else {
-      for (int64_t q = r; q < r1; ++q) cnt[*(const volatile int8_t*)(a.route + q)]++;
+      for (int64_t q = r; q < r1; ++q) {
+        const int b = __ldcg(route + q);
+        cnt[0] += b == 0;
+        cnt[1] += b == 1;
+        cnt[2] += b == 2;
+      }
     }
   }
   s_scan[0][tid] = cnt[0];
@@ -164,20 +171,33 @@ __device__ void compact_routes_last_block(const SoftmaxArgs& a) {
     if (lane == 31) s_tot[warp] = incl;
   }
   __syncthreads();
-  const int off[3] = {0, s_tot[0], s_tot[0] + s_tot[1]};
-  int pos[3] = {off[0] + s_scan[0][tid], off[1] + s_scan[1][tid], off[2] + s_scan[2][tid]};
-  for (int64_t r = r0; r < r1; ++r) {
-    const int b = *(const volatile int8_t*)(a.route + r);
-    const int p = pos[b]++;
-    a.perm[p] = static_cast<int32_t>(r);
-    a.slot[r] = p;
+  int pos0 = s_scan[0][tid], pos1 = s_tot[0] + s_scan[1][tid], pos2 = s_tot[0] + s_tot[1] + s_scan[2][tid];
+  // scatter: the routes come back 16 at a time in one vector load (they were read just
+  // above, so these hit in L2), never one dependent byte load per row
+  for (int64_t r = r0; r < r1; r += 16) {
+    int8_t rb[16];
+    if (r + 16 <= r1) {
+      *reinterpret_cast<uint4*>(rb) = __ldcg(reinterpret_cast<const uint4*>(route + r));
+    } else {
+      for (int q = 0; q < 16; ++q) rb[q] = (r + q < r1) ? __ldcg(route + r + q) : int8_t(0);
+    }
+    const int lim = r + 16 <= r1 ? 16 : static_cast<int>(r1 - r);
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      if (q < lim) {
+        const int b = rb[q];
+        const int p = b == 0 ? pos0++ : (b == 1 ? pos1++ : pos2++);
+        perm[p] = static_cast<int32_t>(r + q);
+        slot[r + q] = p;
+      }
+    }
   }
   if (tid == 0) {
-    a.counts[0] = s_tot[0];
-    a.counts[1] = s_tot[1];
-    a.counts[2] = s_tot[2];
-    a.counts[3] = 0;
-    *a.ticket = 0u;  // ready for the next launch
+    counts[0] = s_tot[0];
+    counts[1] = s_tot[1];
+    counts[2] = s_tot[2];
+    counts[3] = 0;
+    *ticket = 0u;  // ready for the next launch
   }
 }
 
@@ -193,15 +213,103 @@ __device__ __forceinline__ void unpack8_masked(const uint4& u, int e0, int lim, 
 }
 
 // ----------------------------------------------------------------------------------
+// per-vector helpers of the register-resident row kernels (128 threads per block)
+// ----------------------------------------------------------------------------------
+constexpr int kRowThreads = 256;
+
+// max over the valid entries of one 16-byte vector (all 8 valid: packed fp16 max)
+__device__ __forceinline__ float vec_max(const uint4& u, int e0, int lim) {
+  if (e0 + 8 <= lim) {
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+    const __half2 mx = __hmax2(__hmax2(h[0], h[1]), __hmax2(h[2], h[3]));
+    return fmaxf(__low2float(mx), __high2float(mx));
+  }
+  float f[8];
+  unpack8_masked(u, e0, lim, f);
+  float m = kNegInf;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) m = fmaxf(m, f[k]);
+  return m;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 p = __half22float2(h[k]);
+    f[2 * k] = p.x;
+    f[2 * k + 1] = p.y;
+  }
+}
+
+// 2^x on the special-function unit (PTX ex2.approx, relative error ~2^-22)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// masked vector (causal boundary / padding) or the vector holding the row max: kept
+// out of line, it is rare.  Arguments and result by value (registers): references here would put the caller's
+// register-resident row vectors on the stack.
+__device__ __noinline__ float3 vec_stats_masked(uint4 u, int e0, int lim, float m) {
+  float z = 0.f, c = 0.f, t2 = 0.f;
+  float f[8];
+  unpack8_masked(u, e0, lim, f);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const bool valid = f[k] > kNegInf;
+    const float d2 = valid ? (f[k] - m) * kLog2e : 0.f;
+    const float e = valid ? ex2_approx(d2) : 0.f;
+    if (valid && d2 == 0.f) {
+      c += 1.f;
+    } else {
+      z += e;
+    }
+    t2 = fmaf(e, d2, t2);
+  }
+  return make_float3(z, c, t2);
+}
+
+// Entropy statistics of one vector, accumulated in base-2 units: with
+// d2 = (x - m) * log2(e), e = 2^d2, the row needs z = sum e and t2 = sum e * d2
+// (t = t2 * ln 2).  A vector that holds no entry equal to the row max (its max from
+// the first pass is below m) takes the lean path: d2 = fma(x, log2 e, -m log2 e), one
+// ex2, one add, one fma.  The vector holding the max (one per row, normally) takes
+// the exact path: d = x - m is exactly 0 there, those entries are counted in c and
+// kept out of z, so a near one-hot row loses nothing to the 1.0 in the sum.
+__device__ __forceinline__ void vec_stats(const uint4& u, int e0, int lim, float vmax, float m, float mL, float& z,
+                                          float& c, float& t2) {
+  float f[8];
+  if (e0 + 8 <= lim && vmax < m) {
+    unpack8(u, f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float d2 = fmaf(f[k], kLog2e, -mL);
+      const float e = ex2_approx(d2);
+      z += e;
+      t2 = fmaf(e, d2, t2);
+    }
+    return;
+  }
+  const float3 r = vec_stats_masked(u, e0, lim, m);
+  z += r.x;
+  c += r.y;
+  t2 += r.z;
+}
+
+// ----------------------------------------------------------------------------------
 // softmax + entropy, register-resident rows.  128 threads per block, TPR threads per
 // row (32: one warp per row, shuffles only), NV 16-byte vectors (8 fp16) per thread
 // kept as raw fp16 in registers: rows up to TPR*NV*8 columns.  Requires n % 8 == 0,
 // ldx % 8 == 0 and a 16-byte aligned base (and the same for probs).
 // ----------------------------------------------------------------------------------
-constexpr int kRowThreads = 128;
-
-template <int TPR, int NV>
+template <int TPR, int NV, bool kGeneral>
 __global__ void __launch_bounds__(kRowThreads) softmax_entropy_vec_kernel(const SoftmaxArgs a) {
+  // kGeneral = false: no causal mask and no probabilities (the router's case) -- the
+  // lean instantiation, which keeps the hot loop small
   constexpr int RPB = kRowThreads / TPR;
   __shared__ float red[3 * 8];
   const int g = threadIdx.x / TPR, lt = threadIdx.x % TPR;
@@ -209,7 +317,7 @@ __global__ void __launch_bounds__(kRowThreads) softmax_entropy_vec_kernel(const 
   const bool ok = row < a.rows;
   const int n = a.n;
   int lim = ok ? n : 0;
-  if (a.causal && ok) {
+  if (kGeneral && a.causal && ok) {
     const int64_t q = row % a.S;
     lim = q + 1 < n ? static_cast<int>(q + 1) : n;
   }
@@ -220,41 +328,30 @@ __global__ void __launch_bounds__(kRowThreads) softmax_entropy_vec_kernel(const 
     const int e0 = (lt + i * TPR) * 8;
     u[i] = (e0 < lim) ? __ldcs(reinterpret_cast<const uint4*>(xr + e0)) : make_uint4(0u, 0u, 0u, 0u);
   }
+  float vmax[NV];
   float m = kNegInf;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
-    float f[8];
-    unpack8_masked(u[i], (lt + i * TPR) * 8, lim, f);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) m = fmaxf(m, f[k]);
+    const int e0 = (lt + i * TPR) * 8;
+    vmax[i] = (e0 < lim) ? vec_max(u[i], e0, lim) : kNegInf;
+    m = fmaxf(m, vmax[i]);
   }
   m = group_max<TPR>(m, red);
 
-  float z = 0.f, c = 0.f, t = 0.f;
+  const float mL = m * kLog2e;
+  float z = 0.f, c = 0.f, t2 = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
-    float f[8];
-    unpack8_masked(u[i], (lt + i * TPR) * 8, lim, f);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float xk = f[k];
-      if (xk == m) {
-        c += 1.f;
-      } else if (xk > kNegInf) {
-        const float d = xk - m;
-        const float e = __expf(d);
-        z += e;
-        t += e * d;
-      }
-    }
+    const int e0 = (lt + i * TPR) * 8;
+    if (e0 < lim) vec_stats(u[i], e0, lim, vmax[i], m, mL, z, c, t2);
   }
-  group_sum3<TPR>(z, c, t, red);
-  const float h = entropy_from_stats(c, z, t);
+  group_sum3<TPR>(z, c, t2, red);
+  const float h = entropy_from_stats(c, z, t2 * 0.69314718055994531f);
   if (ok && lt == 0) {
     a.H[row] = h;
     if (a.route) a.route[row] = route_of(h, a.tau_low, a.tau_high);
   }
-  if (a.probs != nullptr && ok) {
+  if (kGeneral && a.probs != nullptr && ok) {
     const float inv = div_full(1.f, c + z);
     __half* pr = static_cast<__half*>(a.probs) + row * a.ldp;
 #pragma unroll
@@ -275,7 +372,7 @@ __global__ void __launch_bounds__(kRowThreads) softmax_entropy_vec_kernel(const 
       }
     }
   }
-  if (a.perm != nullptr) compact_routes_last_block<kRowThreads>(a);
+  if (a.perm != nullptr) compact_routes_last_block<kRowThreads>(a.route, a.rows, a.perm, a.slot, a.counts, a.ticket);
 }
 
 // Online softmax statistics (see entropy_from_stats) for the streaming path.
@@ -362,7 +459,7 @@ __global__ void __launch_bounds__(256) softmax_entropy_loop_kernel(const Softmax
       pr[j] = __float2half_rn(e * inv);
     }
   }
-  if (a.perm != nullptr) compact_routes_last_block<256>(a);
+  if (a.perm != nullptr) compact_routes_last_block<256>(a.route, a.rows, a.perm, a.slot, a.counts, a.ticket);
 }
 
 // ----------------------------------------------------------------------------------

@@ -129,24 +129,27 @@ class GatedLayerEngine:
                  self.workspace.data_ptr(), self.workspace.numel(), ctypes.byref(self._handle))
         self._layers = c_layers
 
-    def _on_stream(self, name: str) -> None:
+    def run(self) -> None:
+        """Enqueue every layer eagerly on the current stream."""
+        with torch.cuda.device(self.device):
+            call("ee_engine_run", self._handle, torch.cuda.current_stream(self.device).cuda_stream)
+
+    def capture(self) -> None:
+        """Record the loop into a CUDA graph (on the engine's own stream, ordered after
+        the caller's current stream)."""
         cur = torch.cuda.current_stream(self.device)
         self.stream.wait_stream(cur)
         with torch.cuda.device(self.device):
-            call(name, self._handle, self.stream.cuda_stream)
+            call("ee_engine_capture", self._handle, self.stream.cuda_stream)
         cur.wait_stream(self.stream)
-
-    def run(self) -> None:
-        """Enqueue every layer eagerly (ordered after the caller's current stream)."""
-        self._on_stream("ee_engine_run")
-
-    def capture(self) -> None:
-        """Record the loop into a CUDA graph."""
-        self._on_stream("ee_engine_capture")
+        self._captured = True
 
     def launch(self) -> None:
-        """Replay the recorded graph (records it on first use)."""
-        self._on_stream("ee_engine_launch")
+        """Replay the recorded graph on the current stream (records it on first use)."""
+        if not getattr(self, "_captured", False):
+            self.capture()
+        with torch.cuda.device(self.device):
+            call("ee_engine_launch", self._handle, torch.cuda.current_stream(self.device).cuda_stream)
 
     def close(self) -> None:
         if getattr(self, "_handle", None) and self._handle.value:
