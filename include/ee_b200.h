@@ -21,6 +21,7 @@
  * entropy-engine/ directory):
  *   EE/python/kernels.py:264-312  fused_softmax_entropy_kernel -> ee_softmax_entropy
  *   EE/python/kernels.py:416-453  fused_softmax_entropy        -> ee_fused_softmax_entropy_4d
+ *   EE/python/dispatch.py:243-245 Llama-path attention entropy -> ee_attention_entropy
  *   EE/python/dispatch.py:55-82   PipelinedEntropyDispatcher   -> ee_route_batch_max, ee_route
  *   EE/python/dispatch.py:43-48   quantize_weights_int8        -> ee_quantize_weights_int8
  *   EE/python/kernels.py:330-351  triton_int8_gemm             -> ee_linear_int8
@@ -59,6 +60,10 @@ extern "C" {
 #define EE_FP8 1
 #define EE_FP16 2
 
+/* element types of ee_attention_entropy's probabilities */
+#define EE_DTYPE_F16 0
+#define EE_DTYPE_F32 1
+
 EE_API int ee_abi_version(void);
 EE_API const char* ee_last_error(void);
 
@@ -91,6 +96,16 @@ EE_API int ee_softmax_entropy(const void* x, int64_t rows, int64_t n, int64_t ld
  * Replaces EE/python/kernels.py:416-453. */
 EE_API int ee_fused_softmax_entropy_4d(const void* logits, int64_t B, int64_t Hh, int64_t S, int causal, void* probs,
                                 float* row_entropy, float* batch_entropy, void* stream);
+
+/* Entropy of given attention probabilities, the Llama block's router input:
+ *   row_entropy[r] = -sum_j p[r, j] * ln(p[r, j] + 1e-10)   (fp32 arithmetic)
+ * for `rows` rows of n probabilities (row stride ld elements, dtype EE_DTYPE_F16 or
+ * EE_DTYPE_F32), then batch_entropy[b] = mean of row_entropy over the rows / batches
+ * consecutive rows of batch b (nullable; rows % batches == 0).  row_entropy is
+ * required.  For [B, Hh, S, S] probabilities: rows = B*Hh*S, n = ld = S, batches = B.
+ * Replaces EE/python/dispatch.py:243-245. */
+EE_API int ee_attention_entropy(const void* probs, int dtype, int64_t rows, int64_t n, int64_t ld, float* row_entropy,
+                                int64_t batches, float* batch_entropy, void* stream);
 
 /* ---------------------------------------------------------------- routing
  * route[i] = dual-threshold tier of H[i]                (per-row granularity) */

@@ -112,6 +112,18 @@ def fused_softmax_entropy_4d(logits: np.ndarray, causal: bool = True):
     return p.reshape(logits.shape), H.reshape(B, Hh * S).mean(axis=1)
 
 
+def attention_entropy(p: np.ndarray):
+    """Llama-path entropy of attention probabilities (EE/python/dispatch.py:243-245):
+    per row ``-sum_j p_j * ln(p_j + 1e-10)`` with p widened to fp32 and the 1e-10 added
+    in fp32 (as ``attn_weights.float() + eps``), evaluated in float64; then the mean
+    over every axis but the batch (the first) and the last.  Returns (per-batch [B],
+    per-row [...]) as float64."""
+    p32 = np.asarray(p).astype(np.float32)
+    t = (p32 + np.float32(1e-10)).astype(np.float64)
+    rows = -(p32.astype(np.float64) * np.log(t)).sum(axis=-1)
+    return rows.reshape(rows.shape[0], -1).mean(axis=1), rows
+
+
 # --------------------------------------------------------------------------- routing
 
 

@@ -104,6 +104,21 @@ def test_softmax_argument_checks(pkg, lib):
     assert lib.ee_softmax_entropy(p, 0, 8, 8, 0, 1, None, 8, p, None, 0.0, 0.0, None) == 0
 
 
+def test_attention_entropy_argument_checks(pkg, lib):
+    p = ctypes.c_void_p(256)
+    # bad dtype code
+    assert lib.ee_attention_entropy(p, 7, 4, 8, 8, p, 1, p, None) == EE_ERR_INVALID
+    # rows not a multiple of the batches
+    assert lib.ee_attention_entropy(p, 0, 6, 8, 8, p, 4, p, None) == EE_ERR_INVALID
+    # ld < n, missing row output
+    assert lib.ee_attention_entropy(p, 1, 4, 8, 4, p, 1, p, None) == EE_ERR_INVALID
+    assert lib.ee_attention_entropy(p, 1, 4, 8, 8, None, 1, p, None) == EE_ERR_INVALID
+    # an fp32 pointer that is only 2-byte aligned
+    assert lib.ee_attention_entropy(ctypes.c_void_p(258), 1, 4, 8, 8, p, 1, p, None) == EE_ERR_MISALIGNED
+    # no rows: nothing to do
+    assert lib.ee_attention_entropy(None, 0, 0, 8, 8, None, 0, None, None) == 0
+
+
 def test_errors_raise_runtime_error_in_python(pkg):
     from importlib import import_module
 

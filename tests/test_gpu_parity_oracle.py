@@ -117,6 +117,7 @@ def test_compaction_is_the_stable_bucket_order(pkg, cuda):
     r = pkg.EntropyRouter(*TAU)
     r.reserve(3000, 64, cuda)
     r.route(_dev(inp["logits"], cuda))
+    r.pack_rows(_dev(inp["A"], cuda))  # places the rows: writes perm
     torch.cuda.synchronize()
     route = r.route_ids.cpu().numpy()
     perm_ref, counts_ref = orc.compaction(route)

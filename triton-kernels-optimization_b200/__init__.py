@@ -21,6 +21,7 @@ from .dispatch import (
 from .engine import CubinEngine, GatedLayerEngine
 from .kernels import (
     WeightPack,
+    attention_entropy,
     fused_softmax_entropy,
     gemm_accumulators,
     gemm_int8_prequant,

@@ -33,6 +33,7 @@ SIGNATURES = {
     "ee_softmax_entropy": (c_int, [_P, c_int64, c_int64, c_int64, c_int, c_int64, _P, c_int64, _P, _P, c_double,
                                    c_double, _P]),
     "ee_fused_softmax_entropy_4d": (c_int, [_P, c_int64, c_int64, c_int64, c_int, _P, _P, _P, _P]),
+    "ee_attention_entropy": (c_int, [_P, c_int, c_int64, c_int64, c_int64, _P, c_int64, _P, _P]),
     "ee_route": (c_int, [_P, c_int64, c_double, c_double, _P, _P]),
     "ee_route_batch_max": (c_int, [_P, c_int64, c_double, c_double, _P, _P, _P]),
     "ee_quantize_weights_int8": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, _P, c_int, _P]),

@@ -193,12 +193,14 @@ struct GatedWs {
   int8_t* route;
   float* H;
   float* sa;
+  int4* chunk_tab;  // per 16-row chunk: rows of each bucket in earlier chunks
   uint8_t* buf8;
   void* buf16;
 };
+size_t chunk_tab_bytes(int64_t M) { return align256(sizeof(int4) * size_t((M + 15) / 16)); }
 size_t gated_ws_bytes(int64_t M, int64_t K) {
   return 256 + 2 * align256(sizeof(int32_t) * M) + align256(M) + 2 * align256(sizeof(float) * M) +
-         align256(size_t(M) * K) + align256(size_t(M) * K * 2);
+         chunk_tab_bytes(M) + align256(size_t(M) * K) + align256(size_t(M) * K * 2);
 }
 GatedWs gated_ws(void* ws, int64_t M, int64_t K) {
   uint8_t* p = static_cast<uint8_t*>(ws);
@@ -217,6 +219,8 @@ GatedWs gated_ws(void* ws, int64_t M, int64_t K) {
   p += align256(sizeof(float) * M);
   w.sa = reinterpret_cast<float*>(p);
   p += align256(sizeof(float) * M);
+  w.chunk_tab = reinterpret_cast<int4*>(p);
+  p += chunk_tab_bytes(M);
   w.buf8 = p;
   p += align256(size_t(M) * K);
   w.buf16 = p;
@@ -230,8 +234,10 @@ int check_ws(const void* ws, size_t have, size_t need) {
   return EE_OK;
 }
 
+// gw != nullptr: the rows go to the bucket order of a gated workspace (positions from
+// its chunk table, perm / slot written); else every row keeps its index as position
 int pack_rows(const void* A, int64_t lda, int64_t M, int64_t K, const int8_t* route, int fixed_bucket,
-              const int32_t* slot, float* sa, uint8_t* buf8, int64_t ld8, void* buf16, int64_t ld16, cudaStream_t s) {
+              const GatedWs* gw, float* sa, uint8_t* buf8, int64_t ld8, void* buf16, int64_t ld16, cudaStream_t s) {
   ee::PackArgs p;
   p.A = A;
   p.lda = lda;
@@ -239,7 +245,10 @@ int pack_rows(const void* A, int64_t lda, int64_t M, int64_t K, const int8_t* ro
   p.K = static_cast<int>(K);
   p.route = route;
   p.fixed_bucket = fixed_bucket;
-  p.slot = slot;
+  p.chunk_tab = gw ? gw->chunk_tab : nullptr;
+  p.counts = gw ? gw->counts : nullptr;
+  p.perm = gw ? gw->perm : nullptr;
+  p.slot = gw ? gw->slot : nullptr;
   p.sa = sa;
   p.buf8 = buf8;
   p.ld8 = ld8;
@@ -321,6 +330,24 @@ int ee_fused_softmax_entropy_4d(const void* logits, int64_t B, int64_t Hh, int64
   int st = ee_softmax_entropy(logits, rows, S, S, causal, S, probs, S, row_entropy, nullptr, 0.f, 0.f, stream);
   if (st != EE_OK) return st;
   return check_launch(ee::launch_batch_mean(row_entropy, B, Hh * S, batch_entropy, as_stream(stream)), "batch_mean");
+}
+
+int ee_attention_entropy(const void* probs, int dtype, int64_t rows, int64_t n, int64_t ld, float* row_entropy,
+                         int64_t batches, float* batch_entropy, void* stream) {
+  if (rows < 0 || n < 0 || batches < 0) return fail(EE_ERR_INVALID, "negative shape");
+  if (dtype != EE_DTYPE_F16 && dtype != EE_DTYPE_F32) return fail(EE_ERR_INVALID, "dtype must be EE_DTYPE_F16 or EE_DTYPE_F32");
+  if (rows == 0) return EE_OK;
+  if (probs == nullptr || row_entropy == nullptr) return fail(EE_ERR_INVALID, "probs and row_entropy are required");
+  if (n == 0 || ld < n) return fail(EE_ERR_INVALID, "bad n=%lld / ld=%lld", (long long)n, (long long)ld);
+  const size_t esize = dtype == EE_DTYPE_F32 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(probs) % esize != 0) return fail(EE_ERR_MISALIGNED, "probs misaligned for its dtype");
+  if (batch_entropy != nullptr && (batches <= 0 || rows % batches != 0))
+    return fail(EE_ERR_INVALID, "rows=%lld is not a multiple of batches=%lld", (long long)rows, (long long)batches);
+  cudaStream_t s = as_stream(stream);
+  int st = check_launch(ee::launch_attention_entropy(probs, dtype == EE_DTYPE_F32, rows, n, ld, row_entropy, s),
+                        "attention_entropy");
+  if (st != EE_OK || batch_entropy == nullptr) return st;
+  return check_launch(ee::launch_batch_mean(row_entropy, batches, rows / batches, batch_entropy, s), "batch_mean");
 }
 
 // ------------------------------------------------------------------ routing
@@ -549,8 +576,7 @@ int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double ta
     a.route = w.route;
     a.tau_low = tau_low;
     a.tau_high = tau_high;
-    a.perm = w.perm;
-    a.slot = w.slot;
+    a.chunk_tab = w.chunk_tab;
     a.counts = w.counts;
     a.ticket = w.ticket;
     if ((st = check_launch(ee::launch_softmax_entropy(a, s), "softmax_entropy")) != EE_OK) return st;
@@ -588,7 +614,7 @@ int ee_gated_pack(const void* A, int64_t lda, int64_t M, int64_t K, void* worksp
   if ((st = check_ws(workspace, workspace_bytes, gated_ws_bytes(M, K))) != EE_OK) return st;
   if (M == 0) return EE_OK;
   GatedWs w = gated_ws(workspace, M, K);
-  return pack_rows(A, lda, M, K, w.route, 0, w.slot, w.sa, w.buf8, K, w.buf16, K, as_stream(stream));
+  return pack_rows(A, lda, M, K, w.route, 0, &w, w.sa, w.buf8, K, w.buf16, K, as_stream(stream));
 }
 
 int ee_gated_gemm_packed(int64_t M, int64_t K, const int8_t* W_i8_nk, const uint8_t* W_e4m3_nk,

@@ -526,10 +526,18 @@ __device__ __forceinline__ void feed_retire_pair(const GemmArgs& args, int npair
 }
 
 constexpr int kPairRows = 256;
-constexpr int kStagesPair = 6;
+#ifndef EE_PAIR_STAGES
+#define EE_PAIR_STAGES 7  // 32 KB per stage per CTA: 7 is the most that fits in 227 KB
+#endif
+constexpr int kStagesPair = EE_PAIR_STAGES;
 constexpr int kHalfStageBytes = 128 * kBKBytes;  // 16 KB: one operand half of one CTA
 constexpr int kStageBytesPair = 2 * kHalfStageBytes;
 constexpr size_t kGemmSmemPair = 1024 + size_t(kStagesPair) * kStageBytesPair + kBarrierBytes;
+static_assert(kGemmSmemPair <= 227 * 1024, "pair GEMM shared memory above the 227 KB per-CTA limit");
+// barrier region: 2 per stage, 2 x 2 accumulator, drain, 2 per ring slot; then the TMEM
+// slot, the abort word and the ring itself
+static_assert((2 * kStagesPair + 5 + 2 * kTileRing) * 8 + 8 + 4 * kTileRing <= kBarrierBytes,
+              "pair GEMM barrier region overflows");
 
 template <int KIND>
 __device__ __forceinline__ void mma_stage_pair(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr, bool first) {

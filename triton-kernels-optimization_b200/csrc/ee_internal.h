@@ -30,9 +30,11 @@ struct SoftmaxArgs {
   float* H;           // fp32 [rows], required
   int8_t* route;      // int8 [rows], nullable
   double tau_low, tau_high;  // compared in double, like the reference's Python floats
-  // compaction (all nullable together): rows grouped by route, stable in row order
-  int32_t* perm;      // [rows] position -> row
-  int32_t* slot;      // [rows] row -> position
+  // bucket scan (all nullable together; needs route): the last block to finish counts
+  // the routes per 16-row chunk and writes, per chunk, the rows of each bucket in all
+  // earlier chunks (int4: INT8, FP8, FP16, 0) plus the bucket totals.  A row's
+  // position in the stable bucket order then follows from its own chunk alone.
+  int4* chunk_tab;    // [ceil(rows / 16)]
   int32_t* counts;    // [4] rows per bucket (INT8, FP8, FP16) + spare
   uint32_t* ticket;   // zero-initialised counter; left at zero by the kernel
 };
@@ -45,7 +47,14 @@ struct PackArgs {
   int K;
   const int8_t* route;  // nullable: every row goes to fixed_bucket
   int fixed_bucket;
-  const int32_t* slot;  // nullable: position = row
+  // bucket placement (nullable together, needs route; else position = row): the scan
+  // of SoftmaxArgs.  Each row's position = bucket offset + rows of its bucket in earlier
+  // chunks + rows of its bucket before it in its chunk; perm[position] = row and
+  // slot[row] = position are written on the way.
+  const int4* chunk_tab;
+  const int32_t* counts;
+  int32_t* perm;
+  int32_t* slot;
   float* sa;            // [positions] per-row activation scale (8-bit buckets)
   uint8_t* buf8;        // [positions, K] int8 / e4m3 rows, row stride ld8 bytes
   int64_t ld8;
@@ -62,6 +71,8 @@ int launch_quantize_weights(const void* W, int64_t ldw, int64_t N, int64_t K, in
 int launch_pack_weights(const int8_t* w_kn, const float* scale, int64_t K, int64_t N, int8_t* w_i8,
                         uint8_t* w_e4m3, void* w_f16, cudaStream_t s);
 int launch_batch_mean(const float* H, int64_t B, int64_t per_batch, float* out, cudaStream_t s);
+// per-row attention entropy of probabilities fp16 (f32 = false) or fp32 [rows, n], row stride ld
+int launch_attention_entropy(const void* P, bool f32, int64_t rows, int64_t n, int64_t ld, float* H, cudaStream_t s);
 int launch_batch_max_route(const float* H, int64_t n, double tl, double th, float* max_out, int8_t* tier_out,
                            cudaStream_t s);
 int launch_route(const float* H, int64_t rows, double tl, double th, int8_t* route, cudaStream_t s);

@@ -18,19 +18,19 @@ inline unsigned grid_of(int64_t rows, int per_block) {
   return static_cast<unsigned>((rows + per_block - 1) / per_block);
 }
 
-template <int TPR, int NV>
+template <int TPR, int NV, int MINB = 1>
 int run_softmax_vec(const SoftmaxArgs& a, cudaStream_t s) {
   const unsigned grid = grid_of(a.rows, kRowThreads / TPR);
   if (a.causal || a.probs != nullptr)
-    softmax_entropy_vec_kernel<TPR, NV, true><<<grid, kRowThreads, 0, s>>>(a);
+    softmax_entropy_vec_kernel<TPR, NV, true, 1><<<grid, kRowThreads, 0, s>>>(a);
   else
-    softmax_entropy_vec_kernel<TPR, NV, false><<<grid, kRowThreads, 0, s>>>(a);
+    softmax_entropy_vec_kernel<TPR, NV, false, MINB><<<grid, kRowThreads, 0, s>>>(a);
   return status_of(cudaGetLastError());
 }
 
-template <int TPR, int NV>
+template <int TPR, int NV, int MINB = 1>
 int run_pack_vec(const PackArgs& a, cudaStream_t s) {
-  pack_rows_vec_kernel<TPR, NV><<<grid_of(a.M, kRowThreads / TPR), kRowThreads, 0, s>>>(a);
+  pack_rows_vec_kernel<TPR, NV, MINB><<<grid_of(a.M, kRowThreads / TPR), kRowThreads, 0, s>>>(a);
   return status_of(cudaGetLastError());
 }
 
@@ -55,14 +55,16 @@ int launch_softmax_entropy(const SoftmaxArgs& a, cudaStream_t s) {
                    (a.probs == nullptr || ((a.ldp % 8 == 0) && aligned16(a.probs)));
   if (vec) {
     // one warp per row up to 1024 columns (no block-level synchronisation), then 2 / 4 / 8
-    // warps per row so every thread keeps at most 8 vectors (64 fp16) in registers (a
-    // sweep of these shapes on B200: 2 warps x 8 vectors was fastest at 4096 columns)
+    // warps per row so every thread keeps at most 8 vectors (64 fp16) in registers.  A
+    // sweep on B200 at 4096 columns (4096 and 16384 rows, L2 cold): 2 warps x 8 vectors
+    // with registers capped for 4 resident blocks per SM was fastest (12.7 us / 36.4 us
+    // against 14.7 / 39.4 uncapped).
     const int n = a.n;
     if (n <= 256) return run_softmax_vec<32, 1>(a, s);
     if (n <= 512) return run_softmax_vec<32, 2>(a, s);
     if (n <= 1024) return run_softmax_vec<32, 4>(a, s);
-    if (n <= 2048) return run_softmax_vec<64, 4>(a, s);
-    if (n <= 4096) return run_softmax_vec<64, 8>(a, s);
+    if (n <= 2048) return run_softmax_vec<64, 4, 4>(a, s);
+    if (n <= 4096) return run_softmax_vec<64, 8, 4>(a, s);
     if (n <= 8192) return run_softmax_vec<128, 8>(a, s);
     if (n <= 16384) return run_softmax_vec<256, 8>(a, s);
   }
@@ -74,12 +76,15 @@ int launch_pack_rows(const PackArgs& a, cudaStream_t s) {
   if (a.M <= 0) return 0;
   const int K = a.K;
 
+  // The same sweep for the packing (K = 4096: 4 warps x 4 vectors, 12.7 us against 14.9
+  // for 2 x 8; K = 14336: 8 warps x 7 vectors, which covers the row exactly).
   if (K <= 512) return run_pack_vec<32, 2>(a, s);
   if (K <= 1024) return run_pack_vec<32, 4>(a, s);
-  if (K <= 2048) return run_pack_vec<64, 4>(a, s);
-  if (K <= 4096) return run_pack_vec<64, 8>(a, s);
+  if (K <= 2048) return run_pack_vec<64, 4, 4>(a, s);
+  if (K <= 4096) return run_pack_vec<128, 4, 4>(a, s);
   if (K <= 8192) return run_pack_vec<128, 8>(a, s);
-  if (K <= 16384) return run_pack_vec<256, 8>(a, s);
+  if (K <= 14336) return run_pack_vec<256, 7, 2>(a, s);
+  if (K <= 16384) return run_pack_vec<256, 8, 2>(a, s);
   pack_rows_loop_kernel<<<static_cast<unsigned>(a.M), 256, 0, s>>>(a);
   return status_of(cudaGetLastError());
 }
@@ -97,6 +102,22 @@ int launch_pack_weights(const int8_t* w_kn, const float* scale, int64_t K, int64
   if (K <= 0 || N <= 0) return 0;
   dim3 grid(static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>((N + 31) / 32));
   pack_weights_kernel<<<grid, 256, 0, s>>>(w_kn, scale, K, N, w_i8, w_e4m3, static_cast<__half*>(w_f16));
+  return status_of(cudaGetLastError());
+}
+
+int launch_attention_entropy(const void* P, bool f32, int64_t rows, int64_t n, int64_t ld, float* H, cudaStream_t s) {
+  if (rows <= 0) return 0;
+  const int64_t want = (rows + 7) / 8;  // 8 rows (warps) per block; a few waves of 148 SMs at most
+  const unsigned grid = static_cast<unsigned>(want < int64_t(sm_count()) * 16 ? want : int64_t(sm_count()) * 16);
+  const int width = f32 ? 4 : 8;  // elements per 16-byte vector
+  const bool vec = aligned16(P) && n % width == 0 && ld % width == 0;
+  if (f32) {
+    if (vec) attention_entropy_kernel<true, true><<<grid, 256, 0, s>>>(P, rows, n, ld, H);
+    else attention_entropy_kernel<true, false><<<grid, 256, 0, s>>>(P, rows, n, ld, H);
+  } else {
+    if (vec) attention_entropy_kernel<false, true><<<grid, 256, 0, s>>>(P, rows, n, ld, H);
+    else attention_entropy_kernel<false, false><<<grid, 256, 0, s>>>(P, rows, n, ld, H);
+  }
   return status_of(cudaGetLastError());
 }
 

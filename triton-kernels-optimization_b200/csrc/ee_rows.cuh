@@ -95,19 +95,52 @@ __device__ __forceinline__ int8_t route_of(float h, double tl, double th) {
 }
 
 // ----------------------------------------------------------------------------------
-// stable bucket compaction, run by the last block of a softmax launch to finish
-// (threadfence-reduction pattern).  Positions: bucket INT8 rows first, then FP8, then
-// FP16, each group in increasing row order.  NT = threads per block (128 or 256).
+// stable bucket order.  Positions: INT8 rows first, then FP8, then FP16, each group in
+// increasing row order.  The routes are split into 16-row chunks; the last block of a
+// softmax launch to finish (threadfence-reduction pattern) counts every chunk and
+// writes, per chunk, how many rows of each bucket all earlier chunks hold, plus the
+// bucket totals.  A row's position then needs only its own chunk (bucket_position),
+// so the scatter of perm / slot runs fully parallel in the packing kernel instead of
+// serially in that last block.
 // ----------------------------------------------------------------------------------
+// per-byte route masks of one 32-bit word of routes (values 0, 1, 2): bit 0 of each
+// byte is set where the route equals `b`
+__device__ __forceinline__ uint32_t route_eq_bytes(uint32_t w, int b) {
+  const uint32_t lo = w & 0x01010101u, hi = (w >> 1) & 0x01010101u;
+  return b == kINT8 ? (~(lo | hi) & 0x01010101u) : (b == kFP8 ? lo : hi);
+}
+
+// bucket counts of chunk c (rows [16c, min(16c + 16, M))); `route` 16-byte aligned
+__device__ __forceinline__ int3 chunk_counts(const int8_t* route, int64_t M, int64_t c) {
+  const int64_t r = c * 16;
+  if (r + 16 <= M) {
+    const uint4 u = __ldcg(reinterpret_cast<const uint4*>(route + r));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    int ones = 0, twos = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      ones += __popc(w[i] & 0x01010101u);
+      twos += __popc(w[i] & 0x02020202u);
+    }
+    return make_int3(16 - ones - twos, ones, twos);
+  }
+  int n0 = 0, n1 = 0, n2 = 0;
+  for (int64_t q = r; q < M; ++q) {
+    const int b = __ldcg(route + q);
+    n0 += b == kINT8;
+    n1 += b == kFP8;
+    n2 += b == kFP16;
+  }
+  return make_int3(n0, n1, n2);
+}
+
 // Scalar arguments, never a reference to the kernel's parameter struct: a reference
 // would make every caller keep a copy of that struct on its stack.
 template <int NT>
-__device__ __noinline__ void compact_routes_last_block(const int8_t* route, int64_t M, int32_t* perm,
-                                                       int32_t* slot, int32_t* counts, unsigned* ticket) {
-  constexpr int PER_LANE = NT / 32;  // scan entries per lane of the scanning warp
+__device__ __noinline__ void scan_route_chunks_last_block(const int8_t* route, int64_t M, int4* tab, int32_t* counts,
+                                                          uint32_t* ticket) {
   __shared__ int s_last;
-  __shared__ int s_scan[3][NT];
-  __shared__ int s_tot[3];
+  __shared__ int s_part[3][NT / 32];
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -118,87 +151,84 @@ __device__ __noinline__ void compact_routes_last_block(const int8_t* route, int6
   if (!s_last) return;
   __threadfence();
 
-  const int tid = threadIdx.x;
-  // contiguous chunk per thread, a multiple of 16 routes so it can be read as uint4
-  const int64_t per = ((M + NT - 1) / NT + 15) / 16 * 16;
-  const int64_t r0 = tid * per;
-  const int64_t r1 = r0 + per < M ? r0 + per : M;
-  int cnt[3] = {0, 0, 0};
-  for (int64_t r = r0; r < r1; r += 16) {
-    if (r + 16 <= r1) {
-      const uint4 u = __ldcg(reinterpret_cast<const uint4*>(route + r));
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t nch = (M + 15) / 16;
+  const int64_t per = (nch + NT - 1) / NT;  // contiguous chunks per thread
+  const int64_t c0 = tid * per;
+  const int64_t c1 = c0 + per < nch ? c0 + per : nch;
+  int t0 = 0, t1 = 0, t2 = 0;
+  for (int64_t c = c0; c < c1; ++c) {
+    const int3 k = chunk_counts(route, M, c);
+    t0 += k.x;
+    t1 += k.y;
+    t2 += k.z;
+  }
+  // block-wide exclusive scan of the per-thread totals
+  int i0 = t0, i1 = t1, i2 = t2;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int ones = __popc(w[i] & 0x01010101u);
-        const int twos = __popc(w[i] & 0x02020202u);
-        cnt[1] += ones;
-        cnt[2] += twos;
-        cnt[0] += 4 - ones - twos;
-      }
-    } else {
-      for (int64_t q = r; q < r1; ++q) {
-        const int b = __ldcg(route + q);
-        cnt[0] += b == 0;
-        cnt[1] += b == 1;
-        cnt[2] += b == 2;
-      }
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n0 = __shfl_up_sync(0xffffffffu, i0, o);
+    const int n1 = __shfl_up_sync(0xffffffffu, i1, o);
+    const int n2 = __shfl_up_sync(0xffffffffu, i2, o);
+    if (lane >= o) {
+      i0 += n0;
+      i1 += n1;
+      i2 += n2;
     }
   }
-  s_scan[0][tid] = cnt[0];
-  s_scan[1][tid] = cnt[1];
-  s_scan[2][tid] = cnt[2];
-  __syncthreads();
-  // exclusive scan of each bucket's NT counts by one warp (PER_LANE entries per lane)
-  const int warp = tid >> 5, lane = tid & 31;
-  if (warp < 3) {
-    int v[PER_LANE];
-    int run = 0;
-#pragma unroll
-    for (int i = 0; i < PER_LANE; ++i) {
-      v[i] = run;
-      run += s_scan[warp][lane * PER_LANE + i];
-    }
-    int incl = run;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int n = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += n;
-    }
-    const int excl = incl - run;
-#pragma unroll
-    for (int i = 0; i < PER_LANE; ++i) s_scan[warp][lane * PER_LANE + i] = v[i] + excl;
-    if (lane == 31) s_tot[warp] = incl;
+  if (lane == 31) {
+    s_part[0][warp] = i0;
+    s_part[1][warp] = i1;
+    s_part[2][warp] = i2;
   }
   __syncthreads();
-  int pos0 = s_scan[0][tid], pos1 = s_tot[0] + s_scan[1][tid], pos2 = s_tot[0] + s_tot[1] + s_scan[2][tid];
-  // scatter: the routes come back 16 at a time in one vector load (they were read just
-  // above, so these hit in L2), never one dependent byte load per row
-  for (int64_t r = r0; r < r1; r += 16) {
-    int8_t rb[16];
-    if (r + 16 <= r1) {
-      *reinterpret_cast<uint4*>(rb) = __ldcg(reinterpret_cast<const uint4*>(route + r));
-    } else {
-      for (int q = 0; q < 16; ++q) rb[q] = (r + q < r1) ? __ldcg(route + r + q) : int8_t(0);
-    }
-    const int lim = r + 16 <= r1 ? 16 : static_cast<int>(r1 - r);
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      if (q < lim) {
-        const int b = rb[q];
-        const int p = b == 0 ? pos0++ : (b == 1 ? pos1++ : pos2++);
-        perm[p] = static_cast<int32_t>(r + q);
-        slot[r + q] = p;
-      }
-    }
+  int p0 = i0 - t0, p1 = i1 - t1, p2 = i2 - t2;
+  for (int w = 0; w < warp; ++w) {
+    p0 += s_part[0][w];
+    p1 += s_part[1][w];
+    p2 += s_part[2][w];
   }
-  if (tid == 0) {
-    counts[0] = s_tot[0];
-    counts[1] = s_tot[1];
-    counts[2] = s_tot[2];
+  for (int64_t c = c0; c < c1; ++c) {
+    tab[c] = make_int4(p0, p1, p2, 0);
+    const int3 k = chunk_counts(route, M, c);  // second read: an L1 / L2 hit
+    p0 += k.x;
+    p1 += k.y;
+    p2 += k.z;
+  }
+  if (tid == NT - 1) {  // the last thread's running prefix ends at the totals
+    counts[0] = p0;
+    counts[1] = p1;
+    counts[2] = p2;
     counts[3] = 0;
     *ticket = 0u;  // ready for the next launch
   }
+}
+
+// Position of `row` (bucket b) in the stable bucket order, from the chunk table of the
+// scan above; all loads hit lines that every row of the chunk shares.
+__device__ __forceinline__ int64_t bucket_position(const int8_t* route, int64_t M, const int4* tab,
+                                                   const int32_t* counts, int64_t row, int b) {
+  const int64_t c = row >> 4;
+  const int4 t = tab[c];
+  const int4 tot = *reinterpret_cast<const int4*>(counts);
+  int64_t pos = b == kINT8 ? t.x : (b == kFP8 ? int64_t(tot.x) + t.y : int64_t(tot.x) + tot.y + t.z);
+  const int before = static_cast<int>(row & 15);  // rows of the chunk ahead of this one
+  const int64_t r0 = c * 16;
+  if (r0 + 16 <= M) {
+    const uint4 u = *reinterpret_cast<const uint4*>(route + r0);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int lim = before - 4 * i;  // bytes of this word ahead of the row
+      if (lim > 0) {
+        const uint32_t keep = lim >= 4 ? 0xffffffffu : ((1u << (8 * lim)) - 1u);
+        pos += __popc(route_eq_bytes(w[i], b) & keep);
+      }
+    }
+  } else {
+    for (int q = 0; q < before; ++q) pos += route[r0 + q] == b;
+  }
+  return pos;
 }
 
 // 8 fp16 of a 16-byte vector -> floats, entries at or beyond `lim` -> -inf
@@ -306,8 +336,8 @@ __device__ __forceinline__ void vec_stats(const uint4& u, int e0, int lim, float
 // kept as raw fp16 in registers: rows up to TPR*NV*8 columns.  Requires n % 8 == 0,
 // ldx % 8 == 0 and a 16-byte aligned base (and the same for probs).
 // ----------------------------------------------------------------------------------
-template <int TPR, int NV, bool kGeneral>
-__global__ void __launch_bounds__(kRowThreads) softmax_entropy_vec_kernel(const SoftmaxArgs a) {
+template <int TPR, int NV, bool kGeneral, int MINB>
+__global__ void __launch_bounds__(kRowThreads, MINB) softmax_entropy_vec_kernel(const SoftmaxArgs a) {
   // kGeneral = false: no causal mask and no probabilities (the router's case) -- the
   // lean instantiation, which keeps the hot loop small
   constexpr int RPB = kRowThreads / TPR;
@@ -372,7 +402,7 @@ __global__ void __launch_bounds__(kRowThreads) softmax_entropy_vec_kernel(const 
       }
     }
   }
-  if (a.perm != nullptr) compact_routes_last_block<kRowThreads>(a.route, a.rows, a.perm, a.slot, a.counts, a.ticket);
+  if (a.chunk_tab != nullptr) scan_route_chunks_last_block<kRowThreads>(a.route, a.rows, a.chunk_tab, a.counts, a.ticket);
 }
 
 // Online softmax statistics (see entropy_from_stats) for the streaming path.
@@ -459,7 +489,7 @@ __global__ void __launch_bounds__(256) softmax_entropy_loop_kernel(const Softmax
       pr[j] = __float2half_rn(e * inv);
     }
   }
-  if (a.perm != nullptr) compact_routes_last_block<256>(a.route, a.rows, a.perm, a.slot, a.counts, a.ticket);
+  if (a.chunk_tab != nullptr) scan_route_chunks_last_block<256>(a.route, a.rows, a.chunk_tab, a.counts, a.ticket);
 }
 
 // ----------------------------------------------------------------------------------
@@ -527,8 +557,20 @@ __device__ __forceinline__ float absmax8(const uint4& u, float m) {
   return m;
 }
 
-template <int TPR, int NV>
-__global__ void __launch_bounds__(kRowThreads) pack_rows_vec_kernel(const PackArgs a) {
+// position of a row in the packed buffers; writes perm / slot when the bucket order is on
+__device__ __forceinline__ int64_t pack_position(const PackArgs& a, int64_t row, int b, bool writer) {
+  if (a.chunk_tab == nullptr) return row;
+  const int64_t pos = bucket_position(a.route, a.M, a.chunk_tab, a.counts, row, b);
+  if (writer) {
+    a.perm[pos] = static_cast<int32_t>(row);
+    a.slot[row] = static_cast<int32_t>(pos);
+  }
+  return pos;
+}
+
+// MINB: resident blocks per SM the register allocation must allow
+template <int TPR, int NV, int MINB>
+__global__ void __launch_bounds__(kRowThreads, MINB) pack_rows_vec_kernel(const PackArgs a) {
   constexpr int RPB = kRowThreads / TPR;
   __shared__ float red[8];
   const int g = threadIdx.x / TPR, lt = threadIdx.x % TPR;
@@ -536,7 +578,6 @@ __global__ void __launch_bounds__(kRowThreads) pack_rows_vec_kernel(const PackAr
   const bool ok = row < a.M;
   const int K = ok ? a.K : 0;
   const int b = ok ? (a.route ? static_cast<int>(a.route[row]) : a.fixed_bucket) : kFP16;
-  const int64_t pos = ok ? (a.slot ? static_cast<int64_t>(a.slot[row]) : row) : 0;
   const __half* ar = static_cast<const __half*>(a.A) + (ok ? row : 0) * a.lda;
   uint4 u[NV];
 #pragma unroll
@@ -544,6 +585,8 @@ __global__ void __launch_bounds__(kRowThreads) pack_rows_vec_kernel(const PackAr
     const int e0 = (lt + i * TPR) * 8;
     u[i] = (e0 < K) ? __ldcs(reinterpret_cast<const uint4*>(ar + e0)) : make_uint4(0u, 0u, 0u, 0u);
   }
+  // the row's position (small, cached loads) while its vectors are in flight
+  const int64_t pos = ok ? pack_position(a, row, b, lt == 0) : 0;
   float amax = 0.f;
   if (b != kFP16) {
 #pragma unroll
@@ -584,7 +627,7 @@ __global__ void __launch_bounds__(256) pack_rows_loop_kernel(const PackArgs a) {
   const int64_t row = blockIdx.x;
   const int K = a.K;
   const int b = a.route ? static_cast<int>(a.route[row]) : a.fixed_bucket;
-  const int64_t pos = a.slot ? static_cast<int64_t>(a.slot[row]) : row;
+  const int64_t pos = pack_position(a, row, b, threadIdx.x == 0);
   const __half* ar = static_cast<const __half*>(a.A) + row * a.lda;
   float amax = 0.f;
   for (int e0 = threadIdx.x * 8; e0 < K; e0 += 256 * 8) amax = absmax8(*reinterpret_cast<const uint4*>(ar + e0), amax);
@@ -683,6 +726,62 @@ __global__ void __launch_bounds__(256) batch_mean_kernel(const float* __restrict
     __syncthreads();
   }
   if (threadIdx.x == 0) out[blockIdx.x] = red[0] / static_cast<float>(per_batch);
+}
+
+// ----------------------------------------------------------------------------------
+// Llama-path attention entropy (EE/python/dispatch.py:243-245): per row of attention
+// probabilities p (fp16 or fp32), H = -sum_j p_j * ln(p_j + 1e-10) in fp32.  Written as
+// -ln2 * sum_j p_j * log2(p_j + 1e-10): one lg2.approx per entry (p + 1e-10 >= 1e-10 is
+// never subnormal), so the pass stays at the HBM roofline.  One warp per row, rows
+// in a grid-stride loop; kVec: 16-byte loads (rows 16-byte aligned, n a multiple of
+// the vector width), else one element per lane.
+// ----------------------------------------------------------------------------------
+__device__ __forceinline__ float lg2_approx(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float plog2p(float p) { return p * lg2_approx(p + 1e-10f); }
+
+template <bool kF32, bool kVec>
+__global__ void __launch_bounds__(256) attention_entropy_kernel(const void* __restrict__ P, int64_t rows, int64_t n,
+                                                                int64_t ld, float* __restrict__ H) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * 8;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5); r < rows; r += nw) {
+    float acc = 0.f;
+    if constexpr (kF32) {
+      const float* pr = static_cast<const float*>(P) + r * ld;
+      if constexpr (kVec) {
+#pragma unroll 4
+        for (int64_t j = lane * 4; j < n; j += 128) {
+          const float4 v = __ldcs(reinterpret_cast<const float4*>(pr + j));
+          acc += plog2p(v.x) + plog2p(v.y) + plog2p(v.z) + plog2p(v.w);
+        }
+      } else {
+        for (int64_t j = lane; j < n; j += 32) acc += plog2p(pr[j]);
+      }
+    } else {
+      const __half* pr = static_cast<const __half*>(P) + r * ld;
+      if constexpr (kVec) {
+#pragma unroll 4
+        for (int64_t j = lane * 8; j < n; j += 256) {
+          const uint4 u = __ldcs(reinterpret_cast<const uint4*>(pr + j));
+          const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = __half22float2(h[k]);
+            acc += plog2p(f.x) + plog2p(f.y);
+          }
+        }
+      } else {
+        for (int64_t j = lane; j < n; j += 32) acc += plog2p(__half2float(pr[j]));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) H[r] = -acc * 0.69314718055994531f;
+  }
 }
 
 // reference dispatcher granularity: one tier from the max entropy of a batch

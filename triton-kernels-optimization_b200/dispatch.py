@@ -120,12 +120,14 @@ class EntropyRouter:
     """On-device per-row dispatcher.
 
     ``route(logits)`` launches one kernel over the fp16 logits [M, n]: per-row softmax
-    entropy, dual-threshold route id and the stable compaction of the rows into the
-    INT8 / FP8 / FP16 buckets, all kept in a device workspace.  Every
-    ``gated_linear(A, pack)`` that follows on the same stream reuses that routing for
-    its own activations (row i of A belongs to row i of the logits).  There is no host
-    round trip; ``H``, ``route_ids``, ``counts`` and ``perm`` are views into the
-    workspace, valid until the next ``route``.
+    entropy, dual-threshold route id, the bucket counts and the per-chunk scan that
+    fixes each row's place in the stable INT8 / FP8 / FP16 order, all kept in a device
+    workspace.  Every ``gated_linear(A, pack)`` that follows on the same stream reuses
+    that routing for its own activations (row i of A belongs to row i of the logits).
+    There is no host round trip; ``H``, ``route_ids``, ``counts`` and ``perm`` are views
+    into the workspace, valid until the next ``route``.  ``H``, ``route_ids`` and
+    ``counts`` are filled by ``route``; ``perm`` (position -> row) by the first
+    ``pack_rows`` / ``gated_linear`` after it, which places the rows.
     """
 
     def __init__(self, tau_low: float = 0.41, tau_high: float = 1.68):

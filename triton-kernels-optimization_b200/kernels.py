@@ -288,3 +288,31 @@ def fused_softmax_entropy(logits: torch.Tensor, causal: bool = True):
         call("ee_fused_softmax_entropy_4d", logits.data_ptr(), B, Hh, S, int(bool(causal)), probs.data_ptr(),
              row_entropies.data_ptr(), per_batch.data_ptr(), _stream())
     return probs, per_batch
+
+
+def attention_entropy(attn_weights: torch.Tensor, return_rows: bool = False):
+    """Entropy of attention probabilities as the reference's Llama block computes it
+    (EE/python/dispatch.py:243-245): ``-(p * log(p + 1e-10)).sum(-1)`` in fp32, then
+    the mean over heads and query positions.
+
+    attn_weights: fp16 or fp32 [B, H, S, S_k] (any leading shape with the batch first;
+    the last dim is reduced) -> per-batch mean entropy fp32 [B] (and the per-row
+    entropies [B, H, S] when ``return_rows``).
+    """
+    _check_cuda(attn_weights, "attn_weights")
+    _require(attn_weights.dim() >= 2, "attn_weights needs a batch and a key dimension")
+    p = attn_weights
+    if p.dtype not in (torch.float16, torch.float32):
+        p = p.float()
+    if p.stride(-1) != 1 or not p.is_contiguous():
+        p = p.contiguous()
+    B, n = p.shape[0], p.shape[-1]
+    rows = p.numel() // n if n else 0
+    row_h = torch.empty(p.shape[:-1], dtype=torch.float32, device=p.device)
+    batch_h = torch.empty(B, dtype=torch.float32, device=p.device)
+    dtype = 1 if p.dtype == torch.float32 else 0
+    with torch.cuda.device(p.device):
+        call("ee_attention_entropy", p.data_ptr(), dtype, rows, n, n, row_h.data_ptr(), B,
+             batch_h.data_ptr() if rows else None, _stream())
+    return (batch_h, row_h) if return_rows else batch_h
+
