@@ -207,6 +207,13 @@ EE_API int ee_linear_int8_noalloc(const void* A, int64_t lda, const int8_t* W_nk
 EE_API size_t ee_gated_workspace_bytes(int64_t M, int64_t K);
 EE_API int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high, float* H,
                  int8_t* route, int32_t* bucket_counts, void* workspace, size_t workspace_bytes, void* stream);
+/* ee_gate_rows for callers that already hold one entropy per row (the Llama block's
+ * per-token router: the mean over heads of the attention entropy of each query
+ * position): routes the M rows of H (fp32, device) into the workspace, ready for
+ * ee_gated_gemm / ee_gated_pack.  No counterpart in the reference, which gates whole
+ * batches (EE/python/dispatch.py:64). */
+EE_API int ee_gate_entropies(const float* H, int64_t M, double tau_low, double tau_high, int8_t* route,
+                             int32_t* bucket_counts, void* workspace, size_t workspace_bytes, void* stream);
 EE_API int ee_gated_gemm(const void* A, int64_t lda, int64_t M, int64_t K, const int8_t* W_i8_nk,
                   const uint8_t* W_e4m3_nk, const void* W_f16_nk, const float* w_scale, int64_t N, void* Y,
                   int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);

@@ -75,9 +75,16 @@ def _config1_logits(rng, rows, n):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="reference checkout root")
+    ap.add_argument("--only", choices=["attention"], default=None,
+                    help="write only this fixture (the others are left as they are)")
     args = ap.parse_args(argv)
     pydir = os.path.join(args.reference, "entropy-engine (1)", "entropy-engine", "python")
     sys.path.insert(0, pydir)
+    if args.only == "attention":
+        import dispatch as D  # the reference's dispatch.py
+
+        _attention_goldens(D)
+        return
     _patch_fp8_cast()
     import triton
     import kernels as K  # the reference's kernels.py
@@ -157,7 +164,52 @@ def main(argv=None):
         cases.append({"tau_low": tl_, "tau_high": th_, "submitted": seq, "tiers": tiers, "counts": stats})
     with open(os.path.join(HERE, "golden_dispatch.json"), "w") as f:
         json.dump({"cases": cases}, f, indent=1)
+    _attention_goldens(D)
     print("golden vectors written to", HERE)
+
+
+def _attention_goldens(D):
+    """The Llama-path router input: the reference block's own
+    _attention_with_fused_entropy (EE/python/dispatch.py:212-247) over a small
+    transformers LlamaAttention (eager, CPU), recording the attention probabilities it
+    produced and the per-batch entropy it returned."""
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaAttention, LlamaRotaryEmbedding
+
+    out = {}
+    for tag, (B, S, hidden, heads, kv, dtype) in {"b2s48": (2, 48, 128, 4, 2, torch.float32),
+                                                   "b1s64h": (1, 64, 128, 4, 4, torch.float16),
+                                                   "b3s33": (3, 33, 64, 2, 1, torch.float32)}.items():
+        torch.manual_seed(1234 + S)
+        cfg = LlamaConfig(hidden_size=hidden, num_attention_heads=heads, num_key_value_heads=kv,
+                          intermediate_size=4 * hidden, num_hidden_layers=1, vocab_size=64,
+                          attn_implementation="eager")
+        attn = LlamaAttention(cfg, layer_idx=0).to(dtype).eval()
+        rope = LlamaRotaryEmbedding(cfg)
+        x = (torch.randn(B, S, hidden) * 2.0).to(dtype)
+        pos = torch.arange(S)[None].expand(B, S)
+        cos, sin = rope(x, pos)
+        mask = torch.full((S, S), float("-inf")).triu(1)[None, None].to(dtype)
+
+        class _Block:  # the attributes _attention_with_fused_entropy reads
+            self_attn = attn
+
+        captured = {}
+        real = attn.forward
+
+        def forward(*a, **k):
+            res = real(*a, **k)
+            captured["p"] = res[1].detach().clone()
+            return res
+
+        attn.forward = forward
+        with torch.no_grad():
+            _, entropy_batch, _ = D.EntropyDispatchedLlamaBlock._attention_with_fused_entropy(
+                _Block(), x, attention_mask=mask, position_ids=pos, position_embeddings=(cos, sin))
+        p = captured["p"]
+        out[f"{tag}_p"] = p.numpy()
+        out[f"{tag}_entropy"] = entropy_batch.float().numpy()
+    np.savez_compressed(os.path.join(HERE, "golden_attention.npz"), **out)
 
 
 if __name__ == "__main__":

@@ -88,6 +88,36 @@ def test_4d_surface_against_reference_goldens(pkg, cuda, tag):
     assert np.abs(probs.cpu().numpy().astype(np.float64) - g[f"{tag}_probs"].astype(np.float64)).max() <= 1e-3
 
 
+@pytest.mark.parametrize("tag", ["b2s48", "b1s64h", "b3s33"])
+def test_attention_entropy_against_reference_goldens(pkg, cuda, tag):
+    """Probabilities produced by a transformers LlamaAttention inside the reference's
+    own block code, and the entropy that code returned (fp16 and fp32; n = 33 takes
+    the unvectorised path)."""
+    g = np.load(os.path.join(GOLDEN, "golden_attention.npz"))
+    p = g[f"{tag}_p"]
+    batch, rows = pkg.attention_entropy(_dev(p, cuda), return_rows=True)
+    np.testing.assert_allclose(batch.cpu().numpy(), g[f"{tag}_entropy"], rtol=1e-4, atol=1e-6)
+    _, rows_ref = orc.attention_entropy(p)
+    np.testing.assert_allclose(rows.cpu().numpy(), rows_ref, rtol=1e-4, atol=1e-6)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_attention_entropy_config4_shape(pkg, cuda, dtype):
+    """[B, H, S, S] causal attention probabilities at a config-4-like size."""
+    B, Hh, S = 2, 8, 512
+    g = torch.Generator(device=cuda).manual_seed(44)
+    scores = torch.randn(B, Hh, S, S, generator=g, device=cuda) * 3.0
+    scores = scores.masked_fill(torch.ones(S, S, dtype=torch.bool, device=cuda).triu(1), float("-inf"))
+    p = torch.softmax(scores, dim=-1).to(dtype)
+    batch, rows = pkg.attention_entropy(p, return_rows=True)
+    want_b, want_r = orc.attention_entropy(p.cpu().numpy())
+    np.testing.assert_allclose(batch.cpu().numpy(), want_b, rtol=1e-4)
+    np.testing.assert_allclose(rows.cpu().numpy(), want_r, rtol=1e-4, atol=1e-6)
+    # the reference's own torch expression on the same tensor
+    ref = -(p.float() * torch.log(p.float() + 1e-10)).sum(dim=-1).mean(dim=(1, 2))
+    np.testing.assert_allclose(batch.cpu().numpy(), ref.cpu().numpy(), rtol=1e-4)
+
+
 # ----------------------------------------------------------------------- config 1 (gating step)
 def test_config1_gated_step_against_oracle(pkg, cuda):
     inp = orc.make_gating_inputs(M=1024, n=4096, K=4096, N=4096, seed=101)

@@ -100,3 +100,82 @@ def test_missing_rank_is_detected_on_the_host(tmp_path):
     mp.start_processes(_worker_liveness, args=(2, _free_port(), out), nprocs=2, start_method="spawn")
     msg = open(out).read()
     assert "ranks [1] did not reach 'step1'" in msg
+
+
+class _OracleOps:
+    """Mode T's device operations restated with the CPU oracle (per-row tiers)."""
+
+    def __init__(self, tau_low, tau_high):
+        self.tl, self.th = tau_low, tau_high
+
+    @staticmethod
+    def pack(weight):
+        return orc.quantize_weights_int8(weight.numpy())
+
+    def _lin(self, x, H, w):
+        tiers = orc.route(H.numpy(), self.tl, self.th)
+        xn = x.numpy()
+        out = np.zeros((xn.shape[0], w[0].shape[1]), dtype=np.float16)
+        for t in (0, 1, 2):
+            idx = np.nonzero(tiers == t)[0]
+            if idx.size:
+                out[idx] = orc.linear_by_tier(xn[idx], w[0], w[1], t)
+        return torch.from_numpy(out)
+
+    def gate_up(self, x, H, gate, up):
+        return self._lin(x, H, gate), self._lin(x, H, up)
+
+    def down(self, h, H, down):
+        return self._lin(h, H, down)
+
+
+def _mlp_inputs(m_total=24, d=64, inter=256, seed=11):
+    rng = np.random.default_rng(seed)
+    return {"x": orc.activations(m_total, d, rng, outliers=True),
+            "H": rng.uniform(0.0, 2.5, size=m_total).astype(np.float32),
+            "wg": (rng.standard_normal((inter, d)) * 0.05).astype(np.float16),
+            "wu": (rng.standard_normal((inter, d)) * 0.05).astype(np.float16),
+            "wd": (rng.standard_normal((d, inter)) * 0.05).astype(np.float16)}
+
+
+def _worker_mode_t(rank, world, port, inp, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    sh = _sharding()
+    m = inp["x"].shape[0] // world
+    mlp = sh.ColumnParallelGatedMLP(torch.from_numpy(inp["wg"]), torch.from_numpy(inp["wu"]),
+                                    torch.from_numpy(inp["wd"]), world, rank, ops=_OracleOps(0.41, 1.68))
+    assert mlp.cols[rank][1] - mlp.cols[rank][0] == inp["wg"].shape[0] // world
+    rows = slice(rank * m, (rank + 1) * m)
+    y = mlp.forward(torch.from_numpy(inp["x"][rows]), torch.from_numpy(inp["H"][rows]))
+    y_all = sh.gather_rows(y.view(torch.int16).to(torch.int32), world)  # gloo has no int16
+    if rank == 0:
+        np.save(out_path, y_all.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_column_parallel_mlp_equals_single_rank(tmp_path):
+    """Mode T (gate / up split by column, rows exchanged with an all-gather and an
+    all-to-all) gives the single-rank MLP bit for bit."""
+    inp = _mlp_inputs()
+    out = str(tmp_path / "mode_t.npy")
+    mp.start_processes(_worker_mode_t, args=(2, _free_port(), inp, out), nprocs=2, start_method="spawn")
+    sh = _sharding()
+    single = sh.ColumnParallelGatedMLP(torch.from_numpy(inp["wg"]), torch.from_numpy(inp["wu"]),
+                                       torch.from_numpy(inp["wd"]), 1, 0, ops=_OracleOps(0.41, 1.68))
+    want = single.forward(torch.from_numpy(inp["x"]), torch.from_numpy(inp["H"]))
+    got = np.load(out)
+    assert np.array_equal(got, want.view(torch.int16).to(torch.int32).numpy())
+    tiers = orc.route(inp["H"], 0.41, 1.68)
+    assert set(np.unique(tiers).tolist()) == {0, 1, 2}
+
+
+def test_column_shard_groups():
+    sh = _sharding()
+    spans = [sh.column_shard(14336, 8, r) for r in range(8)]
+    assert spans[0] == (0, 1792) and spans[-1] == (12544, 14336)
+    assert all(a % 128 == 0 and b % 128 == 0 for a, b in spans)
+    with pytest.raises(ValueError):
+        sh.column_shard(100, 2, 0)
+

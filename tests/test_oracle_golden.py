@@ -154,3 +154,14 @@ def test_dispatcher_tiers():
             tiers.append(orc.batch_max_tier(np.atleast_1d(np.array(v, dtype=np.float32)), c["tau_low"],
                                             c["tau_high"]))
         assert tiers == c["tiers"], (c, tiers)
+
+
+@pytest.mark.parametrize("tag", ["b2s48", "b1s64h", "b3s33"])
+def test_attention_entropy_matches_reference_block(tag):
+    """The Llama block's router input: the oracle restatement against the entropy the
+    reference's own _attention_with_fused_entropy returned on the same probabilities."""
+    g = np.load(os.path.join(GOLDEN, "golden_attention.npz"))
+    batch, rows = orc.attention_entropy(g[f"{tag}_p"])
+    np.testing.assert_allclose(batch, g[f"{tag}_entropy"], rtol=2e-6, atol=1e-7)
+    assert rows.shape == g[f"{tag}_p"].shape[:-1]
+

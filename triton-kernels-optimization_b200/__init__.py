@@ -19,6 +19,7 @@ from .dispatch import (
     tier_of,
 )
 from .engine import CubinEngine, GatedLayerEngine
+from .llama import EntropyDispatchedLlamaBlock, build_dispatched_llama
 from .kernels import (
     WeightPack,
     attention_entropy,

@@ -52,6 +52,7 @@ SIGNATURES = {
     "ee_linear_int8_noalloc": (c_int, [_P, c_int64, _P, _P, _P, c_int64, c_int64, c_int64, c_int64, _P]),
     "ee_gated_workspace_bytes": (c_size_t, [c_int64, c_int64]),
     "ee_gate_rows": (c_int, [_P, c_int64, c_int64, c_int64, c_double, c_double, _P, _P, _P, _P, c_size_t, _P]),
+    "ee_gate_entropies": (c_int, [_P, c_int64, c_double, c_double, _P, _P, _P, c_size_t, _P]),
     "ee_gated_gemm": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, _P, _P, c_int64, _P, c_int64, _P, c_size_t,
                               _P]),
     "ee_gated_pack": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_size_t, _P]),

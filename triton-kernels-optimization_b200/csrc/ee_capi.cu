@@ -591,6 +591,29 @@ int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double ta
   return EE_OK;
 }
 
+int ee_gate_entropies(const float* H, int64_t M, double tau_low, double tau_high, int8_t* route, int32_t* bucket_counts,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 0 || M > kMaxDim) return fail(EE_ERR_INVALID, "bad M=%lld", (long long)M);
+  int st = check_ws(workspace, workspace_bytes, gated_ws_bytes(M, 0));
+  if (st != EE_OK) return st;
+  if (H == nullptr && M > 0) return fail(EE_ERR_INVALID, "H is NULL");
+  if (reinterpret_cast<uintptr_t>(H) & 3u) return fail(EE_ERR_MISALIGNED, "H must be 4-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  GatedWs w = gated_ws(workspace, M, 0);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, 128, s);  // ticket, counts, GEMM tile scheduler
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+  if (M > 0 && (st = check_launch(ee::launch_route_entropies(H, M, tau_low, tau_high, w.H, w.route, w.chunk_tab,
+                                                              w.counts, w.ticket, s),
+                                  "route_entropies")) != EE_OK)
+    return st;
+  if (route && M > 0 && (e = cudaMemcpyAsync(route, w.route, M, cudaMemcpyDeviceToDevice, s)) != cudaSuccess)
+    return cuda_fail(e, "cudaMemcpyAsync(route)");
+  if (bucket_counts &&
+      (e = cudaMemcpyAsync(bucket_counts, w.counts, 3 * sizeof(int32_t), cudaMemcpyDeviceToDevice, s)) != cudaSuccess)
+    return cuda_fail(e, "cudaMemcpyAsync(counts)");
+  return EE_OK;
+}
+
 int ee_gated_workspace_layout(int64_t M, int64_t K, int64_t* offsets) {
   if (M < 0 || K < 0 || offsets == nullptr) return fail(EE_ERR_INVALID, "bad arguments");
   char* base = nullptr;

@@ -107,70 +107,104 @@ __device__ __forceinline__ void mma_stage(uint32_t d_tmem, uint32_t a_addr, uint
   }
 }
 
-// Drains one 32-lane quarter of a 128 x 256 accumulator from TMEM (taddr: its lanes,
-// first column), applies the bucket's epilogue and stores the valid rows.  `pos` is
-// this thread's row position; the whole warp must call it (tcgen05.ld is .sync.aligned).
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, const TileGeo& geo, int b, int pos, int n0,
-                                              uint32_t taddr) {
+// Epilogue of one 32-lane quarter of a 128 x 256 accumulator, in two parts.
+// epilogue_prepare runs before the accumulator is ready: the thread's row (output row,
+// activation scale) and, for the 8-bit buckets, 8 of the tile's 256 column scales per
+// lane (columns n0 + 8*lane ..), so no global load is left on the drain's path.
+// epilogue_drain then reads TMEM 32 columns at a time, one chunk ahead of the math,
+// and builds each chunk's 32 column scales from the lanes that hold them by shuffles.
+struct EpiRow {
+  bool valid;
+  int64_t orow;
+  float sa;
+  float sb[8];
+};
+
+__device__ __forceinline__ EpiRow epilogue_prepare(const GemmArgs& args, const TileGeo& geo, int b, int pos, int n0,
+                                                   int lane) {
+  EpiRow e;
   // end of bucket b's positions, by selects: a runtime index into TileGeo would move
   // the whole struct to the stack
   const int end = (b == 0) ? geo.cnt[0] : (b == 1) ? geo.off[1] + geo.cnt[1] : geo.off[2] + geo.cnt[2];
-  const bool valid = pos < end;
-  const int64_t orow = valid ? (args.perm ? static_cast<int64_t>(args.perm[pos]) : static_cast<int64_t>(pos)) : 0;
-  const float sa = (valid && b != kFP16 && args.out_mode == 0) ? args.sa[pos] : 1.f;
-#pragma unroll 1
-  for (int c = 0; c < kBN / 32; ++c) {
-    uint32_t r[32];
-    __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
-    tmem_ld32(taddr + c * 32, r);
-    tmem_ld_wait(r);
-    const int nc = n0 + c * 32;
-    if (!valid || nc >= args.N) continue;
-    if (args.out_mode == 1) {
-      uint32_t* y = static_cast<uint32_t*>(args.Y) + orow * args.ldy + nc;
+  e.valid = pos < end;
+  e.orow = e.valid ? (args.perm ? static_cast<int64_t>(args.perm[pos]) : static_cast<int64_t>(pos)) : 0;
+  e.sa = (e.valid && b != kFP16 && args.out_mode == 0) ? args.sa[pos] : 1.f;
+  const int c8 = n0 + 8 * lane;
+  if (b != kFP16 && args.out_mode == 0 && c8 < args.N) {  // N % 8 == 0: all 8 or none
+    const float4 q0 = __ldg(reinterpret_cast<const float4*>(args.sb + c8));
+    const float4 q1 = __ldg(reinterpret_cast<const float4*>(args.sb + c8 + 4));
+    e.sb[0] = q0.x; e.sb[1] = q0.y; e.sb[2] = q0.z; e.sb[3] = q0.w;
+    e.sb[4] = q1.x; e.sb[5] = q1.y; e.sb[6] = q1.z; e.sb[7] = q1.w;
+  } else {
 #pragma unroll
-      for (int g = 0; g < 8; ++g)
-        if (nc + 4 * g < args.N) *reinterpret_cast<uint4*>(y + 4 * g) = make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
-      continue;
-    }
-    float f[32];
-    if (b == kFP16) {
+    for (int k = 0; k < 8; ++k) e.sb[k] = 0.f;
+  }
+  return e;
+}
+
+// one 32-column chunk c of the drain (r: its accumulator values); reached by the whole
+// warp (the shuffles), stores only for valid rows and columns
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& args, const EpiRow& e, int b, int n0, int c,
+                                               const uint32_t (&r)[32]) {
+  const int nc = n0 + c * 32;
+  float sbv[32];
+  if (b != kFP16) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
-    } else {
-      float sbv[32];
+    for (int j = 0; j < 32; ++j) sbv[j] = __shfl_sync(0xffffffffu, e.sb[j & 7], 4 * c + (j >> 3));
+  }
+  if (!e.valid || nc >= args.N) return;
+  if (args.out_mode == 1) {
+    uint32_t* y = static_cast<uint32_t*>(args.Y) + e.orow * args.ldy + nc;
 #pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        if (nc + 4 * g < args.N) {
-          const float4 q = __ldg(reinterpret_cast<const float4*>(args.sb + nc + 4 * g));
-          sbv[4 * g] = q.x;
-          sbv[4 * g + 1] = q.y;
-          sbv[4 * g + 2] = q.z;
-          sbv[4 * g + 3] = q.w;
-        } else {
-          sbv[4 * g] = sbv[4 * g + 1] = sbv[4 * g + 2] = sbv[4 * g + 3] = 0.f;
-        }
-      }
-      if (b == kINT8) {
+    for (int g = 0; g < 8; ++g)
+      if (nc + 4 * g < args.N) *reinterpret_cast<uint4*>(y + 4 * g) = make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
+    return;
+  }
+  float f[32];
+  if (b == kFP16) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j])), sa), sbv[j]);
-      } else {
+    for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+  } else if (b == kINT8) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__fmul_rn(__uint_as_float(r[j]), sa), sbv[j]);
-      }
-    }
-    __half* y = static_cast<__half*>(args.Y) + orow * args.ldy + nc;
+    for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j])), e.sa), sbv[j]);
+  } else {
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      if (nc + 8 * g < args.N) {
-        uint4 u;
-        __half2* h2 = reinterpret_cast<__half2*>(&u);
+    for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__fmul_rn(__uint_as_float(r[j]), e.sa), sbv[j]);
+  }
+  __half* y = static_cast<__half*>(args.Y) + e.orow * args.ldy + nc;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) h2[k] = __floats2half2_rn(f[8 * g + 2 * k], f[8 * g + 2 * k + 1]);
-        *reinterpret_cast<uint4*>(y + 8 * g) = u;
-      }
+  for (int g = 0; g < 4; ++g) {
+    if (nc + 8 * g < args.N) {
+      uint4 u;
+      __half2* h2 = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) h2[k] = __floats2half2_rn(f[8 * g + 2 * k], f[8 * g + 2 * k + 1]);
+      *reinterpret_cast<uint4*>(y + 8 * g) = u;
     }
   }
+}
+
+// Drains the quarter's 256 columns (taddr: its lanes, first column); the whole warp
+// calls it (tcgen05.ld is .sync.aligned).  The TMEM read of chunk c+1 is in flight
+// while chunk c is converted and stored.
+__device__ __forceinline__ void epilogue_drain(const GemmArgs& args, const EpiRow& e, int b, int n0, uint32_t taddr) {
+  uint32_t ra[32], rb[32];
+  __syncwarp();
+  tmem_ld32(taddr, ra);
+  tmem_ld_wait(ra);
+#pragma unroll 1
+  for (int c = 0; c < kBN / 32; c += 2) {
+    __syncwarp();
+    tmem_ld32(taddr + (c + 1) * 32, rb);
+    epilogue_chunk(args, e, b, n0, c, ra);
+    tmem_ld_wait(rb);
+    const bool more = c + 2 < kBN / 32;
+    __syncwarp();
+    if (more) tmem_ld32(taddr + (c + 2) * 32, ra);
+    epilogue_chunk(args, e, b, n0, c + 1, rb);
+    if (more) tmem_ld_wait(ra);
+  }
+  __syncwarp();
 }
 
 // ---------------------------------------------------------------------------------
@@ -419,6 +453,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!failed && t >= geo.total) break;
       int pos0 = 0, n0 = 0;
       const int b = failed ? 0 : decode_tile(geo, t, kBM, pos0, n0);
+      const EpiRow er = epilogue_prepare(args, geo, b, pos0 + quarter * 32 + lane, n0, lane);
       if (!failed && !mbar_wait(&acc_full[ab], aphase, abort_flag)) failed = true;
       if (failed) {
         if (lane == 0) {
@@ -428,8 +463,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      epilogue_tile(args, geo, b, pos0 + quarter * 32 + lane, n0,
-                    tmem_base + ab * kBN + (static_cast<uint32_t>(quarter * 32) << 16));
+      epilogue_drain(args, er, b, n0, tmem_base + ab * kBN + (static_cast<uint32_t>(quarter * 32) << 16));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
@@ -747,6 +781,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       if (t >= geo.total) break;
       int pos0, n0;
       const int b = decode_tile(geo, t, kPairRows, pos0, n0);
+      const EpiRow er =
+          epilogue_prepare(args, geo, b, pos0 + static_cast<int>(rank) * 128 + quarter * 32 + lane, n0, lane);
       if (!mbar_wait(&acc_full[ab], aphase, abort_flag)) {
         if (lane == 0) {
           atomicOr(&g_device_error, kErrWaitTimeout);
@@ -755,8 +791,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      epilogue_tile(args, geo, b, pos0 + static_cast<int>(rank) * 128 + quarter * 32 + lane, n0,
-                    tmem_base + ab * kBN + (static_cast<uint32_t>(quarter * 32) << 16));
+      epilogue_drain(args, er, b, n0, tmem_base + ab * kBN + (static_cast<uint32_t>(quarter * 32) << 16));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_acc_empty0 + ab * static_cast<uint32_t>(sizeof(uint64_t)));

@@ -76,6 +76,9 @@ int launch_attention_entropy(const void* P, bool f32, int64_t rows, int64_t n, i
 int launch_batch_max_route(const float* H, int64_t n, double tl, double th, float* max_out, int8_t* tier_out,
                            cudaStream_t s);
 int launch_route(const float* H, int64_t rows, double tl, double th, int8_t* route, cudaStream_t s);
+// route ids of given entropies + the bucket scan (SoftmaxArgs' chunk_tab / counts / ticket)
+int launch_route_entropies(const float* H, int64_t rows, double tl, double th, float* Hws, int8_t* route, int4* tab,
+                           int32_t* counts, uint32_t* ticket, cudaStream_t s);
 
 // ----------------------------------------------------------------- gated GEMM
 constexpr int kBM = 128;          // rows per tile (UMMA M)

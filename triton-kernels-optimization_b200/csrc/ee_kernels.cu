@@ -133,6 +133,13 @@ int launch_batch_max_route(const float* H, int64_t n, double tl, double th, floa
   return status_of(cudaGetLastError());
 }
 
+int launch_route_entropies(const float* H, int64_t rows, double tl, double th, float* Hws, int8_t* route, int4* tab,
+                           int32_t* counts, uint32_t* ticket, cudaStream_t s) {
+  if (rows <= 0) return 0;
+  route_entropies_kernel<<<grid_of(rows, 256), 256, 0, s>>>(H, rows, tl, th, Hws, route, tab, counts, ticket);
+  return status_of(cudaGetLastError());
+}
+
 int launch_route(const float* H, int64_t rows, double tl, double th, int8_t* route, cudaStream_t s) {
   if (rows <= 0) return 0;
   route_kernel<<<grid_of(rows, 256), 256, 0, s>>>(H, rows, tl, th, route);

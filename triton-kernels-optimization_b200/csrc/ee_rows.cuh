@@ -141,9 +141,11 @@ __device__ __noinline__ void scan_route_chunks_last_block(const int8_t* route, i
                                                           uint32_t* ticket) {
   __shared__ int s_last;
   __shared__ int s_part[3][NT / 32];
-  __threadfence();
+  // The block's route writes are ordered before thread 0's fence by the barrier, and the
+  // fence is cumulative: one fence per block, not one per thread.
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence();
     const unsigned prev = atomicAdd(ticket, 1u);
     s_last = (prev == gridDim.x - 1) ? 1 : 0;
   }
@@ -782,6 +784,21 @@ __global__ void __launch_bounds__(256) attention_entropy_kernel(const void* __re
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0) H[r] = -acc * 0.69314718055994531f;
   }
+}
+
+// Routing from given per-row entropies (the per-token router of the Llama block):
+// copies H into the workspace, writes the route ids and runs the bucket scan.
+__global__ void __launch_bounds__(256) route_entropies_kernel(const float* __restrict__ Hin, int64_t rows, double tl,
+                                                              double th, float* __restrict__ Hws,
+                                                              int8_t* __restrict__ route, int4* tab, int32_t* counts,
+                                                              uint32_t* ticket) {
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (r < rows) {
+    const float h = Hin[r];
+    Hws[r] = h;
+    route[r] = route_of(h, tl, th);
+  }
+  scan_route_chunks_last_block<256>(route, rows, tab, counts, ticket);  // every thread reaches it
 }
 
 // reference dispatcher granularity: one tier from the max entropy of a batch

@@ -174,6 +174,21 @@ class EntropyRouter:
                  None, self._ws.data_ptr(), self._ws.numel(), _stream())
         return self.route_ids
 
+    def route_entropy(self, H: torch.Tensor) -> torch.Tensor:
+        """Route M rows from given entropies (fp32 [M] on the device) instead of logits;
+        everything after is the same as after ``route``."""
+        _require(H.is_cuda and H.dim() == 1, "H must be a 1-D CUDA tensor")
+        H = H.detach().to(torch.float32).contiguous()
+        M = H.shape[0]
+        self.reserve(M, self._ws_k, H.device)
+        if M != self.M or self.H is None:
+            self._views(M)
+        self.M = M
+        with torch.cuda.device(H.device):
+            call("ee_gate_entropies", H.data_ptr(), M, self.tau_low, self.tau_high, None, None, self._ws.data_ptr(),
+                 self._ws.numel(), _stream())
+        return self.route_ids
+
     def _check(self, a: torch.Tensor, pack: WeightPack):
         a = _check_act(a)
         M, K = a.shape
@@ -246,14 +261,21 @@ class EntropyDispatchedLinear(nn.Module):
         w_int8, w_scale = quantize_weights_int8(linear.weight)
         layer.weight_int8 = w_int8
         layer.weight_scale = w_scale
-        layer.pack = WeightPack(w_int8, w_scale)
+        layer._pack()
         if has_bias:
             layer.bias = linear.bias.detach().to(torch.float16)
         return layer
 
     def _pack(self) -> WeightPack:
-        if self.pack is None or self.pack.w_i8.device != self.weight_int8.device:
-            self.pack = WeightPack(self.weight_int8, self.weight_scale)
+        """The operand packs of the current buffers.  Rebuilt when a buffer moved or
+        changed: ``module.half()`` (as the reference's build_dispatched_llama applies,
+        EE/python/dispatch.py:254) turns ``weight_scale`` into fp16, and the reference
+        kernels then read those fp16-rounded scales -- so do these packs."""
+        w, s = self.weight_int8, self.weight_scale
+        key = (w.data_ptr(), w._version, w.device, s.data_ptr(), s._version, s.dtype)
+        if self.pack is None or getattr(self, "_pack_key", None) != key:
+            self.pack = WeightPack(w, s.to(torch.float32))
+            self._pack_key = key
         return self.pack
 
     def forward(self, x: torch.Tensor, tier: PrecisionTier = PrecisionTier.FP16) -> torch.Tensor:

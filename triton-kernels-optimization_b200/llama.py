@@ -1,0 +1,121 @@
+"""The reference's entropy-dispatched Llama block (EE/python/dispatch.py:150-259) on the
+B200 kernels.
+
+``EntropyDispatchedLlamaBlock`` keeps the reference's constructor, ``forward``
+signature and outputs: the block's own attention module (transformers, eager, so it
+returns the [B, H, S, S] probabilities) -> attention entropy (``attention_entropy``,
+one HBM pass on the device instead of torch's log / mul / sum / mean chain) -> the
+dispatcher -> gate / up / down as ``EntropyDispatchedLinear``.
+
+``routing="batch"`` is the reference's granularity: one tier per block from the
+batch max of the per-batch entropies (dispatch.py:64), read on the host.
+``routing="token"`` routes every token by its own attention entropy (the mean over
+heads of its query row) on the device: the three MLP projections run as gated
+GEMMs over per-token buckets, with no host round trip; gate and up share one packing
+of their input.
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+from .dispatch import EntropyDispatchedLinear, EntropyRouter, PipelinedEntropyDispatcher, PrecisionTier
+from .kernels import _require, attention_entropy
+
+
+class EntropyDispatchedLlamaBlock(nn.Module):
+    """EE/python/dispatch.py:150-247 with the sm_100a kernels."""
+
+    def __init__(self, llama_block, layer_idx: int = 0, routing: str = "batch"):
+        super().__init__()
+        _require(routing in ("batch", "token"), "routing must be 'batch' or 'token'")
+        self.layer_idx = layer_idx
+        self.routing = routing
+        self.self_attn = llama_block.self_attn
+        self.input_layernorm = llama_block.input_layernorm
+        self.post_attention_layernorm = llama_block.post_attention_layernorm
+        self.gate_proj = EntropyDispatchedLinear.from_linear(llama_block.mlp.gate_proj)
+        self.up_proj = EntropyDispatchedLinear.from_linear(llama_block.mlp.up_proj)
+        self.down_proj = EntropyDispatchedLinear.from_linear(llama_block.mlp.down_proj)
+        self.act_fn = nn.SiLU()
+        self.layer_entropy: Optional[torch.Tensor] = None
+        self.token_entropy: Optional[torch.Tensor] = None
+        self._router: Optional[EntropyRouter] = None
+
+    def forward(self, hidden_states: torch.Tensor, dispatcher: Optional[PipelinedEntropyDispatcher] = None,
+                attention_mask: Optional[torch.Tensor] = None, position_ids: Optional[torch.Tensor] = None,
+                past_key_value=None, use_cache: bool = False, **kwargs) -> Tuple[torch.Tensor, ...]:
+        residual = hidden_states
+        hidden_states = self.input_layernorm(hidden_states)
+        attn_output, entropy_batch, present_kv = self._attention_with_fused_entropy(
+            hidden_states, attention_mask=attention_mask, position_ids=position_ids, past_key_value=past_key_value,
+            use_cache=use_cache, **kwargs)
+        self.layer_entropy = entropy_batch
+        if dispatcher is not None:
+            dispatcher.submit_entropy(entropy_batch)
+        hidden_states = residual + attn_output
+
+        residual = hidden_states
+        hidden_states = self.post_attention_layernorm(hidden_states)
+        if self.routing == "token" and dispatcher is not None:
+            hidden_states = self._mlp_per_token(hidden_states, dispatcher)
+        else:
+            tier = dispatcher.get_tier() if dispatcher is not None else PrecisionTier.FP16
+            gate = self.gate_proj(hidden_states, tier=tier)
+            up = self.up_proj(hidden_states, tier=tier)
+            hidden_states = self.down_proj(self.act_fn(gate) * up, tier=tier)
+        hidden_states = residual + hidden_states
+
+        outputs = (hidden_states,)
+        if use_cache:
+            outputs += (present_kv,)
+        return outputs
+
+    def _mlp_per_token(self, x: torch.Tensor, dispatcher: PipelinedEntropyDispatcher) -> torch.Tensor:
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).to(torch.float16).contiguous()
+        M = x2.shape[0]
+        r = self._router
+        if r is None or r.tau_low != dispatcher.tau_low or r.tau_high != dispatcher.tau_high:
+            r = self._router = EntropyRouter(dispatcher.tau_low, dispatcher.tau_high)
+        r.reserve(M, max(self.gate_proj.in_features, self.down_proj.in_features), x2.device)
+        r.route_entropy(self.token_entropy.reshape(-1))
+        r.pack_rows(x2)  # one packing of the post-norm rows serves gate and up
+        gate = r.gemm_packed(self.gate_proj._pack())
+        up = r.gemm_packed(self.up_proj._pack())
+        out = r.gated_linear(self.act_fn(gate) * up, self.down_proj._pack())
+        return out.reshape(shape[:-1] + (self.down_proj.out_features,))
+
+    def _attention_with_fused_entropy(self, hidden_states: torch.Tensor, attention_mask=None, position_ids=None,
+                                      past_key_value=None, use_cache: bool = False, **kwargs):
+        """EE/python/dispatch.py:212-247: the attention module with its probabilities
+        returned, then their entropy (per batch, and per token for token routing)."""
+        attn_kwargs = dict(attention_mask=attention_mask, position_ids=position_ids, past_key_value=past_key_value,
+                           output_attentions=True, use_cache=use_cache)
+        attn_kwargs.update(kwargs)
+        if "position_embeddings" not in attn_kwargs and hasattr(self.self_attn, "rotary_emb"):
+            attn_kwargs["position_embeddings"] = self.self_attn.rotary_emb(hidden_states, position_ids)
+        attn_outputs = self.self_attn(hidden_states, **attn_kwargs)
+        attn_output = attn_outputs[0]
+        attn_weights = attn_outputs[1]  # [B, H, S, S] post-softmax
+        _require(attn_weights is not None, "the attention module returned no probabilities (use eager attention)")
+        present_kv = attn_outputs[2] if use_cache and len(attn_outputs) > 2 else None
+        entropy_batch, rows = attention_entropy(attn_weights, return_rows=True)
+        self.token_entropy = rows.mean(dim=1)  # [B, S]: per query position, mean over heads
+        return attn_output, entropy_batch, present_kv
+
+
+def build_dispatched_llama(model, tau_low: float, tau_high: float, routing: str = "batch"):
+    """EE/python/dispatch.py:250-259: wraps every decoder layer of a transformers Llama
+    model; returns (blocks, dispatcher)."""
+    device = next(model.parameters()).device
+    blocks = []
+    for i, layer in enumerate(model.model.layers):
+        block = EntropyDispatchedLlamaBlock(layer, layer_idx=i, routing=routing)
+        block = block.to(device).half()
+        block.eval()
+        blocks.append(block)
+    dispatcher = PipelinedEntropyDispatcher(tau_low=tau_low, tau_high=tau_high)
+    return blocks, dispatcher
