@@ -25,9 +25,11 @@ the host CPU (oracle/ee_cpu_reference.py) on a bounded sample of rows.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import math
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -66,13 +68,14 @@ DTYPE = "s8/e4m3/f16 operands, s32/f32 accumulate"
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--steps", type=int, default=1500)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--rows", type=int, default=4096, help="token rows per GPU")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the configs 1-3 measurements")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
     return ap.parse_args(argv)
 
@@ -104,7 +107,7 @@ def config_dict(M: int, world: int, mix=None) -> dict:
 class ClockSampler:
     """nvidia-smi sampling during the timed region (start before, stop after)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -122,7 +125,9 @@ class ClockSampler:
         except OSError:
             self.proc = None
 
-    def stop(self) -> dict:
+    def stop(self, window=None) -> dict:
+        """Summary of the samples whose timestamp lies in ``window`` = (t0, t1) host
+        epoch seconds (the timed region); all samples when none falls inside."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         time.sleep(0.15)
@@ -132,23 +137,26 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.fh.close()
-        sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
         with open(self.path) as f:
             for line in f:
                 parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9 or parts[0] not in self.gpus:
+                if len(parts) < 10 or parts[1] not in self.gpus:
                     continue
                 try:
-                    sm.append(float(parts[1]))
-                    smax.append(float(parts[2]))
+                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                    rows.append((ts, float(parts[2]), float(parts[3]), float(parts[4]), parts[6:10]))
                 except ValueError:
                     continue
-                for name, val in zip(names, parts[5:9]):
-                    if val.lower() == "active":
-                        reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        inside = [r for r in rows if window and window[0] - 0.05 <= r[0] <= window[1] + 0.05]
+        use = inside or rows
+        reasons = {n for r in use for n, v in zip(names, r[4]) if v.lower() == "active"}
+        sm = [r[1] for r in use]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_min_mhz": min(sm) if sm else None,
+                "sm_max_mhz": max(r[2] for r in use) if use else None,
+                "power_w_median": statistics.median([r[3] for r in use]) if use else None,
+                "reasons": sorted(reasons), "samples": len(use), "in_timed_region": bool(inside)}
 
 
 # ----------------------------------------------------------------------------- peaks
@@ -301,6 +309,102 @@ def run_reference(args) -> int:
 
 
 # ----------------------------------------------------------------------------- GPU
+def measure_configs(torch, pkg, dev, peaks, flush) -> dict:
+    """Configs 1-3 of the path's scope at their own shapes (one GPU, L2 flushed before
+    every timed call, CUDA events, median of 7):
+      1  gating step, M = 1024: logits [1024, 4096] with per-row scale log-uniform in
+         [0.05, 20]; route + pack + gated GEMM, K = N = 4096;
+      2  the reference surface's standalone INT8 / FP8 linears (triton_int8_gemm /
+         triton_fp8_gemm: activation quantisation included), 1024 x 4096 x 4096, 1 % x20
+         activation outliers;
+      3  the Llama-3-8B projections at M = 16, 128, 1024, 4096 rows: pack + gated GEMM
+         with the bench's routing law.
+    frac = roofline time / measured time, roofline = max(sum_b flops_b / peak_b, bytes /
+    HBM): tensor-bound at large M, weight-streaming (HBM) at small M."""
+    E = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    peak = {0: peaks.get("int8_tops", 2900.0), 1: peaks.get("fp8_tflops", 3000.0), 2: peaks["bf16_tflops"]}
+    hbm = peaks["hbm_gbs"]
+
+    def timed(fn, reps=7):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            flush()
+            torch.cuda._sleep(1_000_000)
+            a, b = E(), E()
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3)
+        return statistics.median(ts)
+
+    def roofline_us(M_b, K, N):
+        flops = sum(2.0 * m * N * K / (peak[b] * 1e12) for b, m in enumerate(M_b))
+        wbytes = sum((N * K * (2 if b == 2 else 1)) for b, m in enumerate(M_b) if m)
+        abytes = sum(m * K * (2 if b == 2 else 1) for b, m in enumerate(M_b)) + 2 * sum(M_b) * N
+        return max(flops, (wbytes + abytes) / (hbm * 1e9)) * 1e6
+
+    g = torch.Generator(device=dev).manual_seed(77)
+    out = {}
+    # ---- config 3 (and config 1 at K = N = 4096, M = 1024)
+    c3 = {}
+    for K, N in [(4096, 4096), (4096, 14336), (14336, 4096)]:
+        w = (torch.randn(N, K, generator=g, device=dev) * 0.02).half()
+        pack = pkg.WeightPack.from_weight(w)
+        del w
+        for M in (16, 128, 1024, 4096):
+            lo, hi = math.log(SCALE_RANGE[0]), math.log(SCALE_RANGE[1])
+            sc = torch.exp(torch.rand(M, 1, generator=g, device=dev) * (hi - lo) + lo)
+            lg = (torch.randn(M, N_LOGIT, generator=g, device=dev) * sc).half()
+            a = torch.randn(M, K, generator=g, device=dev).half()
+            y = torch.empty(M, N, dtype=torch.float16, device=dev)
+            r = pkg.EntropyRouter(*TAU)
+            r.reserve(M, K, dev)
+            r.route(lg)
+            cnt = r.counts.cpu().tolist()
+            us = timed(lambda: (r.pack_rows(a), r.gemm_packed(pack, out=y)))
+            t_roof = roofline_us(cnt, K, N)
+            c3[f"M{M}_K{K}_N{N}"] = {"us": round(us, 2), "tflops": round(2.0 * M * N * K / us / 1e6, 1),
+                                    "roofline_frac": round(t_roof / us, 3), "mix": cnt}
+        del pack
+    out["config3_pack_plus_gated_gemm"] = c3
+    # ---- config 1: route + pack + gated GEMM, M = 1024, the config-1 logit law
+    M, K, N = 1024, 4096, 4096
+    s1 = torch.exp(torch.rand(M, 1, generator=g, device=dev) * (math.log(20.0) - math.log(0.05)) + math.log(0.05))
+    lg = (torch.randn(M, N_LOGIT, generator=g, device=dev) * s1).half()
+    a = torch.randn(M, K, generator=g, device=dev).half()
+    pack = pkg.WeightPack.from_weight((torch.randn(N, K, generator=g, device=dev) * 0.02).half())
+    y = torch.empty(M, N, dtype=torch.float16, device=dev)
+    r = pkg.EntropyRouter(*TAU)
+    r.reserve(M, K, dev)
+    us = timed(lambda: (r.route(lg), r.gated_linear(a, pack, out=y)))
+    cnt = r.counts.cpu().tolist()
+    us_route = timed(lambda: r.route(lg))
+    route_bytes = 2 * M * N_LOGIT + 5 * M
+    out["config1_gating_step"] = {"us": round(us, 2), "tflops": round(2.0 * M * N * K / us / 1e6, 1), "mix": cnt,
+                                  "route_us": round(us_route, 2),
+                                  "route_gbs": round(route_bytes / us_route / 1e3, 1)}
+    # ---- config 2: the reference surface, activation quantisation included
+    a2 = torch.randn(M, K, generator=g, device=dev)
+    a2 = torch.where(torch.rand(M, K, generator=g, device=dev) < 0.01, a2 * 20.0, a2).half()
+    w_kn, w_s = pkg.quantize_weights_int8((torch.randn(N, K, generator=g, device=dev) * 0.02).half())
+    pkg.triton_int8_gemm(a2, w_kn, w_s)  # builds the cached operand packs
+    c2 = {}
+    for name, fn, b in (("int8", pkg.triton_int8_gemm, 0), ("fp8", pkg.triton_fp8_gemm, 1),
+                        ("fp16_w8a16", pkg.triton_fp16_gemm, 2)):
+        us = timed(lambda: fn(a2, w_kn, w_s))
+        Mb = [0, 0, 0]
+        Mb[b] = M
+        c2[name] = {"us": round(us, 2), "tflops": round(2.0 * M * N * K / us / 1e6, 1),
+                    "roofline_frac": round(roofline_us(Mb, K, N) / us, 3)}
+    out["config2_reference_surface_1024x4096x4096"] = c2
+    out["note"] = ("one GPU; L2 flushed before each timed call; roofline = max(flops / measured peak per "
+                   "precision, bytes / measured HBM)")
+    return out
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
     if args.impl == "reference":
@@ -372,14 +476,16 @@ def main(argv=None) -> int:
     if sampler:
         sampler.start()
         time.sleep(0.3)
+    t_region = time.time()
     for k in range(args.steps):
         flush()  # between steps, outside the step's events
         step_evs[k][0].record()
         engine.launch()
         step_evs[k][1].record()
     torch.cuda.synchronize()
+    t_region = (t_region, time.time())
     barrier()
-    clocks = sampler.stop() if sampler else None
+    clocks = sampler.stop(t_region) if sampler else None
     pkg._lib.device_check()
     total_ms = sum(a.elapsed_time(b) for a, b in step_evs)
     if world > 1:
@@ -402,50 +508,82 @@ def main(argv=None) -> int:
     gemm_ms = [[ev[2 + 2 * p].elapsed_time(ev[3 + 2 * p]) for p in range(n_proj)] for ev in evs]
 
     # ------------------------------------------------------------------ e2e (public API, host buffers)
+    # Every step copies its inputs from pinned host memory, runs the public API
+    # (EntropyRouter.route + gated_linear per projection) and copies every output back.
+    # Steps are pipelined the way a serving loop over a stream of batches runs them: copy-in,
+    # compute and copy-out on three streams with two buffer sets, so step k+1's upload and
+    # step k-1's download overlap step k's compute (PCIe is full duplex).  The inputs of a
+    # step (218 MB) exceed L2, so no flush is needed between steps.  The unpipelined time
+    # per step is reported beside it.
     e2e = None
     if not args.no_e2e:
         h_logits = logits.cpu().pin_memory()
         h_acts = [a.cpu().pin_memory() for a in acts]
-        h_ys = [torch.empty(y.shape, dtype=y.dtype, pin_memory=True) for y in ys]
         h2d = h_logits.numel() * 2 + sum(a.numel() * 2 for a in h_acts)
         d2h = sum(y.numel() * 2 for y in ys)
         K2 = max(1, args.e2e_steps)
-        evs2 = [(E(), E()) for _ in range(K2)]
+        NB = 2
+        d_in = [(torch.empty_like(logits), [torch.empty_like(a) for a in acts]) for _ in range(NB)]
+        d_out = [[torch.empty_like(y) for y in ys] for _ in range(NB)]
+        h_out = [[torch.empty(y.shape, dtype=y.dtype, pin_memory=True) for y in ys] for _ in range(NB)]
+        s_in, s_cmp, s_out = (torch.cuda.Stream(device=dev) for _ in range(3))
 
-        def e2e_step(ev):
-            ev[0].record()
-            logits.copy_(h_logits, non_blocking=True)
-            for a, ha in zip(acts, h_acts):
-                a.copy_(ha, non_blocking=True)
-            router.route(logits)
-            for p in range(n_proj):
-                router.gated_linear(acts[p], packs[p], out=ys[p])
-            for y, hy in zip(ys, h_ys):
-                hy.copy_(y, non_blocking=True)
-            ev[1].record()
+        def e2e_run(steps):
+            ev_in = [torch.cuda.Event() for _ in range(steps)]
+            ev_cmp = [torch.cuda.Event() for _ in range(steps)]
+            ev_out = [torch.cuda.Event() for _ in range(steps)]
+            t0, t1 = E(), E()
+            t0.record(s_in)
+            for k in range(steps):
+                b = k % NB
+                d_logits, d_acts = d_in[b]
+                with torch.cuda.stream(s_in):
+                    if k >= NB:
+                        s_in.wait_event(ev_cmp[k - NB])  # buffer set b is free again
+                    d_logits.copy_(h_logits, non_blocking=True)
+                    for a, ha in zip(d_acts, h_acts):
+                        a.copy_(ha, non_blocking=True)
+                    ev_in[k].record(s_in)
+                with torch.cuda.stream(s_cmp):
+                    s_cmp.wait_event(ev_in[k])
+                    if k >= NB:
+                        s_cmp.wait_event(ev_out[k - NB])  # outputs b were downloaded
+                    router.route(d_logits)
+                    for p in range(n_proj):
+                        router.gated_linear(d_acts[p], packs[p], out=d_out[b][p])
+                    ev_cmp[k].record(s_cmp)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(ev_cmp[k])
+                    for y, hy in zip(d_out[b], h_out[b]):
+                        hy.copy_(y, non_blocking=True)
+                    ev_out[k].record(s_out)
+            s_out.wait_stream(s_in)
+            t1.record(s_out)
+            torch.cuda.synchronize()
+            return t0.elapsed_time(t1)
 
-        for _ in range(2):
-            e2e_step((E(), E()))
-        torch.cuda.synchronize()
+        e2e_run(2)  # warm-up
         barrier()
-        for ev in evs2:
-            flush()
-            e2e_step(ev)
-        torch.cuda.synchronize()
+        e2e_total = e2e_run(K2)
+        serial_ms = min(e2e_run(1) for _ in range(3))  # one step alone: nothing to overlap
         barrier()
-        e2e_total = sum(a.elapsed_time(b) for a, b in evs2)
         if world > 1:
             t = torch.tensor([e2e_total], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_total = float(t.item())
         e2e = {"value": world * step_flops(M) * K2 / (e2e_total / 1e3) / 1e12, "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_total / K2,
-               "path": "EntropyRouter.route + EntropyRouter.gated_linear per projection, pinned host in/out"}
+               "ms_per_step_unpipelined": serial_ms, "steps": K2,
+               "path": "EntropyRouter.route + EntropyRouter.gated_linear per projection; pinned host in/out; "
+                       "copy-in / compute / copy-out pipelined over 3 streams, 2 buffer sets"}
 
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(torch, logits, acts, w_host, args.cpu_seconds)
+        configs = None
+        if world == 1 and not args.no_configs:
+            configs = measure_configs(torch, pkg, dev, peaks, flush)
         # roofline of the dominant kernel (the bucketed GEMM): effective mixed peak
         c = counts
         f_b = [sum(2.0 * c[b] * K * N for _, K, N in PROJECTIONS) for b in range(3)]
@@ -454,11 +592,13 @@ def main(argv=None) -> int:
         peak_eff = f_tot / sum(f / p for f, p in zip(f_b, p_b))
         gemm_total_ms = sum(sum(x) for x in gemm_ms)
         achieved = f_tot * n_instr / (gemm_total_ms / 1e3) / 1e12
+        # DRAM bytes per launch of the dominant GEMM launch (mlp_up_gate), from the ncu
+        # capture summarised in profiles/ (one `ncu --set full` of the same shape and mix)
         traffic = None
-        tpath = os.path.join(ROOT, "profiles", "gemm_traffic.json")
+        tpath = os.path.join(ROOT, "profiles", "gated_gemm_pair_mlp_up_4096x14336x4096.md")
         if os.path.exists(tpath):
-            with open(tpath) as f:
-                traffic = json.load(f).get("dram_bytes_per_launch")
+            m_t = re.search(r"^dram_bytes_per_launch: (\d+)", open(tpath).read(), re.M)
+            traffic = int(m_t.group(1)) if m_t else None
         gate_bytes = 2.0 * M * N_LOGIT + 4 * M + M
         gate_gbs = gate_bytes * n_instr / (sum(gate_ms) / 1e3) / 1e9
         value = world * step_flops(M) * args.steps / (total_ms / 1e3) / 1e12
@@ -483,13 +623,16 @@ def main(argv=None) -> int:
             "timing": "value / ms_per_step: CUDA-graph replays of the step (GatedLayerEngine), events around each replay",
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_eff, "unit": "TFLOP/s",
                          "frac": achieved / peak_eff, "traffic": traffic,
-                         "kernel": "gated_gemm_kernel (3 launches per step, one per projection)",
+                         "kernel": "gated_gemm_pair_kernel (3 launches per step, one per projection)",
+                         "traffic_note": "ncu DRAM read + write of the mlp_up_gate launch (4096 x 14336 x 4096); "
+                                         "algorithmic bytes of that launch 372 MB",
                          "peak_basis": "effective peak of the bucket mix: fp16 bucket at measured bf16 burst "
                                        "(MEASURED_PEAKS.json), FP8 / INT8 buckets at cuBLAS fp8 / int8 8192^3 "
                                        "measured in this run"},
             "peaks": peaks,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "configs": configs,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
         }

@@ -68,9 +68,10 @@ EE_API int ee_abi_version(void);
 EE_API const char* ee_last_error(void);
 
 /* GEMM tiling policy for every later call in the process (no counterpart in the
- * reference): 0 = automatic (CTA-pair 256 x 256 tiles when a call has more than 128
- * rows, else single-CTA 128 x 256 tiles), 1 = always single-CTA, 2 = always CTA pairs.
- * Results are identical under every policy. */
+ * reference): 0 = automatic (CTA-pair 256 x 256 tiles above 128 rows; at most 128 rows
+ * -- the call streams its weights -- single-CTA 128 x 256 tiles, or 128 x 64 tiles when
+ * the wide ones would leave SMs idle), 1 = always single-CTA 128 x 256, 2 = always CTA
+ * pairs, 3 = always single-CTA 128 x 64.  Results are identical under every policy. */
 EE_API int ee_set_gemm_policy(int policy);
 
 /* Reads and clears the current device's error word (set by a kernel whose bounded

@@ -1,6 +1,7 @@
-"""Both GEMM kernels -- single-CTA 128 x 256 tiles and CTA-pair (tcgen05 cta_group::2)
-256 x 256 tiles -- forced through ee_set_gemm_policy: exact int32 accumulators, fp32
-accumulators, and the gated linear per bucket against the reference formulas."""
+"""Every GEMM tiling -- single-CTA 128 x 256, CTA-pair (tcgen05 cta_group::2) 256 x 256
+and single-CTA 128 x 64 tiles -- forced through ee_set_gemm_policy: exact int32
+accumulators, fp32 accumulators, and the gated linear per bucket against the reference
+formulas."""
 import pytest
 import torch
 
@@ -9,7 +10,7 @@ pytestmark = pytest.mark.gpu
 from test_gpu_gated import _inputs, _ref_fp8, _ref_fp16, _ref_int8, _relf  # noqa: E402
 
 
-@pytest.fixture(params=[1, 2], ids=["single_cta", "cta_pair"])
+@pytest.fixture(params=[1, 2, 3], ids=["single_cta", "cta_pair", "single_cta_narrow"])
 def policy(request, pkg, cuda):
     lib = pkg.load_library()
     assert lib.ee_set_gemm_policy(request.param) == 0

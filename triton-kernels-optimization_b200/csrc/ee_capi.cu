@@ -107,15 +107,31 @@ int check_gemm_shape(int64_t M, int64_t N, int64_t K, int64_t ldy) {
   return EE_OK;
 }
 
-std::atomic<int> g_gemm_policy{0};  // 0 auto, 1 single-CTA tiles, 2 CTA-pair tiles
+std::atomic<int> g_gemm_policy{0};  // 0 auto, 1 single-CTA 128x256, 2 CTA-pair 256x256, 3 single-CTA 128x64
 
-// Encodes the maps for the operands present and launches the persistent kernel: the
-// CTA-pair kernel (256-row tiles) when the problem has more than 128 rows, else the
-// single-CTA kernel.  Unused slots get a copy of a valid map (never dereferenced).
+// Row tiles a call may produce: with routing on the device the bucket sizes are unknown
+// here, and each bucket boundary can add one partial tile.
+int64_t row_tiles(const ee::GemmArgs& args, bool dynamic_counts, int64_t bm) {
+  if (dynamic_counts) return (args.M_cap + bm - 1) / bm + 2;
+  int64_t t = 0;
+  for (int b = 0; b < 3; ++b) t += (args.counts[b] + bm - 1) / bm;
+  return t;
+}
+
+// Encodes the maps for the operands present and launches the persistent kernel.  Auto
+// policy: more than 128 rows -> the CTA-pair kernel (256 x 256 tiles); at most 128 rows
+// the call streams its weights -> single-CTA tiles, 128 x 256 when their count already
+// covers the SMs, else 128 x 64 so that the weight spreads over every SM (measured on
+// B200: M = 16..128 at N = 4096 36 us instead of 42, at N = 14336 the wide tiles stay
+// faster, 58 us against 95).  Unused map slots get a copy of a valid map (never
+// dereferenced).
 int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cudaStream_t s) {
   const int policy = g_gemm_policy.load(std::memory_order_relaxed);
+  const int64_t wide_tiles = row_tiles(args, dynamic_counts, ee::kBM) * ((args.N + ee::kBN - 1) / ee::kBN);
   const bool pair = policy == 2 || (policy == 0 && args.M_cap > ee::kBM);
-  const int wbox = pair ? ee::kBN / 2 : ee::kBN;
+  const bool narrow = policy == 3 || (policy == 0 && !pair && wide_tiles < num_sms());
+  const int bn = narrow ? ee::kBNNarrow : ee::kBN;
+  const int wbox = pair ? ee::kBN / 2 : bn;
   ee::GemmMaps maps;
   std::memset(&maps, 0, sizeof(maps));
   const CUtensorMap* any = nullptr;
@@ -140,22 +156,16 @@ int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cud
   for (int b = 0; b < 3; ++b)
     if (!op.w[b]) maps.w[b] = op.w[0] ? maps.w[0] : (op.w[1] ? maps.w[1] : maps.w[2]);
 
-  const int64_t ntn = (args.N + ee::kBN - 1) / ee::kBN;
+  const int64_t ntn = (args.N + bn - 1) / bn;
   const int64_t bm = pair ? ee::kPairTileRows : ee::kBM;
-  int64_t tiles;
-  if (dynamic_counts) {
-    tiles = ((args.M_cap + bm - 1) / bm + 2) * ntn;  // bucket boundaries add <= 2 row tiles
-  } else {
-    tiles = 0;
-    for (int b = 0; b < 3; ++b) tiles += ((args.counts[b] + bm - 1) / bm) * ntn;
-  }
+  const int64_t tiles = row_tiles(args, dynamic_counts, bm) * ntn;
   if (pair) {
     const int64_t max_pairs = num_sms() / 2;
     const int pairs = static_cast<int>(tiles < max_pairs ? tiles : max_pairs);
     return check_launch(ee::launch_gated_gemm_pair(maps, args, pairs, s), "gated_gemm_pair_kernel");
   }
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  return check_launch(ee::launch_gated_gemm(maps, args, grid, s), "gated_gemm_kernel");
+  return check_launch(ee::launch_gated_gemm(maps, args, grid, bn, s), "gated_gemm_kernel");
 }
 
 ee::GemmArgs base_args(int64_t M_cap, int64_t N, int64_t K, void* Y, int64_t ldy, int out_mode) {
@@ -276,7 +286,8 @@ extern "C" {
 int ee_abi_version(void) { return EE_ABI_VERSION; }
 
 int ee_set_gemm_policy(int policy) {
-  if (policy < 0 || policy > 2) return fail(EE_ERR_INVALID, "policy must be 0 (auto), 1 (single-CTA) or 2 (CTA pair)");
+  if (policy < 0 || policy > 3)
+    return fail(EE_ERR_INVALID, "policy must be 0 (auto), 1 (single-CTA), 2 (CTA pair) or 3 (single-CTA narrow)");
   g_gemm_policy.store(policy, std::memory_order_relaxed);
   return EE_OK;
 }
@@ -554,6 +565,18 @@ size_t ee_gated_workspace_bytes(int64_t M, int64_t K) {
 
 int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high, float* H,
                  int8_t* route, int32_t* bucket_counts, void* workspace, size_t workspace_bytes, void* stream) {
+  return ee::gate_rows_impl(logits, M, n, ld, tau_low, tau_high, H, route, bucket_counts, workspace, workspace_bytes,
+                            stream, true);
+}
+}  // extern "C"
+
+// ee_gate_rows; clear_header = false skips zeroing the workspace header (ticket, counts,
+// GEMM tile counter) for callers that zeroed it once: every kernel of the path leaves it
+// zero again after a clean run, and without the memset node the router launch chains
+// onto the previous kernel (programmatic dependent launch).
+int ee::gate_rows_impl(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high,
+                       float* H, int8_t* route, int32_t* bucket_counts, void* workspace, size_t workspace_bytes,
+                       void* stream, bool clear_header) {
   if (M < 0 || M > kMaxDim) return fail(EE_ERR_INVALID, "bad M=%lld", (long long)M);
   int st = check_ws(workspace, workspace_bytes, gated_ws_bytes(M, 0));
   if (st != EE_OK) return st;
@@ -562,8 +585,9 @@ int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double ta
   if (reinterpret_cast<uintptr_t>(logits) & 1u) return fail(EE_ERR_MISALIGNED, "logits must be 2-byte aligned");
   cudaStream_t s = as_stream(stream);
   GatedWs w = gated_ws(workspace, M, 0);
-  cudaError_t e = cudaMemsetAsync(workspace, 0, 128, s);  // ticket, counts, GEMM tile scheduler
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+  cudaError_t e = cudaSuccess;
+  if (clear_header && (e = cudaMemsetAsync(workspace, 0, 128, s)) != cudaSuccess)  // ticket, counts, tile counter
+    return cuda_fail(e, "cudaMemsetAsync");
   if (M > 0) {
     ee::SoftmaxArgs a;
     std::memset(&a, 0, sizeof(a));
@@ -590,6 +614,8 @@ int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double ta
     return cuda_fail(e, "cudaMemcpyAsync(counts)");
   return EE_OK;
 }
+
+extern "C" {
 
 int ee_gate_entropies(const float* H, int64_t M, double tau_low, double tau_high, int8_t* route, int32_t* bucket_counts,
                       void* workspace, size_t workspace_bytes, void* stream) {

@@ -51,8 +51,9 @@ int64_t max_k(const ee_engine& e) {
 int run_layers(ee_engine& e, void* stream) {
   for (size_t l = 0; l < e.layers.size(); ++l) {
     const ee_gated_layer& L = e.layers[l];
-    int st = ee_gate_rows(L.logits, e.rows, L.n_logits, L.ld_logits, e.tau_low, e.tau_high, nullptr, nullptr,
-                          nullptr, e.workspace, e.workspace_bytes, stream);
+    // the header was zeroed at creation and every kernel leaves it zero: no memset node
+    int st = ee::gate_rows_impl(L.logits, e.rows, L.n_logits, L.ld_logits, e.tau_low, e.tau_high, nullptr, nullptr,
+                                nullptr, e.workspace, e.workspace_bytes, stream, false);
     if (st != EE_OK) return st;
     for (const ee_projection& p : e.projs[l]) {
       st = ee_gated_gemm(p.A, p.lda, e.rows, p.K, p.w_i8_nk, p.w_e4m3_nk, p.w_f16_nk, p.w_scale, p.N, p.Y, p.ldy,
@@ -106,7 +107,8 @@ int ee_engine_create(int64_t rows, double tau_low, double tau_high, int32_t n_la
   }
   e->workspace = workspace;
   e->workspace_bytes = workspace_bytes;
-  if (cudaGetDevice(&e->device) != cudaSuccess || ee::prepare_device() != 0) {
+  if (cudaGetDevice(&e->device) != cudaSuccess || ee::prepare_device() != 0 ||
+      cudaMemset(workspace, 0, 256) != cudaSuccess) {  // the header: ticket, counts, tile counter
     delete e;
     return engine_fail(EE_ERR_CUDA, "ee_engine_create: CUDA device not usable");
   }

@@ -31,19 +31,27 @@ namespace ee {
 __device__ int g_device_error;  // sticky error word, read back by read_and_clear_device_error
 
 constexpr int kAStageBytes = kBM * kBKBytes;  // 16 KB
-constexpr int kBStageBytes = kBN * kBKBytes;  // 32 KB
-constexpr int kStageBytes = kAStageBytes + kBStageBytes;
 constexpr int kGemmThreads = 192;
 constexpr int kTmemCols = 2 * kBN;  // two accumulators
 constexpr int kBarrierBytes = 256;
-constexpr size_t kGemmSmem = 1024 /*alignment slack*/ + size_t(kStages) * kStageBytes + kBarrierBytes;
+// Single-CTA kernel, per tile width BN: B stage bytes, ring depth and shared memory.
+// BN = 256: 48 KB stages x 4; BN = 64 (weight-streaming calls): 24 KB stages x 8.
+template <int BN>
+struct SingleCfg {
+  static constexpr int kBStageBytes = BN * kBKBytes;
+  static constexpr int kStageBytes = kAStageBytes + kBStageBytes;
+  static constexpr int kStages = BN == kBN ? 4 : 8;
+  static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;  // two accumulators (allocation >= 32 columns)
+  static constexpr size_t kSmem = 1024 /*alignment slack*/ + size_t(kStages) * kStageBytes + kBarrierBytes;
+  static_assert(kSmem <= 227 * 1024, "single-CTA GEMM shared memory above the 227 KB per-CTA limit");
+};
 
 struct TileGeo {
   int cnt[3], off[3], mtiles[3], tiles[3];
   int ntn, total;
 };
 
-__device__ __forceinline__ TileGeo make_geo(const GemmArgs& a, int bm) {
+__device__ __forceinline__ TileGeo make_geo(const GemmArgs& a, int bm, int bn = kBN) {
   TileGeo g;
   if (a.dyn_counts != nullptr) {
 #pragma unroll
@@ -55,7 +63,7 @@ __device__ __forceinline__ TileGeo make_geo(const GemmArgs& a, int bm) {
   g.off[0] = 0;
   g.off[1] = g.cnt[0];
   g.off[2] = g.cnt[0] + g.cnt[1];
-  g.ntn = (a.N + kBN - 1) / kBN;
+  g.ntn = (a.N + bn - 1) / bn;
   g.total = 0;
 #pragma unroll
   for (int b = 0; b < 3; ++b) {
@@ -69,19 +77,19 @@ __device__ __forceinline__ TileGeo make_geo(const GemmArgs& a, int bm) {
 // tile index -> bucket, first position (row of A), first output column.  Tiles run
 // FP16 first (the longest K loops), then FP8, then INT8; m fastest inside a bucket.
 // Written out per bucket: a loop with an early return here kept TileGeo on the stack.
-__device__ __forceinline__ int decode_in(const TileGeo& g, int b, int t, int bm, int& pos0, int& n0) {
+__device__ __forceinline__ int decode_in(const TileGeo& g, int b, int t, int bm, int bn, int& pos0, int& n0) {
   const int mt = t % g.mtiles[b];
   const int nt = t / g.mtiles[b];
   pos0 = g.off[b] + mt * bm;
-  n0 = nt * kBN;
+  n0 = nt * bn;
   return b;
 }
-__device__ __forceinline__ int decode_tile(const TileGeo& g, int t, int bm, int& pos0, int& n0) {
-  if (t < g.tiles[2]) return decode_in(g, 2, t, bm, pos0, n0);
+__device__ __forceinline__ int decode_tile(const TileGeo& g, int t, int bm, int& pos0, int& n0, int bn = kBN) {
+  if (t < g.tiles[2]) return decode_in(g, 2, t, bm, bn, pos0, n0);
   t -= g.tiles[2];
-  if (t < g.tiles[1]) return decode_in(g, 1, t, bm, pos0, n0);
+  if (t < g.tiles[1]) return decode_in(g, 1, t, bm, bn, pos0, n0);
   t -= g.tiles[1];
-  if (t < g.tiles[0]) return decode_in(g, 0, t, bm, pos0, n0);
+  if (t < g.tiles[0]) return decode_in(g, 0, t, bm, bn, pos0, n0);
   pos0 = 0;
   n0 = 0;
   return 0;
@@ -93,11 +101,11 @@ __device__ __forceinline__ int kblocks_of(int b, int K) {
 }
 
 // issue the 4 UMMAs (each K = 32 bytes) of one stage
-template <int KIND>
+template <int KIND, int BN>
 __device__ __forceinline__ void mma_stage(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr, bool first) {
-  constexpr uint32_t idesc = (KIND == kKindI8)   ? make_idesc(2u, 1u, kBM, kBN)   // s32 <- s8 x s8
-                             : (KIND == kKindF8) ? make_idesc(1u, 0u, kBM, kBN)   // f32 <- e4m3 x e4m3
-                                                 : make_idesc(1u, 0u, kBM, kBN);  // f32 <- f16 x f16
+  constexpr uint32_t idesc = (KIND == kKindI8)   ? make_idesc(2u, 1u, kBM, BN)   // s32 <- s8 x s8
+                             : (KIND == kKindF8) ? make_idesc(1u, 0u, kBM, BN)   // f32 <- e4m3 x e4m3
+                                                 : make_idesc(1u, 0u, kBM, BN);  // f32 <- f16 x f16
   const uint64_t da = sdesc_k_sw128(a_addr);
   const uint64_t db = sdesc_k_sw128(b_addr);
 #pragma unroll
@@ -187,18 +195,19 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& args, const EpiRo
 // Drains the quarter's 256 columns (taddr: its lanes, first column); the whole warp
 // calls it (tcgen05.ld is .sync.aligned).  The TMEM read of chunk c+1 is in flight
 // while chunk c is converted and stored.
+template <int BN = kBN>
 __device__ __forceinline__ void epilogue_drain(const GemmArgs& args, const EpiRow& e, int b, int n0, uint32_t taddr) {
   uint32_t ra[32], rb[32];
   __syncwarp();
   tmem_ld32(taddr, ra);
   tmem_ld_wait(ra);
 #pragma unroll 1
-  for (int c = 0; c < kBN / 32; c += 2) {
+  for (int c = 0; c < BN / 32; c += 2) {
     __syncwarp();
     tmem_ld32(taddr + (c + 1) * 32, rb);
     epilogue_chunk(args, e, b, n0, c, ra);
     tmem_ld_wait(rb);
-    const bool more = c + 2 < kBN / 32;
+    const bool more = c + 2 < BN / 32;
     __syncwarp();
     if (more) tmem_ld32(taddr + (c + 2) * 32, ra);
     epilogue_chunk(args, e, b, n0, c + 1, rb);
@@ -275,10 +284,18 @@ __device__ __forceinline__ void feed_retire(const GemmArgs& args) {
   }
 }
 
+template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gated_gemm_kernel(const __grid_constant__ CUtensorMap tm_a8, const __grid_constant__ CUtensorMap tm_a16,
                       const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                       const __grid_constant__ CUtensorMap tm_w2, const GemmArgs args) {
+  using Cfg = SingleCfg<BN>;
+  constexpr int kStages = Cfg::kStages;
+  constexpr int kBStageBytes = Cfg::kBStageBytes;
+  constexpr int kStageBytes = Cfg::kStageBytes;
+  constexpr int kTmemCols = Cfg::kTmemCols;
+  static_assert((2 * kStages + 5 + 2 * kTileRing) * 8 + 8 + 4 * kTileRing <= kBarrierBytes,
+                "single-CTA GEMM barrier region overflows");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -296,7 +313,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int* ring = const_cast<int*>(abort_flag + 1);  // [kTileRing] tile indices
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const TileGeo geo = make_geo(args, kBM);
+  griddep_wait();  // bucket counts, packed rows and the tile counter come from earlier kernels
+  griddep_launch_dependents();
+  const TileGeo geo = make_geo(args, kBM, BN);
   const bool dyn = args.sched != nullptr;
   if (static_cast<int>(blockIdx.x) >= geo.total) {  // uniform for the whole CTA
     feed_retire(args);
@@ -351,7 +370,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (t >= geo.total) break;
       int pos0, n0;
-      const int b = decode_tile(geo, t, kBM, pos0, n0);
+      const int b = decode_tile(geo, t, kBM, pos0, n0, BN);
       const int nkb = kblocks_of(b, K);
       const int kstep = (b == kFP16) ? kBKBytes / 2 : kBKBytes;
       const CUtensorMap* ta = (b == kFP16) ? &tm_a16 : &tm_a8;
@@ -397,14 +416,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (t >= geo.total) break;
       int pos0, n0;
-      const int b = decode_tile(geo, t, kBM, pos0, n0);
+      const int b = decode_tile(geo, t, kBM, pos0, n0, BN);
       const int nkb = kblocks_of(b, K);
       if (!mbar_wait(&acc_empty[ab], aphase ^ 1u, abort_flag)) {
         failed = true;
         break;
       }
       tc_fence_after();
-      const uint32_t d_tmem = tmem_base + ab * kBN;
+      const uint32_t d_tmem = tmem_base + ab * BN;
       for (int kb = 0; kb < nkb; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag)) {
           failed = true;
@@ -415,11 +434,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t a_addr = smem_u32(sA + stage * kAStageBytes);
           const uint32_t b_addr = smem_u32(sB + stage * kBStageBytes);
           if (b == kINT8)
-            mma_stage<kKindI8>(d_tmem, a_addr, b_addr, kb == 0);
+            mma_stage<kKindI8, BN>(d_tmem, a_addr, b_addr, kb == 0);
           else if (b == kFP8)
-            mma_stage<kKindF8>(d_tmem, a_addr, b_addr, kb == 0);
+            mma_stage<kKindF8, BN>(d_tmem, a_addr, b_addr, kb == 0);
           else
-            mma_stage<kKindF16>(d_tmem, a_addr, b_addr, kb == 0);
+            mma_stage<kKindF16, BN>(d_tmem, a_addr, b_addr, kb == 0);
           tc_commit(&empty[stage]);  // frees the stage once these MMAs have read it
         }
         __syncwarp();
@@ -452,7 +471,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool failed = t < 0;
       if (!failed && t >= geo.total) break;
       int pos0 = 0, n0 = 0;
-      const int b = failed ? 0 : decode_tile(geo, t, kBM, pos0, n0);
+      const int b = failed ? 0 : decode_tile(geo, t, kBM, pos0, n0, BN);
       const EpiRow er = epilogue_prepare(args, geo, b, pos0 + quarter * 32 + lane, n0, lane);
       if (!failed && !mbar_wait(&acc_full[ab], aphase, abort_flag)) failed = true;
       if (failed) {
@@ -463,7 +482,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      epilogue_drain(args, er, b, n0, tmem_base + ab * kBN + (static_cast<uint32_t>(quarter * 32) << 16));
+      epilogue_drain<BN>(args, er, b, n0, tmem_base + ab * BN + (static_cast<uint32_t>(quarter * 32) << 16));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
@@ -609,6 +628,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  griddep_wait();  // bucket counts, packed rows and the tile counter come from earlier kernels
+  griddep_launch_dependents();
   const TileGeo geo = make_geo(args, kPairRows);
   const bool dyn = args.sched != nullptr;
   if (pair >= geo.total) {  // the same decision in both CTAs of the pair

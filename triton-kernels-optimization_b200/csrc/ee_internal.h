@@ -83,8 +83,8 @@ int launch_route_entropies(const float* H, int64_t rows, double tl, double th, f
 // ----------------------------------------------------------------- gated GEMM
 constexpr int kBM = 128;          // rows per tile (UMMA M)
 constexpr int kBN = 256;          // columns per tile (UMMA N)
+constexpr int kBNNarrow = 64;     // columns per tile of the single-CTA kernel for few-row (weight-streaming) calls
 constexpr int kBKBytes = 128;     // bytes of K per pipeline stage (one 128B swizzle row)
-constexpr int kStages = 4;
 
 struct GemmArgs {
   int M_cap;               // positions covered by the A tensor maps
@@ -105,14 +105,18 @@ struct GemmMaps {
   CUtensorMap a16;         // fp16  [M_cap, K], box {64, 128}
   CUtensorMap w[3];        // bucket weights [N, K] K-major, box {128 B, 256}
 };
-int launch_gated_gemm(const GemmMaps& maps, const GemmArgs& args, int grid, cudaStream_t s);
+// single-CTA kernel, 128 x bn tiles (bn = kBN, or kBNNarrow for weight-streaming calls)
+int launch_gated_gemm(const GemmMaps& maps, const GemmArgs& args, int grid, int bn, cudaStream_t s);
 // CTA-pair kernel: 256-row tiles; grid = 2 x pairs; the A / W maps use 128-row boxes
 int launch_gated_gemm_pair(const GemmMaps& maps, const GemmArgs& args, int pairs, cudaStream_t s);
 constexpr int kPairTileRows = 256;
-size_t gemm_smem_bytes();
 
 // device error word
 int read_and_clear_device_error(int* value);
+// ee_gate_rows with the workspace-header memset optional (see ee_capi.cu)
+int gate_rows_impl(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high, float* H,
+                   int8_t* route, int32_t* bucket_counts, void* workspace, size_t workspace_bytes, void* stream,
+                   bool clear_header);
 
 // one-time per-device set-up of kernel attributes (safe to call repeatedly); lets a
 // caller finish it before a stream capture starts

@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <utility>
 
 #include "ee_gemm.cuh"
 #include "ee_internal.h"
@@ -14,6 +15,24 @@ namespace ee {
 namespace {
 inline int status_of(cudaError_t e) { return e == cudaSuccess ? 0 : -4; }
 
+// Launch with programmatic stream serialization: the kernel may be scheduled while the
+// previous kernel in the stream finishes (it waits in griddep_wait before reading
+// anything), which hides launch latency between the kernels of a step.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return status_of(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
 inline unsigned grid_of(int64_t rows, int per_block) {
   return static_cast<unsigned>((rows + per_block - 1) / per_block);
 }
@@ -22,16 +41,14 @@ template <int TPR, int NV, int MINB = 1>
 int run_softmax_vec(const SoftmaxArgs& a, cudaStream_t s) {
   const unsigned grid = grid_of(a.rows, kRowThreads / TPR);
   if (a.causal || a.probs != nullptr)
-    softmax_entropy_vec_kernel<TPR, NV, true, 1><<<grid, kRowThreads, 0, s>>>(a);
-  else
-    softmax_entropy_vec_kernel<TPR, NV, false, MINB><<<grid, kRowThreads, 0, s>>>(a);
-  return status_of(cudaGetLastError());
+    return launch_pdl(softmax_entropy_vec_kernel<TPR, NV, true, 1>, dim3(grid), dim3(kRowThreads), 0, s, a);
+  return launch_pdl(softmax_entropy_vec_kernel<TPR, NV, false, MINB>, dim3(grid), dim3(kRowThreads), 0, s, a);
 }
 
 template <int TPR, int NV, int MINB = 1>
 int run_pack_vec(const PackArgs& a, cudaStream_t s) {
-  pack_rows_vec_kernel<TPR, NV, MINB><<<grid_of(a.M, kRowThreads / TPR), kRowThreads, 0, s>>>(a);
-  return status_of(cudaGetLastError());
+  return launch_pdl(pack_rows_vec_kernel<TPR, NV, MINB>, dim3(grid_of(a.M, kRowThreads / TPR)), dim3(kRowThreads), 0,
+                    s, a);
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -68,8 +85,7 @@ int launch_softmax_entropy(const SoftmaxArgs& a, cudaStream_t s) {
     if (n <= 8192) return run_softmax_vec<128, 8>(a, s);
     if (n <= 16384) return run_softmax_vec<256, 8>(a, s);
   }
-  softmax_entropy_loop_kernel<<<static_cast<unsigned>(a.rows), 256, 0, s>>>(a);
-  return status_of(cudaGetLastError());
+  return launch_pdl(softmax_entropy_loop_kernel, dim3(static_cast<unsigned>(a.rows)), dim3(256), 0, s, a);
 }
 
 int launch_pack_rows(const PackArgs& a, cudaStream_t s) {
@@ -85,8 +101,7 @@ int launch_pack_rows(const PackArgs& a, cudaStream_t s) {
   if (K <= 8192) return run_pack_vec<128, 8>(a, s);
   if (K <= 14336) return run_pack_vec<256, 7, 2>(a, s);
   if (K <= 16384) return run_pack_vec<256, 8, 2>(a, s);
-  pack_rows_loop_kernel<<<static_cast<unsigned>(a.M), 256, 0, s>>>(a);
-  return status_of(cudaGetLastError());
+  return launch_pdl(pack_rows_loop_kernel, dim3(static_cast<unsigned>(a.M)), dim3(256), 0, s, a);
 }
 
 int launch_quantize_weights(const void* W, int64_t ldw, int64_t N, int64_t K, int8_t* w_kn, int8_t* w_nk,
@@ -146,16 +161,17 @@ int launch_route(const float* H, int64_t rows, double tl, double th, int8_t* rou
   return status_of(cudaGetLastError());
 }
 
-size_t gemm_smem_bytes() { return kGemmSmem; }
-
 int prepare_device() {
   static std::once_flag attr_once[64];
   static cudaError_t attr_err[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -4;
   std::call_once(attr_once[dev], [dev] {
-    attr_err[dev] = cudaFuncSetAttribute(gated_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kGemmSmem));
+    attr_err[dev] = cudaFuncSetAttribute(gated_gemm_kernel<kBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(SingleCfg<kBN>::kSmem));
+    if (attr_err[dev] == cudaSuccess)
+      attr_err[dev] = cudaFuncSetAttribute(gated_gemm_kernel<kBNNarrow>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(SingleCfg<kBNNarrow>::kSmem));
     if (attr_err[dev] == cudaSuccess)
       attr_err[dev] = cudaFuncSetAttribute(gated_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(kGemmSmemPair));
@@ -166,15 +182,18 @@ int prepare_device() {
 int launch_gated_gemm_pair(const GemmMaps& m, const GemmArgs& args, int pairs, cudaStream_t s) {
   if (prepare_device() != 0) return -4;
   if (pairs <= 0) return 0;
-  gated_gemm_pair_kernel<<<2 * pairs, kGemmThreads, kGemmSmemPair, s>>>(m.a8, m.a16, m.w[0], m.w[1], m.w[2], args);
-  return status_of(cudaGetLastError());
+  return launch_pdl(gated_gemm_pair_kernel, dim3(2 * pairs), dim3(kGemmThreads), kGemmSmemPair, s, m.a8, m.a16, m.w[0],
+                    m.w[1], m.w[2], args);
 }
 
-int launch_gated_gemm(const GemmMaps& m, const GemmArgs& args, int grid, cudaStream_t s) {
+int launch_gated_gemm(const GemmMaps& m, const GemmArgs& args, int grid, int bn, cudaStream_t s) {
   if (prepare_device() != 0) return -4;
   if (grid <= 0) return 0;
-  gated_gemm_kernel<<<grid, kGemmThreads, kGemmSmem, s>>>(m.a8, m.a16, m.w[0], m.w[1], m.w[2], args);
-  return status_of(cudaGetLastError());
+  if (bn == kBNNarrow)
+    return launch_pdl(gated_gemm_kernel<kBNNarrow>, dim3(grid), dim3(kGemmThreads), SingleCfg<kBNNarrow>::kSmem, s,
+                      m.a8, m.a16, m.w[0], m.w[1], m.w[2], args);
+  return launch_pdl(gated_gemm_kernel<kBN>, dim3(grid), dim3(kGemmThreads), SingleCfg<kBN>::kSmem, s, m.a8, m.a16,
+                    m.w[0], m.w[1], m.w[2], args);
 }
 
 int read_and_clear_device_error(int* value) {

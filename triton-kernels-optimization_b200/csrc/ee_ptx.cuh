@@ -32,6 +32,19 @@ __device__ __forceinline__ uint64_t globaltimer() {
 }
 
 // ---------------------------------------------------------------------------------
+// programmatic dependent launch (kernels launched with programmatic stream
+// serialization may start before the previous kernel in the stream has finished)
+// ---------------------------------------------------------------------------------
+// Blocks until the previous grid in the stream has completed and its writes are
+// visible; returns at once when the kernel was launched without the attribute.  Every
+// kernel launched with the attribute calls it before reading anything another kernel
+// may have written.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next grid in the stream launch (it still waits in griddep_wait for this one
+// to finish): its CTAs take SMs as this grid's CTAs retire.
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// ---------------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

@@ -340,6 +340,8 @@ __device__ __forceinline__ void vec_stats(const uint4& u, int e0, int lim, float
 // ----------------------------------------------------------------------------------
 template <int TPR, int NV, bool kGeneral, int MINB>
 __global__ void __launch_bounds__(kRowThreads, MINB) softmax_entropy_vec_kernel(const SoftmaxArgs a) {
+  griddep_wait();  // inputs may come from the previous kernel in the stream
+  griddep_launch_dependents();
   // kGeneral = false: no causal mask and no probabilities (the router's case) -- the
   // lean instantiation, which keeps the hot loop small
   constexpr int RPB = kRowThreads / TPR;
@@ -459,6 +461,8 @@ __device__ __forceinline__ OnlineStats stats_merge(OnlineStats a, OnlineStats b)
 // softmax + entropy for any row length, stride and alignment: one row per 256-thread
 // block, streaming pass with online statistics, second pass for the probabilities.
 __global__ void __launch_bounds__(256) softmax_entropy_loop_kernel(const SoftmaxArgs a) {
+  griddep_wait();  // inputs may come from the previous kernel in the stream
+  griddep_launch_dependents();
   __shared__ OnlineStats red[256];
   const int64_t row = blockIdx.x;
   const int n = a.n;
@@ -573,6 +577,8 @@ __device__ __forceinline__ int64_t pack_position(const PackArgs& a, int64_t row,
 // MINB: resident blocks per SM the register allocation must allow
 template <int TPR, int NV, int MINB>
 __global__ void __launch_bounds__(kRowThreads, MINB) pack_rows_vec_kernel(const PackArgs a) {
+  griddep_wait();  // inputs may come from the previous kernel in the stream
+  griddep_launch_dependents();
   constexpr int RPB = kRowThreads / TPR;
   __shared__ float red[8];
   const int g = threadIdx.x / TPR, lt = threadIdx.x % TPR;
@@ -625,6 +631,8 @@ __global__ void __launch_bounds__(kRowThreads, MINB) pack_rows_vec_kernel(const 
 
 // any K (multiple of 8): one row per block, two passes over the row
 __global__ void __launch_bounds__(256) pack_rows_loop_kernel(const PackArgs a) {
+  griddep_wait();  // inputs may come from the previous kernel in the stream
+  griddep_launch_dependents();
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
   const int K = a.K;
