@@ -19,7 +19,7 @@ from .dispatch import (
     tier_of,
 )
 from .engine import CubinEngine, GatedLayerEngine
-from .llama import EntropyDispatchedLlamaBlock, build_dispatched_llama
+from .llama import EntropyDispatchedLlamaBlock, build_dispatched_llama, dispatched_forward, eval_dispatched
 from .kernels import (
     WeightPack,
     attention_entropy,

@@ -119,3 +119,41 @@ def build_dispatched_llama(model, tau_low: float, tau_high: float, routing: str 
         blocks.append(block)
     dispatcher = PipelinedEntropyDispatcher(tau_low=tau_low, tau_high=tau_high)
     return blocks, dispatcher
+
+
+@torch.no_grad()
+def dispatched_forward(model, blocks, dispatcher, input_ids: torch.Tensor) -> torch.Tensor:
+    """Logits of a transformers Llama model with its decoder layers replaced by
+    ``blocks``: embedding -> fp16 -> rotary -> causal mask -> blocks -> norm -> lm_head,
+    the forward of the reference's evaluation loop (EE/python/quality_eval.py:111-141)."""
+    B, S = input_ids.shape
+    device = input_ids.device
+    hidden = model.model.embed_tokens(input_ids).to(torch.float16)
+    position_ids = torch.arange(S, device=device).unsqueeze(0).expand(B, S)
+    position_embeddings = model.model.rotary_emb(hidden, position_ids)
+    causal_mask = torch.full((1, 1, S, S), torch.finfo(torch.float16).min, device=device, dtype=torch.float16)
+    causal_mask = torch.triu(causal_mask, diagonal=1)
+    for block in blocks:
+        hidden = block(hidden, dispatcher=dispatcher, position_ids=position_ids,
+                       position_embeddings=position_embeddings, attention_mask=causal_mask)[0]
+    hidden = model.model.norm(hidden)
+    return model.lm_head(hidden)
+
+
+@torch.no_grad()
+def eval_dispatched(model, blocks, dispatcher, chunks, device):
+    """EE/python/quality_eval.py:111-152: perplexity of token chunks (each a list of ids,
+    the last one the final target) through the dispatched blocks; returns (ppl, stats)."""
+    import math
+
+    total_loss, total_tokens = 0.0, 0
+    dispatcher.reset_stats()
+    for chunk in chunks:
+        ids = torch.tensor([chunk[:-1]], device=device, dtype=torch.long)
+        target = torch.tensor([chunk[1:]], device=device, dtype=torch.long)
+        logits = dispatched_forward(model, blocks, dispatcher, ids)
+        total_loss += torch.nn.functional.cross_entropy(logits.float().view(-1, logits.size(-1)), target.view(-1),
+                                                        reduction="sum").item()
+        total_tokens += target.numel()
+    return math.exp(total_loss / total_tokens), dispatcher.get_stats()
+
