@@ -227,6 +227,17 @@ EE_API int ee_gated_pack(const void* A, int64_t lda, int64_t M, int64_t K, void*
 EE_API int ee_gated_gemm_packed(int64_t M, int64_t K, const int8_t* W_i8_nk, const uint8_t* W_e4m3_nk,
                                 const void* W_f16_nk, const float* w_scale, int64_t N, void* Y, int64_t ldy,
                                 void* workspace, size_t workspace_bytes, void* stream);
+/* The gated SwiGLU MLP's first half in one GEMM over the rows packed by
+ * ee_gated_pack: Y[i, c] = fp16(silu(gate[i, c]) * up[i, c]) for c < I, where gate / up
+ * are what ee_gated_gemm_packed would write for the gate and up weights (each row in
+ * its bucket's precision) and silu(g) = fp16(g / (1 + exp(-g))) -- the roundings of
+ * torch.nn.functional.silu(gate) * up on those fp16 outputs (EE/python/dispatch.py:
+ * 201-203).  The weight packs and scales hold 2I rows: gate and up interleaved in
+ * groups of 128 (rows 256t .. 256t+127 = gate channels 128t .., the next 128 = the same
+ * up channels); I % 128 == 0.  Y: fp16 [M, I], row stride ldy. */
+EE_API int ee_gated_swiglu_packed(int64_t M, int64_t K, const int8_t* Wgu_i8_nk, const uint8_t* Wgu_e4m3_nk,
+                                  const void* Wgu_f16_nk, const float* wgu_scale, int64_t I, void* Y, int64_t ldy,
+                                  void* workspace, size_t workspace_bytes, void* stream);
 /* Byte offsets, inside a gated workspace for (M, K), of: [0] bucket counts int32[3],
  * [1] perm int32[M] (position -> row), [2] slot int32[M] (row -> position),
  * [3] route int8[M], [4] H fp32[M], [5] activation scales fp32[M], [6] 8-bit rows

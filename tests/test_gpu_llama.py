@@ -139,3 +139,35 @@ def test_build_dispatched_llama(pkg, cuda):
     blocks, disp = pkg.build_dispatched_llama(model, 0.41, 1.68)
     assert len(blocks) == 2 and isinstance(disp, pkg.PipelinedEntropyDispatcher)
     assert blocks[1].layer_idx == 1 and blocks[0].gate_proj.weight_int8.dtype == torch.int8
+
+
+def test_dispatched_forward_tracks_the_model(pkg, cuda):
+    """The whole model through the dispatched blocks (the reference's evaluation
+    forward): with every layer in the FP16 tier the logits stay within the W8A16 weight
+    quantisation error of the transformers model; the gated run gives finite perplexity
+    and a small KL divergence from the all-FP16-tier run."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(5)
+    cfg = LlamaConfig(hidden_size=256, num_attention_heads=4, num_key_value_heads=2, intermediate_size=512,
+                      num_hidden_layers=2, vocab_size=128, attn_implementation="eager")
+    model = LlamaForCausalLM(cfg).to(cuda).half().eval()
+    ids = torch.randint(0, 128, (2, 64), generator=torch.Generator().manual_seed(1)).to(cuda)
+    with torch.no_grad():
+        ref = model(ids).logits.float()
+    blocks, disp = pkg.build_dispatched_llama(model, -1.0, -1.0)  # every layer in the FP16 tier
+    fp16 = pkg.dispatched_forward(model, blocks, disp, ids).float()
+    assert torch.isfinite(fp16).all()
+    assert _relf(fp16.cpu().numpy(), ref.cpu().numpy()) < 5e-2
+    assert disp.get_stats()["FP16"]["count"] == 2
+    for routing in ("batch", "token"):
+        blocks, disp = pkg.build_dispatched_llama(model, 0.41, 1.68, routing=routing)
+        gated = pkg.dispatched_forward(model, blocks, disp, ids).float()
+        lp, lq = torch.log_softmax(gated, -1), torch.log_softmax(fp16, -1)
+        kl = float((lp.exp() * (lp - lq)).sum(-1).mean())
+        assert 0.0 <= kl < 0.05
+        ppl, stats = pkg.eval_dispatched(model, blocks, disp, [list(range(65)), list(range(3, 68))], cuda)
+        assert np.isfinite(ppl) and ppl > 1.0
+        # batch routing reads one tier per layer per chunk on the host; token routing none
+        assert sum(v["count"] for v in stats.values()) == (4 if routing == "batch" else 0)
+

@@ -4,12 +4,13 @@ Drop-in for the hot path of IqtedarU/triton-kernels-optimization (entropy-engine
 the reference's operator names (``triton_int8_gemm``, ``triton_fp8_gemm``,
 ``triton_fp16_gemm``, ``fused_softmax_entropy``, ``quantize_weights_int8``,
 ``PrecisionTier``, ``PipelinedEntropyDispatcher``, ``EntropyDispatchedLinear``,
-``CubinEngine``) backed by hand-written tcgen05 / TMA kernels behind the C ABI of
+``EntropyDispatchedLlamaBlock``, ``build_dispatched_llama``, ``CubinEngine``) backed by
+hand-written tcgen05 / TMA kernels behind the C ABI of
 ``libee_b200.so`` (include/ee_b200.h).  The package directory name contains dashes,
 so it is imported through ``__graft_entry__.load_package()`` (module name
 ``tko_b200``).
 """
-from . import _lib
+from . import _lib, sharding
 from .dispatch import (
     EntropyDispatchedLinear,
     EntropyRouter,
@@ -21,6 +22,7 @@ from .dispatch import (
 from .engine import CubinEngine, GatedLayerEngine
 from .llama import EntropyDispatchedLlamaBlock, build_dispatched_llama, dispatched_forward, eval_dispatched
 from .kernels import (
+    SwiGLUPack,
     WeightPack,
     attention_entropy,
     fused_softmax_entropy,

@@ -57,6 +57,7 @@ SIGNATURES = {
                               _P]),
     "ee_gated_pack": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_size_t, _P]),
     "ee_gated_gemm_packed": (c_int, [c_int64, c_int64, _P, _P, _P, _P, c_int64, _P, c_int64, _P, c_size_t, _P]),
+    "ee_gated_swiglu_packed": (c_int, [c_int64, c_int64, _P, _P, _P, _P, c_int64, _P, c_int64, _P, c_size_t, _P]),
     "ee_gated_workspace_layout": (c_int, [c_int64, c_int64, POINTER(c_int64)]),
     "ee_engine_workspace_bytes": (c_size_t, [c_int64, c_int32, _P]),
     "ee_engine_create": (c_int, [c_int64, c_double, c_double, c_int32, _P, _P, c_size_t, _P]),

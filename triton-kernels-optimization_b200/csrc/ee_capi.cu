@@ -129,7 +129,8 @@ int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cud
   const int policy = g_gemm_policy.load(std::memory_order_relaxed);
   const int64_t wide_tiles = row_tiles(args, dynamic_counts, ee::kBM) * ((args.N + ee::kBN - 1) / ee::kBN);
   const bool pair = policy == 2 || (policy == 0 && args.M_cap > ee::kBM);
-  const bool narrow = policy == 3 || (policy == 0 && !pair && wide_tiles < num_sms());
+  // the SwiGLU epilogue pairs 128-column groups inside a 256-column tile
+  const bool narrow = args.out_mode != 2 && (policy == 3 || (policy == 0 && !pair && wide_tiles < num_sms()));
   const int bn = narrow ? ee::kBNNarrow : ee::kBN;
   const int wbox = pair ? ee::kBN / 2 : bn;
   ee::GemmMaps maps;
@@ -691,6 +692,37 @@ int ee_gated_gemm_packed(int64_t M, int64_t K, const int8_t* W_i8_nk, const uint
   args.perm = w.perm;
   args.sa = w.sa;
   args.sb = w_scale;
+  args.sched = w.sched;
+  return run_gemm(op, args, true, as_stream(stream));
+}
+
+int ee_gated_swiglu_packed(int64_t M, int64_t K, const int8_t* Wgu_i8_nk, const uint8_t* Wgu_e4m3_nk,
+                           const void* Wgu_f16_nk, const float* wgu_scale, int64_t I, void* Y, int64_t ldy,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  if (I <= 0 || I % 128 != 0) return fail(EE_ERR_UNSUPPORTED, "I=%lld must be a positive multiple of 128", (long long)I);
+  int st = check_gemm_shape(M, 2 * I, K, 2 * I);
+  if (st != EE_OK) return st;
+  if (ldy < I || ldy % 8 != 0) return fail(EE_ERR_MISALIGNED, "ldy=%lld must be >= I and a multiple of 8", (long long)ldy);
+  if ((st = check_ws(workspace, workspace_bytes, gated_ws_bytes(M, K))) != EE_OK) return st;
+  if (M == 0) return EE_OK;
+  if (!Wgu_i8_nk || !Wgu_e4m3_nk || !Wgu_f16_nk || !wgu_scale || !Y)
+    return fail(EE_ERR_INVALID, "all three weight packs, the scales and Y are required");
+  if (!al16(Wgu_i8_nk) || !al16(Wgu_e4m3_nk) || !al16(Wgu_f16_nk) || !al16(wgu_scale) || !al16(Y))
+    return fail(EE_ERR_MISALIGNED, "weights, scales and Y must be 16-byte aligned");
+  GatedWs w = gated_ws(workspace, M, K);
+  GemmOperands op;
+  op.a8 = w.buf8;
+  op.ld8 = K;
+  op.a16 = w.buf16;
+  op.ld16 = K;
+  op.w[ee::kINT8] = Wgu_i8_nk;
+  op.w[ee::kFP8] = Wgu_e4m3_nk;
+  op.w[ee::kFP16] = Wgu_f16_nk;
+  ee::GemmArgs args = base_args(M, 2 * I, K, Y, ldy, 2);
+  args.dyn_counts = w.counts;
+  args.perm = w.perm;
+  args.sa = w.sa;
+  args.sb = wgu_scale;
   args.sched = w.sched;
   return run_gemm(op, args, true, as_stream(stream));
 }

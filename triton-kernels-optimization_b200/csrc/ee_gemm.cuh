@@ -136,9 +136,9 @@ __device__ __forceinline__ EpiRow epilogue_prepare(const GemmArgs& args, const T
   const int end = (b == 0) ? geo.cnt[0] : (b == 1) ? geo.off[1] + geo.cnt[1] : geo.off[2] + geo.cnt[2];
   e.valid = pos < end;
   e.orow = e.valid ? (args.perm ? static_cast<int64_t>(args.perm[pos]) : static_cast<int64_t>(pos)) : 0;
-  e.sa = (e.valid && b != kFP16 && args.out_mode == 0) ? args.sa[pos] : 1.f;
+  e.sa = (e.valid && b != kFP16 && args.out_mode != 1) ? args.sa[pos] : 1.f;
   const int c8 = n0 + 8 * lane;
-  if (b != kFP16 && args.out_mode == 0 && c8 < args.N) {  // N % 8 == 0: all 8 or none
+  if (b != kFP16 && args.out_mode != 1 && c8 < args.N) {  // N % 8 == 0: all 8 or none
     const float4 q0 = __ldg(reinterpret_cast<const float4*>(args.sb + c8));
     const float4 q1 = __ldg(reinterpret_cast<const float4*>(args.sb + c8 + 4));
     e.sb[0] = q0.x; e.sb[1] = q0.y; e.sb[2] = q0.z; e.sb[3] = q0.w;
@@ -192,11 +192,77 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& args, const EpiRo
   }
 }
 
+// SwiGLU epilogue (out_mode 2): the weight rows come interleaved in groups of 128 --
+// tile columns [0, 128) are gate channels n0/2 + [0, 128), columns [128, 256) the
+// matching up channels -- and the output is h = silu(gate) * up with I = N/2 columns.
+// Every value is rounded where the unfused sequence rounds it: gate and up to fp16 as
+// the bucket's GEMM writes them, silu(g) = g / (1 + exp(-g)) in fp32 (IEEE division)
+// to fp16, then the fp16 product -- what torch.nn.functional.silu(gate) * up computes
+// on the GEMMs' fp16 outputs.
+__device__ __forceinline__ float swiglu_dequant(uint32_t r, int b, float sa, float sb) {
+  if (b == kFP16) return __uint_as_float(r);
+  const float acc = (b == kINT8) ? static_cast<float>(static_cast<int32_t>(r)) : __uint_as_float(r);
+  return __fmul_rn(__fmul_rn(acc, sa), sb);
+}
+
+__device__ __forceinline__ void swiglu_chunk(const GemmArgs& args, const EpiRow& e, int b, int n0, int c,
+                                             const uint32_t (&rg)[32], const uint32_t (&ru)[32]) {
+  float sg[32], su[32];
+  if (b != kFP16) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      sg[j] = __shfl_sync(0xffffffffu, e.sb[j & 7], 4 * c + (j >> 3));
+      su[j] = __shfl_sync(0xffffffffu, e.sb[j & 7], 16 + 4 * c + (j >> 3));
+    }
+  }
+  const int inter = args.N / 2;
+  const int oc = n0 / 2 + c * 32;  // first output column of the chunk
+  if (!e.valid || oc >= inter) return;
+  __half* y = static_cast<__half*>(args.Y) + e.orow * args.ldy + oc;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    if (oc + 8 * g < inter) {
+      uint4 out;
+      __half* o = reinterpret_cast<__half*>(&out);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int j = 8 * g + k;
+        const float gate = __half2float(__float2half_rn(swiglu_dequant(rg[j], b, e.sa, b == kFP16 ? 1.f : sg[j])));
+        const float up = __half2float(__float2half_rn(swiglu_dequant(ru[j], b, e.sa, b == kFP16 ? 1.f : su[j])));
+        const float act = __half2float(__float2half_rn(__fdiv_rn(gate, 1.f + expf(-gate))));
+        o[k] = __float2half_rn(act * up);
+      }
+      *reinterpret_cast<uint4*>(y + 8 * g) = out;
+    }
+  }
+}
+
+__device__ __forceinline__ void epilogue_drain_swiglu(const GemmArgs& args, const EpiRow& e, int b, int n0,
+                                                      uint32_t taddr) {
+  uint32_t rg[32], ru[32];
+#pragma unroll 1
+  for (int c = 0; c < kBN / 64; ++c) {
+    __syncwarp();
+    tmem_ld32(taddr + c * 32, rg);
+    tmem_ld32(taddr + kBN / 2 + c * 32, ru);
+    tmem_ld_wait(rg);
+    tmem_ld_wait(ru);
+    swiglu_chunk(args, e, b, n0, c, rg, ru);
+  }
+  __syncwarp();
+}
+
 // Drains the quarter's 256 columns (taddr: its lanes, first column); the whole warp
 // calls it (tcgen05.ld is .sync.aligned).  The TMEM read of chunk c+1 is in flight
 // while chunk c is converted and stored.
 template <int BN = kBN>
 __device__ __forceinline__ void epilogue_drain(const GemmArgs& args, const EpiRow& e, int b, int n0, uint32_t taddr) {
+  if constexpr (BN == kBN) {
+    if (args.out_mode == 2) {
+      epilogue_drain_swiglu(args, e, b, n0, taddr);
+      return;
+    }
+  }
   uint32_t ra[32], rb[32];
   __syncwarp();
   tmem_ld32(taddr, ra);

@@ -96,7 +96,8 @@ struct GemmArgs {
   const float* sb;         // [N] weight scale per output channel (INT8 / FP8 buckets)
   void* Y;                 // fp16 [rows, N] (out_mode 0) or 32-bit [rows, N] (out_mode 1)
   int64_t ldy;             // elements
-  int out_mode;            // 0: dequantised fp16, 1: raw accumulators (int32 / fp32)
+  int out_mode;            // 0: dequantised fp16, 1: raw accumulators (int32 / fp32),
+                           // 2: SwiGLU of gate / up rows interleaved by 128 (fp16 [rows, N/2])
   uint32_t* sched;         // nullable: [0] next tile, [1] CTAs done -- zero at launch, left zero;
                            // null = static round-robin tile order
 };

@@ -24,6 +24,7 @@ import torch.nn as nn
 from . import _lib
 from ._lib import call
 from .kernels import (
+    SwiGLUPack,
     WeightPack,
     _check_act,
     _ptr,
@@ -215,6 +216,18 @@ class EntropyRouter:
         with torch.cuda.device(y.device):
             call("ee_gated_gemm_packed", M, K, pack.w_i8.data_ptr(), pack.w_e4m3.data_ptr(), pack.w_f16.data_ptr(),
                  pack.scale.data_ptr(), pack.N, y.data_ptr(), y.stride(0), self._ws.data_ptr(), self._ws.numel(),
+                 _stream())
+        return y
+
+    def swiglu_packed(self, pack: "SwiGLUPack", out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """silu(gate) * up over the rows packed by ``pack_rows``, in one bucketed GEMM with
+        the SwiGLU epilogue; the same values as ``silu(gemm_packed(gate)) * gemm_packed(up)``."""
+        M, K = self.M, pack.K
+        _require(getattr(self, "_packed_k", None) == K, "pack_rows(A) with A of width K must come first")
+        y = out if out is not None else torch.empty(M, pack.I, dtype=torch.float16, device=self._ws.device)
+        with torch.cuda.device(y.device):
+            call("ee_gated_swiglu_packed", M, K, pack.w_i8.data_ptr(), pack.w_e4m3.data_ptr(), pack.w_f16.data_ptr(),
+                 pack.scale.data_ptr(), pack.I, y.data_ptr(), y.stride(0), self._ws.data_ptr(), self._ws.numel(),
                  _stream())
         return y
 

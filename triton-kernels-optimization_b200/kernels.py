@@ -72,6 +72,28 @@ class WeightPack:
         return sum(t.numel() * t.element_size() for t in (self.w_i8, self.w_e4m3, self.w_f16, self.scale))
 
 
+class SwiGLUPack:
+    """Gate and up weight packs of a gated SwiGLU MLP, interleaved for the fused GEMM
+    (``ee_gated_swiglu_packed``): rows 256t .. 256t+127 are gate channels 128t .., the
+    next 128 rows the same up channels; ``N`` = 2I rows, ``I`` output channels."""
+
+    def __init__(self, gate: WeightPack, up: WeightPack):
+        _require(gate.K == up.K and gate.N == up.N, "gate and up must have the same shape")
+        _require(gate.N % 128 == 0, f"the intermediate size ({gate.N}) must be a multiple of 128")
+        self.K, self.I, self.N = gate.K, gate.N, 2 * gate.N
+        groups = gate.N // 128
+
+        def interleave(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+            rest = tuple(a.shape[1:])
+            return torch.stack([a.reshape(groups, 128, *rest), b.reshape(groups, 128, *rest)], dim=1) \
+                .reshape(2 * gate.N, *rest).contiguous()
+
+        self.w_i8 = interleave(gate.w_i8, up.w_i8)
+        self.w_e4m3 = interleave(gate.w_e4m3, up.w_e4m3)
+        self.w_f16 = interleave(gate.w_f16, up.w_f16)
+        self.scale = interleave(gate.scale, up.scale)
+
+
 _PACK_CACHE: "OrderedDict[tuple, WeightPack]" = OrderedDict()
 _PACK_CACHE_SIZE = 8
 

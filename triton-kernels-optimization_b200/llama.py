@@ -10,9 +10,9 @@ dispatcher -> gate / up / down as ``EntropyDispatchedLinear``.
 ``routing="batch"`` is the reference's granularity: one tier per block from the
 batch max of the per-batch entropies (dispatch.py:64), read on the host.
 ``routing="token"`` routes every token by its own attention entropy (the mean over
-heads of its query row) on the device: the three MLP projections run as gated
-GEMMs over per-token buckets, with no host round trip; gate and up share one packing
-of their input.
+heads of its query row) on the device: the MLP runs as gated GEMMs over per-token
+buckets, with no host round trip; gate and up share one packing of their input and
+one GEMM whose epilogue applies SiLU and the product (``SwiGLUPack``).
 """
 from __future__ import annotations
 
@@ -22,7 +22,7 @@ import torch
 import torch.nn as nn
 
 from .dispatch import EntropyDispatchedLinear, EntropyRouter, PipelinedEntropyDispatcher, PrecisionTier
-from .kernels import _require, attention_entropy
+from .kernels import SwiGLUPack, _require, attention_entropy
 
 
 class EntropyDispatchedLlamaBlock(nn.Module):
@@ -83,9 +83,15 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         r.reserve(M, max(self.gate_proj.in_features, self.down_proj.in_features), x2.device)
         r.route_entropy(self.token_entropy.reshape(-1))
         r.pack_rows(x2)  # one packing of the post-norm rows serves gate and up
-        gate = r.gemm_packed(self.gate_proj._pack())
-        up = r.gemm_packed(self.up_proj._pack())
-        out = r.gated_linear(self.act_fn(gate) * up, self.down_proj._pack())
+        gp, up = self.gate_proj._pack(), self.up_proj._pack()
+        if gp.N % 128 == 0:
+            key = (id(gp), id(up))
+            if getattr(self, "_gu_key", None) != key:
+                self._gu, self._gu_key = SwiGLUPack(gp, up), key
+            h = r.swiglu_packed(self._gu)  # gate, up, SiLU and the product in one GEMM
+        else:
+            h = self.act_fn(r.gemm_packed(gp)) * r.gemm_packed(up)
+        out = r.gated_linear(h, self.down_proj._pack())
         return out.reshape(shape[:-1] + (self.down_proj.out_features,))
 
     def _attention_with_fused_entropy(self, hidden_states: torch.Tensor, attention_mask=None, position_ids=None,
