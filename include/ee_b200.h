@@ -108,6 +108,22 @@ EE_API int ee_fused_softmax_entropy_4d(const void* logits, int64_t B, int64_t Hh
 EE_API int ee_attention_entropy(const void* probs, int dtype, int64_t rows, int64_t n, int64_t ld, float* row_entropy,
                                 int64_t batches, float* batch_entropy, void* stream);
 
+/* Causal (or full) attention with the entropy of every query row, in one pass over K
+ * and V (flash attention on tcgen05): the Llama block's attention output and router
+ * input without the [B, Hq, S, S] probabilities the reference materialises
+ * (EE/python/dispatch.py:236-245).  Q fp16 [B, Hq, S, head_dim], K and V fp16
+ * [B, Hkv, S, head_dim] (contiguous; Hq % Hkv == 0: grouped-query heads), head_dim 64 or
+ * 128.  Scores follow the reference's eager path -- fp16(Q K^T), times `scale`, rounded
+ * to fp16, causal mask, softmax in fp32 -- and O = softmax . V is written fp16
+ * [B, S, Hq, head_dim] (the layout o_proj reads); H fp32 [B, Hq, S] receives
+ * -sum_k p_k ln p_k of each row.  Workspace: ee_attention_workspace_bytes (V transposed),
+ * 256-byte aligned.  No counterpart in the reference's kernels (its entropy needs the
+ * probabilities in HBM). */
+EE_API size_t ee_attention_workspace_bytes(int64_t B, int64_t Hkv, int64_t S, int64_t head_dim);
+EE_API int ee_flash_attention_entropy(const void* Q, const void* K, const void* V, int64_t B, int64_t Hq, int64_t Hkv,
+                                      int64_t S, int64_t head_dim, int causal, float scale, void* O, float* H,
+                                      void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------- routing
  * route[i] = dual-threshold tier of H[i]                (per-row granularity) */
 EE_API int ee_route(const float* H, int64_t rows, double tau_low, double tau_high, int8_t* route, void* stream);

@@ -25,6 +25,7 @@ from .kernels import (
     SwiGLUPack,
     WeightPack,
     attention_entropy,
+    flash_attention_entropy,
     fused_softmax_entropy,
     gemm_accumulators,
     gemm_int8_prequant,

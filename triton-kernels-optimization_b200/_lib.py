@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_char_p, c_double, c_int, c_int8, c_int32, c_int64, c_size_t, c_uint8, c_void_p
+from ctypes import POINTER, c_char_p, c_double, c_float, c_int, c_int8, c_int32, c_int64, c_size_t, c_uint8, c_void_p
 
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG_DIR, "libee_b200.so")
@@ -34,6 +34,9 @@ SIGNATURES = {
                                    c_double, _P]),
     "ee_fused_softmax_entropy_4d": (c_int, [_P, c_int64, c_int64, c_int64, c_int, _P, _P, _P, _P]),
     "ee_attention_entropy": (c_int, [_P, c_int, c_int64, c_int64, c_int64, _P, c_int64, _P, _P]),
+    "ee_attention_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64]),
+    "ee_flash_attention_entropy": (c_int, [_P, _P, _P, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_float, _P,
+                                           _P, _P, c_size_t, _P]),
     "ee_route": (c_int, [_P, c_int64, c_double, c_double, _P, _P]),
     "ee_route_batch_max": (c_int, [_P, c_int64, c_double, c_double, _P, _P, _P]),
     "ee_quantize_weights_int8": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, _P, c_int, _P]),

@@ -362,6 +362,50 @@ int ee_attention_entropy(const void* probs, int dtype, int64_t rows, int64_t n, 
   return check_launch(ee::launch_batch_mean(row_entropy, batches, rows / batches, batch_entropy, s), "batch_mean");
 }
 
+size_t ee_attention_workspace_bytes(int64_t B, int64_t Hkv, int64_t S, int64_t head_dim) {
+  if (B < 0 || Hkv < 0 || S < 0 || head_dim < 0) return 0;
+  const int64_t s_pad = (S + 63) / 64 * 64;
+  return align256(sizeof(uint16_t) * size_t(B) * Hkv * head_dim * s_pad);
+}
+
+int ee_flash_attention_entropy(const void* Q, const void* K, const void* V, int64_t B, int64_t Hq, int64_t Hkv,
+                               int64_t S, int64_t head_dim, int causal, float scale, void* O, float* H,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || S < 0) return fail(EE_ERR_INVALID, "bad shape");
+  if (Hq % Hkv != 0) return fail(EE_ERR_INVALID, "Hq=%lld is not a multiple of Hkv=%lld", (long long)Hq, (long long)Hkv);
+  if (head_dim != 64 && head_dim != 128) return fail(EE_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (causal != 0 && causal != 1) return fail(EE_ERR_INVALID, "causal must be 0 or 1");
+  if (B == 0 || S == 0) return EE_OK;
+  if (B * Hq * S >= (int64_t(1) << 31) || B * Hkv * head_dim >= (int64_t(1) << 31))
+    return fail(EE_ERR_UNSUPPORTED, "more than 2^31 rows");
+  if (!Q || !K || !V || !O || !H) return fail(EE_ERR_INVALID, "Q, K, V, O and H are required");
+  if (!al16(Q) || !al16(K) || !al16(V) || !al16(O) || (reinterpret_cast<uintptr_t>(H) & 3u))
+    return fail(EE_ERR_MISALIGNED, "Q, K, V and O must be 16-byte aligned, H 4-byte aligned");
+  int st = check_ws(workspace, workspace_bytes, ee_attention_workspace_bytes(B, Hkv, S, head_dim));
+  if (st != EE_OK) return st;
+  cudaStream_t s = as_stream(stream);
+  const int64_t s_pad = (S + 63) / 64 * 64;
+  if ((st = check_launch(ee::launch_transpose_v(V, B * Hkv, S, s_pad, head_dim, workspace, s), "transpose_v")) != EE_OK)
+    return st;
+  ee::AttnLaunch a;
+  std::memset(&a, 0, sizeof(a));
+  if ((st = encode_kmajor(&a.q, Q, B * Hq * S, head_dim, head_dim, 2, ee::kAttnTile)) != EE_OK) return st;
+  if ((st = encode_kmajor(&a.k, K, B * Hkv * S, head_dim, head_dim, 2, ee::kAttnTile)) != EE_OK) return st;
+  if ((st = encode_kmajor(&a.vt, workspace, B * Hkv * head_dim, s_pad, s_pad, 2, static_cast<int>(head_dim))) != EE_OK)
+    return st;
+  a.B = B;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.S = S;
+  a.S_pad = s_pad;
+  a.D = head_dim;
+  a.scale = scale;
+  a.causal = causal;
+  a.O = O;
+  a.H = H;
+  return check_launch(ee::launch_flash_attention(a, s), "flash_attention_entropy");
+}
+
 // ------------------------------------------------------------------ routing
 int ee_route(const float* H, int64_t rows, double tau_low, double tau_high, int8_t* route, void* stream) {
   if (rows < 0) return fail(EE_ERR_INVALID, "rows < 0");

@@ -114,6 +114,19 @@ constexpr int kPairTileRows = 256;
 
 // device error word
 int read_and_clear_device_error(int* value);
+// flash attention with row entropy (ee_attention.cuh): Q [B*Hq*S, D], K [B*Hkv*S, D],
+// V^T [B*Hkv*D, S_pad] maps (box 64 x 128 / 64 x D), outputs O [B, S, Hq, D], H [B, Hq, S]
+constexpr int kAttnTile = 128;  // queries per attention CTA and keys per KV tile
+struct AttnLaunch {
+  CUtensorMap q, k, vt;
+  int64_t B, Hq, Hkv, S, S_pad, D;
+  float scale;
+  int causal;
+  void* O;
+  float* H;
+};
+int launch_flash_attention(const AttnLaunch& a, cudaStream_t s);
+int launch_transpose_v(const void* V, int64_t heads, int64_t S, int64_t S_pad, int64_t D, void* VT, cudaStream_t s);
 // ee_gate_rows with the workspace-header memset optional (see ee_capi.cu)
 int gate_rows_impl(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high, float* H,
                    int8_t* route, int32_t* bucket_counts, void* workspace, size_t workspace_bytes, void* stream,

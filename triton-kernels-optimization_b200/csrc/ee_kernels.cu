@@ -6,6 +6,7 @@
 #include <mutex>
 #include <utility>
 
+#include "ee_attention.cuh"
 #include "ee_gemm.cuh"
 #include "ee_internal.h"
 #include "ee_rows.cuh"
@@ -194,6 +195,49 @@ int launch_gated_gemm(const GemmMaps& m, const GemmArgs& args, int grid, int bn,
                       m.a8, m.a16, m.w[0], m.w[1], m.w[2], args);
   return launch_pdl(gated_gemm_kernel<kBN>, dim3(grid), dim3(kGemmThreads), SingleCfg<kBN>::kSmem, s, m.a8, m.a16,
                     m.w[0], m.w[1], m.w[2], args);
+}
+
+int launch_transpose_v(const void* V, int64_t heads, int64_t S, int64_t S_pad, int64_t D, void* VT, cudaStream_t s) {
+  if (heads <= 0 || S_pad <= 0) return 0;
+  const dim3 grid(static_cast<unsigned>((S_pad + 31) / 32), static_cast<unsigned>(heads));
+  if (D == 64)
+    return launch_pdl(transpose_v_kernel<64>, grid, dim3(256), 0, s, static_cast<const __half*>(V), S, S_pad,
+                      static_cast<__half*>(VT));
+  return launch_pdl(transpose_v_kernel<128>, grid, dim3(256), 0, s, static_cast<const __half*>(V), S, S_pad,
+                    static_cast<__half*>(VT));
+}
+
+int launch_flash_attention(const AttnLaunch& a, cudaStream_t s) {
+  static std::once_flag once[64];
+  static cudaError_t err[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -4;
+  std::call_once(once[dev], [dev] {
+    err[dev] = cudaFuncSetAttribute(flash_attention_entropy_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(AttnCfg<64>::kSmem));
+    if (err[dev] == cudaSuccess)
+      err[dev] = cudaFuncSetAttribute(flash_attention_entropy_kernel<128>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(AttnCfg<128>::kSmem));
+  });
+  if (err[dev] != cudaSuccess) return -4;
+  AttnArgs args;
+  args.B = a.B;
+  args.Hq = a.Hq;
+  args.Hkv = a.Hkv;
+  args.S = a.S;
+  args.S_pad = a.S_pad;
+  args.scale = a.scale;
+  args.causal = a.causal;
+  args.O = static_cast<__half*>(a.O);
+  args.H = a.H;
+  const int64_t nqt = (a.S + kAttnTile - 1) / kAttnTile;
+  const dim3 grid(static_cast<unsigned>(a.B * a.Hq * nqt));
+  if (a.D == 64)
+    return launch_pdl(flash_attention_entropy_kernel<64>, grid, dim3(kAttnThreads), AttnCfg<64>::kSmem, s, a.q, a.k,
+                      a.vt, args);
+  return launch_pdl(flash_attention_entropy_kernel<128>, grid, dim3(kAttnThreads), AttnCfg<128>::kSmem, s, a.q, a.k,
+                    a.vt, args);
 }
 
 int read_and_clear_device_error(int* value) {

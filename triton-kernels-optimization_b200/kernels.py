@@ -338,3 +338,29 @@ def attention_entropy(attn_weights: torch.Tensor, return_rows: bool = False):
              batch_h.data_ptr() if rows else None, _stream())
     return (batch_h, row_h) if return_rows else batch_h
 
+
+def flash_attention_entropy(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
+                            scale: float | None = None, return_rows: bool = False):
+    """Attention with the entropy of every query row in one pass (no [B, H, S, S]
+    probabilities): q fp16 [B, Hq, S, d], k / v fp16 [B, Hkv, S, d] (grouped heads),
+    d = 64 or 128.  Returns (attn_output fp16 [B, S, Hq, d] -- the layout o_proj reads --,
+    per-batch mean entropy fp32 [B]) and, with ``return_rows``, the per-row entropies
+    [B, Hq, S].  The entropy is -sum p ln p of the softmax of the reference's fp16 scores
+    (EE/python/dispatch.py:243-245 computes it from the materialised probabilities)."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _check_cuda(t, n)
+        _require(t.dim() == 4 and t.dtype == torch.float16, f"{n} must be fp16 [B, H, S, d]")
+    B, Hq, S, d = q.shape
+    Hkv = k.shape[1]
+    _require(k.shape == (B, Hkv, S, d) and v.shape == k.shape, "k and v must be [B, Hkv, S, d] like q")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    scale = float(d ** -0.5 if scale is None else scale)
+    out = torch.empty(B, S, Hq, d, dtype=torch.float16, device=q.device)
+    rows = torch.empty(B, Hq, S, dtype=torch.float32, device=q.device)
+    ws = _workspace(_lib.load().ee_attention_workspace_bytes(B, Hkv, S, d), q.device)
+    with torch.cuda.device(q.device):
+        call("ee_flash_attention_entropy", q.data_ptr(), k.data_ptr(), v.data_ptr(), B, Hq, Hkv, S, d,
+             int(bool(causal)), scale, out.data_ptr(), rows.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
+    batch = rows.mean(dim=(1, 2))
+    return (out, batch, rows) if return_rows else (out, batch)
+

@@ -22,17 +22,19 @@ import torch
 import torch.nn as nn
 
 from .dispatch import EntropyDispatchedLinear, EntropyRouter, PipelinedEntropyDispatcher, PrecisionTier
-from .kernels import SwiGLUPack, _require, attention_entropy
+from .kernels import SwiGLUPack, _require, attention_entropy, flash_attention_entropy
 
 
 class EntropyDispatchedLlamaBlock(nn.Module):
     """EE/python/dispatch.py:150-247 with the sm_100a kernels."""
 
-    def __init__(self, llama_block, layer_idx: int = 0, routing: str = "batch"):
+    def __init__(self, llama_block, layer_idx: int = 0, routing: str = "batch", attention: str = "eager"):
         super().__init__()
         _require(routing in ("batch", "token"), "routing must be 'batch' or 'token'")
+        _require(attention in ("eager", "flash"), "attention must be 'eager' or 'flash'")
         self.layer_idx = layer_idx
         self.routing = routing
+        self.attention = attention
         self.self_attn = llama_block.self_attn
         self.input_layernorm = llama_block.input_layernorm
         self.post_attention_layernorm = llama_block.post_attention_layernorm
@@ -94,10 +96,38 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         out = r.gated_linear(h, self.down_proj._pack())
         return out.reshape(shape[:-1] + (self.down_proj.out_features,))
 
+    def _flash_attention(self, hidden_states: torch.Tensor, position_embeddings):
+        """The attention module's projections and rotary embedding, then causal flash
+        attention with the row entropies in one kernel (no [B, H, S, S] probabilities)."""
+        from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
+
+        attn = self.self_attn
+        B, S, _ = hidden_states.shape
+        d = attn.head_dim
+        q = attn.q_proj(hidden_states).view(B, S, -1, d).transpose(1, 2)
+        k = attn.k_proj(hidden_states).view(B, S, -1, d).transpose(1, 2)
+        v = attn.v_proj(hidden_states).view(B, S, -1, d).transpose(1, 2)
+        cos, sin = position_embeddings
+        q, k = apply_rotary_pos_emb(q, k, cos, sin)
+        out, batch, rows = flash_attention_entropy(q.half(), k.half(), v.half(), causal=True, scale=attn.scaling,
+                                                   return_rows=True)
+        return attn.o_proj(out.reshape(B, S, -1).to(hidden_states.dtype)), batch, rows
+
     def _attention_with_fused_entropy(self, hidden_states: torch.Tensor, attention_mask=None, position_ids=None,
                                       past_key_value=None, use_cache: bool = False, **kwargs):
         """EE/python/dispatch.py:212-247: the attention module with its probabilities
-        returned, then their entropy (per batch, and per token for token routing)."""
+        returned, then their entropy (per batch, and per token for token routing).  With
+        ``attention="flash"`` the probabilities never reach HBM: causal flash attention
+        computes the output and every row's entropy in one pass (the explicit
+        ``attention_mask`` is then taken to be the causal mask; no KV cache)."""
+        if self.attention == "flash":
+            _require(not use_cache and past_key_value is None, "flash attention here has no KV cache")
+            pe = kwargs.get("position_embeddings")
+            if pe is None:
+                pe = self.self_attn.rotary_emb(hidden_states, position_ids)
+            attn_output, entropy_batch, rows = self._flash_attention(hidden_states, pe)
+            self.token_entropy = rows.mean(dim=1)
+            return attn_output, entropy_batch, None
         attn_kwargs = dict(attention_mask=attention_mask, position_ids=position_ids, past_key_value=past_key_value,
                            output_attentions=True, use_cache=use_cache)
         attn_kwargs.update(kwargs)
@@ -113,13 +143,14 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         return attn_output, entropy_batch, present_kv
 
 
-def build_dispatched_llama(model, tau_low: float, tau_high: float, routing: str = "batch"):
+def build_dispatched_llama(model, tau_low: float, tau_high: float, routing: str = "batch",
+                           attention: str = "eager"):
     """EE/python/dispatch.py:250-259: wraps every decoder layer of a transformers Llama
     model; returns (blocks, dispatcher)."""
     device = next(model.parameters()).device
     blocks = []
     for i, layer in enumerate(model.model.layers):
-        block = EntropyDispatchedLlamaBlock(layer, layer_idx=i, routing=routing)
+        block = EntropyDispatchedLlamaBlock(layer, layer_idx=i, routing=routing, attention=attention)
         block = block.to(device).half()
         block.eval()
         blocks.append(block)
