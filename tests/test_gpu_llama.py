@@ -171,3 +171,22 @@ def test_dispatched_forward_tracks_the_model(pkg, cuda):
         # batch routing reads one tier per layer per chunk on the host; token routing none
         assert sum(v["count"] for v in stats.values()) == (4 if routing == "batch" else 0)
 
+
+@pytest.mark.parametrize("routing", ["batch", "token"])
+def test_flash_attention_block_tracks_eager(pkg, cuda, layer, routing):
+    """attention="flash": the same block with the attention computed by the flash kernel
+    (no probabilities in HBM) -- entropies and outputs track the eager block."""
+    lay, x, pos, pe, mask = layer
+    eager = pkg.EntropyDispatchedLlamaBlock(lay, routing=routing).to(cuda)
+    flash = pkg.EntropyDispatchedLlamaBlock(lay, routing=routing, attention="flash").to(cuda)
+    d1 = pkg.PipelinedEntropyDispatcher(-1.0, -1.0)  # every token in FP16: compares the attention paths
+    d2 = pkg.PipelinedEntropyDispatcher(-1.0, -1.0)
+    with torch.no_grad():
+        out_e = eager(x, dispatcher=d1, attention_mask=mask, position_ids=pos, position_embeddings=pe)[0]
+        out_f = flash(x, dispatcher=d2, attention_mask=mask, position_ids=pos, position_embeddings=pe)[0]
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(flash.layer_entropy.cpu().numpy(), eager.layer_entropy.cpu().numpy(), rtol=2e-3)
+    np.testing.assert_allclose(flash.token_entropy.cpu().numpy(), eager.token_entropy.cpu().numpy(), rtol=5e-3,
+                               atol=5e-3)
+    assert _relf(out_f.float().cpu().numpy(), out_e.float().cpu().numpy()) < 1e-2
+

@@ -6,7 +6,8 @@ TinyLlama's weights and WikiText-2 are not on this machine, so the reference's
 perplexity evaluation (EE/python/quality_eval.py) is replaced by this seeded stand-in:
 ids uniform in [0, vocab), KL(softmax(fp32 logits_gated) || softmax(fp32 logits_fp16))
 averaged over tokens.  Attention is the model's own transformers module in eager mode,
-as in the reference (it must return the probabilities the router reads).
+as in the reference (it must return the probabilities the router reads), or this
+library's flash attention with online entropy (``attention="flash"``).
 
     python triton-kernels-optimization_b200/eval_llama.py --batch 8 --seq 2048
 """
@@ -79,12 +80,15 @@ def main(argv=None) -> int:
 
     runs = {}
     base_lp = None
-    for name, (tl, th), routing in [("all_fp16_tier", (-1.0, -1.0), "batch"),
-                                    ("batch_0.41_1.68", (0.41, 1.68), "batch"),
-                                    ("token_0.41_1.68", (0.41, 1.68), "token"),
-                                    ("batch_2.34_6.03", (2.34, 6.03), "batch"),
-                                    ("token_2.34_6.03", (2.34, 6.03), "token")]:
-        blocks, disp = pkg.build_dispatched_llama(model, tl, th, routing=routing)
+    for name, (tl, th), routing, attention in [("all_fp16_tier", (-1.0, -1.0), "batch", "eager"),
+                                               ("batch_0.41_1.68", (0.41, 1.68), "batch", "eager"),
+                                               ("token_0.41_1.68", (0.41, 1.68), "token", "eager"),
+                                               ("batch_2.34_6.03", (2.34, 6.03), "batch", "eager"),
+                                               ("token_2.34_6.03", (2.34, 6.03), "token", "eager"),
+                                               ("flash_all_fp16_tier", (-1.0, -1.0), "batch", "flash"),
+                                               ("flash_token_2.34_6.03", (2.34, 6.03), "token", "flash"),
+                                               ("flash_batch_2.34_6.03", (2.34, 6.03), "batch", "flash")]:
+        blocks, disp = pkg.build_dispatched_llama(model, tl, th, routing=routing, attention=attention)
         disp.reset_stats()
         logits, ms = timed(lambda: pkg.dispatched_forward(model, blocks, disp, ids))
         lp = logprobs(logits)
@@ -103,7 +107,7 @@ def main(argv=None) -> int:
             base_lp = lp
         else:
             kl = (lp.exp() * (lp - base_lp)).sum(-1).mean()
-            entry["kl_vs_all_fp16_tier"] = float(kl)
+            entry["kl_vs_all_fp16_tier"] = float(kl)  # against the eager all-FP16-tier run
         runs[name] = entry
         del blocks, logits, lp
         torch.cuda.empty_cache()
