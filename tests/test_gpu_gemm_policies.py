@@ -53,3 +53,34 @@ def test_gated_linear(pkg, cuda, policy, M, n, K, N):
         assert _relf(y[rows[1]], _ref_fp8(a[rows[1]], p)) < 1e-2
     if rows[2].numel():
         assert _relf(y[rows[2]], _ref_fp16(a[rows[2]], p)) < 1e-2
+
+
+@pytest.mark.parametrize("counts", [(100, 300, 40), (130, 257, 128), (256, 129, 1), (0, 128, 384)])
+def test_bucket_edge_sizes(pkg, cuda, policy, counts):
+    """Bucket sizes at the row-tile edges (a last tile of 1, 128, 129 or 256 rows: the
+    CTA-pair kernel runs tiles of at most 128 rows as M = 128 pair tiles), routed from
+    given entropies in a shuffled row order."""
+    M, K, N = sum(counts), 512, 768
+    g = torch.Generator(device=cuda).manual_seed(sum(counts) + policy)
+    H = torch.cat([torch.full((c,), v, device=cuda) for c, v in zip(counts, (0.1, 1.0, 3.0))])
+    H = H[torch.randperm(M, generator=g, device=cuda)]
+    a = torch.randn(M, K, generator=g, device=cuda)
+    a = torch.where(torch.rand(M, K, generator=g, device=cuda) < 0.01, a * 20.0, a).half()
+    w = (torch.randn(N, K, generator=g, device=cuda) * 0.05).half()
+    p = pkg.WeightPack(*pkg.quantize_weights_int8(w))
+    r = pkg.EntropyRouter(0.41, 1.68)
+    r.reserve(M, K, cuda)
+    r.route_entropy(H)
+    y = r.gated_linear(a, p)
+    torch.cuda.synchronize()
+    assert pkg._lib.device_check() == 0
+    assert r.counts.cpu().tolist() == list(counts)
+    route = r.route_ids
+    rows = [torch.nonzero(route == b).flatten() for b in range(3)]
+    if rows[0].numel():
+        assert torch.equal(y[rows[0]].view(torch.int16), _ref_int8(a[rows[0]], p).view(torch.int16))
+    if rows[1].numel():
+        assert _relf(y[rows[1]], _ref_fp8(a[rows[1]], p)) < 1e-2
+    if rows[2].numel():
+        assert _relf(y[rows[2]], _ref_fp16(a[rows[2]], p)) < 1e-2
+

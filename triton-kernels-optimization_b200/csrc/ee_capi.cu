@@ -139,10 +139,13 @@ int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cud
   int st;
   if (op.a8) {
     if ((st = encode_kmajor(&maps.a8, op.a8, args.M_cap, args.K, op.ld8, 1, ee::kBM)) != EE_OK) return st;
+    if (pair && (st = encode_kmajor(&maps.a8h, op.a8, args.M_cap, args.K, op.ld8, 1, ee::kBM / 2)) != EE_OK) return st;
     any = &maps.a8;
   }
   if (op.a16) {
     if ((st = encode_kmajor(&maps.a16, op.a16, args.M_cap, args.K, op.ld16, 2, ee::kBM)) != EE_OK) return st;
+    if (pair && (st = encode_kmajor(&maps.a16h, op.a16, args.M_cap, args.K, op.ld16, 2, ee::kBM / 2)) != EE_OK)
+      return st;
     any = any ? any : &maps.a16;
   }
   for (int b = 0; b < 3; ++b) {
@@ -154,6 +157,8 @@ int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cud
   if (any == nullptr) return fail(EE_ERR_INVALID, "GEMM without an A operand");
   if (!op.a8) maps.a8 = *any;
   if (!op.a16) maps.a16 = *any;
+  if (!pair || !op.a8) maps.a8h = maps.a8;  // never dereferenced then
+  if (!pair || !op.a16) maps.a16h = maps.a16;
   for (int b = 0; b < 3; ++b)
     if (!op.w[b]) maps.w[b] = op.w[0] ? maps.w[0] : (op.w[1] ? maps.w[1] : maps.w[2]);
 

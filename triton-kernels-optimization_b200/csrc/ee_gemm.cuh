@@ -48,10 +48,13 @@ struct SingleCfg {
 
 struct TileGeo {
   int cnt[3], off[3], mtiles[3], tiles[3];
+  int halfmt[3];  // the bucket's half row tile (last m-tile with at most bm / 2 rows), or -1
   int ntn, total;
 };
 
-__device__ __forceinline__ TileGeo make_geo(const GemmArgs& a, int bm, int bn = kBN) {
+// half_tiles: the CTA-pair kernel runs a bucket's last row tile as an M = 128 pair tile
+// when it holds at most 128 rows (instead of an M = 256 tile that is mostly padding)
+__device__ __forceinline__ TileGeo make_geo(const GemmArgs& a, int bm, int bn = kBN, bool half_tiles = false) {
   TileGeo g;
   if (a.dyn_counts != nullptr) {
 #pragma unroll
@@ -70,6 +73,8 @@ __device__ __forceinline__ TileGeo make_geo(const GemmArgs& a, int bm, int bn = 
     g.mtiles[b] = (g.cnt[b] + bm - 1) / bm;
     g.tiles[b] = g.mtiles[b] * g.ntn;
     g.total += g.tiles[b];
+    const int rem = g.cnt[b] % bm;
+    g.halfmt[b] = (half_tiles && rem >= 1 && rem <= bm / 2) ? g.mtiles[b] - 1 : -1;
   }
   return g;
 }
@@ -77,22 +82,29 @@ __device__ __forceinline__ TileGeo make_geo(const GemmArgs& a, int bm, int bn = 
 // tile index -> bucket, first position (row of A), first output column.  Tiles run
 // FP16 first (the longest K loops), then FP8, then INT8; m fastest inside a bucket.
 // Written out per bucket: a loop with an early return here kept TileGeo on the stack.
-__device__ __forceinline__ int decode_in(const TileGeo& g, int b, int t, int bm, int bn, int& pos0, int& n0) {
+__device__ __forceinline__ int decode_in(const TileGeo& g, int b, int t, int bm, int bn, int& pos0, int& n0,
+                                         bool& half) {
   const int mt = t % g.mtiles[b];
   const int nt = t / g.mtiles[b];
   pos0 = g.off[b] + mt * bm;
   n0 = nt * bn;
+  half = mt == g.halfmt[b];
   return b;
 }
-__device__ __forceinline__ int decode_tile(const TileGeo& g, int t, int bm, int& pos0, int& n0, int bn = kBN) {
-  if (t < g.tiles[2]) return decode_in(g, 2, t, bm, bn, pos0, n0);
+__device__ __forceinline__ int decode_tile(const TileGeo& g, int t, int bm, int& pos0, int& n0, int bn, bool& half) {
+  if (t < g.tiles[2]) return decode_in(g, 2, t, bm, bn, pos0, n0, half);
   t -= g.tiles[2];
-  if (t < g.tiles[1]) return decode_in(g, 1, t, bm, bn, pos0, n0);
+  if (t < g.tiles[1]) return decode_in(g, 1, t, bm, bn, pos0, n0, half);
   t -= g.tiles[1];
-  if (t < g.tiles[0]) return decode_in(g, 0, t, bm, bn, pos0, n0);
+  if (t < g.tiles[0]) return decode_in(g, 0, t, bm, bn, pos0, n0, half);
   pos0 = 0;
   n0 = 0;
+  half = false;
   return 0;
+}
+__device__ __forceinline__ int decode_tile(const TileGeo& g, int t, int bm, int& pos0, int& n0, int bn = kBN) {
+  bool half;
+  return decode_tile(g, t, bm, pos0, n0, bn, half);
 }
 
 __device__ __forceinline__ int kblocks_of(int b, int K) {
@@ -255,8 +267,11 @@ __device__ __forceinline__ void epilogue_drain_swiglu(const GemmArgs& args, cons
 // Drains the quarter's 256 columns (taddr: its lanes, first column); the whole warp
 // calls it (tcgen05.ld is .sync.aligned).  The TMEM read of chunk c+1 is in flight
 // while chunk c is converted and stored.
+// nchunks TMEM chunks of 32 columns from taddr, output chunks chunk0 .. chunk0 + nchunks - 1
+// of the tile (an even count: two per iteration).
 template <int BN = kBN>
-__device__ __forceinline__ void epilogue_drain(const GemmArgs& args, const EpiRow& e, int b, int n0, uint32_t taddr) {
+__device__ __forceinline__ void epilogue_drain(const GemmArgs& args, const EpiRow& e, int b, int n0, uint32_t taddr,
+                                               int chunk0 = 0, int nchunks = BN / 32) {
   if constexpr (BN == kBN) {
     if (args.out_mode == 2) {
       epilogue_drain_swiglu(args, e, b, n0, taddr);
@@ -268,15 +283,15 @@ __device__ __forceinline__ void epilogue_drain(const GemmArgs& args, const EpiRo
   tmem_ld32(taddr, ra);
   tmem_ld_wait(ra);
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; c += 2) {
+  for (int c = 0; c < nchunks; c += 2) {
     __syncwarp();
     tmem_ld32(taddr + (c + 1) * 32, rb);
-    epilogue_chunk(args, e, b, n0, c, ra);
+    epilogue_chunk(args, e, b, n0, chunk0 + c, ra);
     tmem_ld_wait(rb);
-    const bool more = c + 2 < BN / 32;
+    const bool more = c + 2 < nchunks;
     __syncwarp();
     if (more) tmem_ld32(taddr + (c + 2) * 32, ra);
-    epilogue_chunk(args, e, b, n0, c + 1, rb);
+    epilogue_chunk(args, e, b, n0, chunk0 + c + 1, rb);
     if (more) tmem_ld_wait(ra);
   }
   __syncwarp();
@@ -670,10 +685,31 @@ __device__ __forceinline__ void mma_stage_pair(uint32_t d_tmem, uint32_t a_addr,
     tc_mma_pair<KIND>(d_tmem, da + 2u * k, db + 2u * k, idesc, (first && k == 0) ? 0u : 1u);
 }
 
+// M = 128 pair tile: each CTA supplies 64 rows of A; the accumulator of CTA r holds rows
+// 64 r .. 64 r + 63 with columns [0, 128) in TMEM lanes 0..63 and columns [128, 256) in
+// lanes 64..127, both at TMEM columns [0, 128) (measured on B200 with a probe MMA of
+// known operands: every one of the 128 x 128 results at that place).
+template <int KIND>
+__device__ __forceinline__ void mma_stage_pair_half(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr, bool first) {
+  constexpr uint32_t idesc = (KIND == kKindI8)   ? make_idesc(2u, 1u, kPairRows / 2, kBN)
+                             : (KIND == kKindF8) ? make_idesc(1u, 0u, kPairRows / 2, kBN)
+                                                 : make_idesc(1u, 0u, kPairRows / 2, kBN);
+  const uint64_t da = sdesc_k_sw128(a_addr);
+  const uint64_t db = sdesc_k_sw128(b_addr);
+#pragma unroll
+  for (int k = 0; k < kBKBytes / 32; ++k)
+    tc_mma_pair<KIND>(d_tmem, da + 2u * k, db + 2u * k, idesc, (first && k == 0) ? 0u : 1u);
+}
+
+// A half tile's epilogue: warp quarter q drains rows (q & 1) * 32 + lane of its CTA's 64
+// and output columns (q >> 1) * 128 .. + 127 -- TMEM lanes 32 q .., columns 0 .. 127:
+// epilogue_drain over 4 chunks starting at chunk (q >> 1) * 4.
+
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gated_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a8, const __grid_constant__ CUtensorMap tm_a16,
                            const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
-                           const __grid_constant__ CUtensorMap tm_w2, const GemmArgs args) {
+                           const __grid_constant__ CUtensorMap tm_w2, const __grid_constant__ CUtensorMap tm_a8h,
+                           const __grid_constant__ CUtensorMap tm_a16h, const GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -696,7 +732,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
   griddep_wait();  // bucket counts, packed rows and the tile counter come from earlier kernels
   griddep_launch_dependents();
-  const TileGeo geo = make_geo(args, kPairRows);
+  // half tiles need each thread's gate and up columns in one lane: not with SwiGLU
+  const TileGeo geo = make_geo(args, kPairRows, kBN, args.out_mode != 2);
   const bool dyn = args.sched != nullptr;
   if (pair >= geo.total) {  // the same decision in both CTAs of the pair
     if (leader) feed_retire_pair(args, npairs);
@@ -752,12 +789,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       }
       if (t >= geo.total) break;
       int pos0, n0;
-      const int b = decode_tile(geo, t, kPairRows, pos0, n0);
+      bool half;
+      const int b = decode_tile(geo, t, kPairRows, pos0, n0, kBN, half);
       const int nkb = kblocks_of(b, K);
       const int kstep = (b == kFP16) ? kBKBytes / 2 : kBKBytes;
-      const CUtensorMap* ta = (b == kFP16) ? &tm_a16 : &tm_a8;
+      const CUtensorMap* ta = half ? ((b == kFP16) ? &tm_a16h : &tm_a8h) : ((b == kFP16) ? &tm_a16 : &tm_a8);
       const CUtensorMap* tw = (b == kINT8) ? &tm_w0 : (b == kFP8 ? &tm_w1 : &tm_w2);
-      const int arow = pos0 + static_cast<int>(rank) * 128;
+      const int arow = pos0 + static_cast<int>(rank) * (half ? 64 : 128);
+      const uint32_t stage_tx = half ? 2u * (kHalfStageBytes / 2 + kHalfStageBytes) : 2u * kStageBytesPair;
       const int brow = n0 + static_cast<int>(rank) * (kBN / 2);
       for (int kb = 0; kb < nkb; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
@@ -765,7 +804,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           break;
         }
         if (lane == 0) {
-          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kStageBytesPair);
+          if (leader) mbar_arrive_expect_tx(&full[stage], stage_tx);
           const uint32_t bar = map_to_cta(smem_u32(&full[stage]), 0);
           tma_load_2d_pair(sA + stage * kHalfStageBytes, ta, bar, kb * kstep, arow);
           tma_load_2d_pair(sB + stage * kHalfStageBytes, tw, bar, kb * kstep, brow);
@@ -803,7 +842,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         }
         if (t >= geo.total) break;
         int pos0, n0;
-        const int b = decode_tile(geo, t, kPairRows, pos0, n0);
+        bool half;
+        const int b = decode_tile(geo, t, kPairRows, pos0, n0, kBN, half);
         const int nkb = kblocks_of(b, K);
         if (!mbar_wait<true>(&acc_empty[ab], aphase ^ 1u, abort_flag)) {
           failed = true;
@@ -820,12 +860,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           if (lane == 0) {
             const uint32_t a_addr = smem_u32(sA + stage * kHalfStageBytes);
             const uint32_t b_addr = smem_u32(sB + stage * kHalfStageBytes);
-            if (b == kINT8)
+            if (half) {
+              if (b == kINT8)
+                mma_stage_pair_half<kKindI8>(d_tmem, a_addr, b_addr, kb == 0);
+              else if (b == kFP8)
+                mma_stage_pair_half<kKindF8>(d_tmem, a_addr, b_addr, kb == 0);
+              else
+                mma_stage_pair_half<kKindF16>(d_tmem, a_addr, b_addr, kb == 0);
+            } else if (b == kINT8) {
               mma_stage_pair<kKindI8>(d_tmem, a_addr, b_addr, kb == 0);
-            else if (b == kFP8)
+            } else if (b == kFP8) {
               mma_stage_pair<kKindF8>(d_tmem, a_addr, b_addr, kb == 0);
-            else
+            } else {
               mma_stage_pair<kKindF16>(d_tmem, a_addr, b_addr, kb == 0);
+            }
             tc_commit_pair_both(&empty[stage], 0x3);
           }
           __syncwarp();
@@ -867,9 +915,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       }
       if (t >= geo.total) break;
       int pos0, n0;
-      const int b = decode_tile(geo, t, kPairRows, pos0, n0);
-      const EpiRow er =
-          epilogue_prepare(args, geo, b, pos0 + static_cast<int>(rank) * 128 + quarter * 32 + lane, n0, lane);
+      bool half;
+      const int b = decode_tile(geo, t, kPairRows, pos0, n0, kBN, half);
+      const int row = half ? static_cast<int>(rank) * 64 + (quarter & 1) * 32 + lane
+                           : static_cast<int>(rank) * 128 + quarter * 32 + lane;
+      const EpiRow er = epilogue_prepare(args, geo, b, pos0 + row, n0, lane);
       if (!mbar_wait(&acc_full[ab], aphase, abort_flag)) {
         if (lane == 0) {
           atomicOr(&g_device_error, kErrWaitTimeout);
@@ -878,7 +928,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      epilogue_drain(args, er, b, n0, tmem_base + ab * kBN + (static_cast<uint32_t>(quarter * 32) << 16));
+      epilogue_drain(args, er, b, n0, tmem_base + ab * kBN + (static_cast<uint32_t>(quarter * 32) << 16),
+                     half ? (quarter >> 1) * 4 : 0, half ? 4 : kBN / 32);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_acc_empty0 + ab * static_cast<uint32_t>(sizeof(uint64_t)));

@@ -105,6 +105,7 @@ struct GemmMaps {
   CUtensorMap a8;          // uint8 [M_cap, K], box {128, 128}
   CUtensorMap a16;         // fp16  [M_cap, K], box {64, 128}
   CUtensorMap w[3];        // bucket weights [N, K] K-major, box {128 B, 256}
+  CUtensorMap a8h, a16h;   // the same A tensors with 64-row boxes (CTA-pair half tiles)
 };
 // single-CTA kernel, 128 x bn tiles (bn = kBN, or kBNNarrow for weight-streaming calls)
 int launch_gated_gemm(const GemmMaps& maps, const GemmArgs& args, int grid, int bn, cudaStream_t s);

@@ -184,7 +184,7 @@ int launch_gated_gemm_pair(const GemmMaps& m, const GemmArgs& args, int pairs, c
   if (prepare_device() != 0) return -4;
   if (pairs <= 0) return 0;
   return launch_pdl(gated_gemm_pair_kernel, dim3(2 * pairs), dim3(kGemmThreads), kGemmSmemPair, s, m.a8, m.a16, m.w[0],
-                    m.w[1], m.w[2], args);
+                    m.w[1], m.w[2], m.a8h, m.a16h, args);
 }
 
 int launch_gated_gemm(const GemmMaps& m, const GemmArgs& args, int grid, int bn, cudaStream_t s) {
