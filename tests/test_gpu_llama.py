@@ -190,3 +190,31 @@ def test_flash_attention_block_tracks_eager(pkg, cuda, layer, routing):
                                atol=5e-3)
     assert _relf(out_f.float().cpu().numpy(), out_e.float().cpu().numpy()) < 1e-2
 
+
+@pytest.mark.parametrize("routing", ["batch", "token"])
+def test_every_linear_routed(pkg, cuda, routing):
+    """route_all: q / k / v / o dispatched too.  With every tier forced to FP16 the
+    model tracks the transformers model within the W8A16 quantisation error; with the
+    real thresholds the routed model's KL from the all-FP16 run stays small."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    torch.manual_seed(11)
+    cfg = LlamaConfig(hidden_size=256, num_attention_heads=4, num_key_value_heads=2, intermediate_size=512,
+                      num_hidden_layers=3, vocab_size=128, attn_implementation="eager")
+    model = LlamaForCausalLM(cfg).to(cuda).half().eval()
+    ids = torch.randint(0, 128, (2, 128), generator=torch.Generator().manual_seed(2)).to(cuda)
+    with torch.no_grad():
+        ref = model(ids).logits.float()
+    blocks, disp = pkg.build_dispatched_llama(model, -1.0, -1.0, routing=routing, attention="flash", route_all=True)
+    fp16 = pkg.dispatched_forward(model, blocks, disp, ids).float()
+    assert torch.isfinite(fp16).all()
+    assert _relf(fp16.cpu().numpy(), ref.cpu().numpy()) < 5e-2
+    lo, hi = (0.41, 1.68) if routing == "batch" else tuple(
+        float(v) for v in np.quantile(torch.cat([b.token_entropy.reshape(-1) for b in blocks]).cpu().numpy(),
+                                      [0.3, 0.7]))
+    blocks, disp = pkg.build_dispatched_llama(model, lo, hi, routing=routing, attention="flash", route_all=True)
+    gated = pkg.dispatched_forward(model, blocks, disp, ids).float()
+    lp, lq = torch.log_softmax(gated, -1), torch.log_softmax(fp16, -1)
+    kl = float((lp.exp() * (lp - lq)).sum(-1).mean())
+    assert 0.0 <= kl < 0.1
+

@@ -5,7 +5,8 @@ divergence of the gated model's next-token distribution from the all-FP16-tier o
 TinyLlama's weights and WikiText-2 are not on this machine, so the reference's
 perplexity evaluation (EE/python/quality_eval.py) is replaced by this seeded stand-in:
 ids uniform in [0, vocab), KL(softmax(fp32 logits_gated) || softmax(fp32 logits_fp16))
-averaged over tokens.  Attention is the model's own transformers module in eager mode,
+averaged over tokens; "every linear routed" (q / k / v / o dispatched too, ``route_all``)
+against the reference's MLP-only mode.  Attention is the model's own transformers module in eager mode,
 as in the reference (it must return the probabilities the router reads), or this
 library's flash attention with online entropy (``attention="flash"``).
 
@@ -87,8 +88,12 @@ def main(argv=None) -> int:
                                                ("token_2.34_6.03", (2.34, 6.03), "token", "eager"),
                                                ("flash_all_fp16_tier", (-1.0, -1.0), "batch", "flash"),
                                                ("flash_token_2.34_6.03", (2.34, 6.03), "token", "flash"),
-                                               ("flash_batch_2.34_6.03", (2.34, 6.03), "batch", "flash")]:
-        blocks, disp = pkg.build_dispatched_llama(model, tl, th, routing=routing, attention=attention)
+                                               ("flash_batch_2.34_6.03", (2.34, 6.03), "batch", "flash"),
+                                               ("flash_token_all_2.34_6.03", (2.34, 6.03), "token", "flash+all"),
+                                               ("flash_token_all_0.41_1.68", (0.41, 1.68), "token", "flash+all")]:
+        route_all = attention.endswith("+all")
+        blocks, disp = pkg.build_dispatched_llama(model, tl, th, routing=routing, attention=attention.split("+")[0],
+                                                  route_all=route_all)
         disp.reset_stats()
         logits, ms = timed(lambda: pkg.dispatched_forward(model, blocks, disp, ids))
         lp = logprobs(logits)

@@ -28,13 +28,16 @@ from .kernels import SwiGLUPack, _require, attention_entropy, flash_attention_en
 class EntropyDispatchedLlamaBlock(nn.Module):
     """EE/python/dispatch.py:150-247 with the sm_100a kernels."""
 
-    def __init__(self, llama_block, layer_idx: int = 0, routing: str = "batch", attention: str = "eager"):
+    def __init__(self, llama_block, layer_idx: int = 0, routing: str = "batch", attention: str = "eager",
+                 route_all: bool = False):
         super().__init__()
         _require(routing in ("batch", "token"), "routing must be 'batch' or 'token'")
         _require(attention in ("eager", "flash"), "attention must be 'eager' or 'flash'")
+        _require(not route_all or attention == "flash", "route_all needs attention='flash'")
         self.layer_idx = layer_idx
         self.routing = routing
         self.attention = attention
+        self.route_all = route_all
         self.self_attn = llama_block.self_attn
         self.input_layernorm = llama_block.input_layernorm
         self.post_attention_layernorm = llama_block.post_attention_layernorm
@@ -42,6 +45,13 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         self.up_proj = EntropyDispatchedLinear.from_linear(llama_block.mlp.up_proj)
         self.down_proj = EntropyDispatchedLinear.from_linear(llama_block.mlp.down_proj)
         self.act_fn = nn.SiLU()
+        if route_all:
+            # every linear of the block entropy-dispatched: q / k / v as one concatenated
+            # projection (per-output-channel scales: concatenation changes nothing), o
+            a = llama_block.self_attn
+            self.qkv_proj = EntropyDispatchedLinear.from_linear(_concat_linears(a.q_proj, a.k_proj, a.v_proj))
+            self.o_proj = EntropyDispatchedLinear.from_linear(a.o_proj)
+            self._qkv_split = (a.q_proj.out_features, a.k_proj.out_features, a.v_proj.out_features)
         self.layer_entropy: Optional[torch.Tensor] = None
         self.token_entropy: Optional[torch.Tensor] = None
         self._router: Optional[EntropyRouter] = None
@@ -51,12 +61,16 @@ class EntropyDispatchedLlamaBlock(nn.Module):
                 past_key_value=None, use_cache: bool = False, **kwargs) -> Tuple[torch.Tensor, ...]:
         residual = hidden_states
         hidden_states = self.input_layernorm(hidden_states)
+        if self.route_all:
+            kwargs["_dispatcher"] = dispatcher
         attn_output, entropy_batch, present_kv = self._attention_with_fused_entropy(
             hidden_states, attention_mask=attention_mask, position_ids=position_ids, past_key_value=past_key_value,
             use_cache=use_cache, **kwargs)
         self.layer_entropy = entropy_batch
-        if dispatcher is not None:
-            dispatcher.submit_entropy(entropy_batch)
+        if dispatcher is not None and not (self.route_all and self.routing == "batch"):
+            dispatcher.submit_entropy(entropy_batch)  # (route_all / batch submitted it before o)
+        if dispatcher is not None and self.routing == "token":
+            dispatcher._prev_token_entropy = self.token_entropy.reshape(-1)  # the next layer's q / k / v
         hidden_states = residual + attn_output
 
         residual = hidden_states
@@ -79,10 +93,7 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         shape = x.shape
         x2 = x.reshape(-1, shape[-1]).to(torch.float16).contiguous()
         M = x2.shape[0]
-        r = self._router
-        if r is None or r.tau_low != dispatcher.tau_low or r.tau_high != dispatcher.tau_high:
-            r = self._router = EntropyRouter(dispatcher.tau_low, dispatcher.tau_high)
-        r.reserve(M, max(self.gate_proj.in_features, self.down_proj.in_features), x2.device)
+        r = self._router_for(dispatcher, M, max(self.gate_proj.in_features, self.down_proj.in_features), x2.device)
         r.route_entropy(self.token_entropy.reshape(-1))
         r.pack_rows(x2)  # one packing of the post-norm rows serves gate and up
         gp, up = self.gate_proj._pack(), self.up_proj._pack()
@@ -96,22 +107,58 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         out = r.gated_linear(h, self.down_proj._pack())
         return out.reshape(shape[:-1] + (self.down_proj.out_features,))
 
-    def _flash_attention(self, hidden_states: torch.Tensor, position_embeddings):
+    def _flash_attention(self, hidden_states: torch.Tensor, position_embeddings, dispatcher=None):
         """The attention module's projections and rotary embedding, then causal flash
-        attention with the row entropies in one kernel (no [B, H, S, S] probabilities)."""
+        attention with the row entropies in one kernel (no [B, H, S, S] probabilities).
+        With ``route_all`` the q / k / v projection runs in the precision of the previous
+        layer's entropy (per token, or its batch tier) and o in this layer's."""
         from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
 
         attn = self.self_attn
         B, S, _ = hidden_states.shape
         d = attn.head_dim
-        q = attn.q_proj(hidden_states).view(B, S, -1, d).transpose(1, 2)
-        k = attn.k_proj(hidden_states).view(B, S, -1, d).transpose(1, 2)
-        v = attn.v_proj(hidden_states).view(B, S, -1, d).transpose(1, 2)
+        if self.route_all:
+            qkv = self._routed(hidden_states, self.qkv_proj, dispatcher, prev=True)
+            q, k, v = qkv.split(self._qkv_split, dim=-1)
+        else:
+            q, k, v = attn.q_proj(hidden_states), attn.k_proj(hidden_states), attn.v_proj(hidden_states)
+        q = q.reshape(B, S, -1, d).transpose(1, 2)
+        k = k.reshape(B, S, -1, d).transpose(1, 2)
+        v = v.reshape(B, S, -1, d).transpose(1, 2)
         cos, sin = position_embeddings
         q, k = apply_rotary_pos_emb(q, k, cos, sin)
         out, batch, rows = flash_attention_entropy(q.half(), k.half(), v.half(), causal=True, scale=attn.scaling,
                                                    return_rows=True)
-        return attn.o_proj(out.reshape(B, S, -1).to(hidden_states.dtype)), batch, rows
+        out = out.reshape(B, S, -1).to(hidden_states.dtype)
+        self.token_entropy = rows.mean(dim=1)
+        if self.route_all:
+            if self.routing == "batch" and dispatcher is not None:
+                dispatcher.submit_entropy(batch)
+            return self._routed(out, self.o_proj, dispatcher, prev=False), batch, rows
+        return attn.o_proj(out), batch, rows
+
+    def _routed(self, x: torch.Tensor, proj: "EntropyDispatchedLinear", dispatcher, prev: bool) -> torch.Tensor:
+        """One linear of the attention in the precision the dispatcher chose: per token
+        (``routing="token"``) from the previous layer's token entropies (prev) or this
+        layer's; per batch from the dispatcher's current tier.  No entropy yet: FP16."""
+        if self.routing == "batch" or dispatcher is None:
+            tier = dispatcher.get_tier() if dispatcher is not None else PrecisionTier.FP16
+            return proj(x, tier=tier)
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).to(torch.float16).contiguous()
+        H = getattr(dispatcher, "_prev_token_entropy", None) if prev else self.token_entropy.reshape(-1)
+        if H is None or H.numel() != x2.shape[0] or (prev and self.layer_idx == 0):  # the first layer: FP16
+            H = torch.full((x2.shape[0],), float("inf"), device=x2.device)
+        r = self._router_for(dispatcher, x2.shape[0], max(proj.in_features, self.down_proj.in_features), x2.device)
+        r.route_entropy(H)
+        return r.gated_linear(x2, proj._pack()).reshape(shape[:-1] + (proj.out_features,))
+
+    def _router_for(self, dispatcher, M: int, K: int, device) -> EntropyRouter:
+        r = self._router
+        if r is None or r.tau_low != dispatcher.tau_low or r.tau_high != dispatcher.tau_high:
+            r = self._router = EntropyRouter(dispatcher.tau_low, dispatcher.tau_high)
+        r.reserve(M, K, device)
+        return r
 
     def _attention_with_fused_entropy(self, hidden_states: torch.Tensor, attention_mask=None, position_ids=None,
                                       past_key_value=None, use_cache: bool = False, **kwargs):
@@ -125,8 +172,7 @@ class EntropyDispatchedLlamaBlock(nn.Module):
             pe = kwargs.get("position_embeddings")
             if pe is None:
                 pe = self.self_attn.rotary_emb(hidden_states, position_ids)
-            attn_output, entropy_batch, rows = self._flash_attention(hidden_states, pe)
-            self.token_entropy = rows.mean(dim=1)
+            attn_output, entropy_batch, rows = self._flash_attention(hidden_states, pe, kwargs.get("_dispatcher"))
             return attn_output, entropy_batch, None
         attn_kwargs = dict(attention_mask=attention_mask, position_ids=position_ids, past_key_value=past_key_value,
                            output_attentions=True, use_cache=use_cache)
@@ -143,14 +189,24 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         return attn_output, entropy_batch, present_kv
 
 
+def _concat_linears(*linears: nn.Linear) -> nn.Linear:
+    out = nn.Linear(linears[0].in_features, sum(l.out_features for l in linears), bias=False)
+    out = out.to(device=linears[0].weight.device, dtype=linears[0].weight.dtype)
+    with torch.no_grad():
+        out.weight.copy_(torch.cat([l.weight for l in linears], dim=0))
+    return out
+
+
 def build_dispatched_llama(model, tau_low: float, tau_high: float, routing: str = "batch",
-                           attention: str = "eager"):
+                           attention: str = "eager", route_all: bool = False):
     """EE/python/dispatch.py:250-259: wraps every decoder layer of a transformers Llama
-    model; returns (blocks, dispatcher)."""
+    model; returns (blocks, dispatcher).  ``route_all`` also dispatches q / k / v / o
+    (with ``attention="flash"``)."""
     device = next(model.parameters()).device
     blocks = []
     for i, layer in enumerate(model.model.layers):
-        block = EntropyDispatchedLlamaBlock(layer, layer_idx=i, routing=routing, attention=attention)
+        block = EntropyDispatchedLlamaBlock(layer, layer_idx=i, routing=routing, attention=attention,
+                                            route_all=route_all)
         block = block.to(device).half()
         block.eval()
         blocks.append(block)
