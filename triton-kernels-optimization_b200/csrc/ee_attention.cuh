@@ -3,17 +3,20 @@
 // [B, H, S, S] probabilities (the reference's transformers attention returns them and
 // computes -sum p log(p + 1e-10) in torch, EE/python/dispatch.py:236-245).
 //
-// One CTA per (batch, query head, 128-query tile), 192 threads:
+// One CTA per (batch, query head, 128-query tile), 384 threads:
 //   warp 0     TMA producer: Q once, then K and V^T tiles of 128 keys into 2-deep rings;
 //   warp 1     TMEM owner + single-thread UMMA issuer: S_j = Q K_j^T (M 128, N 128) into
 //              one of two 128-column TMEM buffers, O_j = P_j V_j (M 128, N d) into one of
 //              two d-column buffers;
-//   warps 2-5  one query row per thread: scores from TMEM, the reference's fp16
-//              roundings of the scores (fp16 Q K^T, times the scale, fp16), causal mask,
-//              running max / sum / sum of p (x - max) in base 2, P = 2^(x - max) as fp16
-//              into shared memory in the UMMA SW128 K-major layout, then
-//              O += alpha * O_j from TMEM in registers; at the end O / l and
-//              H = ln(l) - t / l.
+//   warps 2-3  idle (they complete the producer warpgroup, which hands its registers to
+//              the softmax warpgroups);
+//   warps 4-11 two warpgroups, one half row per thread (64 of the tile's 128 scores,
+//              half of O's columns): scores from TMEM into registers with the
+//              reference's fp16 roundings (fp16 Q K^T, times the scale, fp16), causal
+//              mask, the row max shared with the other half through shared memory,
+//              running sum and sum of p (x - max) in base 2, P = 2^(x - max) as fp16 into
+//              shared memory in the UMMA SW128 K-major layout, then O += alpha * O_j from
+//              TMEM in registers; at the end O / l and H = ln(l) - t / l.
 // V is consumed transposed (V^T [d, keys] per head, written by transpose_v_kernel) so
 // both UMMA operands of P V are K-major.  Every wait is bounded (2 s); on expiry the CTA
 // records an error word, drains its own MMAs and TMA loads, frees TMEM and exits.
@@ -29,7 +32,13 @@
 
 namespace ee {
 
-constexpr int kAttnThreads = 192;
+constexpr int kAttnThreads = 384;  // producer warpgroup (TMA, MMA, two idle warps), two softmax warpgroups
+// registers per thread: 168 at launch (384 threads, one CTA per SM); the producer
+// warpgroup gives its share to the softmax warpgroups (56 + 2 x 224 = 3 x 168)
+constexpr int kAttnLaunchRegs = 168;
+constexpr int kAttnProducerRegs = 56;
+constexpr int kAttnSoftmaxRegs = 224;
+static_assert(kAttnProducerRegs + 2 * kAttnSoftmaxRegs <= 3 * kAttnLaunchRegs, "register split above the launch budget");
 constexpr int kAttnTileBytes = kAttnTile * 128;  // one 128-byte-wide swizzled box of 128 rows: 16 KB
 
 template <int D>
@@ -40,7 +49,7 @@ struct AttnCfg {
   static constexpr int kKBytes = kKBlocks * kAttnTileBytes;    // one K tile
   static constexpr int kVBytes = 2 * (D * 128);                // one V^T tile: D rows x 128 keys, 2 blocks
   static constexpr int kPBytes = 2 * kAttnTileBytes;           // one P tile: 128 rows x 128 keys
-  static constexpr int kBarrierBytes = 256;
+  static constexpr int kBarrierBytes = 256 + 2 * 128 * 4;  // barriers, then the row-max exchange
   static constexpr size_t kSmem = 1024 + size_t(kQBytes) + 2 * size_t(kKBytes) + 2 * size_t(kVBytes) +
                                   2 * size_t(kPBytes) + kBarrierBytes;
   static_assert(kSmem <= 227 * 1024, "attention shared memory above the 227 KB per-CTA limit");
@@ -119,11 +128,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&s_empty[i], 8);  // eight softmax warps
+      mbar_init(&p_full[i], 8);
       mbar_init(&p_empty[i], 1);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 4);
+      mbar_init(&o_empty[i], 8);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -145,7 +154,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t tmem_s = tmem_base;            // columns [0, 256): two S buffers
   const uint32_t tmem_o = tmem_base + 2 * 128;  // columns [256, 256 + 2 D): two O buffers
-
+  // the register budgets change inside each role's branch: code after a join would be
+  // compiled for the smaller budget
+  if (warp < 4) {
+  warpgroup_reg_dealloc<kAttnProducerRegs>();
   if (warp == 0) {
     // -------------------------------------------------------------- TMA producer
     bool failed = false;
@@ -256,29 +268,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       (void)mbar_wait(drain, 0u, nullptr);
     }
+  }  // warps 2 and 3: nothing to do
   } else {
+    warpgroup_reg_alloc<kAttnSoftmaxRegs>();
     // -------------------------------------------------------------- softmax / entropy / output
+    // Two warpgroups: thread (half h, quarter q, lane) owns row q * 32 + lane, score
+    // columns 64 h .. 64 h + 63 and output columns h * D / 2 ..; the row max is exchanged
+    // through shared memory once per tile, the sums stay per half until the end.
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;  // query row of the tile owned by this thread
+    const int half = (warp - 4) >> 2;
+    const int row = quarter * 32 + lane;
     const int64_t q = static_cast<int64_t>(qt) * kAttnTile + row;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     constexpr float kLog2eF = 1.4426950408889634f;
+    constexpr int kOH = D / 2;  // output columns per thread
+    float* red = reinterpret_cast<float*>(bars + 32);  // [2 halves][128 rows]: row maxima, then sums
     float m2 = -__builtin_huge_valf(), l = 0.f, t2 = 0.f, alpha_prev = 0.f;
-    float o[D];
+    float o[kOH];
 #pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.f;
+    for (int i = 0; i < kOH; ++i) o[i] = 0.f;
     bool failed = false;
 
     auto consume_o = [&](int j, float alpha) -> bool {
       const int s = j & 1;
       const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
-      if (!mbar_wait(&o_full[s], ph, abort_flag)) return false;
+      if (!mbar_wait_warp(&o_full[s], ph, abort_flag)) return false;
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < kOH / 32; ++c) {
         uint32_t r[32];
         __syncwarp();
-        tmem_ld32(tmem_o + s * D + c * 32 + lane_off, r);
+        tmem_ld32(tmem_o + s * D + half * kOH + c * 32 + lane_off, r);
         tmem_ld_wait(r);
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha, __uint_as_float(r[i]));
@@ -289,88 +309,90 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       return true;
     };
 
-    for (int j = 0; j < nkv && !failed; ++j) {
+    // Every softmax warp runs every iteration, failed or not: the named barriers below
+    // need all eight warps each time (a warp that gave up skips only the work).
+    for (int j = 0; j < nkv; ++j) {
       const int s = j & 1;
       const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
-      if (!mbar_wait(&s_full[s], ph, abort_flag)) {
-        failed = true;
-        break;
-      }
-      tc_fence_after();
-      const int key0 = j * kAttnTile;
-      // keys this row may see in this tile: causal limit and the sequence end
+      if (!failed && !mbar_wait_warp(&s_full[s], ph, abort_flag)) failed = true;
+      if (failed && lane == 0) *abort_flag = 1;  // every role of the CTA stops waiting
+      const int key0 = j * kAttnTile + half * 64;
+      // keys this thread may see: causal limit and the sequence end
       int lim = static_cast<int>(args.S - key0);
       if (args.causal) {
         const int64_t c = q - key0 + 1;
         lim = c < lim ? static_cast<int>(c) : lim;
       }
-      lim = lim < 0 ? 0 : (lim > kAttnTile ? kAttnTile : lim);
-      // pass 1: row max (base-2 units) of the reference's fp16 scores
+      lim = lim < 0 ? 0 : (lim > 64 ? 64 : lim);
+      // the reference's fp16 scores (fp16 Q K^T, times the scale, fp16) -- kept as the
+      // fp16 values they are (masked: -inf), two per register
+      __half2 xs[32];
       float mx = -__builtin_huge_valf();
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        __syncwarp();
-        tmem_ld32(tmem_s + s * 128 + c * 32 + lane_off, r);
-        tmem_ld_wait(r);
+      if (!failed) {
+        tc_fence_after();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float sc = __half2float(__float2half_rn(__half2float(__float2half_rn(__uint_as_float(r[i]))) * args.scale));
-          if (c * 32 + i < lim) mx = fmaxf(mx, sc * kLog2eF);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld32(tmem_s + s * 128 + half * 64 + c * 32 + lane_off, r);
+          tmem_ld_wait(r);
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const int col = c * 32 + i;
+            const __half lo = __float2half_rn(__half2float(__float2half_rn(__uint_as_float(r[i]))) * args.scale);
+            const __half hi = __float2half_rn(__half2float(__float2half_rn(__uint_as_float(r[i + 1]))) * args.scale);
+            const __half2 v = __halves2half2(col < lim ? lo : __ushort_as_half(0xFC00u),
+                                             col + 1 < lim ? hi : __ushort_as_half(0xFC00u));
+            xs[col >> 1] = v;
+            mx = fmaxf(mx, fmaxf(__low2float(v), __high2float(v)));
+          }
         }
+        mx *= kLog2eF;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_empty[s]);  // the scores are in registers: S buffer free
       }
-      const float m_new = fmaxf(m2, mx);
+      // exchange the half-row maxima (barrier 1: the eight softmax warps); the first
+      // barrier keeps this tile's writes behind the partner's read of the previous tile
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      red[half * 128 + row] = mx;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      const float m_new = fmaxf(m2, fmaxf(mx, red[(half ^ 1) * 128 + row]));
       const float alpha = (m2 == -__builtin_huge_valf()) ? 0.f : ex2f(m2 - m_new);
       // P may overwrite buffer s once the P V of tile j - 2 has read it
-      if (!mbar_wait(&p_empty[s], ph ^ 1u, abort_flag)) {
-        failed = true;
-        break;
-      }
-      // pass 2: p = 2^(x - m), sums, P (fp16) into shared memory
-      float sp = 0.f, spt = 0.f;
-      uint8_t* pbuf = sP + s * Cfg::kPBytes;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        __syncwarp();
-        tmem_ld32(tmem_s + s * 128 + c * 32 + lane_off, r);
-        tmem_ld_wait(r);
+      if (!failed && !mbar_wait_warp(&p_empty[s], ph ^ 1u, abort_flag)) failed = true;
+      if (failed && lane == 0) *abort_flag = 1;
+      if (!failed) {
+        float sp = 0.f, spt = 0.f;
+        uint8_t* pbuf = sP + s * Cfg::kPBytes;
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
+        for (int g = 0; g < 8; ++g) {
           uint4 pk;
           __half* ph8 = reinterpret_cast<__half*>(&pk);
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
-            const int col = c * 32 + g * 8 + k;
-            const float sc =
-                __half2float(__float2half_rn(__half2float(__float2half_rn(__uint_as_float(r[g * 8 + k]))) * args.scale));
-            const float d2 = sc * kLog2eF - m_new;
-            const float p = col < lim ? ex2f(d2) : 0.f;
+            const __half2 v = xs[(g * 8 + k) >> 1];
+            const float d2 = fmaf((k & 1) ? __high2float(v) : __low2float(v), kLog2eF, -m_new);
+            const float p = g * 8 + k < lim ? ex2f(d2) : 0.f;
             sp += p;
-            spt = col < lim ? fmaf(p, d2, spt) : spt;
+            spt = g * 8 + k < lim ? fmaf(p, d2, spt) : spt;
             ph8[k] = __float2half_rn(p);
           }
-          *reinterpret_cast<uint4*>(pbuf + p_offset(row, c * 32 + g * 8)) = pk;
+          *reinterpret_cast<uint4*>(pbuf + p_offset(row, half * 64 + g * 8)) = pk;
         }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[s]);
-      fence_proxy_async_smem();  // the P stores, visible to the tensor core's operand reads
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[s]);
-      // running statistics (base 2): l = sum p, t2 = sum p (x - m)
-      if (m2 == -__builtin_huge_valf()) {
-        l = sp;
-        t2 = spt;
-      } else {
-        t2 = alpha * (t2 + l * (m2 - m_new)) + spt;
-        l = alpha * l + sp;
-      }
-      m2 = m_new;
-      if (j > 0 && !consume_o(j - 1, alpha_prev)) {
-        failed = true;
-        break;
+        fence_proxy_async_smem();  // the P stores, visible to the tensor core's operand reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[s]);
+        // running statistics of this half (base 2): l = sum p, t2 = sum p (x - m)
+        if (m2 == -__builtin_huge_valf()) {
+          l = sp;
+          t2 = spt;
+        } else {
+          t2 = alpha * (t2 + l * (m2 - m_new)) + spt;
+          l = alpha * l + sp;
+        }
+        m2 = m_new;
+        if (j > 0 && !consume_o(j - 1, alpha_prev)) failed = true;
       }
       alpha_prev = alpha;
     }
@@ -380,18 +402,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         atomicOr(&g_device_error, kErrWaitTimeout);
         *abort_flag = 1;
       }
-    } else if (q < args.S) {
-      const float inv = 1.f / l;
-      __half* out = args.O + ((b * args.S + q) * args.Hq + h) * D;
+    }
+    // the two halves' sums (every softmax thread reaches this barrier, failed or not)
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    red[half * 128 + row] = l;
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    const float l_all = l + red[(half ^ 1) * 128 + row];
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    red[half * 128 + row] = t2;
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    const float t2_all = t2 + red[(half ^ 1) * 128 + row];
+    if (!failed && q < args.S) {
+      const float inv = 1.f / l_all;
+      __half* out = args.O + ((b * args.S + q) * args.Hq + h) * D + half * kOH;
 #pragma unroll
-      for (int g = 0; g < D / 8; ++g) {
+      for (int g = 0; g < kOH / 8; ++g) {
         uint4 pk;
         __half* h8 = reinterpret_cast<__half*>(&pk);
 #pragma unroll
         for (int k = 0; k < 8; ++k) h8[k] = __float2half_rn(o[g * 8 + k] * inv);
         *reinterpret_cast<uint4*>(out + g * 8) = pk;
       }
-      args.H[bh * args.S + q] = 0.69314718055994531f * (__log2f(l) - t2 / l);
+      if (half == 0) args.H[bh * args.S + q] = 0.69314718055994531f * (__log2f(l_all) - t2_all / l_all);
     }
   }
 

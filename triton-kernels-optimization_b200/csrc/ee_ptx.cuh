@@ -44,6 +44,20 @@ __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wa
 // to finish): its CTAs take SMs as this grid's CTAs retire.
 __device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
+// Per-thread register budget of the calling warpgroup (every warp of the warpgroup runs
+// the same call).  The budgets of all warpgroups must add up to at most the registers
+// the block was launched with, or the increase waits for registers that never come.
+template <uint32_t kRegs>
+__device__ __forceinline__ void warpgroup_reg_dealloc() {
+  static_assert(kRegs % 8 == 0 && kRegs >= 24 && kRegs <= 256, "setmaxnreg range");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void warpgroup_reg_alloc() {
+  static_assert(kRegs % 8 == 0 && kRegs >= 24 && kRegs <= 256, "setmaxnreg range");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
 // ---------------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------------
@@ -104,6 +118,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
       if (globaltimer() - t0 > EE_WAIT_NS) return false;
     }
   }
+}
+
+// mbar_wait by a whole converged warp, with a warp-uniform result: when any lane gave
+// up, every lane reports failure, so the warp leaves its loop together and never meets
+// a .sync.aligned instruction or a __syncwarp with part of its lanes.
+template <bool kClusterScope = false>
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+  const bool ok = mbar_wait<kClusterScope>(bar, parity, abort);
+  return __all_sync(0xffffffffu, ok) != 0;
 }
 
 // ---------------------------------------------------------------------------------
