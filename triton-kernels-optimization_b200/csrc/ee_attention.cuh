@@ -34,10 +34,10 @@ namespace ee {
 
 constexpr int kAttnThreads = 384;  // producer warpgroup (TMA, MMA, two idle warps), two softmax warpgroups
 // registers per thread: 168 at launch (384 threads, one CTA per SM); the producer
-// warpgroup gives its share to the softmax warpgroups (56 + 2 x 224 = 3 x 168)
+// warpgroup gives its share to the softmax warpgroups (96 + 2 x 200 <= 3 x 168)
 constexpr int kAttnLaunchRegs = 168;
-constexpr int kAttnProducerRegs = 56;
-constexpr int kAttnSoftmaxRegs = 224;
+constexpr int kAttnProducerRegs = 96;
+constexpr int kAttnSoftmaxRegs = 200;
 static_assert(kAttnProducerRegs + 2 * kAttnSoftmaxRegs <= 3 * kAttnLaunchRegs, "register split above the launch budget");
 constexpr int kAttnTileBytes = kAttnTile * 128;  // one 128-byte-wide swizzled box of 128 rows: 16 KB
 
@@ -72,6 +72,24 @@ __device__ __forceinline__ float ex2f(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+constexpr unsigned short kHalfLowest = 0xFBFFu;  // -65504
+
+// fp16 pair {lo, hi} (lo in the low half), both rounded to nearest
+__device__ __forceinline__ uint32_t pack_half2_rn(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// fp16(fp32(fp16(s)) * scale) for two raw fp32 scores: the rounding of an fp16 matmul
+// output, then the fp16 tensor times a Python float (computed in fp32, rounded to fp16)
+__device__ __forceinline__ __half2 scaled_scores(uint32_t s0, uint32_t s1, float2 sc2) {
+  const uint32_t h = pack_half2_rn(__uint_as_float(s0), __uint_as_float(s1));
+  const float2 x = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&h)), sc2);
+  const uint32_t r = pack_half2_rn(x.x, x.y);
+  return *reinterpret_cast<const __half2*>(&r);
 }
 
 // byte offset of element (row, col) of a [128 rows x 128 fp16] tile stored as two
@@ -284,9 +302,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     constexpr int kOH = D / 2;  // output columns per thread
     float* red = reinterpret_cast<float*>(bars + 32);  // [2 halves][128 rows]: row maxima, then sums
     float m2 = -__builtin_huge_valf(), l = 0.f, t2 = 0.f, alpha_prev = 0.f;
-    float o[kOH];
+    float2 o[kOH / 2];  // output columns 2 i, 2 i + 1 of this thread's half
 #pragma unroll
-    for (int i = 0; i < kOH; ++i) o[i] = 0.f;
+    for (int i = 0; i < kOH / 2; ++i) o[i] = make_float2(0.f, 0.f);
     bool failed = false;
 
     auto consume_o = [&](int j, float alpha) -> bool {
@@ -294,6 +312,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
       if (!mbar_wait_warp(&o_full[s], ph, abort_flag)) return false;
       tc_fence_after();
+      const float2 a2 = make_float2(alpha, alpha);
 #pragma unroll
       for (int c = 0; c < kOH / 32; ++c) {
         uint32_t r[32];
@@ -301,7 +320,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_ld32(tmem_o + s * D + half * kOH + c * 32 + lane_off, r);
         tmem_ld_wait(r);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha, __uint_as_float(r[i]));
+        for (int i = 0; i < 16; ++i)
+          o[c * 16 + i] = __ffma2_rn(o[c * 16 + i], a2, make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])));
       }
       tc_fence_before();
       __syncwarp();
@@ -324,34 +344,38 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         lim = c < lim ? static_cast<int>(c) : lim;
       }
       lim = lim < 0 ? 0 : (lim > 64 ? 64 : lim);
-      // the reference's fp16 scores (fp16 Q K^T, times the scale, fp16) -- kept as the
-      // fp16 values they are (masked: -inf), two per register
+      // the reference's fp16 scores: fp16 Q K^T, times the scale in fp32, fp16; a key
+      // outside the causal / length limit gets -65504 (the fp16 lowest the reference's
+      // additive mask drives it to), whose probability is exactly 0 -- two per register
       __half2 xs[32];
-      float mx = -__builtin_huge_valf();
+      __half2 mx2 = __half2half2(__ushort_as_half(kHalfLowest));
       if (!failed) {
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t r[32];
-          __syncwarp();
-          tmem_ld32(tmem_s + s * 128 + half * 64 + c * 32 + lane_off, r);
-          tmem_ld_wait(r);
-#pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const int col = c * 32 + i;
-            const __half lo = __float2half_rn(__half2float(__float2half_rn(__uint_as_float(r[i]))) * args.scale);
-            const __half hi = __float2half_rn(__half2float(__float2half_rn(__uint_as_float(r[i + 1]))) * args.scale);
-            const __half2 v = __halves2half2(col < lim ? lo : __ushort_as_half(0xFC00u),
-                                             col + 1 < lim ? hi : __ushort_as_half(0xFC00u));
-            xs[col >> 1] = v;
-            mx = fmaxf(mx, fmaxf(__low2float(v), __high2float(v)));
-          }
-        }
-        mx *= kLog2eF;
+        uint32_t ra[32], rb[32];
+        __syncwarp();
+        tmem_ld32(tmem_s + s * 128 + half * 64 + lane_off, ra);
+        tmem_ld32(tmem_s + s * 128 + half * 64 + 32 + lane_off, rb);
+        tmem_ld_wait(ra);
+        regs_after_wait(rb);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty[s]);  // the scores are in registers: S buffer free
+        const float2 sc2 = make_float2(args.scale, args.scale);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          xs[i] = scaled_scores(ra[2 * i], ra[2 * i + 1], sc2);
+          xs[16 + i] = scaled_scores(rb[2 * i], rb[2 * i + 1], sc2);
+        }
+        if (!__all_sync(0xffffffffu, lim >= 64)) {  // a tile on the diagonal or the sequence end
+          const __half neg = __ushort_as_half(kHalfLowest);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            xs[i] = __halves2half2(2 * i < lim ? __low2half(xs[i]) : neg, 2 * i + 1 < lim ? __high2half(xs[i]) : neg);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx2 = __hmax2(mx2, xs[i]);
       }
+      const float mx = fmaxf(__low2float(mx2), __high2float(mx2)) * kLog2eF;
       // exchange the half-row maxima (barrier 1: the eight softmax warps); the first
       // barrier keeps this tile's writes behind the partner's read of the previous tile
       asm volatile("bar.sync 1, 256;" ::: "memory");
@@ -363,26 +387,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!failed && !mbar_wait_warp(&p_empty[s], ph ^ 1u, abort_flag)) failed = true;
       if (failed && lane == 0) *abort_flag = 1;
       if (!failed) {
-        float sp = 0.f, spt = 0.f;
+        // p = 2^(x log2 e - m): masked keys give 2^(-94500 - m) = 0 and p (x - m) = 0
+        float2 sp2 = make_float2(0.f, 0.f), spt2 = make_float2(0.f, 0.f);
+        const float2 lg2 = make_float2(kLog2eF, kLog2eF), negm = make_float2(-m_new, -m_new);
         uint8_t* pbuf = sP + s * Cfg::kPBytes;
 #pragma unroll
         for (int g = 0; g < 8; ++g) {
           uint4 pk;
-          __half* ph8 = reinterpret_cast<__half*>(&pk);
+          uint32_t* w = reinterpret_cast<uint32_t*>(&pk);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const __half2 v = xs[(g * 8 + k) >> 1];
-            const float d2 = fmaf((k & 1) ? __high2float(v) : __low2float(v), kLog2eF, -m_new);
-            const float p = g * 8 + k < lim ? ex2f(d2) : 0.f;
-            sp += p;
-            spt = g * 8 + k < lim ? fmaf(p, d2, spt) : spt;
-            ph8[k] = __float2half_rn(p);
+          for (int k = 0; k < 4; ++k) {
+            const float2 d2 = __ffma2_rn(__half22float2(xs[g * 4 + k]), lg2, negm);
+            const float2 p = make_float2(ex2f(d2.x), ex2f(d2.y));
+            sp2 = __fadd2_rn(sp2, p);
+            spt2 = __ffma2_rn(p, d2, spt2);
+            w[k] = pack_half2_rn(p.x, p.y);
           }
           *reinterpret_cast<uint4*>(pbuf + p_offset(row, half * 64 + g * 8)) = pk;
         }
         fence_proxy_async_smem();  // the P stores, visible to the tensor core's operand reads
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[s]);
+        const float sp = sp2.x + sp2.y, spt = spt2.x + spt2.y;
         // running statistics of this half (base 2): l = sum p, t2 = sum p (x - m)
         if (m2 == -__builtin_huge_valf()) {
           l = sp;
@@ -420,7 +446,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         uint4 pk;
         __half* h8 = reinterpret_cast<__half*>(&pk);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) h8[k] = __float2half_rn(o[g * 8 + k] * inv);
+        for (int k = 0; k < 8; k += 2) {
+          const float2 v = o[(g * 8 + k) >> 1];
+          h8[k] = __float2half_rn(v.x * inv);
+          h8[k + 1] = __float2half_rn(v.y * inv);
+        }
         *reinterpret_cast<uint4*>(out + g * 8) = pk;
       }
       if (half == 0) args.H[bh * args.S + q] = 0.69314718055994531f * (__log2f(l_all) - t2_all / l_all);
