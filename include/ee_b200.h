@@ -69,10 +69,18 @@ EE_API const char* ee_last_error(void);
 
 /* GEMM tiling policy for every later call in the process (no counterpart in the
  * reference): 0 = automatic (CTA-pair 256 x 256 tiles above 128 rows; at most 128 rows
- * -- the call streams its weights -- single-CTA 128 x 256 tiles, or 128 x 64 tiles when
- * the wide ones would leave SMs idle), 1 = always single-CTA 128 x 256, 2 = always CTA
- * pairs, 3 = always single-CTA 128 x 64.  Results are identical under every policy. */
+ * -- the call streams its weights -- the weight-streaming kernel: 128-channel tiles
+ * against all of a bucket's rows, K split over a thread-block cluster), 1 = always
+ * single-CTA 128 x 256, 2 = always CTA pairs, 3 = always single-CTA 128 x 64, 4 = the
+ * weight-streaming kernel where the call has at most 128 rows (else automatic).  INT8
+ * results are identical under every policy; FP8 / FP16 results of the weight-streaming
+ * kernel with K split differ from the others in the last bits (fp32 partial sums added
+ * in rank order: deterministic, not the single-pass accumulation order). */
 EE_API int ee_set_gemm_policy(int policy);
+
+/* K splits per 128-channel tile of the weight-streaming kernel for every later call:
+ * 0 = chosen per call (about one CTA per resident slot), 1 .. 8 = forced. */
+EE_API int ee_set_gemm_splits(int splits);
 
 /* Reads and clears the current device's error word (set by a kernel whose bounded
  * wait gave up).  Synchronous.  EE_OK if clear, EE_ERR_DEVICE otherwise; *value

@@ -29,6 +29,7 @@ SIGNATURES = {
     "ee_abi_version": (c_int, []),
     "ee_last_error": (c_char_p, []),
     "ee_set_gemm_policy": (c_int, [c_int]),
+    "ee_set_gemm_splits": (c_int, [c_int]),
     "ee_device_check": (c_int, [POINTER(c_int)]),
     "ee_softmax_entropy": (c_int, [_P, c_int64, c_int64, c_int64, c_int, c_int64, _P, c_int64, _P, _P, c_double,
                                    c_double, _P]),

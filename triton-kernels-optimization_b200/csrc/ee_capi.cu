@@ -5,6 +5,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <atomic>
 #include <cstring>
 #include <mutex>
@@ -107,7 +108,24 @@ int check_gemm_shape(int64_t M, int64_t N, int64_t K, int64_t ldy) {
   return EE_OK;
 }
 
-std::atomic<int> g_gemm_policy{0};  // 0 auto, 1 single-CTA 128x256, 2 CTA-pair 256x256, 3 single-CTA 128x64
+std::atomic<int> g_gemm_policy{0};  // 0 auto, 1 single-CTA 128x256, 2 CTA-pair 256x256, 3 single-CTA 128x64,
+                                    // 4 weight-streaming (skinny) where the call has at most 128 rows
+std::atomic<int> g_gemm_splits{0};  // skinny kernel's K splits per tile: 0 = chosen per call
+
+// K splits of the skinny kernel: about one CTA per resident slot over the three buckets'
+// 128-channel tiles, at most 8 (a portable cluster), at least 4 K blocks per split
+int skinny_splits(const ee::GemmArgs& args, int nb) {
+  const int forced = g_gemm_splits.load(std::memory_order_relaxed);
+  const int nkb = (args.K + ee::kBKBytes - 1) / ee::kBKBytes;  // 8-bit buckets: the fewest K blocks
+  int s = forced;
+  if (s <= 0) {
+    const int64_t ntn = (args.N + 127) / 128;
+    const int64_t slots = int64_t(num_sms()) * (nb <= 64 ? 2 : 1);
+    s = static_cast<int>((slots + 3 * ntn - 1) / (3 * ntn));
+    s = std::min(s, std::max(1, nkb / 4));
+  }
+  return std::max(1, std::min(s, ee::kSkinnyMaxSplits));
+}
 
 // Row tiles a call may produce: with routing on the device the bucket sizes are unknown
 // here, and each bucket boundary can add one partial tile.
@@ -127,6 +145,34 @@ int64_t row_tiles(const ee::GemmArgs& args, bool dynamic_counts, int64_t bm) {
 // dereferenced).
 int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cudaStream_t s) {
   const int policy = g_gemm_policy.load(std::memory_order_relaxed);
+  if (args.out_mode != 2 && args.M_cap <= ee::kSkinnyMaxRows && (policy == 0 || policy == 4)) {
+    const int nb = args.M_cap <= 16 ? 16 : args.M_cap <= 32 ? 32 : args.M_cap <= 64 ? 64 : 128;
+    ee::GemmMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    const CUtensorMap* any = nullptr;
+    int st;
+    if (op.a8) {
+      if ((st = encode_kmajor(&maps.a8, op.a8, args.M_cap, args.K, op.ld8, 1, nb)) != EE_OK) return st;
+      any = &maps.a8;
+    }
+    if (op.a16) {
+      if ((st = encode_kmajor(&maps.a16, op.a16, args.M_cap, args.K, op.ld16, 2, nb)) != EE_OK) return st;
+      any = any ? any : &maps.a16;
+    }
+    for (int b = 0; b < 3; ++b) {
+      if (op.w[b]) {
+        const int eb = (b == ee::kFP16) ? 2 : 1;
+        if ((st = encode_kmajor(&maps.w[b], op.w[b], args.N, args.K, args.K, eb, 128)) != EE_OK) return st;
+      }
+    }
+    if (any == nullptr) return fail(EE_ERR_INVALID, "GEMM without an A operand");
+    if (!op.a8) maps.a8 = *any;
+    if (!op.a16) maps.a16 = *any;
+    for (int b = 0; b < 3; ++b)
+      if (!op.w[b]) maps.w[b] = op.w[0] ? maps.w[0] : (op.w[1] ? maps.w[1] : maps.w[2]);
+    return check_launch(ee::launch_gated_gemm_skinny(maps, args, nb, skinny_splits(args, nb), s),
+                        "gated_gemm_skinny_kernel");
+  }
   const int64_t wide_tiles = row_tiles(args, dynamic_counts, ee::kBM) * ((args.N + ee::kBN - 1) / ee::kBN);
   const bool pair = policy == 2 || (policy == 0 && args.M_cap > ee::kBM);
   // the SwiGLU epilogue pairs 128-column groups inside a 256-column tile
@@ -292,9 +338,16 @@ extern "C" {
 int ee_abi_version(void) { return EE_ABI_VERSION; }
 
 int ee_set_gemm_policy(int policy) {
-  if (policy < 0 || policy > 3)
-    return fail(EE_ERR_INVALID, "policy must be 0 (auto), 1 (single-CTA), 2 (CTA pair) or 3 (single-CTA narrow)");
+  if (policy < 0 || policy > 4)
+    return fail(EE_ERR_INVALID,
+                "policy must be 0 (auto), 1 (single-CTA), 2 (CTA pair), 3 (single-CTA narrow) or 4 (weight-streaming)");
   g_gemm_policy.store(policy, std::memory_order_relaxed);
+  return EE_OK;
+}
+
+int ee_set_gemm_splits(int splits) {
+  if (splits < 0 || splits > ee::kSkinnyMaxSplits) return fail(EE_ERR_INVALID, "splits must be 0 (automatic) .. 8");
+  g_gemm_splits.store(splits, std::memory_order_relaxed);
   return EE_OK;
 }
 

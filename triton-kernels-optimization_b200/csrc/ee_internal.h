@@ -15,6 +15,7 @@ enum Bucket : int { kINT8 = 0, kFP8 = 1, kFP16 = 2 };
 enum DeviceError : int {
   kErrWaitTimeout = 1,  // an mbarrier wait in the GEMM gave up
   kErrTmem = 2,         // tensor-memory allocation returned an unusable address
+  kErrShape = 4,        // a bucket holds more rows than the kernel's tile was launched for
 };
 
 // ----------------------------------------------------------------- row kernels
@@ -112,6 +113,12 @@ int launch_gated_gemm(const GemmMaps& maps, const GemmArgs& args, int grid, int 
 // CTA-pair kernel: 256-row tiles; grid = 2 x pairs; the A / W maps use 128-row boxes
 int launch_gated_gemm_pair(const GemmMaps& maps, const GemmArgs& args, int pairs, cudaStream_t s);
 constexpr int kPairTileRows = 256;
+// weight-streaming kernel for at most 128 rows (ee_gemm_skinny.cuh): 128-channel tiles,
+// nb = activation rows per tile (16, 32, 64 or 128, >= the rows of every bucket), K split
+// over clusters of `splits` CTAs; the A maps use nb-row boxes, the W maps 128-row boxes
+int launch_gated_gemm_skinny(const GemmMaps& maps, const GemmArgs& args, int nb, int splits, cudaStream_t s);
+constexpr int kSkinnyMaxRows = 128;
+constexpr int kSkinnyMaxSplits = 8;
 
 // device error word
 int read_and_clear_device_error(int* value);

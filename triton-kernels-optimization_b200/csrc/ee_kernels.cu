@@ -8,6 +8,7 @@
 
 #include "ee_attention.cuh"
 #include "ee_gemm.cuh"
+#include "ee_gemm_skinny.cuh"
 #include "ee_internal.h"
 #include "ee_rows.cuh"
 
@@ -31,6 +32,27 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return status_of(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
+// launch_pdl for a kernel whose CTAs form clusters of cluster_x along x (runtime size)
+template <typename... KArgs, typename... Args>
+int launch_cluster_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, unsigned cluster_x, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
   return status_of(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
@@ -176,6 +198,18 @@ int prepare_device() {
     if (attr_err[dev] == cudaSuccess)
       attr_err[dev] = cudaFuncSetAttribute(gated_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(kGemmSmemPair));
+    if (attr_err[dev] == cudaSuccess)
+      attr_err[dev] = cudaFuncSetAttribute(gated_gemm_skinny_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(SkinnyCfg<16>::kSmem));
+    if (attr_err[dev] == cudaSuccess)
+      attr_err[dev] = cudaFuncSetAttribute(gated_gemm_skinny_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(SkinnyCfg<32>::kSmem));
+    if (attr_err[dev] == cudaSuccess)
+      attr_err[dev] = cudaFuncSetAttribute(gated_gemm_skinny_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(SkinnyCfg<64>::kSmem));
+    if (attr_err[dev] == cudaSuccess)
+      attr_err[dev] = cudaFuncSetAttribute(gated_gemm_skinny_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(SkinnyCfg<128>::kSmem));
   });
   return attr_err[dev] == cudaSuccess ? 0 : -4;
 }
@@ -195,6 +229,32 @@ int launch_gated_gemm(const GemmMaps& m, const GemmArgs& args, int grid, int bn,
                       m.a8, m.a16, m.w[0], m.w[1], m.w[2], args);
   return launch_pdl(gated_gemm_kernel<kBN>, dim3(grid), dim3(kGemmThreads), SingleCfg<kBN>::kSmem, s, m.a8, m.a16,
                     m.w[0], m.w[1], m.w[2], args);
+}
+
+int launch_gated_gemm_skinny(const GemmMaps& m, const GemmArgs& args, int nb, int splits, cudaStream_t s) {
+  if (prepare_device() != 0) return -4;
+  if (splits < 1 || splits > kSkinnyMaxSplits) return -1;
+  const unsigned ntn = static_cast<unsigned>((args.N + kSkinnyRows - 1) / kSkinnyRows);
+  if (ntn == 0) return 0;
+  const dim3 grid(ntn * static_cast<unsigned>(splits), 3);
+  const dim3 block(kSkinnyThreads);
+  const unsigned cx = static_cast<unsigned>(splits);
+  switch (nb) {
+    case 16:
+      return launch_cluster_pdl(gated_gemm_skinny_kernel<16>, grid, block, SkinnyCfg<16>::kSmem, cx, s, m.a8, m.a16,
+                                m.w[0], m.w[1], m.w[2], args);
+    case 32:
+      return launch_cluster_pdl(gated_gemm_skinny_kernel<32>, grid, block, SkinnyCfg<32>::kSmem, cx, s, m.a8, m.a16,
+                                m.w[0], m.w[1], m.w[2], args);
+    case 64:
+      return launch_cluster_pdl(gated_gemm_skinny_kernel<64>, grid, block, SkinnyCfg<64>::kSmem, cx, s, m.a8, m.a16,
+                                m.w[0], m.w[1], m.w[2], args);
+    case 128:
+      return launch_cluster_pdl(gated_gemm_skinny_kernel<128>, grid, block, SkinnyCfg<128>::kSmem, cx, s, m.a8,
+                                m.a16, m.w[0], m.w[1], m.w[2], args);
+    default:
+      return -1;
+  }
 }
 
 int launch_transpose_v(const void* V, int64_t heads, int64_t S, int64_t S_pad, int64_t D, void* VT, cudaStream_t s) {
