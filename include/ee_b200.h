@@ -68,9 +68,11 @@ EE_API int ee_abi_version(void);
 EE_API const char* ee_last_error(void);
 
 /* GEMM tiling policy for every later call in the process (no counterpart in the
- * reference): 0 = automatic (CTA-pair 256 x 256 tiles above 128 rows; at most 128 rows
- * -- the call streams its weights -- the weight-streaming kernel: 128-channel tiles
- * against all of a bucket's rows, K split over a thread-block cluster), 1 = always
+ * reference): 0 = automatic (CTA-pair 256 x 256 tiles above 128 rows; 65 .. 128 rows
+ * single-CTA 128 x 256 tiles, or 128 x 64 tiles when the wide ones would leave SMs idle;
+ * at most 64 rows -- the call streams its weights -- the weight-streaming kernel:
+ * 128-channel tiles against all of a bucket's rows, K split over a thread-block
+ * cluster), 1 = always
  * single-CTA 128 x 256, 2 = always CTA pairs, 3 = always single-CTA 128 x 64, 4 = the
  * weight-streaming kernel where the call has at most 128 rows (else automatic).  INT8
  * results are identical under every policy; FP8 / FP16 results of the weight-streaming

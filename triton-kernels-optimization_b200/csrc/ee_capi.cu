@@ -112,8 +112,11 @@ std::atomic<int> g_gemm_policy{0};  // 0 auto, 1 single-CTA 128x256, 2 CTA-pair 
                                     // 4 weight-streaming (skinny) where the call has at most 128 rows
 std::atomic<int> g_gemm_splits{0};  // skinny kernel's K splits per tile: 0 = chosen per call
 
-// K splits of the skinny kernel: about one CTA per resident slot over the three buckets'
-// 128-channel tiles, at most 8 (a portable cluster), at least 4 K blocks per split
+// K splits of the skinny kernel: one per 2048 of K (about 0.5 MB of fp16 weight per
+// CTA), but no more than keep the three buckets' 128-channel tiles in one wave of
+// resident CTAs (a second, partial wave costs more than the split saves), at most 8 (a
+// portable cluster), at least 4 K blocks per split.  Measured on B200 at M = 16 .. 64:
+// N = K = 4096 best at 2 splits, K = 14336 at 3-4, N = 14336 unsplit.
 int skinny_splits(const ee::GemmArgs& args, int nb) {
   const int forced = g_gemm_splits.load(std::memory_order_relaxed);
   const int nkb = (args.K + ee::kBKBytes - 1) / ee::kBKBytes;  // 8-bit buckets: the fewest K blocks
@@ -121,7 +124,7 @@ int skinny_splits(const ee::GemmArgs& args, int nb) {
   if (s <= 0) {
     const int64_t ntn = (args.N + 127) / 128;
     const int64_t slots = int64_t(num_sms()) * (nb <= 64 ? 2 : 1);
-    s = static_cast<int>((slots + 3 * ntn - 1) / (3 * ntn));
+    s = static_cast<int>(std::min<int64_t>(slots / (3 * ntn), (args.K + 2047) / 2048));
     s = std::min(s, std::max(1, nkb / 4));
   }
   return std::max(1, std::min(s, ee::kSkinnyMaxSplits));
@@ -145,7 +148,10 @@ int64_t row_tiles(const ee::GemmArgs& args, bool dynamic_counts, int64_t bm) {
 // dereferenced).
 int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cudaStream_t s) {
   const int policy = g_gemm_policy.load(std::memory_order_relaxed);
-  if (args.out_mode != 2 && args.M_cap <= ee::kSkinnyMaxRows && (policy == 0 || policy == 4)) {
+  // weight-streaming kernel: forced (policy 4) up to 128 rows, automatic up to 64 (at 128
+  // rows the 128 x 64 tiles of the persistent kernel measured faster on B200)
+  if (args.out_mode != 2 &&
+      ((policy == 4 && args.M_cap <= ee::kSkinnyMaxRows) || (policy == 0 && args.M_cap <= ee::kSkinnyAutoRows))) {
     const int nb = args.M_cap <= 16 ? 16 : args.M_cap <= 32 ? 32 : args.M_cap <= 64 ? 64 : 128;
     ee::GemmMaps maps;
     std::memset(&maps, 0, sizeof(maps));

@@ -75,10 +75,10 @@ __device__ __forceinline__ void mma_stage_skinny(uint32_t d_tmem, uint32_t w_add
   for (int k = 0; k < kBKBytes / 32; ++k) tc_mma<KIND>(d_tmem, dw + 2u * k, da + 2u * k, idesc, (first && k == 0) ? 0u : 1u);
 }
 
-// y[row of position pos, channel n] from one accumulator value (the persistent kernel's
-// dequantisation: INT8 fp16((fp32(acc) sa) sb), FP8 fp16((acc sa) sb), FP16 fp16(acc))
-__device__ __forceinline__ void skinny_store(const GemmArgs& args, int b, int pos, int n, float sb, uint32_t acc) {
-  const int64_t orow = args.perm ? static_cast<int64_t>(args.perm[pos]) : static_cast<int64_t>(pos);
+// y[orow, channel n] from one accumulator value (the persistent kernel's dequantisation:
+// INT8 fp16((fp32(acc) sa) sb), FP8 fp16((acc sa) sb), FP16 fp16(acc))
+__device__ __forceinline__ void skinny_store(const GemmArgs& args, int b, int64_t orow, int n, float sa, float sb,
+                                             uint32_t acc) {
   if (args.out_mode == 1) {
     static_cast<uint32_t*>(args.Y)[orow * args.ldy + n] = acc;
     return;
@@ -87,11 +87,43 @@ __device__ __forceinline__ void skinny_store(const GemmArgs& args, int b, int po
   if (b == kFP16)
     v = __uint_as_float(acc);
   else if (b == kINT8)
-    v = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc)), args.sa[pos]), sb);
+    v = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(acc)), sa), sb);
   else
-    v = __fmul_rn(__fmul_rn(__uint_as_float(acc), args.sa[pos]), sb);
+    v = __fmul_rn(__fmul_rn(__uint_as_float(acc), sa), sb);
   static_cast<__half*>(args.Y)[orow * args.ldy + n] = __float2half_rn(v);
 }
+
+// Output row and activation scale of every column (bucket row) of the tile, spread over
+// the lanes: column c lives in lane c % 32, slot c / 32, and reaches the other lanes by
+// shuffles (one global load per lane instead of one per column and thread).
+template <int NB>
+struct SkinnyCols {
+  static constexpr int kSlots = NB < 32 ? 1 : NB / 32;
+  int orow[kSlots];
+  float sa[kSlots];
+  __device__ __forceinline__ void load(const GemmArgs& args, int b, int pos0, int Mb, int lane) {
+#pragma unroll
+    for (int j = 0; j < kSlots; ++j) {
+      const int c = j * 32 + lane;
+      const bool ok = c < Mb;
+      orow[j] = ok ? (args.perm ? args.perm[pos0 + c] : pos0 + c) : 0;
+      sa[j] = (ok && b != kFP16 && args.out_mode != 1) ? args.sa[pos0 + c] : 1.f;
+    }
+  }
+  // column c (any value below NB; the slot is picked by selects, not a runtime index)
+  __device__ __forceinline__ void get(int c, int64_t& o, float& s) const {
+    const int j = c >> 5;
+    int oo = orow[0];
+    float ss = sa[0];
+#pragma unroll
+    for (int k = 1; k < kSlots; ++k) {
+      oo = (j == k) ? orow[k] : oo;
+      ss = (j == k) ? sa[k] : ss;
+    }
+    o = __shfl_sync(0xffffffffu, oo, c & 31);
+    s = __shfl_sync(0xffffffffu, ss, c & 31);
+  }
+};
 
 template <int NB>
 __global__ void __launch_bounds__(kSkinnyThreads, 1)
@@ -119,24 +151,14 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
   const uint32_t rank = cluster_ctarank();
   const int n0 = static_cast<int>(blockIdx.x / S) * kSkinnyRows;
   const int b = 2 - static_cast<int>(blockIdx.y);  // FP16, FP8, INT8
-  griddep_wait();  // bucket counts and packed rows come from earlier kernels
-  griddep_launch_dependents();
-  int cnt[3];
-#pragma unroll
-  for (int i = 0; i < 3; ++i)
-    cnt[i] = args.dyn_counts ? *(const volatile int32_t*)(args.dyn_counts + i) : args.counts[i];
-  const int Mb = (b == 0) ? cnt[0] : (b == 1) ? cnt[1] : cnt[2];
-  const int pos0 = (b == 0) ? 0 : (b == 1) ? cnt[0] : cnt[0] + cnt[1];
-  // the same for every CTA of the cluster (same bucket): the whole cluster leaves together
-  if (Mb <= 0) return;
-  if (Mb > NB) {
-    if (threadIdx.x == 0) atomicOr(&g_device_error, kErrShape);
-    return;
-  }
   const int nkb = kblocks_of(b, args.K);
   const int kb0 = static_cast<int>((static_cast<int64_t>(rank) * nkb) / S);
   const int kb1 = static_cast<int>((static_cast<int64_t>(rank + 1) * nkb) / S);
+  const int kstep = (b == kFP16) ? kBKBytes / 2 : kBKBytes;
+  const CUtensorMap* ta = (b == kFP16) ? &tm_a16 : &tm_a8;
+  const CUtensorMap* tw = (b == kINT8) ? &tm_w0 : (b == kFP8 ? &tm_w1 : &tm_w2);
 
+  // ---- before the previous kernel has finished: nothing here reads its results
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -147,12 +169,41 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
+  __syncthreads();
+  // The weights are never produced by an earlier kernel of the stream (packs are written by
+  // plain launches, which complete before anything after them starts), so the first ring's
+  // weight boxes load now; their full barriers get the activation bytes and the arrival later.
+  const int pre = (kb1 - kb0) < kStages ? (kb1 - kb0) : kStages;
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(b == kFP16 ? &tm_a16 : &tm_a8);
-    tma_prefetch_desc(b == kINT8 ? &tm_w0 : (b == kFP8 ? &tm_w1 : &tm_w2));
+    tma_prefetch_desc(ta);
+    tma_prefetch_desc(tw);
+    for (int s = 0; s < pre; ++s) {
+      mbar_expect_tx(&full[s], Cfg::kWStageBytes);
+      tma_load_2d(sW + s * Cfg::kWStageBytes, tw, &full[s], (kb0 + s) * kstep, n0);
+    }
   }
+  griddep_wait();  // bucket counts and packed rows come from earlier kernels
+  griddep_launch_dependents();
+  int cnt[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+    cnt[i] = args.dyn_counts ? *(const volatile int32_t*)(args.dyn_counts + i) : args.counts[i];
+  const int Mb = (b == 0) ? cnt[0] : (b == 1) ? cnt[1] : cnt[2];
+  const int pos0 = (b == 0) ? 0 : (b == 1) ? cnt[0] : cnt[0] + cnt[1];
+  // the same for every CTA of the cluster (same bucket): the whole cluster leaves together
+  if (Mb <= 0 || Mb > NB) {
+    if (Mb > NB && threadIdx.x == 0) atomicOr(&g_device_error, kErrShape);
+    if (warp == 0) {  // let the early weight loads land before the shared memory goes away
+      if (lane == 0)
+        for (int s = 0; s < pre; ++s) mbar_arrive(&full[s]);
+      __syncwarp();
+      for (int s = 0; s < pre; ++s) (void)mbar_wait(&full[s], 0u, nullptr);
+    }
+    return;
+  }
+
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);  // after griddep_wait: an earlier GEMM may still hold TMEM
     tmem_relinquish();
   }
   tc_fence_before();
@@ -162,19 +213,21 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    const int kstep = (b == kFP16) ? kBKBytes / 2 : kBKBytes;
-    const CUtensorMap* ta = (b == kFP16) ? &tm_a16 : &tm_a8;
-    const CUtensorMap* tw = (b == kINT8) ? &tm_w0 : (b == kFP8 ? &tm_w1 : &tm_w2);
     uint32_t stage = 0, phase = 0, issued_mask = 0, issued_parity = 0;
     bool failed = false;
     for (int kb = kb0; kb < kb1; ++kb) {
-      if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+      const bool early = kb - kb0 < pre;  // weight box already in flight, stage never used
+      if (!early && !mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
         failed = true;
         break;
       }
       if (lane == 0) {
-        mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-        tma_load_2d(sW + stage * Cfg::kWStageBytes, tw, &full[stage], kb * kstep, n0);
+        if (early) {
+          mbar_arrive_expect_tx(&full[stage], Cfg::kAStageBytes);
+        } else {
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          tma_load_2d(sW + stage * Cfg::kWStageBytes, tw, &full[stage], kb * kstep, n0);
+        }
         tma_load_2d(sA + stage * Cfg::kAStageBytes, ta, &full[stage], kb * kstep, pos0);
       }
       issued_mask |= 1u << stage;
@@ -242,6 +295,8 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
     }
     tc_fence_after();
     const float sb = (b != kFP16 && args.out_mode != 1 && n < args.N) ? __ldg(args.sb + n) : 1.f;
+    SkinnyCols<NB> cols;
+    if (S == 1) cols.load(args, b, pos0, Mb, lane);
 #pragma unroll
     for (int c0 = 0; c0 < NB; c0 += 32) {
       uint32_t r[32];
@@ -253,10 +308,14 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
         for (int i = 0; i < 32; ++i) r[i] = 0u;
       }
       if (S == 1) {
-        if (!failed && n < args.N) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c0 + i < NB && c0 + i < Mb) skinny_store(args, b, pos0 + c0 + i, n, sb, r[i]);
+        for (int i = 0; i < 32; ++i) {
+          if (c0 + i < NB) {
+            int64_t orow;
+            float sa;
+            cols.get(c0 + i, orow, sa);
+            if (!failed && n < args.N && c0 + i < Mb) skinny_store(args, b, orow, n, sa, sb, r[i]);
+          }
         }
       } else {
 #pragma unroll
@@ -274,19 +333,40 @@ __global__ void __launch_bounds__(kSkinnyThreads, 1)
       const int ch = (warp & 3) * 32 + lane;
       const int n = n0 + ch;
       const float sb = (b != kFP16 && args.out_mode != 1 && n < args.N) ? __ldg(args.sb + n) : 1.f;
+      SkinnyCols<NB> cols;
+      cols.load(args, b, pos0, Mb, lane);
       const uint32_t red_base = smem_u32(red);
-      for (int c = static_cast<int>(rank); c < Mb; c += static_cast<int>(S)) {
-        const uint32_t off = static_cast<uint32_t>((c * kSkinnyRows + ch) * 4);
-        uint32_t sum_i = 0;
-        float sum_f = 0.f;
-        for (uint32_t q = 0; q < S; ++q) {
-          const uint32_t v = ld_shared_cluster_u32(map_to_cta(red_base + off, q));
-          if (b == kINT8)
-            sum_i += v;  // int32 partials: exact in any order
-          else
-            sum_f += __uint_as_float(v);  // rank order
+      // four of this CTA's columns at a time, every rank's partial of them in flight at once
+      for (int c0 = static_cast<int>(rank); c0 < Mb; c0 += 4 * static_cast<int>(S)) {
+        uint32_t v[4][kSkinnyMaxSplits];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + u * static_cast<int>(S);
+          const uint32_t addr = red_base + static_cast<uint32_t>((c * kSkinnyRows + ch) * 4);
+#pragma unroll
+          for (int q = 0; q < kSkinnyMaxSplits; ++q)
+            v[u][q] = (c < Mb && q < static_cast<int>(S)) ? ld_shared_cluster_u32(map_to_cta(addr, q)) : 0u;
         }
-        if (n < args.N && *abort_flag == 0) skinny_store(args, b, pos0 + c, n, sb, b == kINT8 ? sum_i : __float_as_uint(sum_f));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + u * static_cast<int>(S);
+          uint32_t sum_i = 0;
+          float sum_f = 0.f;
+#pragma unroll
+          for (int q = 0; q < kSkinnyMaxSplits; ++q) {
+            if (q < static_cast<int>(S)) {
+              if (b == kINT8)
+                sum_i += v[u][q];  // int32 partials: exact in any order
+              else
+                sum_f += __uint_as_float(v[u][q]);  // rank order
+            }
+          }
+          int64_t orow;
+          float sa;
+          cols.get(c, orow, sa);  // the whole warp: c is the same in every lane
+          if (c < Mb && n < args.N && *abort_flag == 0)
+            skinny_store(args, b, orow, n, sa, sb, b == kINT8 ? sum_i : __float_as_uint(sum_f));
+        }
       }
     }
     cluster_sync_all();  // no CTA leaves while a peer may still read its partials

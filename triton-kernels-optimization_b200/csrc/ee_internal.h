@@ -118,6 +118,7 @@ constexpr int kPairTileRows = 256;
 // over clusters of `splits` CTAs; the A maps use nb-row boxes, the W maps 128-row boxes
 int launch_gated_gemm_skinny(const GemmMaps& maps, const GemmArgs& args, int nb, int splits, cudaStream_t s);
 constexpr int kSkinnyMaxRows = 128;
+constexpr int kSkinnyAutoRows = 64;
 constexpr int kSkinnyMaxSplits = 8;
 
 // device error word

@@ -44,15 +44,19 @@ int launch_cluster_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[3];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   attr[1].id = cudaLaunchAttributeClusterDimension;
   attr[1].val.clusterDim.x = cluster_x;
   attr[1].val.clusterDim.y = 1;
   attr[1].val.clusterDim.z = 1;
+  // let a cluster's CTAs share SMs (two per SM where shared memory allows) instead of
+  // spreading them one per SM
+  attr[2].id = cudaLaunchAttributeClusterSchedulingPolicyPreference;
+  attr[2].val.clusterSchedulingPolicyPreference = cudaClusterSchedulingPolicyLoadBalancing;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = 3;
   return status_of(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
