@@ -234,6 +234,16 @@ EE_API int ee_linear_int8_noalloc(const void* A, int64_t lda, const int8_t* W_nk
 EE_API size_t ee_gated_workspace_bytes(int64_t M, int64_t K);
 EE_API int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high, float* H,
                  int8_t* route, int32_t* bucket_counts, void* workspace, size_t workspace_bytes, void* stream);
+/* ee_gate_rows without zeroing the workspace head (its first
+ * ee_gated_workspace_head_bytes() bytes: bucket counters, tile counters and the router's
+ * single-pass scan state), for callers that zeroed it once -- every kernel of the path
+ * leaves it consistent after a clean run -- and saw no device error since (after one,
+ * zero it again or call ee_gate_rows).  Saves the memset, and lets the router launch
+ * start while the previous kernel of the stream drains. */
+EE_API int ee_gate_rows_keep(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high,
+                             float* H, int8_t* route, int32_t* bucket_counts, void* workspace,
+                             size_t workspace_bytes, void* stream);
+EE_API size_t ee_gated_workspace_head_bytes(void);
 /* ee_gate_rows for callers that already hold one entropy per row (the Llama block's
  * per-token router: the mean over heads of the attention entropy of each query
  * position): routes the M rows of H (fp32, device) into the workspace, ready for

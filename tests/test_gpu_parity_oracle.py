@@ -277,3 +277,23 @@ def test_all_zero_rows_follow_the_reference(pkg, cuda):
     for r in (0, 2, 3):
         assert (y8[r] == 0).all() and np.isnan(yf8[r]).all() and (y16[r] == 0).all()
     assert np.isfinite(yf8[1]).all()
+
+
+@pytest.mark.parametrize("M,n", [(16, 4096), (17, 1024), (300, 64), (50000, 512), (4096, 4096)])
+def test_router_bucket_scan(pkg, cuda, M, n):
+    """The router fast path's bucket scan (a one-block launch chained after the router):
+    one chunk, a ragged last chunk, many chunks per scan thread, and the bench's shape;
+    twice in a row on the same workspace, the second without the header memset."""
+    inp = orc.make_gating_inputs(M=M, n=n, K=16, N=16, seed=M + n)
+    r = pkg.EntropyRouter(*TAU)
+    r.reserve(M, 16, cuda)
+    x = _dev(inp["logits"], cuda)
+    for _ in range(2):
+        r.route(x)
+        r.pack_rows(_dev(inp["A"], cuda))
+        torch.cuda.synchronize()
+        assert pkg._lib.device_check() == 0
+        route = r.route_ids.cpu().numpy()
+        perm_ref, counts_ref = orc.compaction(route)
+        assert np.array_equal(r.counts.cpu().numpy(), counts_ref)
+        assert np.array_equal(r.perm.cpu().numpy(), perm_ref)

@@ -59,3 +59,34 @@ def test_route_ids(pkg, cuda):
     far = ((H_ref - tl).abs() >= 1e-6) & ((H_ref - th).abs() >= 1e-6)
     torch.cuda.synchronize()
     assert torch.equal(route[far], want[far])
+
+
+@pytest.mark.parametrize("rows,n", [(1, 8), (3, 64), (257, 1000), (20000, 1024), (9, 2048), (5000, 2048),
+                                    (4096, 4096), (10000, 4096), (1, 4096)])
+def test_router_rows(pkg, cuda, rows, n):
+    """The router's path (entropy + route, no probabilities, no mask): one warp per row,
+    rows dealt to a grid that fills the GPU once, several rows per warp at the larger
+    counts; near one-hot rows (the exact pass) and rows with ties at the max included."""
+    x = _config1_logits(rows, n, rows * 3 + n, cuda)
+    if rows >= 3:
+        x[0] = 0.0                    # uniform row: n entries at the max
+        x[1, :] = -30.0
+        x[1, n // 2] = 30.0           # one-hot to fp32 precision
+        x[2, :] = -8.0
+        x[2, : min(3, n)] = 8.0       # three-way tie at the max, tiny rest
+    _, H, route = pkg.softmax_entropy_rows(x, want_probs=False, tau_low=0.41, tau_high=1.68)
+    _, H_ref = _ref(x)
+    torch.cuda.synchronize()
+    assert torch.allclose(H.double(), H_ref, rtol=1e-4, atol=1e-6), (H.double() - H_ref).abs().max()
+    want = torch.where(H_ref < 0.41, 0, torch.where(H_ref < 1.68, 1, 2)).to(torch.int8)
+    far = ((H_ref - 0.41).abs() >= 1e-6) & ((H_ref - 1.68).abs() >= 1e-6)
+    assert torch.equal(route[far], want[far])
+
+
+def test_router_strided_rows(pkg, cuda):
+    """Rows with a stride above n (a column slice of a wider matrix)."""
+    x = _config1_logits(700, 3072, 9, cuda)[:, : 2048]
+    _, H, _ = pkg.softmax_entropy_rows(x, want_probs=False)
+    _, H_ref = _ref(x)
+    torch.cuda.synchronize()
+    assert torch.allclose(H.double(), H_ref, rtol=1e-4, atol=1e-6)

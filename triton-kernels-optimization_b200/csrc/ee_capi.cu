@@ -266,8 +266,14 @@ struct GatedWs {
   void* buf16;
 };
 size_t chunk_tab_bytes(int64_t M) { return align256(sizeof(int4) * size_t((M + 15) / 16)); }
+// the header (bucket counters, ticket, GEMM tile counters): the part a caller zeroes
+// once (ee_gate_rows zeroes it on every call)
+constexpr size_t kWsHeadBytes = 256;
+}  // namespace
+size_t ee::gated_ws_head_bytes() { return kWsHeadBytes; }
+namespace {
 size_t gated_ws_bytes(int64_t M, int64_t K) {
-  return 256 + 2 * align256(sizeof(int32_t) * M) + align256(M) + 2 * align256(sizeof(float) * M) +
+  return kWsHeadBytes + 2 * align256(sizeof(int32_t) * M) + align256(M) + 2 * align256(sizeof(float) * M) +
          chunk_tab_bytes(M) + align256(size_t(M) * K) + align256(size_t(M) * K * 2);
 }
 GatedWs gated_ws(void* ws, int64_t M, int64_t K) {
@@ -276,7 +282,7 @@ GatedWs gated_ws(void* ws, int64_t M, int64_t K) {
   w.ticket = reinterpret_cast<uint32_t*>(p);
   w.counts = reinterpret_cast<int32_t*>(p + 16);
   w.sched = reinterpret_cast<uint32_t*>(p + 64);
-  p += 256;
+  p += kWsHeadBytes;
   w.perm = reinterpret_cast<int32_t*>(p);
   p += align256(sizeof(int32_t) * M);
   w.slot = reinterpret_cast<int32_t*>(p);
@@ -677,6 +683,14 @@ int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double ta
   return ee::gate_rows_impl(logits, M, n, ld, tau_low, tau_high, H, route, bucket_counts, workspace, workspace_bytes,
                             stream, true);
 }
+
+int ee_gate_rows_keep(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high, float* H,
+                      int8_t* route, int32_t* bucket_counts, void* workspace, size_t workspace_bytes, void* stream) {
+  return ee::gate_rows_impl(logits, M, n, ld, tau_low, tau_high, H, route, bucket_counts, workspace, workspace_bytes,
+                            stream, false);
+}
+
+size_t ee_gated_workspace_head_bytes(void) { return kWsHeadBytes; }
 }  // extern "C"
 
 // ee_gate_rows; clear_header = false skips zeroing the workspace header (ticket, counts,
@@ -695,7 +709,8 @@ int ee::gate_rows_impl(const void* logits, int64_t M, int64_t n, int64_t ld, dou
   cudaStream_t s = as_stream(stream);
   GatedWs w = gated_ws(workspace, M, 0);
   cudaError_t e = cudaSuccess;
-  if (clear_header && (e = cudaMemsetAsync(workspace, 0, 128, s)) != cudaSuccess)  // ticket, counts, tile counter
+  // ticket, counts, tile counters
+  if (clear_header && (e = cudaMemsetAsync(workspace, 0, kWsHeadBytes, s)) != cudaSuccess)
     return cuda_fail(e, "cudaMemsetAsync");
   if (M > 0) {
     ee::SoftmaxArgs a;

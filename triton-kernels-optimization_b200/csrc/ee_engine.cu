@@ -108,7 +108,8 @@ int ee_engine_create(int64_t rows, double tau_low, double tau_high, int32_t n_la
   e->workspace = workspace;
   e->workspace_bytes = workspace_bytes;
   if (cudaGetDevice(&e->device) != cudaSuccess || ee::prepare_device() != 0 ||
-      cudaMemset(workspace, 0, 256) != cudaSuccess) {  // the header: ticket, counts, tile counter
+      cudaMemset(workspace, 0, ee::gated_ws_head_bytes()) != cudaSuccess) {  // ticket, counts, tile
+                                                                             // counter, look-back epoch
     delete e;
     return engine_fail(EE_ERR_CUDA, "ee_engine_create: CUDA device not usable");
   }

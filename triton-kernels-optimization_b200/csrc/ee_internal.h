@@ -137,6 +137,8 @@ struct AttnLaunch {
 int launch_flash_attention(const AttnLaunch& a, cudaStream_t s);
 int launch_transpose_v(const void* V, int64_t heads, int64_t S, int64_t S_pad, int64_t D, void* VT, cudaStream_t s);
 // ee_gate_rows with the workspace-header memset optional (see ee_capi.cu)
+// bytes at the start of a gated workspace that a caller zeroes once (header + look-back)
+size_t gated_ws_head_bytes();
 int gate_rows_impl(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high, float* H,
                    int8_t* route, int32_t* bucket_counts, void* workspace, size_t workspace_bytes, void* stream,
                    bool clear_header);

@@ -93,10 +93,39 @@ int sm_count() {
   return cache[dev];
 }
 
+// Router fast path: two blocks per SM (the ring's shared memory), never more blocks than
+// rows; the bucket scan follows as a one-block launch that starts while the router drains.
+template <int NV>
+int run_route_tma(const SoftmaxArgs& a, cudaStream_t s) {
+  constexpr size_t kSmem = 128 + size_t(kRouteSlots) * NV * 32 * 16 + 2 * kRouteSlots * 8 + 16;
+  static std::once_flag once[64];
+  static cudaError_t err[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -4;
+  std::call_once(once[dev], [dev] {
+    err[dev] = cudaFuncSetAttribute(route_rows_tma_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kSmem));
+  });
+  if (err[dev] != cudaSuccess) return -4;
+  const int64_t fill = int64_t(sm_count()) * 2;
+  const unsigned grid = static_cast<unsigned>(a.rows < fill ? a.rows : fill);
+  int st = launch_pdl(route_rows_tma_kernel<NV>, dim3(grid), dim3(kRouteThreads), kSmem, s, a);
+  if (st != 0 || a.chunk_tab == nullptr) return st;
+  return launch_pdl(route_chunk_scan_kernel, dim3(1), dim3(kScanThreads), 0, s, static_cast<const int8_t*>(a.route),
+                    a.rows, a.chunk_tab, a.counts);
+}
+
 int launch_softmax_entropy(const SoftmaxArgs& a, cudaStream_t s) {
   if (a.rows <= 0) return 0;
   const bool vec = (a.n % 8 == 0) && (a.ldx % 8 == 0) && aligned16(a.x) &&
                    (a.probs == nullptr || ((a.ldp % 8 == 0) && aligned16(a.probs)));
+  if (vec && !a.causal && a.probs == nullptr && a.n <= 4096) {
+    // entropy + route only (the gating step): rows staged by TMA bulk copies, one
+    // consumer warp per row (route_rows_tma_kernel)
+    if (a.n <= 1024) return run_route_tma<4>(a, s);
+    if (a.n <= 2048) return run_route_tma<8>(a, s);
+    return run_route_tma<16>(a, s);
+  }
   if (vec) {
     // one warp per row up to 1024 columns (no block-level synchronisation), then 2 / 4 / 8
     // warps per row so every thread keeps at most 8 vectors (64 fp16) in registers.  A

@@ -9,6 +9,7 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 
+#include "ee_gemm.cuh"  // the device error word shared by every kernel of the library
 #include "ee_internal.h"
 #include "ee_ptx.cuh"
 
@@ -136,23 +137,11 @@ __device__ __forceinline__ int3 chunk_counts(const int8_t* route, int64_t M, int
 
 // Scalar arguments, never a reference to the kernel's parameter struct: a reference
 // would make every caller keep a copy of that struct on its stack.
+// The scan itself, by every thread of one block (NT threads): per-chunk counts, an
+// exclusive prefix per chunk and bucket into `tab`, the totals into `counts`.
 template <int NT>
-__device__ __noinline__ void scan_route_chunks_last_block(const int8_t* route, int64_t M, int4* tab, int32_t* counts,
-                                                          uint32_t* ticket) {
-  __shared__ int s_last;
+__device__ __forceinline__ void scan_route_chunks_block(const int8_t* route, int64_t M, int4* tab, int32_t* counts) {
   __shared__ int s_part[3][NT / 32];
-  // The block's route writes are ordered before thread 0's fence by the barrier, and the
-  // fence is cumulative: one fence per block, not one per thread.
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned prev = atomicAdd(ticket, 1u);
-    s_last = (prev == gridDim.x - 1) ? 1 : 0;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t nch = (M + 15) / 16;
   const int64_t per = (nch + NT - 1) / NT;  // contiguous chunks per thread
@@ -202,8 +191,38 @@ __device__ __noinline__ void scan_route_chunks_last_block(const int8_t* route, i
     counts[1] = p1;
     counts[2] = p2;
     counts[3] = 0;
-    *ticket = 0u;  // ready for the next launch
   }
+}
+
+// The scan by the last block of a row kernel to finish (threadfence-reduction ticket).
+template <int NT>
+__device__ __noinline__ void scan_route_chunks_last_block(const int8_t* route, int64_t M, int4* tab, int32_t* counts,
+                                                          uint32_t* ticket) {
+  __shared__ int s_last;
+  // The block's route writes are ordered before thread 0's fence by the barrier, and the
+  // fence is cumulative: one fence per block, not one per thread.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(ticket, 1u);
+    s_last = (prev == gridDim.x - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  scan_route_chunks_block<NT>(route, M, tab, counts);
+  if (threadIdx.x == 0) *ticket = 0u;  // ready for the next launch
+}
+
+// The scan as a kernel of its own (one block), chained after the router fast path: the
+// router's blocks leave as soon as their rows are done, and this launch is scheduled
+// while they drain.
+constexpr int kScanThreads = 1024;
+__global__ void __launch_bounds__(kScanThreads, 1) route_chunk_scan_kernel(const int8_t* route, int64_t M, int4* tab,
+                                                                           int32_t* counts) {
+  griddep_wait();  // the routes come from the router launch just before
+  griddep_launch_dependents();
+  scan_route_chunks_block<kScanThreads>(route, M, tab, counts);
 }
 
 // Position of `row` (bucket b) in the stable bucket order, from the chunk table of the
@@ -407,6 +426,152 @@ __global__ void __launch_bounds__(kRowThreads, MINB) softmax_entropy_vec_kernel(
     }
   }
   if (a.chunk_tab != nullptr) scan_route_chunks_last_block<kRowThreads>(a.route, a.rows, a.chunk_tab, a.counts, a.ticket);
+}
+
+// ----------------------------------------------------------------------------------
+// Router fast path (no causal mask, no probabilities -- the gating step's case), rows
+// staged through shared memory by the TMA engine: in every block one producer thread
+// streams the block's rows (rows blockIdx.x, blockIdx.x + gridDim.x, ...) with 1-D bulk
+// copies into a ring of kRouteSlots row buffers, and 8 consumer warps each take every
+// 8th of those rows: copy it to registers (16-byte vectors, conflict-free), release the
+// slot, and reduce it with shuffles only.  The HBM stream runs ahead of the arithmetic by
+// the ring's depth in every block, so no phase of the kernel waits on another.
+// One pass over the row per element: d = x - m (exact: both fp16), d2 = d log2(e),
+// e = 2^d2, Z += e, T += e d2, two elements per packed f32x2 operation; the max entries
+// give d = 0 and contribute exactly 1 to Z and 0 to T.  H = log1p(Z - 1) - T ln2 / Z:
+// near a one-hot row Z - 1 carries the rounding of Z (absolute error <= 2^-24 in H).
+// Entries at -inf are lifted to the fp16 lowest first, so they give e = 0 and e d2 = 0
+// (the reference's -inf guard).  Requires n % 8 == 0, ldx % 8 == 0, a 16-byte aligned
+// base and n <= 256 NV.
+// ----------------------------------------------------------------------------------
+constexpr int kRouteConsumers = 8;
+constexpr int kRouteSlots = 8;  // row buffers per block
+constexpr int kRouteThreads = 32 * (kRouteConsumers + 1);  // warp 0 produces
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int NV>
+__device__ __forceinline__ float row_entropy_warp(const uint4 (&u)[NV], int n, int lane) {
+  const __half2 lowest = __half2half2(__ushort_as_half(static_cast<unsigned short>(0xFBFFu)));  // -65504
+  // four independent chains (one per fp16 pair of a vector) for the max and the sums:
+  // the reductions are latency chains otherwise
+  __half2 mx[4] = {lowest, lowest, lowest, lowest};
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if ((lane + i * 32) * 8 < n) {
+      const __half2* h = reinterpret_cast<const __half2*>(&u[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) mx[k] = __hmax2(mx[k], h[k]);
+    }
+  }
+  const __half2 mx2 = __hmax2(__hmax2(mx[0], mx[1]), __hmax2(mx[2], mx[3]));
+  float m = fmaxf(__low2float(mx2), __high2float(mx2));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float2 nm = make_float2(-m, -m), l2 = make_float2(kLog2e, kLog2e);
+  float2 zz[4], tt[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) zz[k] = tt[k] = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if ((lane + i * 32) * 8 < n) {
+      const __half2* h = reinterpret_cast<const __half2*>(&u[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 d2 = __fmul2_rn(__fadd2_rn(__half22float2(__hmax2(h[k], lowest)), nm), l2);
+        const float2 e = make_float2(ex2_approx(d2.x), ex2_approx(d2.y));
+        zz[k] = __fadd2_rn(zz[k], e);
+        tt[k] = __ffma2_rn(e, d2, tt[k]);
+      }
+    }
+  }
+  const float2 z2 = __fadd2_rn(__fadd2_rn(zz[0], zz[1]), __fadd2_rn(zz[2], zz[3]));
+  const float2 t2 = __fadd2_rn(__fadd2_rn(tt[0], tt[1]), __fadd2_rn(tt[2], tt[3]));
+  const float Z = warp_sum(z2.x + z2.y);
+  const float T = warp_sum(t2.x + t2.y);
+  return log1pf(Z - 1.f) - (T * 0.69314718055994531f) / Z;
+}
+
+template <int NV>
+__global__ void __launch_bounds__(kRouteThreads, 2) route_rows_tma_kernel(const SoftmaxArgs a) {
+  constexpr int kRowBytes = NV * 32 * 16;  // one row buffer (n <= NV * 256 columns)
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kRouteSlots * kRowBytes);  // [kRouteSlots]
+  uint64_t* empty = full + kRouteSlots;                                           // [kRouteSlots]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kRouteSlots);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRouteSlots; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  griddep_wait();  // the logits may come from the previous kernel in the stream
+  griddep_launch_dependents();
+  const int n = a.n;
+  const uint32_t bytes = static_cast<uint32_t>(n) * 2u;
+  const int64_t nrows = a.rows > blockIdx.x ? (a.rows - 1 - blockIdx.x) / gridDim.x + 1 : 0;  // this block's rows
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int64_t issued = 0;
+      bool failed = false;
+      for (int64_t j = 0; j < nrows; ++j) {
+        const int slot = static_cast<int>(j % kRouteSlots);
+        const uint32_t use = static_cast<uint32_t>(j / kRouteSlots);
+        if (!mbar_wait(&empty[slot], (use & 1u) ^ 1u, abort_flag)) {
+          failed = true;
+          break;
+        }
+        const int64_t row = blockIdx.x + j * gridDim.x;
+        mbar_arrive_expect_tx(&full[slot], bytes);
+        bulk_load(ring + slot * kRowBytes, static_cast<const __half*>(a.x) + row * a.ldx, bytes, &full[slot]);
+        issued = j + 1;
+      }
+      if (failed) {
+        atomicOr(&g_device_error, kErrWaitTimeout);
+        *abort_flag = 1;
+        // let the copies already issued land before the shared memory goes away
+        for (int64_t j = issued > kRouteSlots ? issued - kRouteSlots : 0; j < issued; ++j)
+          (void)mbar_wait(&full[j % kRouteSlots], static_cast<uint32_t>(j / kRouteSlots) & 1u, nullptr);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int c = warp - 1;
+    for (int64_t j = c; j < nrows; j += kRouteConsumers) {
+      const int slot = static_cast<int>(j % kRouteSlots);
+      const uint32_t use = static_cast<uint32_t>(j / kRouteSlots);
+      if (!mbar_wait_warp(&full[slot], use & 1u, abort_flag)) {
+        if (lane == 0) {
+          atomicOr(&g_device_error, kErrWaitTimeout);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      uint4 u[NV];
+      const uint4* src = reinterpret_cast<const uint4*>(ring + slot * kRowBytes);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) u[i] = (lane + i * 32) * 8 < n ? src[lane + i * 32] : make_uint4(0u, 0u, 0u, 0u);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);  // the row is in registers: the slot may refill
+      const float h = row_entropy_warp<NV>(u, n, lane);
+      if (lane == 0) {
+        const int64_t row = blockIdx.x + j * gridDim.x;
+        a.H[row] = h;
+        if (a.route) a.route[row] = route_of(h, a.tau_low, a.tau_high);
+      }
+    }
+  }
 }
 
 // Online softmax statistics (see entropy_from_stats) for the streaming path.

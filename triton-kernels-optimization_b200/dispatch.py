@@ -149,7 +149,16 @@ class EntropyRouter:
         device = torch.device(device)
         if self._ws is None or self._ws.numel() < need or self._ws.device != device:
             self._ws = torch.empty(need, dtype=torch.uint8, device=device)
+            self.reset_workspace()
             self.H = None  # views of the old workspace are stale
+
+    def reset_workspace(self) -> None:
+        """Zero the workspace head (bucket and tile counters, the router's scan state).
+        Done at allocation; every kernel of the path leaves the head consistent after a
+        clean run, so ``route`` skips the memset.  Call it again after a device error
+        (``device_check`` != 0) before the next ``route``."""
+        if self._ws is not None:
+            self._ws[: _lib.load().ee_gated_workspace_head_bytes()].zero_()
 
     def _views(self, M: int) -> None:
         off = (ctypes.c_int64 * 8)()
@@ -171,8 +180,8 @@ class EntropyRouter:
             self._views(M)
         self.M = M
         with torch.cuda.device(logits.device):
-            call("ee_gate_rows", logits.data_ptr(), M, n, logits.stride(0), self.tau_low, self.tau_high, None, None,
-                 None, self._ws.data_ptr(), self._ws.numel(), _stream())
+            call("ee_gate_rows_keep", logits.data_ptr(), M, n, logits.stride(0), self.tau_low, self.tau_high, None,
+                 None, None, self._ws.data_ptr(), self._ws.numel(), _stream())
         return self.route_ids
 
     def route_entropy(self, H: torch.Tensor) -> torch.Tensor:
