@@ -133,6 +133,34 @@ EE_API size_t ee_attention_workspace_bytes(int64_t B, int64_t Hkv, int64_t S, in
 EE_API int ee_flash_attention_entropy(const void* Q, const void* K, const void* V, int64_t B, int64_t Hq, int64_t Hkv,
                                       int64_t S, int64_t head_dim, int causal, float scale, void* O, float* H,
                                       void* workspace, size_t workspace_bytes, void* stream);
+/* ee_flash_attention_entropy on the projections' outputs as they come: q rows
+ * [B*S, Hq*head_dim] (row stride ldq), k and v rows [B*S, Hkv*head_dim] (ldk, ldv), and
+ * the rotary tables cos / sin [B*S, head_dim] (row stride ld_cs, fp16: what transformers'
+ * LlamaRotaryEmbedding returns).  One pass applies the rotary embedding to q and k with
+ * the roundings of transformers' apply_rotary_pos_emb on fp16 tensors --
+ * fp16(fp16(x * cos) + fp16(rotate_half(x) * sin)) -- and writes them in the [B, H, S,
+ * head_dim] layouts, V is transposed from its rows, then the attention runs as above.
+ * Replaces the block's reshape / transpose / rotate_half / cat / multiply / add chain
+ * (EE/python/dispatch.py:237 through transformers' attention).  Workspace:
+ * ee_attention_rope_workspace_bytes, 256-byte aligned; all rows 16-byte aligned with
+ * strides that are multiples of 8 elements. */
+EE_API size_t ee_attention_rope_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t S, int64_t head_dim);
+EE_API int ee_flash_attention_rope_entropy(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                                           int64_t ldv, const void* cos, const void* sin, int64_t ld_cs, int64_t B,
+                                           int64_t Hq, int64_t Hkv, int64_t S, int64_t head_dim, int causal,
+                                           float scale, void* O, float* H, void* workspace, size_t workspace_bytes,
+                                           void* stream);
+
+/* The Llama block's RMSNorm with the residual add before it folded in (transformers'
+ * LlamaRMSNorm.forward and the block's `residual + x`, EE/python/dispatch.py:166-210):
+ * with residual: s = fp16(residual + x), stored to sum_out when given; without: s = x;
+ * y = fp16(weight * fp16(fp32(s) * rsqrt(mean(fp32(s)^2) + eps))).  x, residual,
+ * sum_out, y: fp16 rows of d (8 .. 8192, a multiple of 8) with the given strides; weight
+ * fp16 [d].  The sum of squares is taken in a different order than torch's reduction,
+ * so an output may differ from transformers' by up to two fp16 ulps (one in the
+ * normalised value, carried through the weight product); over 99 % are equal. */
+EE_API int ee_add_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, void* sum_out, int64_t lds,
+                          const void* weight, float eps, void* y, int64_t ldy, int64_t M, int64_t d, void* stream);
 
 /* ---------------------------------------------------------------- routing
  * route[i] = dual-threshold tier of H[i]                (per-row granularity) */

@@ -24,8 +24,10 @@ from .llama import EntropyDispatchedLlamaBlock, build_dispatched_llama, dispatch
 from .kernels import (
     SwiGLUPack,
     WeightPack,
+    add_rmsnorm,
     attention_entropy,
     flash_attention_entropy,
+    flash_attention_rope_entropy,
     fused_softmax_entropy,
     gemm_accumulators,
     gemm_int8_prequant,

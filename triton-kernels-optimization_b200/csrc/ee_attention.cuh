@@ -463,25 +463,4 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
 }
 
-// V [B*Hkv, S, D] -> V^T [B*Hkv, D, S_pad], zero past S: the P V operand, K-major.
-template <int D>
-__global__ void __launch_bounds__(256) transpose_v_kernel(const __half* __restrict__ V, int64_t S, int64_t S_pad,
-                                                          __half* __restrict__ VT) {
-  __shared__ __half tile[32][D + 2];
-  const int64_t head = blockIdx.y;
-  const int64_t k0 = static_cast<int64_t>(blockIdx.x) * 32;
-  griddep_wait();
-  for (int i = threadIdx.x; i < 32 * D; i += 256) {
-    const int r = i / D, c = i % D;
-    const int64_t k = k0 + r;
-    tile[r][c] = k < S ? V[(head * S + k) * D + c] : __float2half(0.f);
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < 32 * D; i += 256) {
-    const int c = i / 32, r = i % 32;
-    const int64_t k = k0 + r;
-    if (k < S_pad) VT[(head * D + c) * S_pad + k] = tile[r][c];
-  }
-}
-
 }  // namespace ee

@@ -2,6 +2,7 @@
 // status codes, workspace layout, TMA tensor-map encoding and kernel sequencing.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 
 #include <cstdarg>
 #include <cstdio>
@@ -455,7 +456,9 @@ int ee_flash_attention_entropy(const void* Q, const void* K, const void* V, int6
   if (st != EE_OK) return st;
   cudaStream_t s = as_stream(stream);
   const int64_t s_pad = (S + 63) / 64 * 64;
-  if ((st = check_launch(ee::launch_transpose_v(V, B * Hkv, S, s_pad, head_dim, workspace, s), "transpose_v")) != EE_OK)
+  if ((st = check_launch(ee::launch_transpose_v(V, B, Hkv, S, s_pad, head_dim, Hkv * S * head_dim, S * head_dim,
+                                                head_dim, workspace, s),
+                         "transpose_v")) != EE_OK)
     return st;
   ee::AttnLaunch a;
   std::memset(&a, 0, sizeof(a));
@@ -474,6 +477,103 @@ int ee_flash_attention_entropy(const void* Q, const void* K, const void* V, int6
   a.O = O;
   a.H = H;
   return check_launch(ee::launch_flash_attention(a, s), "flash_attention_entropy");
+}
+
+size_t ee_attention_rope_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t S, int64_t head_dim) {
+  if (B < 0 || Hq < 0 || Hkv < 0 || S < 0 || head_dim < 0) return 0;
+  return align256(sizeof(uint16_t) * size_t(B) * Hq * S * head_dim) +
+         align256(sizeof(uint16_t) * size_t(B) * Hkv * S * head_dim) + ee_attention_workspace_bytes(B, Hkv, S, head_dim);
+}
+
+int ee_flash_attention_rope_entropy(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                                    const void* cos, const void* sin, int64_t ld_cs, int64_t B, int64_t Hq, int64_t Hkv,
+                                    int64_t S, int64_t head_dim, int causal, float scale, void* O, float* H,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || S < 0) return fail(EE_ERR_INVALID, "bad shape");
+  if (Hq % Hkv != 0) return fail(EE_ERR_INVALID, "Hq=%lld is not a multiple of Hkv=%lld", (long long)Hq, (long long)Hkv);
+  if (head_dim != 64 && head_dim != 128) return fail(EE_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (causal != 0 && causal != 1) return fail(EE_ERR_INVALID, "causal must be 0 or 1");
+  if (B == 0 || S == 0) return EE_OK;
+  if (B * Hq * S >= (int64_t(1) << 31) || B * Hkv * head_dim >= (int64_t(1) << 31))
+    return fail(EE_ERR_UNSUPPORTED, "more than 2^31 rows");
+  if (!q || !k || !v || !cos || !sin || !O || !H) return fail(EE_ERR_INVALID, "q, k, v, cos, sin, O and H are required");
+  if (ldq < Hq * head_dim || ldk < Hkv * head_dim || ldv < Hkv * head_dim || ld_cs < head_dim)
+    return fail(EE_ERR_INVALID, "row strides below the rows");
+  if (!al16(q) || !al16(k) || !al16(v) || !al16(cos) || !al16(sin) || !al16(O) || (reinterpret_cast<uintptr_t>(H) & 3u) ||
+      ldq % 8 || ldk % 8 || ldv % 8 || ld_cs % 8)
+    return fail(EE_ERR_MISALIGNED, "q, k, v, cos, sin and O must be 16-byte aligned with row strides of 8 elements");
+  int st = check_ws(workspace, workspace_bytes, ee_attention_rope_workspace_bytes(B, Hq, Hkv, S, head_dim));
+  if (st != EE_OK) return st;
+  cudaStream_t s = as_stream(stream);
+  uint8_t* p = static_cast<uint8_t*>(workspace);
+  __half* qr = reinterpret_cast<__half*>(p);
+  p += align256(sizeof(uint16_t) * size_t(B) * Hq * S * head_dim);
+  __half* kr = reinterpret_cast<__half*>(p);
+  p += align256(sizeof(uint16_t) * size_t(B) * Hkv * S * head_dim);
+  void* vt = p;
+  ee::RopeArgs r;
+  r.q = static_cast<const __half*>(q);
+  r.ldq = ldq;
+  r.k = static_cast<const __half*>(k);
+  r.ldk = ldk;
+  r.cos = static_cast<const __half*>(cos);
+  r.sin = static_cast<const __half*>(sin);
+  r.ld_cs = ld_cs;
+  r.B = B;
+  r.S = S;
+  r.Hq = static_cast<int>(Hq);
+  r.Hkv = static_cast<int>(Hkv);
+  r.q_out = qr;
+  r.k_out = kr;
+  if ((st = check_launch(ee::launch_rope_layout(r, static_cast<int>(head_dim), s), "rope_layout")) != EE_OK) return st;
+  const int64_t s_pad = (S + 63) / 64 * 64;
+  if ((st = check_launch(ee::launch_transpose_v(v, B, Hkv, S, s_pad, head_dim, S * ldv, head_dim, ldv, vt, s),
+                         "transpose_v")) != EE_OK)
+    return st;
+  ee::AttnLaunch a;
+  std::memset(&a, 0, sizeof(a));
+  if ((st = encode_kmajor(&a.q, qr, B * Hq * S, head_dim, head_dim, 2, ee::kAttnTile)) != EE_OK) return st;
+  if ((st = encode_kmajor(&a.k, kr, B * Hkv * S, head_dim, head_dim, 2, ee::kAttnTile)) != EE_OK) return st;
+  if ((st = encode_kmajor(&a.vt, vt, B * Hkv * head_dim, s_pad, s_pad, 2, static_cast<int>(head_dim))) != EE_OK)
+    return st;
+  a.B = B;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.S = S;
+  a.S_pad = s_pad;
+  a.D = head_dim;
+  a.scale = scale;
+  a.causal = causal;
+  a.O = O;
+  a.H = H;
+  return check_launch(ee::launch_flash_attention(a, s), "flash_attention_entropy");
+}
+
+// ------------------------------------------------------------------ the block's norms
+int ee_add_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, void* sum_out, int64_t lds,
+                   const void* weight, float eps, void* y, int64_t ldy, int64_t M, int64_t d, void* stream) {
+  if (M < 0 || d <= 0 || d > 8192 || d % 8) return fail(EE_ERR_UNSUPPORTED, "d=%lld: 8 .. 8192, a multiple of 8", (long long)d);
+  if (M == 0) return EE_OK;
+  if (!x || !weight || !y) return fail(EE_ERR_INVALID, "x, weight and y are required");
+  if (sum_out && !residual) return fail(EE_ERR_INVALID, "sum_out needs residual");
+  if (ldx < d || ldy < d || (residual && ldr < d) || (sum_out && lds < d)) return fail(EE_ERR_INVALID, "row strides below d");
+  if (!al16(x) || !al16(weight) || !al16(y) || (residual && !al16(residual)) || (sum_out && !al16(sum_out)) ||
+      ldx % 8 || ldy % 8 || (residual && ldr % 8) || (sum_out && lds % 8))
+    return fail(EE_ERR_MISALIGNED, "16-byte aligned rows with strides of 8 elements required");
+  ee::AddNormArgs a;
+  a.x = static_cast<const __half*>(x);
+  a.ldx = ldx;
+  a.res = static_cast<const __half*>(residual);
+  a.ldr = ldr;
+  a.sum_out = static_cast<__half*>(sum_out);
+  a.lds = lds;
+  a.w = static_cast<const __half*>(weight);
+  a.y = static_cast<__half*>(y);
+  a.ldy = ldy;
+  a.M = M;
+  a.d = static_cast<int>(d);
+  a.eps = eps;
+  return check_launch(ee::launch_add_rmsnorm(a, as_stream(stream)), "add_rmsnorm");
 }
 
 // ------------------------------------------------------------------ routing

@@ -5,6 +5,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 
 namespace ee {
 
@@ -135,7 +136,40 @@ struct AttnLaunch {
   float* H;
 };
 int launch_flash_attention(const AttnLaunch& a, cudaStream_t s);
-int launch_transpose_v(const void* V, int64_t heads, int64_t S, int64_t S_pad, int64_t D, void* VT, cudaStream_t s);
+// V element (b, h, s, c) at V + b * sb + h * sh + s * ss + c  ->  V^T [B*Hkv, D, S_pad]
+int launch_transpose_v(const void* V, int64_t B, int64_t Hkv, int64_t S, int64_t S_pad, int64_t D, int64_t sb,
+                       int64_t sh, int64_t ss, void* VT, cudaStream_t s);
+
+// the Llama block's elementwise passes (ee_block.cuh)
+struct AddNormArgs {
+  const __half* x;      // [M, d], row stride ldx
+  int64_t ldx;
+  const __half* res;    // nullable: residual [M, d], row stride ldr (s = fp16(res + x))
+  int64_t ldr;
+  __half* sum_out;      // nullable (needs res): s, row stride lds
+  int64_t lds;
+  const __half* w;      // [d] RMSNorm weight
+  __half* y;            // [M, d], row stride ldy
+  int64_t ldy;
+  int64_t M;
+  int d;
+  float eps;
+};
+int launch_add_rmsnorm(const AddNormArgs& a, cudaStream_t s);
+struct RopeArgs {
+  const __half* q;      // [B*S, Hq*D] rows of the q projection, row stride ldq
+  int64_t ldq;
+  const __half* k;      // [B*S, Hkv*D], row stride ldk
+  int64_t ldk;
+  const __half* cos;    // [B*S, D], row stride ld_cs
+  const __half* sin;
+  int64_t ld_cs;
+  int64_t B, S;
+  int Hq, Hkv;
+  __half* q_out;        // [B, Hq, S, D]
+  __half* k_out;        // [B, Hkv, S, D]
+};
+int launch_rope_layout(const RopeArgs& a, int D, cudaStream_t s);
 // ee_gate_rows with the workspace-header memset optional (see ee_capi.cu)
 // bytes at the start of a gated workspace that a caller zeroes once (header + look-back)
 size_t gated_ws_head_bytes();

@@ -7,6 +7,7 @@
 #include <utility>
 
 #include "ee_attention.cuh"
+#include "ee_block.cuh"
 #include "ee_gemm.cuh"
 #include "ee_gemm_skinny.cuh"
 #include "ee_internal.h"
@@ -290,14 +291,36 @@ int launch_gated_gemm_skinny(const GemmMaps& m, const GemmArgs& args, int nb, in
   }
 }
 
-int launch_transpose_v(const void* V, int64_t heads, int64_t S, int64_t S_pad, int64_t D, void* VT, cudaStream_t s) {
-  if (heads <= 0 || S_pad <= 0) return 0;
-  const dim3 grid(static_cast<unsigned>((S_pad + 31) / 32), static_cast<unsigned>(heads));
+int launch_transpose_v(const void* V, int64_t B, int64_t Hkv, int64_t S, int64_t S_pad, int64_t D, int64_t sb,
+                       int64_t sh, int64_t ss, void* VT, cudaStream_t s) {
+  if (B * Hkv <= 0 || S_pad <= 0) return 0;
+  const dim3 grid(static_cast<unsigned>((S_pad + 31) / 32), static_cast<unsigned>(B * Hkv));
   if (D == 64)
-    return launch_pdl(transpose_v_kernel<64>, grid, dim3(256), 0, s, static_cast<const __half*>(V), S, S_pad,
-                      static_cast<__half*>(VT));
-  return launch_pdl(transpose_v_kernel<128>, grid, dim3(256), 0, s, static_cast<const __half*>(V), S, S_pad,
-                    static_cast<__half*>(VT));
+    return launch_pdl(transpose_v_kernel<64>, grid, dim3(256), 0, s, static_cast<const __half*>(V), Hkv, S, S_pad, sb,
+                      sh, ss, static_cast<__half*>(VT));
+  return launch_pdl(transpose_v_kernel<128>, grid, dim3(256), 0, s, static_cast<const __half*>(V), Hkv, S, S_pad, sb,
+                    sh, ss, static_cast<__half*>(VT));
+}
+
+int launch_add_rmsnorm(const AddNormArgs& a, cudaStream_t s) {
+  if (a.M <= 0) return 0;
+  // TPR threads per row, NV 16-byte vectors per thread (rows up to TPR * NV * 8)
+  if (a.d <= 1024)
+    return launch_pdl(add_rmsnorm_kernel<32, 4>, dim3(grid_of(a.M, kNormThreads / 32)), dim3(kNormThreads), 0, s, a);
+  if (a.d <= 2048)
+    return launch_pdl(add_rmsnorm_kernel<64, 4>, dim3(grid_of(a.M, kNormThreads / 64)), dim3(kNormThreads), 0, s, a);
+  if (a.d <= 4096)
+    return launch_pdl(add_rmsnorm_kernel<128, 4>, dim3(grid_of(a.M, kNormThreads / 128)), dim3(kNormThreads), 0, s, a);
+  if (a.d <= 8192)
+    return launch_pdl(add_rmsnorm_kernel<256, 4>, dim3(grid_of(a.M, 1)), dim3(kNormThreads), 0, s, a);
+  return -1;
+}
+
+int launch_rope_layout(const RopeArgs& a, int D, cudaStream_t s) {
+  if (a.B * a.S <= 0) return 0;
+  const dim3 grid(static_cast<unsigned>(a.B * a.S));
+  if (D == 64) return launch_pdl(rope_layout_kernel<64>, grid, dim3(256), 0, s, a);
+  return launch_pdl(rope_layout_kernel<128>, grid, dim3(256), 0, s, a);
 }
 
 int launch_flash_attention(const AttnLaunch& a, cudaStream_t s) {

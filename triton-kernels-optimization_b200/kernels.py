@@ -364,3 +364,62 @@ def flash_attention_entropy(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, c
     batch = rows.mean(dim=(1, 2))
     return (out, batch, rows) if return_rows else (out, batch)
 
+
+def flash_attention_rope_entropy(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor,
+                                 sin: torch.Tensor, num_heads: int, num_kv_heads: int, causal: bool = True,
+                                 scale: float | None = None, return_rows: bool = False):
+    """flash_attention_entropy on the projections' outputs: q fp16 [B, S, Hq*d], k / v fp16
+    [B, S, Hkv*d] (any row stride, unit column stride), cos / sin fp16 [B, S, d] (what
+    transformers' LlamaRotaryEmbedding returns).  The rotary embedding is applied in the
+    same launch chain with the roundings of transformers' apply_rotary_pos_emb on fp16
+    tensors, so the result equals flash_attention_entropy(apply_rotary_pos_emb(...)) bit
+    for bit.  Returns what flash_attention_entropy returns."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (cos, "cos"), (sin, "sin")):
+        _check_cuda(t, n)
+        _require(t.dim() == 3 and t.dtype == torch.float16 and t.stride(-1) == 1, f"{n} must be fp16 [B, S, n] rows")
+    B, S, _ = q.shape
+    Hq, Hkv = int(num_heads), int(num_kv_heads)
+    d = q.shape[2] // Hq
+    _require(q.shape[2] == Hq * d and k.shape == (B, S, Hkv * d) and v.shape == k.shape, "q / k / v widths")
+    _require(cos.shape == (B, S, d) and sin.shape == cos.shape, "cos / sin must be [B, S, d]")
+    rows_of = lambda t: t if t.stride(0) == t.stride(1) * S else t.contiguous()  # noqa: E731
+    q, k, v, cos, sin = (rows_of(t) for t in (q, k, v, cos, sin))
+    scale = float(d ** -0.5 if scale is None else scale)
+    out = torch.empty(B, S, Hq, d, dtype=torch.float16, device=q.device)
+    rows = torch.empty(B, Hq, S, dtype=torch.float32, device=q.device)
+    ws = _workspace(_lib.load().ee_attention_rope_workspace_bytes(B, Hq, Hkv, S, d), q.device)
+    with torch.cuda.device(q.device):
+        call("ee_flash_attention_rope_entropy", q.data_ptr(), q.stride(1), k.data_ptr(), k.stride(1), v.data_ptr(),
+             v.stride(1), cos.data_ptr(), sin.data_ptr(), cos.stride(1), B, Hq, Hkv, S, d, int(bool(causal)), scale,
+             out.data_ptr(), rows.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
+    batch = rows.mean(dim=(1, 2))
+    return (out, batch, rows) if return_rows else (out, batch)
+
+
+def add_rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: torch.Tensor | None = None):
+    """transformers' LlamaRMSNorm (weight, eps) of x, or of fp16(residual + x) when a
+    residual is given, in one pass.  Returns y, or (y, s) with s = residual + x."""
+    _check_cuda(x, "x")
+    _require(x.dtype == torch.float16 and weight.dtype == torch.float16, "x and weight must be fp16")
+    d = x.shape[-1]
+    x2 = x.reshape(-1, d)
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    y = torch.empty(M, d, dtype=torch.float16, device=x.device)
+    s = None
+    r2 = None
+    if residual is not None:
+        _require(residual.shape == x.shape and residual.dtype == torch.float16, "residual must match x")
+        r2 = residual.reshape(-1, d)
+        if r2.stride(1) != 1:
+            r2 = r2.contiguous()
+        s = torch.empty(M, d, dtype=torch.float16, device=x.device)
+    w = weight.contiguous()
+    with torch.cuda.device(x.device):
+        call("ee_add_rmsnorm", x2.data_ptr(), x2.stride(0), r2.data_ptr() if r2 is not None else None,
+             r2.stride(0) if r2 is not None else 0, s.data_ptr() if s is not None else None, d,
+             w.data_ptr(), float(eps), y.data_ptr(), d, M, d, _stream())
+    y = y.reshape(x.shape)
+    return y if s is None else (y, s.reshape(x.shape))
+

@@ -22,7 +22,8 @@ import torch
 import torch.nn as nn
 
 from .dispatch import EntropyDispatchedLinear, EntropyRouter, PipelinedEntropyDispatcher, PrecisionTier
-from .kernels import SwiGLUPack, _require, attention_entropy, flash_attention_entropy
+from .kernels import (SwiGLUPack, _require, add_rmsnorm, attention_entropy, flash_attention_entropy,
+                      flash_attention_rope_entropy)
 
 
 class EntropyDispatchedLlamaBlock(nn.Module):
@@ -60,7 +61,12 @@ class EntropyDispatchedLlamaBlock(nn.Module):
                 attention_mask: Optional[torch.Tensor] = None, position_ids: Optional[torch.Tensor] = None,
                 past_key_value=None, use_cache: bool = False, **kwargs) -> Tuple[torch.Tensor, ...]:
         residual = hidden_states
-        hidden_states = self.input_layernorm(hidden_states)
+        fused = self.attention == "flash" and hidden_states.dtype == torch.float16
+        if fused:  # one pass instead of transformers' chain of fp32 ops
+            hidden_states = add_rmsnorm(hidden_states, self.input_layernorm.weight,
+                                        self.input_layernorm.variance_epsilon)
+        else:
+            hidden_states = self.input_layernorm(hidden_states)
         if self.route_all:
             kwargs["_dispatcher"] = dispatcher
         attn_output, entropy_batch, present_kv = self._attention_with_fused_entropy(
@@ -71,10 +77,13 @@ class EntropyDispatchedLlamaBlock(nn.Module):
             dispatcher.submit_entropy(entropy_batch)  # (route_all / batch submitted it before o)
         if dispatcher is not None and self.routing == "token":
             dispatcher._prev_token_entropy = self.token_entropy.reshape(-1)  # the next layer's q / k / v
-        hidden_states = residual + attn_output
-
-        residual = hidden_states
-        hidden_states = self.post_attention_layernorm(hidden_states)
+        if fused:  # residual + attention output and the second norm in one pass
+            hidden_states, residual = add_rmsnorm(attn_output, self.post_attention_layernorm.weight,
+                                                  self.post_attention_layernorm.variance_epsilon, residual=residual)
+        else:
+            hidden_states = residual + attn_output
+            residual = hidden_states
+            hidden_states = self.post_attention_layernorm(hidden_states)
         if self.routing == "token" and dispatcher is not None:
             hidden_states = self._mlp_per_token(hidden_states, dispatcher)
         else:
@@ -122,13 +131,19 @@ class EntropyDispatchedLlamaBlock(nn.Module):
             q, k, v = qkv.split(self._qkv_split, dim=-1)
         else:
             q, k, v = attn.q_proj(hidden_states), attn.k_proj(hidden_states), attn.v_proj(hidden_states)
-        q = q.reshape(B, S, -1, d).transpose(1, 2)
-        k = k.reshape(B, S, -1, d).transpose(1, 2)
-        v = v.reshape(B, S, -1, d).transpose(1, 2)
         cos, sin = position_embeddings
-        q, k = apply_rotary_pos_emb(q, k, cos, sin)
-        out, batch, rows = flash_attention_entropy(q.half(), k.half(), v.half(), causal=True, scale=attn.scaling,
-                                                   return_rows=True)
+        if q.dtype == torch.float16 and cos.dtype == torch.float16:
+            # rotary embedding, head layout and V transpose in the attention's own launches
+            Hkv = k.shape[-1] // d
+            out, batch, rows = flash_attention_rope_entropy(q, k, v, cos, sin, q.shape[-1] // d, Hkv, causal=True,
+                                                            scale=attn.scaling, return_rows=True)
+        else:
+            q = q.reshape(B, S, -1, d).transpose(1, 2)
+            k = k.reshape(B, S, -1, d).transpose(1, 2)
+            v = v.reshape(B, S, -1, d).transpose(1, 2)
+            q, k = apply_rotary_pos_emb(q, k, cos, sin)
+            out, batch, rows = flash_attention_entropy(q.half(), k.half(), v.half(), causal=True,
+                                                       scale=attn.scaling, return_rows=True)
         out = out.reshape(B, S, -1).to(hidden_states.dtype)
         self.token_entropy = rows.mean(dim=1)
         if self.route_all:
