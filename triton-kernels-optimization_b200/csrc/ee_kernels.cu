@@ -347,8 +347,8 @@ int launch_flash_attention(const AttnLaunch& a, cudaStream_t s) {
   args.causal = a.causal;
   args.O = static_cast<__half*>(a.O);
   args.H = a.H;
-  const int64_t nqt = (a.S + kAttnTile - 1) / kAttnTile;
-  const dim3 grid(static_cast<unsigned>(a.B * a.Hq * nqt));
+  const int64_t nqc = (a.S + 2 * kAttnTile - 1) / (2 * kAttnTile);  // 256 query rows per CTA
+  const dim3 grid(static_cast<unsigned>(a.B * a.Hq * nqc));
   if (a.D == 64)
     return launch_pdl(flash_attention_entropy_kernel<64>, grid, dim3(kAttnThreads), AttnCfg<64>::kSmem, s, a.q, a.k,
                       a.vt, args);
