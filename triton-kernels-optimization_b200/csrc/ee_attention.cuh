@@ -174,14 +174,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_vt);
   }
-  if (warp == 1) {
+  griddep_wait();  // Q, K, V^T may come from the previous kernel in the stream
+  if (warp == 1) {  // after the wait: a kernel still draining before this one may hold TMEM
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  griddep_wait();  // Q, K, V^T may come from the previous kernel in the stream
   const uint32_t tmem_base = *tmem_slot;
 
   // the register budgets change inside each role's branch: code after a join would be
