@@ -297,3 +297,32 @@ def test_router_bucket_scan(pkg, cuda, M, n):
         perm_ref, counts_ref = orc.compaction(route)
         assert np.array_equal(r.counts.cpu().numpy(), counts_ref)
         assert np.array_equal(r.perm.cpu().numpy(), perm_ref)
+
+
+def test_int8_row_quantisation_exhaustive(pkg, cuda):
+    """q = trunc(x / s) with the reference's IEEE division, against the oracle bit for
+    bit, over every positive fp16 x up to each row's abs-max and the exact multiples
+    n * s (integer quotients: the case a rounded product could miss), for abs-max values
+    across the whole fp16 range (subnormal scales included)."""
+    bits = np.arange(0x0001, 0x7C00, dtype=np.uint16)  # every positive finite fp16
+    allv = bits.view(np.float16).astype(np.float32)
+    rows = []
+    for e in range(-14, 16):
+        for frac in (1.0, 1.125, 1.5, 1.875, 1.99):
+            amax = np.float16(2.0 ** e * frac)
+            if not np.isfinite(amax) or amax == 0:
+                continue
+            s = np.float32(np.float16(np.float32(amax) * (np.float32(1.0) / np.float32(127.0))))
+            cand = allv[allv <= np.float32(amax)]
+            mult = (np.arange(1, 128, dtype=np.float32) * s).astype(np.float16).astype(np.float32)
+            mult = mult[(mult <= np.float32(amax)) & (mult > 0)]
+            pick = np.concatenate([mult, cand[np.linspace(0, cand.size - 1, 4096 - 1 - mult.size).astype(int)]])
+            row = np.concatenate([[np.float32(amax)], pick])[:4096]
+            sign = np.where(np.arange(row.size) % 3 == 1, -1.0, 1.0).astype(np.float32)
+            sign[0] = 1.0
+            rows.append((row * sign).astype(np.float16))
+    a = np.stack(rows)
+    q, s = pkg.quant_rows_int8(_dev(a, cuda))
+    q_ref, s_ref = orc.quant_rows_int8(a)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy(), q_ref)

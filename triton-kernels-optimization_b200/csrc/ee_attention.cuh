@@ -354,13 +354,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // drives them to), whose probability is exactly 0
       __half2 xs[KT / 2];
 #pragma unroll
-      for (int c0 = 0; c0 < KT; c0 += 32) {
-        uint32_t r[32];
+      for (int c0 = 0; c0 < KT; c0 += 64) {  // two TMEM loads in flight per wait
+        uint32_t ra[32], rb[32];
         __syncwarp();
-        tmem_ld32(t_s + c0, r);
-        tmem_ld_wait(r);
+        tmem_ld32(t_s + c0, ra);
+        tmem_ld32(t_s + c0 + 32, rb);
+        tmem_ld_wait(ra);
+        regs_after_wait(rb);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) xs[c0 / 2 + i] = scaled_scores(r[2 * i], r[2 * i + 1], sc2);
+        for (int i = 0; i < 16; ++i) {
+          xs[c0 / 2 + i] = scaled_scores(ra[2 * i], ra[2 * i + 1], sc2);
+          xs[c0 / 2 + 16 + i] = scaled_scores(rb[2 * i], rb[2 * i + 1], sc2);
+        }
       }
       tc_fence_before();
       __syncwarp();

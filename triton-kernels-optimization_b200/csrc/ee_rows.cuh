@@ -691,6 +691,34 @@ __device__ __forceinline__ RowScale row_scale(float amax, int bucket) {
   return r;
 }
 
+// 8 fp16 -> 8 int8: q = trunc(RN(x / s)) without a division per element.  x and s are
+// both fp16 values (s = fp16(amax / 127) > 0), so x / s = (A / S) 2^e with A, S integers
+// below 2^11: a quotient that is not an integer lies at least 2^-21 from every integer,
+// well above half an fp32 ulp of |x / s| <= 127.06, so rounding the quotient to fp32
+// never moves it across an integer and trunc(RN(x / s)) = trunc(x / s).  That is found
+// from q = trunc(|x| r) (r = RN(1 / s): off by at most one) and two exact checks --
+// (q + 1) s and q s carry at most 19 significant bits, so fma(q + 1, s, -|x|) and
+// fma(q, s, -|x|) have the exact sign of (q + 1) s - |x| and q s - |x| (the integer
+// quotient correction of division by an invariant divisor: Granlund and Montgomery,
+// PLDI 1994).  Callers with s = 0 or a non-finite s use quant8_int8 below.
+__device__ __forceinline__ uint2 quant8_int8_fast(const uint4& u, float s, float r) {
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+  uint32_t w[2] = {0u, 0u};
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float x = (k & 1) ? __high2float(h[k >> 1]) : __low2float(h[k >> 1]);
+    const float ax = fabsf(x);
+    float q = truncf(ax * r);
+    q = (fmaf(q + 1.f, s, -ax) <= 0.f) ? q + 1.f : q;
+    q = (fmaf(q, s, -ax) > 0.f) ? q - 1.f : q;
+    int qi = static_cast<int>(q);
+    qi = x < 0.f ? -qi : qi;
+    qi = qi > 127 ? 127 : (qi < -128 ? -128 : qi);
+    w[k >> 2] |= (static_cast<uint32_t>(qi) & 0xFFu) << (8 * (k & 3));
+  }
+  return make_uint2(w[0], w[1]);
+}
+
 // 8 fp16 -> 8 int8: q = trunc(x / s) with IEEE division (in-range values never clamp)
 __device__ __forceinline__ uint2 quant8_int8(const uint4& u, float s) {
   const __half* h = reinterpret_cast<const __half*>(&u);
@@ -779,10 +807,19 @@ __global__ void __launch_bounds__(kRowThreads, MINB) pack_rows_vec_kernel(const 
   const RowScale rs = row_scale(amax, b);
   uint8_t* dst = a.buf8 + pos * a.ld8;
   if (b == kINT8) {
+    if (rs.s > 0.f && rs.s <= 65504.f) {  // every finite, non-zero fp16 scale
+      const float r = __fdiv_rn(1.f, rs.s);
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int e0 = (lt + i * TPR) * 8;
-      if (e0 < K) *reinterpret_cast<uint2*>(dst + e0) = quant8_int8(u[i], rs.s);
+      for (int i = 0; i < NV; ++i) {
+        const int e0 = (lt + i * TPR) * 8;
+        if (e0 < K) *reinterpret_cast<uint2*>(dst + e0) = quant8_int8_fast(u[i], rs.s, r);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int e0 = (lt + i * TPR) * 8;
+        if (e0 < K) *reinterpret_cast<uint2*>(dst + e0) = quant8_int8(u[i], rs.s);
+      }
     }
   } else {
 #pragma unroll
