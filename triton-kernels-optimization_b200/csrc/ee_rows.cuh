@@ -446,6 +446,13 @@ __global__ void __launch_bounds__(kRowThreads, MINB) softmax_entropy_vec_kernel(
 // ----------------------------------------------------------------------------------
 constexpr int kRouteConsumers = 8;
 constexpr int kRouteSlots = 8;  // row buffers per block
+// Consumer c takes rows c, c + kRouteConsumers, ...; with kRouteSlots a multiple of
+// kRouteConsumers every slot then belongs to one consumer, which waits for the slot's
+// phases one after the other.  Otherwise two consumers would share a slot and one could
+// wait on a phase parity two phases ahead -- a wait that passes at once -- and arrive
+// early on the empty barrier, which lets the producer's transaction count run past the
+// phase (a GPU fault).
+static_assert(kRouteSlots % kRouteConsumers == 0, "each ring slot must belong to one consumer warp");
 constexpr int kRouteThreads = 32 * (kRouteConsumers + 1);  // warp 0 produces
 
 __device__ __forceinline__ float warp_sum(float v) {
