@@ -258,8 +258,17 @@ EE_API int ee_linear_int8_noalloc(const void* A, int64_t lda, const int8_t* W_nk
  * routing, with its own A of M rows and width K) may follow on the same stream.
  * ee_gated_linear = ee_gate_rows + ee_gated_gemm.
  * H (fp32 [M]) and route (int8 [M]) are outputs; NULL keeps them in the workspace.
- * bucket_counts (int32 [3], device, nullable) receives the rows per bucket. */
+ * bucket_counts (int32 [3], device, nullable) receives the rows per bucket.
+ * K split: a workspace larger than ee_gated_workspace_bytes(M, K) of the call lends
+ * the rest to its GEMM for K-split partial sums.  When a call has few tiles for the SMs
+ * (mid-size M: e.g. 128 or 1024 rows at Llama-3-8B widths) the GEMM then cuts each
+ * tile's K loop into ranges run by different CTAs and adds the ranges' int32 / fp32
+ * partials in range order in a second kernel: INT8 results bit-identical to the unsplit
+ * run, FP8 / FP16 within the last bits (deterministic).  ee_gated_workspace_split_bytes
+ * (M, K) is the recommended size (the base plus four 128 KiB partial blocks per SM;
+ * just the base for M <= 64, where the weight-streaming kernel splits K itself). */
 EE_API size_t ee_gated_workspace_bytes(int64_t M, int64_t K);
+EE_API size_t ee_gated_workspace_split_bytes(int64_t M, int64_t K);
 EE_API int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high, float* H,
                  int8_t* route, int32_t* bucket_counts, void* workspace, size_t workspace_bytes, void* stream);
 /* ee_gate_rows without zeroing the workspace head (its first

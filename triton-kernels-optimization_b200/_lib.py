@@ -61,6 +61,7 @@ SIGNATURES = {
     "ee_linear_fp8": (c_int, [_P, c_int64, _P, _P, _P, c_int64, c_int64, c_int64, c_int64, _P, c_size_t, _P]),
     "ee_linear_int8_noalloc": (c_int, [_P, c_int64, _P, _P, _P, c_int64, c_int64, c_int64, c_int64, _P]),
     "ee_gated_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "ee_gated_workspace_split_bytes": (c_size_t, [c_int64, c_int64]),
     "ee_gate_rows": (c_int, [_P, c_int64, c_int64, c_int64, c_double, c_double, _P, _P, _P, _P, c_size_t, _P]),
     "ee_gate_rows_keep": (c_int, [_P, c_int64, c_int64, c_int64, c_double, c_double, _P, _P, _P, _P, c_size_t, _P]),
     "ee_gated_workspace_head_bytes": (c_size_t, []),

@@ -182,8 +182,23 @@ int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cud
   }
   const int64_t wide_tiles = row_tiles(args, dynamic_counts, ee::kBM) * ((args.N + ee::kBN - 1) / ee::kBN);
   const bool pair = policy == 2 || (policy == 0 && args.M_cap > ee::kBM);
+  // K split: with partial storage, 256-column tiles, when the call has at most two tiles
+  // per CTA (pair) of the launch -- the device then plans the ranges from the bucket counts
+  const int64_t slots = pair ? num_sms() / 2 : num_sms();
+  const int64_t split_tiles = pair ? row_tiles(args, dynamic_counts, ee::kPairTileRows) * ((args.N + ee::kBN - 1) / ee::kBN)
+                                   : wide_tiles;
+  // (measured on B200: splitting pays for long K loops -- K >= 8192 -- with whole tiles
+  // for at most 3/4 of the slots; at K = 4096 the 128 x 64 tiles or the unsplit pairs are
+  // as fast, and where the device plans no split the reduction launch alone costs ~5 us)
+  const bool split = args.part != nullptr && policy != 3 && args.K >= 8192 && 4 * split_tiles <= 3 * slots;
+  if (!split) {
+    args.part = nullptr;
+    args.part_blocks = 0;
+    args.split_plan = nullptr;
+  }
   // the SwiGLU epilogue pairs 128-column groups inside a 256-column tile
-  const bool narrow = args.out_mode != 2 && (policy == 3 || (policy == 0 && !pair && wide_tiles < num_sms()));
+  const bool narrow =
+      !split && args.out_mode != 2 && (policy == 3 || (policy == 0 && !pair && wide_tiles < num_sms()));
   const int bn = narrow ? ee::kBNNarrow : ee::kBN;
   const int wbox = pair ? ee::kBN / 2 : bn;
   ee::GemmMaps maps;
@@ -218,14 +233,18 @@ int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cud
   const int64_t ntn = (args.N + bn - 1) / bn;
   const int64_t bm = pair ? ee::kPairTileRows : ee::kBM;
   const int64_t tiles = row_tiles(args, dynamic_counts, bm) * ntn;
-  if (pair) {
-    const int64_t max_pairs = num_sms() / 2;
-    const int pairs = static_cast<int>(tiles < max_pairs ? tiles : max_pairs);
-    return check_launch(ee::launch_gated_gemm_pair(maps, args, pairs, s), "gated_gemm_pair_kernel");
-  }
-  const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  return check_launch(ee::launch_gated_gemm(maps, args, grid, bn, s), "gated_gemm_kernel");
+  // a split call runs one CTA (pair) per slot: its units outnumber its tiles
+  const int grid = static_cast<int>(split ? slots : (tiles < slots ? tiles : slots));
+  args.split_slots = split ? grid : 0;
+  int st2 = pair ? check_launch(ee::launch_gated_gemm_pair(maps, args, grid, s), "gated_gemm_pair_kernel")
+                 : check_launch(ee::launch_gated_gemm(maps, args, grid, bn, s), "gated_gemm_kernel");
+  if (st2 != EE_OK || !split) return st2;
+  return check_launch(ee::launch_reduce_partials(args, pair, tiles, s), "reduce_partials_kernel");
 }
+
+// The part of a gated workspace past this call's own layout (M rows, K) holds the K-split
+// partial blocks of its GEMM; a workspace without that room runs every tile whole.
+void attach_split_area(ee::GemmArgs& args, void* ws, size_t ws_bytes, int64_t M, int64_t K);
 
 ee::GemmArgs base_args(int64_t M_cap, int64_t N, int64_t K, void* Y, int64_t ldy, int out_mode) {
   ee::GemmArgs a;
@@ -300,6 +319,23 @@ GatedWs gated_ws(void* ws, int64_t M, int64_t K) {
   p += align256(size_t(M) * K);
   w.buf16 = p;
   return w;
+}
+
+void attach_split_area(ee::GemmArgs& args, void* ws, size_t ws_bytes, int64_t M, int64_t K) {
+  const size_t base = gated_ws_bytes(M, K);  // a multiple of 256
+  if (ws == nullptr || ws_bytes < base + 256 + 2 * size_t(ee::kPartBlockBytes)) return;
+  const size_t blocks = (ws_bytes - base - 256) / ee::kPartBlockBytes;
+  uint8_t* p = static_cast<uint8_t*>(ws) + base;
+  args.split_plan = reinterpret_cast<int32_t*>(p);  // 256 bytes: the plan, then the blocks
+  args.part = reinterpret_cast<uint32_t*>(p + 256);
+  args.part_blocks = static_cast<int>(blocks < size_t(1) << 30 ? blocks : size_t(1) << 30);
+}
+
+// recommended room for the K-split partials: four blocks per SM (a split plan can run up
+// to four ranges per CTA of the launch); none for calls the weight-streaming kernel takes
+size_t split_area_bytes(int64_t M) {
+  if (M <= ee::kSkinnyAutoRows) return 0;
+  return 256 + size_t(4) * size_t(num_sms()) * size_t(ee::kPartBlockBytes);
 }
 
 int check_ws(const void* ws, size_t have, size_t need) {
@@ -780,6 +816,11 @@ size_t ee_gated_workspace_bytes(int64_t M, int64_t K) {
   return gated_ws_bytes(M, K);
 }
 
+size_t ee_gated_workspace_split_bytes(int64_t M, int64_t K) {
+  if (M < 0 || K < 0) return 0;
+  return gated_ws_bytes(M, K) + split_area_bytes(M);
+}
+
 int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high, float* H,
                  int8_t* route, int32_t* bucket_counts, void* workspace, size_t workspace_bytes, void* stream) {
   return ee::gate_rows_impl(logits, M, n, ld, tau_low, tau_high, H, route, bucket_counts, workspace, workspace_bytes,
@@ -918,6 +959,7 @@ int ee_gated_gemm_packed(int64_t M, int64_t K, const int8_t* W_i8_nk, const uint
   args.sa = w.sa;
   args.sb = w_scale;
   args.sched = w.sched;
+  attach_split_area(args, workspace, workspace_bytes, M, K);
   return run_gemm(op, args, true, as_stream(stream));
 }
 
@@ -949,6 +991,7 @@ int ee_gated_swiglu_packed(int64_t M, int64_t K, const int8_t* Wgu_i8_nk, const 
   args.sa = w.sa;
   args.sb = wgu_scale;
   args.sched = w.sched;
+  attach_split_area(args, workspace, workspace_bytes, M, K);
   return run_gemm(op, args, true, as_stream(stream));
 }
 

@@ -46,15 +46,119 @@ struct SingleCfg {
   static_assert(kSmem <= 227 * 1024, "single-CTA GEMM shared memory above the 227 KB per-CTA limit");
 };
 
+__device__ __forceinline__ int kblocks_of(int b, int K) {
+  const int per = (b == kFP16) ? (kBKBytes / 2) : kBKBytes;  // elements per stage
+  return (K + per - 1) / per;
+}
+
+// Work geometry of one call.  A work unit is one tile, or one K range of a tile whose K
+// loop is split (spl[b] ranges per tile of bucket b).  Units run FP16 first (the longest
+// K loops), then FP8, then INT8; inside a bucket the ranges of one tile are adjacent and
+// the row tile varies fastest, so CTAs that run together share a weight tile.
 struct TileGeo {
   int cnt[3], off[3], mtiles[3], tiles[3];
   int halfmt[3];  // the bucket's half row tile (last m-tile with at most bm / 2 rows), or -1
-  int ntn, total;
+  int spl[3];     // K ranges per tile
+  int ntn, ntiles;
+  int total;      // work units
 };
 
+// makespan estimate, in K stages per slot, of running every tile of bucket b as S[b]
+// ranges on `slots` CTAs (pairs) taking units longest first: the costliest group's
+// rounds, or the whole work levelled in units of the cheapest range, whichever is
+// longer.  A unit costs its stages + 1 (pipeline fill) + kSplitStoreCost when it stores
+// a partial block (128 KiB per CTA); a split plan adds kSplitOverhead for the reduction
+// pass's launch (plan_splits_warp adds its reads).  Costs measured on B200: one K stage
+// of a 128 x 256 (pair: 256 x 256) tile about 0.4 us.  32-bit arithmetic: plan_splits only plans for K loops of at most
+// kSplitMaxKBlocks stages and at most kSplitMaxTiles tiles.
+constexpr int kSplitOverhead = 8;
+constexpr int kSplitStoreCost = 2;
+constexpr int kSplitBlocksPerStage = 12;
+constexpr int kSplitMaxKBlocks = 1 << 12;
+constexpr int kSplitMaxTiles = 1024;
+__device__ __forceinline__ int split_estimate(const int (&tiles)[3], const int (&nkb)[3], const int (&S)[3],
+                                              int slots) {
+  int work = 0, cmax = 0, cmin = 1 << 30, nhi = 0;
+  bool split = false;
+#pragma unroll
+  for (int b = 0; b < 3; ++b) {
+    if (tiles[b] == 0) continue;
+    const int c = (nkb[b] + S[b] - 1) / S[b] + 1 + (S[b] > 1 ? kSplitStoreCost : 0);
+    const int u = tiles[b] * S[b];
+    work += u * c;
+    if (c > cmax) {
+      cmax = c;
+      nhi = u;
+    } else if (c == cmax) {
+      nhi += u;
+    }
+    cmin = c < cmin ? c : cmin;
+    split |= S[b] > 1;
+  }
+  if (cmax == 0) return 0;
+  const int hi = cmax * ((nhi + slots - 1) / slots);
+  const int lvl = cmin * ((work + slots * cmin - 1) / (slots * cmin));
+  return (hi > lvl ? hi : lvl) + (split ? kSplitOverhead : 0);
+}
+
+// K-split plan, evaluated by one whole warp (the same result in every CTA and in the
+// reduction kernel): lane l scores the range length C = ceil(longest K loop / (l + 1)),
+// each bucket split into ceil(nkb / C) ranges (so ranges of all buckets are about
+// equally long), ranges of at least kSplitMinKBlocks stages, the partial blocks within
+// part_blocks; the smallest estimate wins, ties to fewer ranges.  Lanes >= kMaxKSplits
+// and invalid candidates score "never".
+__device__ __forceinline__ void plan_splits_warp(TileGeo& g, const GemmArgs& a, int ranks, int lane) {
+  g.spl[0] = g.spl[1] = g.spl[2] = 1;
+  if (a.part == nullptr || a.split_slots <= 0 || a.part_blocks <= 0 || g.ntiles > kSplitMaxTiles) return;
+  int nkb[3];
+  const int tiles[3] = {g.tiles[0], g.tiles[1], g.tiles[2]};
+  int maxkb = 0;
+#pragma unroll
+  for (int b = 0; b < 3; ++b) {
+    nkb[b] = kblocks_of(b, a.K);
+    if (tiles[b] > 0 && nkb[b] > maxkb) maxkb = nkb[b];
+  }
+  if (maxkb < 2 * kSplitMinKBlocks || maxkb > kSplitMaxKBlocks) return;
+  const int j = lane + 1;
+  const int C = (maxkb + j - 1) / j;
+  int S[3];
+  int units = 0;
+#pragma unroll
+  for (int b = 0; b < 3; ++b) {
+    int sb = (nkb[b] + C - 1) / C;
+    sb = sb < 1 ? 1 : (sb > kMaxKSplits ? kMaxKSplits : sb);
+    S[b] = sb;
+    units += tiles[b] * sb;
+  }
+  const bool ok = j <= kMaxKSplits && (j == 1 || (C >= kSplitMinKBlocks && units * ranks <= a.part_blocks));
+  // the reduction pass reads every partial block once: about one K stage of one slot per
+  // kSplitBlocksPerStage blocks
+  int e = ok ? split_estimate(tiles, nkb, S, a.split_slots) + (j > 1 ? units * ranks / kSplitBlocksPerStage : 0)
+             : (1 << 30);
+  // a split must beat the whole tiles by a margin (the estimate is coarse)
+  const int e1 = __shfl_sync(0xffffffffu, e, 0);
+  if (j > 1 && 8ll * e >= 7ll * e1) e = 1 << 30;
+  // argmin over the warp of (estimate, j)
+  unsigned long long key = (static_cast<unsigned long long>(static_cast<unsigned>(e)) << 8) | static_cast<unsigned>(j);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+    key = other < key ? other : key;
+  }
+  const int jb = static_cast<int>(key & 0xffu);
+  const int Cb = (maxkb + jb - 1) / jb;
+#pragma unroll
+  for (int b = 0; b < 3; ++b) {
+    int sb = (nkb[b] + Cb - 1) / Cb;
+    g.spl[b] = sb < 1 ? 1 : (sb > kMaxKSplits ? kMaxKSplits : sb);
+  }
+}
+
 // half_tiles: the CTA-pair kernel runs a bucket's last row tile as an M = 128 pair tile
-// when it holds at most 128 rows (instead of an M = 256 tile that is mostly padding)
-__device__ __forceinline__ TileGeo make_geo(const GemmArgs& a, int bm, int bn = kBN, bool half_tiles = false) {
+// when it holds at most 128 rows (instead of an M = 256 tile that is mostly padding).
+// K splits only for 256-column tiles (one partial block per CTA of a tile).  Called by
+// one whole warp (the split plan is spread over its lanes).
+__device__ __forceinline__ TileGeo make_geo_warp(const GemmArgs& a, int bm, int bn, bool half_tiles, int lane) {
   TileGeo g;
   if (a.dyn_counts != nullptr) {
 #pragma unroll
@@ -67,49 +171,91 @@ __device__ __forceinline__ TileGeo make_geo(const GemmArgs& a, int bm, int bn = 
   g.off[1] = g.cnt[0];
   g.off[2] = g.cnt[0] + g.cnt[1];
   g.ntn = (a.N + bn - 1) / bn;
-  g.total = 0;
+  g.ntiles = 0;
 #pragma unroll
   for (int b = 0; b < 3; ++b) {
     g.mtiles[b] = (g.cnt[b] + bm - 1) / bm;
     g.tiles[b] = g.mtiles[b] * g.ntn;
-    g.total += g.tiles[b];
+    g.ntiles += g.tiles[b];
     const int rem = g.cnt[b] % bm;
     g.halfmt[b] = (half_tiles && rem >= 1 && rem <= bm / 2) ? g.mtiles[b] - 1 : -1;
   }
+  if (bn == kBN) {
+    plan_splits_warp(g, a, bm == 2 * kBM ? 2 : 1, lane);
+  } else {
+    g.spl[0] = g.spl[1] = g.spl[2] = 1;
+  }
+  g.total = g.tiles[0] * g.spl[0] + g.tiles[1] * g.spl[1] + g.tiles[2] * g.spl[2];
   return g;
 }
 
-// tile index -> bucket, first position (row of A), first output column.  Tiles run
-// FP16 first (the longest K loops), then FP8, then INT8; m fastest inside a bucket.
-// Written out per bucket: a loop with an early return here kept TileGeo on the stack.
-__device__ __forceinline__ int decode_in(const TileGeo& g, int b, int t, int bm, int bn, int& pos0, int& n0,
-                                         bool& half) {
-  const int mt = t % g.mtiles[b];
-  const int nt = t / g.mtiles[b];
-  pos0 = g.off[b] + mt * bm;
-  n0 = nt * bn;
-  half = mt == g.halfmt[b];
-  return b;
-}
-__device__ __forceinline__ int decode_tile(const TileGeo& g, int t, int bm, int& pos0, int& n0, int bn, bool& half) {
-  if (t < g.tiles[2]) return decode_in(g, 2, t, bm, bn, pos0, n0, half);
-  t -= g.tiles[2];
-  if (t < g.tiles[1]) return decode_in(g, 1, t, bm, bn, pos0, n0, half);
-  t -= g.tiles[1];
-  if (t < g.tiles[0]) return decode_in(g, 0, t, bm, bn, pos0, n0, half);
-  pos0 = 0;
-  n0 = 0;
-  half = false;
-  return 0;
-}
-__device__ __forceinline__ int decode_tile(const TileGeo& g, int t, int bm, int& pos0, int& n0, int bn = kBN) {
-  bool half;
-  return decode_tile(g, t, bm, pos0, n0, bn, half);
+// the geometry of a CTA, computed by warp 0 into shared memory: the roles read the few
+// fields they need per unit instead of holding all of it in registers
+// (the first CTA also publishes the split plan for the reduction kernel)
+__device__ __forceinline__ void make_geo_shared(TileGeo* sg, const GemmArgs& a, int bm, int bn, bool half_tiles) {
+  if (threadIdx.x < 32) {
+    const TileGeo g = make_geo_warp(a, bm, bn, half_tiles, static_cast<int>(threadIdx.x));
+    if (threadIdx.x == 0) {
+      *sg = g;
+      if (blockIdx.x == 0 && a.split_plan != nullptr) {
+        a.split_plan[0] = g.spl[0];
+        a.split_plan[1] = g.spl[1];
+        a.split_plan[2] = g.spl[2];
+      }
+    }
+  }
+  __syncthreads();
 }
 
-__device__ __forceinline__ int kblocks_of(int b, int K) {
-  const int per = (b == kFP16) ? (kBKBytes / 2) : kBKBytes;  // elements per stage
-  return (K + per - 1) / per;
+// One work unit: bucket, first position (row of A), first output column, half tile,
+// K stages [kb0, kb1) and whether the tile is split.  Written out per bucket: a loop
+// with an early return here kept TileGeo on the stack.
+struct Unit {
+  int b, pos0, n0, kb0, kb1;
+  bool half, split;
+};
+__device__ __forceinline__ Unit unit_in(const TileGeo& g, int b, int u, int bm, int bn, int K) {
+  const int S = g.spl[b];
+  const int t = u / S, r = u % S;
+  const int mt = t % g.mtiles[b];
+  const int nt = t / g.mtiles[b];
+  const int nkb = kblocks_of(b, K);
+  Unit w;
+  w.b = b;
+  w.pos0 = g.off[b] + mt * bm;
+  w.n0 = nt * bn;
+  w.half = mt == g.halfmt[b];
+  w.split = S > 1;
+  w.kb0 = r * nkb / S;  // S > 1 only for nkb <= kSplitMaxKBlocks
+  w.kb1 = (r + 1) * nkb / S;
+  return w;
+}
+__device__ __forceinline__ Unit decode_unit(const TileGeo& g, int v, int bm, int bn, int K) {
+  const int u2 = g.tiles[2] * g.spl[2], u1 = g.tiles[1] * g.spl[1];
+  if (v < u2) return unit_in(g, 2, v, bm, bn, K);
+  v -= u2;
+  if (v < u1) return unit_in(g, 1, v, bm, bn, K);
+  v -= u1;
+  return unit_in(g, 0, v, bm, bn, K);
+}
+
+// a split unit's raw accumulator -> its partial block.  Warp `quarter` stores TMEM chunk
+// j (32 columns of its 32 lanes, from taddr) to sub-block quarter * 8 + j, laid out as [8
+// groups of 4 columns][32 lanes][4]: each of a chunk's 8 stores writes 512 contiguous
+// bytes.  Whole warp (tcgen05.ld is .sync.aligned).
+constexpr int kPartSubWords = 32 * 32;  // one sub-block: 32 rows x 32 columns
+__device__ __forceinline__ void store_partial(uint32_t* blk, int quarter, uint32_t taddr, int nchunks, int lane) {
+#pragma unroll 1
+  for (int j = 0; j < nchunks; ++j) {
+    uint32_t r[32];
+    __syncwarp();
+    tmem_ld32(taddr + j * 32, r);
+    tmem_ld_wait(r);
+    uint4* d = reinterpret_cast<uint4*>(blk + (quarter * 8 + j) * kPartSubWords) + lane;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) d[g * 32] = make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
+  }
+  __syncwarp();
 }
 
 // issue the 4 UMMAs (each K = 32 bytes) of one stage
@@ -396,12 +542,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   griddep_wait();  // bucket counts, packed rows and the tile counter come from earlier kernels
   griddep_launch_dependents();
-  const TileGeo geo = make_geo(args, kBM, BN);
-  const bool dyn = args.sched != nullptr;
+  // the geometry lives in shared memory: the roles read the few fields they need per
+  // unit instead of holding all of it in registers for the whole kernel
+  __shared__ TileGeo s_geo;
+  make_geo_shared(&s_geo, args, kBM, BN, false);
+  const TileGeo& geo = s_geo;
   if (static_cast<int>(blockIdx.x) >= geo.total) {  // uniform for the whole CTA
     feed_retire(args);
     return;
   }
+  const bool dyn = args.sched != nullptr;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -450,13 +600,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       if (t >= geo.total) break;
-      int pos0, n0;
-      const int b = decode_tile(geo, t, kBM, pos0, n0, BN);
-      const int nkb = kblocks_of(b, K);
+      const Unit w = decode_unit(geo, t, kBM, BN, K);
+      const int b = w.b, pos0 = w.pos0, n0 = w.n0;
       const int kstep = (b == kFP16) ? kBKBytes / 2 : kBKBytes;
       const CUtensorMap* ta = (b == kFP16) ? &tm_a16 : &tm_a8;
       const CUtensorMap* tw = (b == kINT8) ? &tm_w0 : (b == kFP8 ? &tm_w1 : &tm_w2);
-      for (int kb = 0; kb < nkb; ++kb) {
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
           failed = true;
           break;
@@ -496,16 +645,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       if (t >= geo.total) break;
-      int pos0, n0;
-      const int b = decode_tile(geo, t, kBM, pos0, n0, BN);
-      const int nkb = kblocks_of(b, K);
+      const Unit w = decode_unit(geo, t, kBM, BN, K);
+      const int b = w.b;
       if (!mbar_wait(&acc_empty[ab], aphase ^ 1u, abort_flag)) {
         failed = true;
         break;
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + ab * BN;
-      for (int kb = 0; kb < nkb; ++kb) {
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag)) {
           failed = true;
           break;
@@ -515,11 +663,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t a_addr = smem_u32(sA + stage * kAStageBytes);
           const uint32_t b_addr = smem_u32(sB + stage * kBStageBytes);
           if (b == kINT8)
-            mma_stage<kKindI8, BN>(d_tmem, a_addr, b_addr, kb == 0);
+            mma_stage<kKindI8, BN>(d_tmem, a_addr, b_addr, kb == w.kb0);
           else if (b == kFP8)
-            mma_stage<kKindF8, BN>(d_tmem, a_addr, b_addr, kb == 0);
+            mma_stage<kKindF8, BN>(d_tmem, a_addr, b_addr, kb == w.kb0);
           else
-            mma_stage<kKindF16, BN>(d_tmem, a_addr, b_addr, kb == 0);
+            mma_stage<kKindF16, BN>(d_tmem, a_addr, b_addr, kb == w.kb0);
           tc_commit(&empty[stage]);  // frees the stage once these MMAs have read it
         }
         __syncwarp();
@@ -551,9 +699,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int t = feed_consume(feed, dyn, ring, ring_full, ring_empty, lane, abort_flag);
       bool failed = t < 0;
       if (!failed && t >= geo.total) break;
-      int pos0 = 0, n0 = 0;
-      const int b = failed ? 0 : decode_tile(geo, t, kBM, pos0, n0, BN);
-      const EpiRow er = epilogue_prepare(args, geo, b, pos0 + quarter * 32 + lane, n0, lane);
+      Unit w;
+      if (failed) {
+        w.b = 0;
+        w.pos0 = w.n0 = 0;
+        w.split = false;
+      } else {
+        w = decode_unit(geo, t, kBM, BN, K);
+      }
+      const int b = w.b, n0 = w.n0;
+      const EpiRow er = epilogue_prepare(args, geo, b, w.pos0 + quarter * 32 + lane, n0, lane);
       if (!failed && !mbar_wait(&acc_full[ab], aphase, abort_flag)) failed = true;
       if (failed) {
         if (lane == 0) {
@@ -563,7 +718,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      epilogue_drain<BN>(args, er, b, n0, tmem_base + ab * BN + (static_cast<uint32_t>(quarter * 32) << 16));
+      const uint32_t taddr = tmem_base + ab * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+      if (w.split)  // a K range of a split tile: raw partial, reduced by reduce_partials_kernel
+        store_partial(args.part + static_cast<size_t>(t) * (kPartBlockBytes / 4), quarter, taddr, BN / 32, lane);
+      else
+        epilogue_drain<BN>(args, er, b, n0, taddr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
@@ -732,13 +891,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
   griddep_wait();  // bucket counts, packed rows and the tile counter come from earlier kernels
   griddep_launch_dependents();
-  // half tiles need each thread's gate and up columns in one lane: not with SwiGLU
-  const TileGeo geo = make_geo(args, kPairRows, kBN, args.out_mode != 2);
-  const bool dyn = args.sched != nullptr;
+  // half tiles need each thread's gate and up columns in one lane: not with SwiGLU.  The
+  // geometry lives in shared memory (see gated_gemm_kernel).
+  __shared__ TileGeo s_geo;
+  make_geo_shared(&s_geo, args, kPairRows, kBN, args.out_mode != 2);
+  const TileGeo& geo = s_geo;
   if (pair >= geo.total) {  // the same decision in both CTAs of the pair
     if (leader) feed_retire_pair(args, npairs);
     return;
   }
+  const bool dyn = args.sched != nullptr;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStagesPair; ++s) {
@@ -788,17 +950,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         break;
       }
       if (t >= geo.total) break;
-      int pos0, n0;
-      bool half;
-      const int b = decode_tile(geo, t, kPairRows, pos0, n0, kBN, half);
-      const int nkb = kblocks_of(b, K);
+      const Unit w = decode_unit(geo, t, kPairRows, kBN, K);
+      const int b = w.b, pos0 = w.pos0, n0 = w.n0;
+      const bool half = w.half;
       const int kstep = (b == kFP16) ? kBKBytes / 2 : kBKBytes;
       const CUtensorMap* ta = half ? ((b == kFP16) ? &tm_a16h : &tm_a8h) : ((b == kFP16) ? &tm_a16 : &tm_a8);
       const CUtensorMap* tw = (b == kINT8) ? &tm_w0 : (b == kFP8 ? &tm_w1 : &tm_w2);
       const int arow = pos0 + static_cast<int>(rank) * (half ? 64 : 128);
       const uint32_t stage_tx = half ? 2u * (kHalfStageBytes / 2 + kHalfStageBytes) : 2u * kStageBytesPair;
       const int brow = n0 + static_cast<int>(rank) * (kBN / 2);
-      for (int kb = 0; kb < nkb; ++kb) {
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
           failed = true;
           break;
@@ -841,17 +1002,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           break;
         }
         if (t >= geo.total) break;
-        int pos0, n0;
-        bool half;
-        const int b = decode_tile(geo, t, kPairRows, pos0, n0, kBN, half);
-        const int nkb = kblocks_of(b, K);
+        const Unit w = decode_unit(geo, t, kPairRows, kBN, K);
+        const int b = w.b;
+        const bool half = w.half;
         if (!mbar_wait<true>(&acc_empty[ab], aphase ^ 1u, abort_flag)) {
           failed = true;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + ab * kBN;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          const bool first = kb == w.kb0;
           if (!mbar_wait(&full[stage], phase, abort_flag)) {
             failed = true;
             break;
@@ -862,17 +1023,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
             const uint32_t b_addr = smem_u32(sB + stage * kHalfStageBytes);
             if (half) {
               if (b == kINT8)
-                mma_stage_pair_half<kKindI8>(d_tmem, a_addr, b_addr, kb == 0);
+                mma_stage_pair_half<kKindI8>(d_tmem, a_addr, b_addr, first);
               else if (b == kFP8)
-                mma_stage_pair_half<kKindF8>(d_tmem, a_addr, b_addr, kb == 0);
+                mma_stage_pair_half<kKindF8>(d_tmem, a_addr, b_addr, first);
               else
-                mma_stage_pair_half<kKindF16>(d_tmem, a_addr, b_addr, kb == 0);
+                mma_stage_pair_half<kKindF16>(d_tmem, a_addr, b_addr, first);
             } else if (b == kINT8) {
-              mma_stage_pair<kKindI8>(d_tmem, a_addr, b_addr, kb == 0);
+              mma_stage_pair<kKindI8>(d_tmem, a_addr, b_addr, first);
             } else if (b == kFP8) {
-              mma_stage_pair<kKindF8>(d_tmem, a_addr, b_addr, kb == 0);
+              mma_stage_pair<kKindF8>(d_tmem, a_addr, b_addr, first);
             } else {
-              mma_stage_pair<kKindF16>(d_tmem, a_addr, b_addr, kb == 0);
+              mma_stage_pair<kKindF16>(d_tmem, a_addr, b_addr, first);
             }
             tc_commit_pair_both(&empty[stage], 0x3);
           }
@@ -914,12 +1075,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         break;
       }
       if (t >= geo.total) break;
-      int pos0, n0;
-      bool half;
-      const int b = decode_tile(geo, t, kPairRows, pos0, n0, kBN, half);
+      const Unit w = decode_unit(geo, t, kPairRows, kBN, K);
+      const int b = w.b, n0 = w.n0;
+      const bool half = w.half;
       const int row = half ? static_cast<int>(rank) * 64 + (quarter & 1) * 32 + lane
                            : static_cast<int>(rank) * 128 + quarter * 32 + lane;
-      const EpiRow er = epilogue_prepare(args, geo, b, pos0 + row, n0, lane);
+      const EpiRow er = epilogue_prepare(args, geo, b, w.pos0 + row, n0, lane);
       if (!mbar_wait(&acc_full[ab], aphase, abort_flag)) {
         if (lane == 0) {
           atomicOr(&g_device_error, kErrWaitTimeout);
@@ -928,8 +1089,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      epilogue_drain(args, er, b, n0, tmem_base + ab * kBN + (static_cast<uint32_t>(quarter * 32) << 16),
-                     half ? (quarter >> 1) * 4 : 0, half ? 4 : kBN / 32);
+      const uint32_t taddr = tmem_base + ab * kBN + (static_cast<uint32_t>(quarter * 32) << 16);
+      if (w.split)  // a K range of a split tile: raw partial of this CTA's half
+        store_partial(args.part + (2 * static_cast<size_t>(t) + rank) * (kPartBlockBytes / 4), quarter, taddr,
+                      half ? 4 : kBN / 32, lane);
+      else
+        epilogue_drain(args, er, b, n0, taddr, half ? (quarter >> 1) * 4 : 0, half ? 4 : kBN / 32);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_acc_empty0 + ab * static_cast<uint32_t>(sizeof(uint64_t)));
@@ -943,6 +1108,108 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
   if (leader) feed_retire_pair(args, npairs);
+}
+
+// ---------------------------------------------------------------------------------
+// Reduction of the K-split tiles, launched after either GEMM kernel (programmatic
+// dependent launch: it starts with the grid dependency wait, so the partial blocks are
+// complete).  Block = (tile, CTA of the tile, warp quarter q), 8 warps: warp j adds the
+// ranges of output chunk j of the quarter's 32 rows (4 chunks in a half tile; with the
+// SwiGLU epilogue warp j < 4 takes gate chunk j and up chunk j + 4) in range order --
+// int32 for INT8, fp32 otherwise, so the result does not depend on timing -- and runs
+// the tile's epilogue on the sums: the same row, column and scale mapping as the GEMM
+// kernels' own epilogue.
+// ---------------------------------------------------------------------------------
+constexpr int kReduceThreads = 256;
+
+__device__ __forceinline__ void add_partial(uint32_t (&r)[32], const uint4 (&v)[8], bool as_int) {
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    const uint32_t w[4] = {v[g].x, v[g].y, v[g].z, v[g].w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      r[4 * g + k] = as_int ? static_cast<uint32_t>(static_cast<int32_t>(r[4 * g + k]) + static_cast<int32_t>(w[k]))
+                            : __float_as_uint(__uint_as_float(r[4 * g + k]) + __uint_as_float(w[k]));
+  }
+}
+
+// sum over ranges s = 0 .. S-1 of sub-block `sub` of blocks blk0 + s * stride, added in
+// range order (one range's 8 loads in flight per thread; two blocks per SM keep the
+// memory system busy)
+__device__ __forceinline__ void sum_partial_chunk(const uint32_t* part, size_t blk0, size_t stride, int S, int sub,
+                                                  int lane, bool as_int, uint32_t (&r)[32]) {
+  constexpr size_t kBlockVecs = kPartBlockBytes / 16;
+  const uint4* src = reinterpret_cast<const uint4*>(part) + blk0 * kBlockVecs + sub * (kPartSubWords / 4) + lane;
+  uint4 v[8];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) v[g] = __ldcg(src + g * 32);
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    r[4 * g] = v[g].x;
+    r[4 * g + 1] = v[g].y;
+    r[4 * g + 2] = v[g].z;
+    r[4 * g + 3] = v[g].w;
+  }
+#pragma unroll 1
+  for (int s = 1; s < S; ++s) {
+    const uint4* p = src + static_cast<size_t>(s) * stride * kBlockVecs;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) v[g] = __ldcg(p + g * 32);
+    add_partial(r, v, as_int);
+  }
+}
+
+__global__ void __launch_bounds__(kReduceThreads, 2) reduce_partials_kernel(const GemmArgs args, int bm, int ranks,
+                                                                         int half_tiles) {
+  griddep_wait();  // every partial block of the GEMM before it in the stream is written
+  griddep_launch_dependents();
+  // the GEMM's split plan (the same as planning again, without the cost)
+  int spl[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) spl[i] = __ldcg(args.split_plan + i);
+  if (spl[0] <= 1 && spl[1] <= 1 && spl[2] <= 1) return;  // every tile was written whole
+  GemmArgs base = args;
+  base.part = nullptr;  // tile geometry without planning
+  TileGeo geo = make_geo_warp(base, bm, kBN, half_tiles != 0, 0);
+#pragma unroll
+  for (int i = 0; i < 3; ++i) geo.spl[i] = spl[i] < 1 ? 1 : spl[i];
+  const int q = static_cast<int>(blockIdx.x & 3u);
+  const int rank = static_cast<int>(blockIdx.x >> 2) % ranks;
+  const int T = static_cast<int>(blockIdx.x >> 2) / ranks;
+  if (T >= geo.ntiles) return;
+  // the tile's bucket (FP16 tiles first, then FP8, then INT8), by selects
+  const int t2 = geo.tiles[2], t1 = geo.tiles[1];
+  const int b = T < t2 ? 2 : (T < t2 + t1 ? 1 : 0);
+  const int lt = b == 2 ? T : (b == 1 ? T - t2 : T - t2 - t1);
+  const int S = b == 2 ? geo.spl[2] : (b == 1 ? geo.spl[1] : geo.spl[0]);
+  if (S <= 1) return;  // written by the GEMM kernel itself
+  const int mtiles = b == 2 ? geo.mtiles[2] : (b == 1 ? geo.mtiles[1] : geo.mtiles[0]);
+  const int halfmt = b == 2 ? geo.halfmt[2] : (b == 1 ? geo.halfmt[1] : geo.halfmt[0]);
+  const int off = b == 2 ? geo.off[2] : (b == 1 ? geo.off[1] : geo.off[0]);
+  const int mt = lt % mtiles, nt = lt / mtiles;
+  const bool half = mt == halfmt;
+  const int pos0 = off + mt * bm, n0 = nt * kBN;
+  const int ubase = b == 2 ? 0 : (b == 1 ? t2 * geo.spl[2] : t2 * geo.spl[2] + t1 * geo.spl[1]);
+  const int u0 = ubase + lt * S;  // the tile's first unit
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = ranks == 2 ? (half ? rank * 64 + (q & 1) * 32 + lane : rank * 128 + q * 32 + lane) : q * 32 + lane;
+  const size_t blk0 = static_cast<size_t>(u0) * ranks + rank;
+  const bool as_int = b == kINT8;
+  if (args.out_mode == 2) {
+    if (warp >= 4) return;
+    const EpiRow er = epilogue_prepare(args, geo, b, pos0 + row, n0, lane);
+    uint32_t rg[32], ru[32];
+    sum_partial_chunk(args.part, blk0, ranks, S, q * 8 + warp, lane, as_int, rg);
+    sum_partial_chunk(args.part, blk0, ranks, S, q * 8 + warp + 4, lane, as_int, ru);
+    swiglu_chunk(args, er, b, n0, warp, rg, ru);
+    return;
+  }
+  const int nchunks = half ? 4 : kBN / 32;
+  if (warp >= nchunks) return;
+  const EpiRow er = epilogue_prepare(args, geo, b, pos0 + row, n0, lane);
+  uint32_t r[32];
+  sum_partial_chunk(args.part, blk0, ranks, S, q * 8 + warp, lane, as_int, r);
+  epilogue_chunk(args, er, b, n0, (half ? (q >> 1) * 4 : 0) + warp, r);
 }
 
 }  // namespace ee

@@ -102,7 +102,20 @@ struct GemmArgs {
                            // 2: SwiGLU of gate / up rows interleaved by 128 (fp16 [rows, N/2])
   uint32_t* sched;         // nullable: [0] next tile, [1] CTAs done -- zero at launch, left zero;
                            // null = static round-robin tile order
+  // K-split of the tiles (part == null: every tile whole).  The kernel splits the K loop
+  // of a tile into up to kMaxKSplits ranges (the same choice in every CTA, from the
+  // bucket counts, K and split_slots), each range's raw accumulator goes to one partial
+  // block, and reduce_partials_kernel adds a split tile's blocks in range order and runs
+  // its epilogue.
+  uint32_t* part;          // part_blocks blocks of kPartBlockBytes (int32 / fp32 partials)
+  int part_blocks;
+  int split_slots;         // CTAs (single-CTA kernel) or CTA pairs of the launch
+  int32_t* split_plan;     // [3] ranges per tile of each bucket, written by the GEMM's first
+                           // CTA for the reduction kernel (with part)
 };
+constexpr int kPartBlockBytes = 128 * 256 * 4;  // one CTA's 128 x 256 accumulator
+constexpr int kMaxKSplits = 16;
+constexpr int kSplitMinKBlocks = 8;             // fewest K stages of one split range
 struct GemmMaps {
   CUtensorMap a8;          // uint8 [M_cap, K], box {128, 128}
   CUtensorMap a16;         // fp16  [M_cap, K], box {64, 128}
@@ -113,6 +126,10 @@ struct GemmMaps {
 int launch_gated_gemm(const GemmMaps& maps, const GemmArgs& args, int grid, int bn, cudaStream_t s);
 // CTA-pair kernel: 256-row tiles; grid = 2 x pairs; the A / W maps use 128-row boxes
 int launch_gated_gemm_pair(const GemmMaps& maps, const GemmArgs& args, int pairs, cudaStream_t s);
+// the K-split tiles' reduction and epilogue after either kernel (args.part != null):
+// one 256-thread block per (tile, CTA of the tile, 32-row quarter); tiles = an upper
+// bound of the call's tiles
+int launch_reduce_partials(const GemmArgs& args, bool pair, int64_t tiles, cudaStream_t s);
 constexpr int kPairTileRows = 256;
 // weight-streaming kernel for at most 128 rows (ee_gemm_skinny.cuh): 128-channel tiles,
 // nb = activation rows per tile (16, 32, 64 or 128, >= the rows of every bucket), K split

@@ -265,6 +265,14 @@ int launch_gated_gemm(const GemmMaps& m, const GemmArgs& args, int grid, int bn,
                     m.w[0], m.w[1], m.w[2], args);
 }
 
+int launch_reduce_partials(const GemmArgs& args, bool pair, int64_t tiles, cudaStream_t s) {
+  if (args.part == nullptr || tiles <= 0) return 0;
+  const int ranks = pair ? 2 : 1;
+  const dim3 grid(static_cast<unsigned>(tiles * ranks * 4));
+  return launch_pdl(reduce_partials_kernel, grid, dim3(kReduceThreads), 0, s, args, pair ? kPairRows : kBM, ranks,
+                    (pair && args.out_mode != 2) ? 1 : 0);
+}
+
 int launch_gated_gemm_skinny(const GemmMaps& m, const GemmArgs& args, int nb, int splits, cudaStream_t s) {
   if (prepare_device() != 0) return -4;
   if (splits < 1 || splits > kSkinnyMaxSplits) return -1;

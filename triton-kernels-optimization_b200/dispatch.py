@@ -129,11 +129,17 @@ class EntropyRouter:
     into the workspace, valid until the next ``route``.  ``H``, ``route_ids`` and
     ``counts`` are filled by ``route``; ``perm`` (position -> row) by the first
     ``pack_rows`` / ``gated_linear`` after it, which places the rows.
+
+    ``k_split`` (default on) sizes the workspace with room for K-split partial sums
+    (``ee_gated_workspace_split_bytes``: about 0.5 MiB per SM for more than 64 rows), so
+    GEMMs with few tiles for the SMs split their K loops: INT8 outputs bit-identical,
+    FP8 / FP16 within the last bits of the unsplit run.
     """
 
-    def __init__(self, tau_low: float = 0.41, tau_high: float = 1.68):
+    def __init__(self, tau_low: float = 0.41, tau_high: float = 1.68, k_split: bool = True):
         self.tau_low = float(tau_low)
         self.tau_high = float(tau_high)
+        self.k_split = bool(k_split)
         self.M = 0
         self._ws: Optional[torch.Tensor] = None
         self._ws_k = 16
@@ -145,7 +151,8 @@ class EntropyRouter:
     def reserve(self, M: int, K: int, device) -> None:
         """Size the workspace for M rows and activations up to width K."""
         self._ws_k = max(self._ws_k, int(K))
-        need = _lib.load().ee_gated_workspace_bytes(M, self._ws_k)
+        lib = _lib.load()
+        need = (lib.ee_gated_workspace_split_bytes if self.k_split else lib.ee_gated_workspace_bytes)(M, self._ws_k)
         device = torch.device(device)
         if self._ws is None or self._ws.numel() < need or self._ws.device != device:
             self._ws = torch.empty(need, dtype=torch.uint8, device=device)
