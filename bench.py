@@ -574,6 +574,50 @@ def main(argv=None) -> int:
         router.route(logits)  # the step's routing again
         torch.cuda.synchronize()
 
+    # the same at the row count a GPU routes in config 5 (16384 tokens): router + bucket
+    # scan, and the router kernel alone (entropy + route id per row, no scan), over three
+    # logits buffers of 134 MB each
+    gate_rows_16k = None
+    if rank == 0:
+        M16 = 16384
+        g16 = torch.Generator(device=dev).manual_seed(16)
+        lg16 = [(torch.randn(M16, N_LOGIT, generator=g16, device=dev) * float(logits.float().std())).half()
+                for _ in range(3)]
+        r16 = pkg.EntropyRouter(*TAU, k_split=False)
+        r16.reserve(M16, 64, dev)
+
+        def stream_us(fn):
+            for x in lg16:
+                fn(x)
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                for _ in range(4):
+                    for x in lg16:
+                        fn(x)
+            gr.replay()
+            torch.cuda.synchronize()
+            tt = []
+            for _ in range(5):
+                flush()
+                a, b = E(), E()
+                a.record()
+                gr.replay()
+                b.record()
+                b.synchronize()
+                tt.append(a.elapsed_time(b) * 1e3 / (4 * len(lg16)))
+            del gr
+            return statistics.median(tt)
+
+        us_route = stream_us(r16.route)
+        us_rows = stream_us(lambda x: pkg.softmax_entropy_rows(x, want_probs=False, tau_low=TAU[0], tau_high=TAU[1]))
+        b16 = 2.0 * M16 * N_LOGIT + 5 * M16
+        gate_rows_16k = {"rows": M16, "us_per_call": us_route, "gbs": b16 / us_route / 1e3,
+                         "frac": b16 / us_route / 1e3 / peaks["hbm_gbs"],
+                         "router_kernel_only": {"us_per_call": us_rows, "gbs": b16 / us_rows / 1e3,
+                                                "frac": b16 / us_rows / 1e3 / peaks["hbm_gbs"]}}
+        del lg16, r16
+
     # ------------------------------------------------------------------ e2e (public API, host buffers)
     # Every step copies its inputs from pinned host memory, runs the public API
     # (EntropyRouter.route + gated_linear per projection) and copies every output back.
@@ -678,12 +722,15 @@ def main(argv=None) -> int:
             "softmax_entropy": {"gbs": gate_bytes / gate_stream_us / 1e3,
                                 "frac": gate_bytes / gate_stream_us / 1e3 / peaks["hbm_gbs"],
                                 "us_per_call": gate_stream_us, "bytes_per_call": gate_bytes,
+                                "at_16384_rows": gate_rows_16k,
                                 "gbs_single_call_eager": gate_gbs,
                                 "us_single_call_eager": 1e3 * sum(gate_ms) / len(gate_ms),
                                 "note": "router (entropy + route per row) and its bucket scan; algorithmic bytes "
                                         "2Mn + 4M + M; gbs from back-to-back calls replayed from a CUDA graph over "
                                         "8 logits buffers (above L2), the eager single call (events around it, "
-                                        "after an L2 flush) beside it"} if gate_stream_us else None,
+                                        "after an L2 flush) beside it; at_16384_rows: the same at config 5's "
+                                        "rows per GPU, with the router kernel alone (no bucket scan) beside it"}
+            if gate_stream_us else None,
             "per_projection_tflops": {
                 name: 2.0 * M * K * N * n_instr / (sum(g[p] for g in gemm_ms) / 1e3) / 1e12
                 for p, (name, K, N) in enumerate(PROJECTIONS)},

@@ -1,12 +1,18 @@
 """Runs one small case of the gated path a few times, for kernel captures with ncu.
 
-Each repetition launches, in order: the router (softmax + entropy + route +
-compaction) over logits [rows, 4096], the row packing of A [rows, K] and the gated
-GEMM against a [N, K] weight.  Inputs follow bench.py's laws (route mix about
-24 / 55 / 21 %); device footprint is about 4*N*K + 5*rows*K + 2*rows*N bytes.
+--case gated (default): each repetition launches, in order, the router (softmax +
+entropy + route + bucket scan) over logits [rows, 4096], the row packing of A [rows, K]
+and the gated GEMM against a [N, K] weight (the router's workspace has room for K-split
+partials, as EntropyRouter sizes it by default).  Inputs follow bench.py's laws (route
+mix about 24 / 55 / 21 %); device footprint is about 4*N*K + 5*rows*K + 2*rows*N bytes
+(+ 77 MB of split room above 64 rows).
+
+--case attention: each repetition runs flash_attention_entropy (causal, output and
+per-row entropy) on q [B, Hq, S, D], k / v [B, Hkv, S, D].
 
     python triton-kernels-optimization_b200/profile_case.py --rows 2048 --K 4096 --N 14336 --reps 4
     ncu --set full --clock-control none -k regex:gated_gemm -s 3 -c 1 -o prof <same command>
+    python triton-kernels-optimization_b200/profile_case.py --case attention --B 1 --Hq 32 --Hkv 4 --S 2048 --D 64
 """
 from __future__ import annotations
 
@@ -27,6 +33,12 @@ def main(argv=None) -> int:
     ap.add_argument("--N", type=int, default=14336)
     ap.add_argument("--n-logits", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=4)
+    ap.add_argument("--case", choices=("gated", "attention"), default="gated")
+    ap.add_argument("--B", type=int, default=1)
+    ap.add_argument("--Hq", type=int, default=32)
+    ap.add_argument("--Hkv", type=int, default=4)
+    ap.add_argument("--S", type=int, default=2048)
+    ap.add_argument("--D", type=int, default=64)
     args = ap.parse_args(argv)
 
     import torch
@@ -36,6 +48,16 @@ def main(argv=None) -> int:
     pkg = ge.load_package()
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev).manual_seed(7)
+    if args.case == "attention":
+        q = torch.randn(args.B, args.Hq, args.S, args.D, generator=g, device=dev).half()
+        k = torch.randn(args.B, args.Hkv, args.S, args.D, generator=g, device=dev).half()
+        v = torch.randn(args.B, args.Hkv, args.S, args.D, generator=g, device=dev).half()
+        for _ in range(args.reps):
+            out, hb = pkg.flash_attention_entropy(q, k, v, causal=True)
+        torch.cuda.synchronize()
+        pkg._lib.device_check()
+        print("attention", tuple(q.shape), "kv", tuple(k.shape), "batch entropy", hb.cpu().tolist())
+        return 0
     M, K, N = args.rows, args.K, args.N
     s = torch.exp(torch.rand(M, 1, generator=g, device=dev) * (math.log(9.5) - math.log(7.0)) + math.log(7.0))
     logits = (torch.randn(M, args.n_logits, generator=g, device=dev) * s).half()
