@@ -8,8 +8,9 @@
 //              head_dim 64, 64 for 128) into 2-deep rings;
 //   warp 1     TMEM owner + single-thread UMMA issuer: S_w = Q_w K_j^T (M 128, N KT) into
 //              the S buffer of query tile w, O_w += P_w V_j (M 128, N d) into the O
-//              accumulator of tile w, interleaved S_0 S_1 | P_0V S_0' P_1V S_1' | ... so the
-//              tensor core works for one warpgroup while the other runs its softmax;
+//              accumulator of tile w, in the order S_0 S_1 | S_0' S_1' P_0V P_1V | ...: the
+//              next S of a warpgroup is issued as soon as its softmax holds the current
+//              one in registers, so it runs under that softmax's exponentials;
 //   warps 2-3  idle (they complete the producer warpgroup, which hands its registers to
 //              the softmax warpgroups);
 //   warps 4-11 warpgroup w = query tile w, one whole row per thread: scores from TMEM into
@@ -44,6 +45,12 @@ constexpr int kAttnSoftmaxRegs = 200;
 static_assert(kAttnProducerRegs + 2 * kAttnSoftmaxRegs <= 3 * kAttnLaunchRegs, "register split above the launch budget");
 constexpr int kAttnTileBytes = kAttnTile * 128;  // one 128-byte-wide swizzled box of 128 rows: 16 KB
 
+#ifndef EE_ATTN_STAGES64
+#define EE_ATTN_STAGES64 2
+#endif
+#ifndef EE_ATTN_STAGES128
+#define EE_ATTN_STAGES128 2
+#endif
 template <int D>
 struct AttnCfg {
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
@@ -54,7 +61,7 @@ struct AttnCfg {
   static constexpr int kKBytes = kKBlocks * KT * 128;          // one K tile: KT rows x D
   static constexpr int kVBytes = kVBlocks * D * 128;           // one V^T tile: D rows x KT keys
   static constexpr int kPBytes = kVBlocks * kAttnTileBytes;    // one P tile: 128 rows x KT keys
-  static constexpr int kStages = 2;                            // K / V ring depth
+  static constexpr int kStages = D == 64 ? EE_ATTN_STAGES64 : EE_ATTN_STAGES128;  // K / V ring depth
   static constexpr int kBarrierBytes = 256;
   static constexpr size_t kSmem = 1024 + 2 * size_t(kQTileBytes) + kStages * size_t(kKBytes + kVBytes) +
                                   2 * size_t(kPBytes) + kBarrierBytes;
@@ -92,6 +99,17 @@ __device__ __forceinline__ uint32_t pack_half2_rn(float lo, float hi) {
   return r;
 }
 
+// fp16(fp32(fp16(s)) * scale) for two raw fp32 scores when the scale is an fp16 number
+// (head_dim 64: 1/8): the fp32 product of two
+// fp16 numbers is exact, so its fp16 rounding is the correctly rounded fp16 product --
+// one mul.rn.f16x2 (no flush to zero: fp16 subnormals round as in the fp32 path)
+__device__ __forceinline__ __half2 scaled_scores_f16(uint32_t s0, uint32_t s1, uint32_t sch2) {
+  const uint32_t h = pack_half2_rn(__uint_as_float(s0), __uint_as_float(s1));
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(h), "r"(sch2));
+  return *reinterpret_cast<const __half2*>(&r);
+}
+
 // fp16(fp32(fp16(s)) * scale) for two raw fp32 scores: the rounding of an fp16 matmul
 // output, then the fp16 tensor times a Python float (computed in fp32, rounded to fp16)
 __device__ __forceinline__ __half2 scaled_scores(uint32_t s0, uint32_t s1, float2 sc2) {
@@ -122,16 +140,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sP = sV + Cfg::kStages * Cfg::kVBytes;       // [2 warpgroups]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * Cfg::kPBytes);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;    // [kStages]
-  uint64_t* k_empty = bars + 3;   // [kStages]
-  uint64_t* v_full = bars + 5;    // [kStages]
-  uint64_t* v_empty = bars + 7;   // [kStages]
-  uint64_t* s_full = bars + 9;    // [2 warpgroups] S_w ready (MMA commit)
-  uint64_t* s_free = bars + 11;   // [2] S_w read into registers (4 warps)
-  uint64_t* p_full = bars + 13;   // [2] P_w written, O_w corrected (4 warps)
-  uint64_t* o_done = bars + 15;   // [2] P_w V done: P_w free, O_w stable (MMA commit)
-  uint64_t* drain = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  constexpr int NS = Cfg::kStages;
+  uint64_t* k_full = bars + 1;            // [kStages]
+  uint64_t* k_empty = bars + 1 + NS;      // [kStages]
+  uint64_t* v_full = bars + 1 + 2 * NS;   // [kStages]
+  uint64_t* v_empty = bars + 1 + 3 * NS;  // [kStages]
+  uint64_t* s_full = bars + 1 + 4 * NS;   // [2 warpgroups] S_w ready (MMA commit)
+  uint64_t* s_free = s_full + 2;          // [2] S_w read into registers (4 warps)
+  uint64_t* p_full = s_full + 4;          // [2] P_w written, O_w corrected (4 warps)
+  uint64_t* o_done = s_full + 6;          // [2] P_w V done: P_w free, O_w stable (MMA commit)
+  uint64_t* drain = s_full + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 9);
+  static_assert((1 + 4 * NS + 9) * 8 + 8 <= Cfg::kBarrierBytes, "attention barrier region overflows");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -155,11 +175,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 4);  // the four warps of the warpgroup
       mbar_init(&p_full[i], 4);
@@ -200,8 +222,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tma_load_2d(sQ + t * Cfg::kQTileBytes + kb * kAttnTileBytes, &tm_q, q_full, kb * 64, q_row0 + t * kAttnTile);
     }
     for (int j = 0; j < nkv_max && !failed; ++j) {
-      const int s = j & 1;
-      const uint32_t ph = static_cast<uint32_t>(j >> 1) & 1u;
+      const int s = j % NS;
+      const uint32_t ph = static_cast<uint32_t>(j / NS) & 1u;
       if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag)) {
         failed = true;
         break;
@@ -233,7 +255,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       // let the loads already issued land before the CTA can exit (bounded, no abort)
       (void)mbar_wait(q_full, 0u, nullptr);
-      for (int s = 0; s < 2; ++s) {
+      for (int s = 0; s < NS; ++s) {
         if (k_issued & (1u << s)) (void)mbar_wait(&k_full[s], (k_par >> s) & 1u, nullptr);
         if (v_issued & (1u << s)) (void)mbar_wait(&v_full[s], (v_par >> s) & 1u, nullptr);
       }
@@ -248,8 +270,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     bool failed = !mbar_wait(q_full, 0u, abort_flag);
     tc_fence_after();
     auto issue_s = [&](int w, int j) -> bool {
-      const int s = j & 1;
-      if (!mbar_wait(&k_full[s], static_cast<uint32_t>(j >> 1) & 1u, abort_flag) ||
+      const int s = j % NS;
+      if (!mbar_wait(&k_full[s], static_cast<uint32_t>(j / NS) & 1u, abort_flag) ||
           !mbar_wait(&s_free[w], (static_cast<uint32_t>(j) & 1u) ^ 1u, abort_flag))
         return false;
       tc_fence_after();
@@ -268,8 +290,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       return true;
     };
     auto issue_pv = [&](int w, int j) -> bool {
-      const int s = j & 1;
-      if (!mbar_wait(&v_full[s], static_cast<uint32_t>(j >> 1) & 1u, abort_flag) ||
+      const int s = j % NS;
+      if (!mbar_wait(&v_full[s], static_cast<uint32_t>(j / NS) & 1u, abort_flag) ||
           !mbar_wait(&p_full[w], static_cast<uint32_t>(j) & 1u, abort_flag))
         return false;
       tc_fence_after();
@@ -292,16 +314,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (!failed && lane == 0) tc_commit(&k_empty[0]);
     __syncwarp();
     for (int j = 0; j < nkv_max && !failed; ++j) {
-      if (j < nkv0 && !issue_pv(0, j)) failed = true;
-      if (!failed && j + 1 < nkv0 && !issue_s(0, j + 1)) failed = true;
-      if (!failed && !issue_pv(1, j)) failed = true;
-      if (!failed && lane == 0) tc_commit(&v_empty[j & 1]);  // both P V of tile j issued
-      __syncwarp();
+      // the next S of each warpgroup first: its TMEM columns are free as soon as the
+      // softmax holds S_j in registers (s_free), so it runs under this tile's
+      // exponentials instead of after them
+      if (j + 1 < nkv0 && !issue_s(0, j + 1)) failed = true;
       if (!failed && j + 1 < nkv1) {
         if (!issue_s(1, j + 1)) failed = true;
-        if (!failed && lane == 0) tc_commit(&k_empty[(j + 1) & 1]);  // both S of tile j + 1 issued
+        if (!failed && lane == 0) tc_commit(&k_empty[(j + 1) % NS]);  // both S of tile j + 1 issued
         __syncwarp();
       }
+      if (!failed && j < nkv0 && !issue_pv(0, j)) failed = true;
+      if (!failed && !issue_pv(1, j)) failed = true;
+      if (!failed && lane == 0) tc_commit(&v_empty[j % NS]);  // both P V of tile j issued
+      __syncwarp();
     }
     if (failed) {
       if (lane == 0) {
@@ -333,6 +358,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     constexpr float kLog2eF = 1.4426950408889634f;
     constexpr float kRescale = 8.f;  // log2 of the largest p allowed before m moves
     const float2 sc2 = make_float2(args.scale, args.scale);
+    const __half sch = __float2half_rn(args.scale);
+    const bool scale_is_f16 = __half2float(sch) == args.scale;  // uniform for the kernel
+    const uint32_t sch2 = static_cast<uint32_t>(__half_as_ushort(sch)) * 0x10001u;
     uint8_t* pbuf = sP + w * Cfg::kPBytes;
     float m2 = -__builtin_huge_valf(), l = 0.f, t2 = 0.f;
     bool failed = false;
@@ -361,10 +389,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_ld32(t_s + c0 + 32, rb);
         tmem_ld_wait(ra);
         regs_after_wait(rb);
+        if (scale_is_f16) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          xs[c0 / 2 + i] = scaled_scores(ra[2 * i], ra[2 * i + 1], sc2);
-          xs[c0 / 2 + 16 + i] = scaled_scores(rb[2 * i], rb[2 * i + 1], sc2);
+          for (int i = 0; i < 16; ++i) {
+            xs[c0 / 2 + i] = scaled_scores_f16(ra[2 * i], ra[2 * i + 1], sch2);
+            xs[c0 / 2 + 16 + i] = scaled_scores_f16(rb[2 * i], rb[2 * i + 1], sch2);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            xs[c0 / 2 + i] = scaled_scores(ra[2 * i], ra[2 * i + 1], sc2);
+            xs[c0 / 2 + 16 + i] = scaled_scores(rb[2 * i], rb[2 * i + 1], sc2);
+          }
         }
       }
       tc_fence_before();
