@@ -266,7 +266,8 @@ EE_API int ee_linear_int8_noalloc(const void* A, int64_t lda, const int8_t* W_nk
  * partials in range order in a second kernel: INT8 results bit-identical to the unsplit
  * run, FP8 / FP16 within the last bits (deterministic).  ee_gated_workspace_split_bytes
  * (M, K) is the recommended size (the base plus four 128 KiB partial blocks per SM;
- * just the base for M <= 64, where the weight-streaming kernel splits K itself). */
+ * just the base for M <= 64, where the weight-streaming kernel splits K itself, and for
+ * M > 4096, where the tiles already fill the SMs). */
 EE_API size_t ee_gated_workspace_bytes(int64_t M, int64_t K);
 EE_API size_t ee_gated_workspace_split_bytes(int64_t M, int64_t K);
 EE_API int ee_gate_rows(const void* logits, int64_t M, int64_t n, int64_t ld, double tau_low, double tau_high, float* H,

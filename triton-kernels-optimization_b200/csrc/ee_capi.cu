@@ -333,8 +333,10 @@ void attach_split_area(ee::GemmArgs& args, void* ws, size_t ws_bytes, int64_t M,
 
 // recommended room for the K-split partials: four blocks per SM (a split plan can run up
 // to four ranges per CTA of the launch); none for calls the weight-streaming kernel takes
+// and none above 4096 rows, where the tiles of any projection of useful width already
+// fill the SMs (the host never splits there)
 size_t split_area_bytes(int64_t M) {
-  if (M <= ee::kSkinnyAutoRows) return 0;
+  if (M <= ee::kSkinnyAutoRows || M > 4096) return 0;
   return 256 + size_t(4) * size_t(num_sms()) * size_t(ee::kPartBlockBytes);
 }
 
