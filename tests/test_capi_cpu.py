@@ -88,6 +88,17 @@ def test_workspace_checks(pkg, lib):
     assert lib.ee_linear_workspace_bytes(-1, 5) == 0
 
 
+def test_split_workspace_sizing(pkg, lib):
+    """K-split room: none at <= 64 rows (the weight-streaming kernel) and above 4096 rows;
+    otherwise 256 bytes of plan + four 128 KiB partial blocks per SM (148 without a GPU)."""
+    for M, K in [(16, 4096), (64, 14336), (5000, 4096), (16384, 2048)]:
+        assert lib.ee_gated_workspace_split_bytes(M, K) == lib.ee_gated_workspace_bytes(M, K)
+    for M, K in [(65, 4096), (128, 14336), (1024, 4096), (4096, 14336)]:
+        extra = lib.ee_gated_workspace_split_bytes(M, K) - lib.ee_gated_workspace_bytes(M, K)
+        assert extra == 256 + 4 * 148 * 128 * 256 * 4
+    assert lib.ee_gated_workspace_split_bytes(-1, 8) == 0
+
+
 def test_workspace_layout_offsets(pkg, lib):
     off = (ctypes.c_int64 * 8)()
     assert lib.ee_gated_workspace_layout(1000, 512, off) == 0

@@ -140,6 +140,29 @@ int64_t row_tiles(const ee::GemmArgs& args, bool dynamic_counts, int64_t bm) {
   return t;
 }
 
+// K split allowed for a call whose whole 256-column tiles number `tiles` on `slots`
+// CTAs (pairs): long K loops, tiles for at most 3/4 of the slots (measured on B200:
+// splitting pays for K >= 8192; at K = 4096 the unsplit tiles are as fast, and where the
+// device plans no split the reduction launch alone costs ~5 us)
+bool split_eligible(const ee::GemmArgs& args, int64_t tiles, int64_t slots) {
+  return args.part != nullptr && args.K >= 8192 && 4 * tiles <= 3 * slots;
+}
+
+// Automatic policy between 129 and 512 rows: single-CTA 128 x 256 tiles instead of CTA
+// pairs when they need fewer rounds of the persistent grid, or when only they qualify
+// for the K split (measured on B200 with 20/60/20 routing, back-to-back calls: 256 rows
+// x N 14336 49 us against 58, 512 rows x K 14336 69 us against 82; pairs stay ahead or
+// equal on the other Llama-3-8B shapes and above 512 rows).
+bool single_beats_pairs(const ee::GemmArgs& args, bool dynamic_counts) {
+  if (args.M_cap > 512) return false;
+  const int64_t ntn = (args.N + ee::kBN - 1) / ee::kBN;
+  const int64_t st = row_tiles(args, dynamic_counts, ee::kBM) * ntn;
+  const int64_t pt = row_tiles(args, dynamic_counts, ee::kPairTileRows) * ntn;
+  const int64_t sms = num_sms(), pairs = num_sms() / 2;
+  const int64_t s_rounds = (st + sms - 1) / sms, p_rounds = (pt + pairs - 1) / pairs;
+  return s_rounds < p_rounds || (split_eligible(args, st, sms) && !split_eligible(args, pt, pairs));
+}
+
 // Encodes the maps for the operands present and launches the persistent kernel.  Auto
 // policy: more than 128 rows -> the CTA-pair kernel (256 x 256 tiles); at most 128 rows
 // the call streams its weights -> single-CTA tiles, 128 x 256 when their count already
@@ -181,24 +204,21 @@ int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cud
                         "gated_gemm_skinny_kernel");
   }
   const int64_t wide_tiles = row_tiles(args, dynamic_counts, ee::kBM) * ((args.N + ee::kBN - 1) / ee::kBN);
-  const bool pair = policy == 2 || (policy == 0 && args.M_cap > ee::kBM);
-  // K split: with partial storage, 256-column tiles, when the call has at most two tiles
-  // per CTA (pair) of the launch -- the device then plans the ranges from the bucket counts
+  const bool pair = policy == 2 || (policy == 0 && args.M_cap > ee::kBM && !single_beats_pairs(args, dynamic_counts));
+  // K split (split_eligible): 256-column tiles, the device then plans the ranges from the
+  // bucket counts
   const int64_t slots = pair ? num_sms() / 2 : num_sms();
   const int64_t split_tiles = pair ? row_tiles(args, dynamic_counts, ee::kPairTileRows) * ((args.N + ee::kBN - 1) / ee::kBN)
                                    : wide_tiles;
-  // (measured on B200: splitting pays for long K loops -- K >= 8192 -- with whole tiles
-  // for at most 3/4 of the slots; at K = 4096 the 128 x 64 tiles or the unsplit pairs are
-  // as fast, and where the device plans no split the reduction launch alone costs ~5 us)
-  const bool split = args.part != nullptr && policy != 3 && args.K >= 8192 && 4 * split_tiles <= 3 * slots;
+  const bool split = policy != 3 && split_eligible(args, split_tiles, slots);
   if (!split) {
     args.part = nullptr;
     args.part_blocks = 0;
     args.split_plan = nullptr;
   }
   // the SwiGLU epilogue pairs 128-column groups inside a 256-column tile
-  const bool narrow =
-      !split && args.out_mode != 2 && (policy == 3 || (policy == 0 && !pair && wide_tiles < num_sms()));
+  const bool narrow = !split && args.out_mode != 2 &&
+                      (policy == 3 || (policy == 0 && !pair && args.M_cap <= ee::kBM && wide_tiles < num_sms()));
   const int bn = narrow ? ee::kBNNarrow : ee::kBN;
   const int wbox = pair ? ee::kBN / 2 : bn;
   ee::GemmMaps maps;
