@@ -4,8 +4,8 @@
 // computes -sum p log(p + 1e-10) in torch, EE/python/dispatch.py:236-245).
 //
 // One CTA per (batch, query head, 256 query rows = two 128-row query tiles), 384 threads:
-//   warp 0     TMA producer: both Q tiles once, then K and V^T tiles of KT keys (128 for
-//              head_dim 64, 64 for 128) into 2-deep rings;
+//   warp 0     TMA producer: both Q tiles once, then K and V^T tiles of 128 keys into
+//              rings (K 2 deep; V 2 deep at head_dim 64, 1 at 128);
 //   warp 1     TMEM owner + single-thread UMMA issuer: S_w = Q_w K_j^T (M 128, N KT) into
 //              the S buffer of query tile w, O_w += P_w V_j (M 128, N d) into the O
 //              accumulator of tile w, in the order S_0 S_1 | S_0' S_1' P_0V P_1V | ...: the
@@ -38,33 +38,31 @@ namespace ee {
 
 constexpr int kAttnThreads = 384;  // producer warpgroup (TMA, MMA, two idle warps), two softmax warpgroups
 // registers per thread: 168 at launch (384 threads, one CTA per SM); the producer
-// warpgroup gives its share to the softmax warpgroups (96 + 2 x 200 <= 3 x 168)
+// warpgroup gives its share to the softmax warpgroups (104 + 2 x 200 <= 3 x 168)
 constexpr int kAttnLaunchRegs = 168;
-constexpr int kAttnProducerRegs = 96;
+constexpr int kAttnProducerRegs = 104;
 constexpr int kAttnSoftmaxRegs = 200;
 static_assert(kAttnProducerRegs + 2 * kAttnSoftmaxRegs <= 3 * kAttnLaunchRegs, "register split above the launch budget");
 constexpr int kAttnTileBytes = kAttnTile * 128;  // one 128-byte-wide swizzled box of 128 rows: 16 KB
 
-#ifndef EE_ATTN_STAGES64
-#define EE_ATTN_STAGES64 2
-#endif
-#ifndef EE_ATTN_STAGES128
-#define EE_ATTN_STAGES128 2
-#endif
 template <int D>
 struct AttnCfg {
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
-  static constexpr int KT = D == 64 ? 128 : 64;                // keys per K / V tile
+  // keys per K / V tile: 128 for both head dims (a tcgen05.mma costs about the same
+  // whatever its N, so the S MMA is made as wide as TMEM allows: 2 x (128 S + D O) columns)
+  static constexpr int KT = 128;
   static constexpr int kKBlocks = D / 64;                      // 128-byte column blocks of Q / K rows
   static constexpr int kVBlocks = KT / 64;                     // 128-byte column blocks of V^T rows (keys)
   static constexpr int kQTileBytes = kKBlocks * kAttnTileBytes;  // one 128-row Q tile
   static constexpr int kKBytes = kKBlocks * KT * 128;          // one K tile: KT rows x D
   static constexpr int kVBytes = kVBlocks * D * 128;           // one V^T tile: D rows x KT keys
   static constexpr int kPBytes = kVBlocks * kAttnTileBytes;    // one P tile: 128 rows x KT keys
-  static constexpr int kStages = D == 64 ? EE_ATTN_STAGES64 : EE_ATTN_STAGES128;  // K / V ring depth
+  // ring depths: K 2, V 2 at head_dim 64; K 2, V 1 at 128 (shared memory: 230.7 KB)
+  static constexpr int kKStages = 2;
+  static constexpr int kVStages = D == 64 ? 2 : 1;
   static constexpr int kBarrierBytes = 256;
-  static constexpr size_t kSmem = 1024 + 2 * size_t(kQTileBytes) + kStages * size_t(kKBytes + kVBytes) +
-                                  2 * size_t(kPBytes) + kBarrierBytes;
+  static constexpr size_t kSmem = 1024 + 2 * size_t(kQTileBytes) + kKStages * size_t(kKBytes) +
+                                  kVStages * size_t(kVBytes) + 2 * size_t(kPBytes) + kBarrierBytes;
   static_assert(kSmem <= 227 * 1024, "attention shared memory above the 227 KB per-CTA limit");
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kTmemS = 0;        // S of warpgroup w: columns [w KT, (w + 1) KT)
@@ -135,23 +133,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                   // [2 query tiles]
-  uint8_t* sK = sQ + 2 * Cfg::kQTileBytes;              // [kStages]
-  uint8_t* sV = sK + Cfg::kStages * Cfg::kKBytes;       // [kStages]
-  uint8_t* sP = sV + Cfg::kStages * Cfg::kVBytes;       // [2 warpgroups]
+  uint8_t* sK = sQ + 2 * Cfg::kQTileBytes;              // [kKStages]
+  uint8_t* sV = sK + Cfg::kKStages * Cfg::kKBytes;      // [kVStages]
+  uint8_t* sP = sV + Cfg::kVStages * Cfg::kVBytes;      // [2 warpgroups]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * Cfg::kPBytes);
   uint64_t* q_full = bars;
-  constexpr int NS = Cfg::kStages;
-  uint64_t* k_full = bars + 1;            // [kStages]
-  uint64_t* k_empty = bars + 1 + NS;      // [kStages]
-  uint64_t* v_full = bars + 1 + 2 * NS;   // [kStages]
-  uint64_t* v_empty = bars + 1 + 3 * NS;  // [kStages]
-  uint64_t* s_full = bars + 1 + 4 * NS;   // [2 warpgroups] S_w ready (MMA commit)
+  constexpr int NS = Cfg::kKStages, NV = Cfg::kVStages;
+  uint64_t* k_full = bars + 1;                 // [kKStages]
+  uint64_t* k_empty = bars + 1 + NS;           // [kKStages]
+  uint64_t* v_full = bars + 1 + 2 * NS;        // [kVStages]
+  uint64_t* v_empty = bars + 1 + 2 * NS + NV;  // [kVStages]
+  uint64_t* s_full = bars + 1 + 2 * NS + 2 * NV;  // [2 warpgroups] S_w ready (MMA commit)
   uint64_t* s_free = s_full + 2;          // [2] S_w read into registers (4 warps)
   uint64_t* p_full = s_full + 4;          // [2] P_w written, O_w corrected (4 warps)
   uint64_t* o_done = s_full + 6;          // [2] P_w V done: P_w free, O_w stable (MMA commit)
   uint64_t* drain = s_full + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 9);
-  static_assert((1 + 4 * NS + 9) * 8 + 8 <= Cfg::kBarrierBytes, "attention barrier region overflows");
+  static_assert((1 + 2 * NS + 2 * NV + 9) * 8 + 8 <= Cfg::kBarrierBytes, "attention barrier region overflows");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -178,6 +176,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int i = 0; i < NS; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < NV; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
@@ -221,13 +221,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int kb = 0; kb < Cfg::kKBlocks; ++kb)
           tma_load_2d(sQ + t * Cfg::kQTileBytes + kb * kAttnTileBytes, &tm_q, q_full, kb * 64, q_row0 + t * kAttnTile);
     }
-    for (int j = 0; j < nkv_max && !failed; ++j) {
+    // K runs one tile ahead of V: S_{j+1} is issued (as soon as the softmax holds S_j)
+    // before P V_j (once P_j is written)
+    auto load_k = [&](int j) -> bool {
       const int s = j % NS;
       const uint32_t ph = static_cast<uint32_t>(j / NS) & 1u;
-      if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag)) {
-        failed = true;
-        break;
-      }
+      if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag)) return false;
       if (lane == 0) {
         mbar_arrive_expect_tx(&k_full[s], Cfg::kKBytes);
         for (int kb = 0; kb < Cfg::kKBlocks; ++kb)
@@ -235,18 +234,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       k_issued |= 1u << s;
       k_par = (k_par & ~(1u << s)) | (ph << s);
-      if (!mbar_wait(&v_empty[s], ph ^ 1u, abort_flag)) {
+      __syncwarp();
+      return true;
+    };
+    auto load_v = [&](int j) -> bool {
+      const int sv = j % NV;
+      const uint32_t phv = static_cast<uint32_t>(j / NV) & 1u;
+      if (!mbar_wait(&v_empty[sv], phv ^ 1u, abort_flag)) return false;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&v_full[sv], Cfg::kVBytes);
+        for (int vb = 0; vb < Cfg::kVBlocks; ++vb)
+          tma_load_2d(sV + sv * Cfg::kVBytes + vb * (D * 128), &tm_vt, &v_full[sv], j * KT + vb * 64, v_row0);
+      }
+      v_issued |= 1u << sv;
+      v_par = (v_par & ~(1u << sv)) | (phv << sv);
+      __syncwarp();
+      return true;
+    };
+    if (nkv_max > 0 && !load_k(0)) failed = true;
+    for (int j = 0; j < nkv_max && !failed; ++j) {
+      if (j + 1 < nkv_max && !load_k(j + 1)) {
         failed = true;
         break;
       }
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&v_full[s], Cfg::kVBytes);
-        for (int vb = 0; vb < Cfg::kVBlocks; ++vb)
-          tma_load_2d(sV + s * Cfg::kVBytes + vb * (D * 128), &tm_vt, &v_full[s], j * KT + vb * 64, v_row0);
-      }
-      v_issued |= 1u << s;
-      v_par = (v_par & ~(1u << s)) | (ph << s);
-      __syncwarp();
+      if (!load_v(j)) failed = true;
     }
     if (failed) {
       if (lane == 0) {
@@ -255,10 +266,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       // let the loads already issued land before the CTA can exit (bounded, no abort)
       (void)mbar_wait(q_full, 0u, nullptr);
-      for (int s = 0; s < NS; ++s) {
+      for (int s = 0; s < NS; ++s)
         if (k_issued & (1u << s)) (void)mbar_wait(&k_full[s], (k_par >> s) & 1u, nullptr);
+      for (int s = 0; s < NV; ++s)
         if (v_issued & (1u << s)) (void)mbar_wait(&v_full[s], (v_par >> s) & 1u, nullptr);
-      }
     }
   } else if (warp == 1) {
     // -------------------------------------------------------------- UMMA issuer
@@ -290,8 +301,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       return true;
     };
     auto issue_pv = [&](int w, int j) -> bool {
-      const int s = j % NS;
-      if (!mbar_wait(&v_full[s], static_cast<uint32_t>(j / NS) & 1u, abort_flag) ||
+      const int s = j % NV;
+      if (!mbar_wait(&v_full[s], static_cast<uint32_t>(j / NV) & 1u, abort_flag) ||
           !mbar_wait(&p_full[w], static_cast<uint32_t>(j) & 1u, abort_flag))
         return false;
       tc_fence_after();
@@ -325,7 +336,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       if (!failed && j < nkv0 && !issue_pv(0, j)) failed = true;
       if (!failed && !issue_pv(1, j)) failed = true;
-      if (!failed && lane == 0) tc_commit(&v_empty[j % NS]);  // both P V of tile j issued
+      if (!failed && lane == 0) tc_commit(&v_empty[j % NV]);  // both P V of tile j issued
       __syncwarp();
     }
     if (failed) {

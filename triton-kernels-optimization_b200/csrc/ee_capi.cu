@@ -522,7 +522,7 @@ int ee_flash_attention_entropy(const void* Q, const void* K, const void* V, int6
   std::memset(&a, 0, sizeof(a));
   if ((st = encode_kmajor(&a.q, Q, B * Hq * S, head_dim, head_dim, 2, ee::kAttnTile)) != EE_OK) return st;
   // K tiles of 128 keys for head_dim 64, 64 keys for 128 (the kernel's KT)
-  if ((st = encode_kmajor(&a.k, K, B * Hkv * S, head_dim, head_dim, 2, head_dim == 64 ? 128 : 64)) != EE_OK) return st;
+  if ((st = encode_kmajor(&a.k, K, B * Hkv * S, head_dim, head_dim, 2, 128)) != EE_OK) return st;
   if ((st = encode_kmajor(&a.vt, workspace, B * Hkv * head_dim, s_pad, s_pad, 2, static_cast<int>(head_dim))) != EE_OK)
     return st;
   a.B = B;
@@ -592,7 +592,7 @@ int ee_flash_attention_rope_entropy(const void* q, int64_t ldq, const void* k, i
   ee::AttnLaunch a;
   std::memset(&a, 0, sizeof(a));
   if ((st = encode_kmajor(&a.q, qr, B * Hq * S, head_dim, head_dim, 2, ee::kAttnTile)) != EE_OK) return st;
-  if ((st = encode_kmajor(&a.k, kr, B * Hkv * S, head_dim, head_dim, 2, head_dim == 64 ? 128 : 64)) != EE_OK)
+  if ((st = encode_kmajor(&a.k, kr, B * Hkv * S, head_dim, head_dim, 2, 128)) != EE_OK)
     return st;
   if ((st = encode_kmajor(&a.vt, vt, B * Hkv * head_dim, s_pad, s_pad, 2, static_cast<int>(head_dim))) != EE_OK)
     return st;
