@@ -49,6 +49,28 @@ def test_matches_eager_attention(pkg, cuda, B, Hq, Hkv, S, d, causal):
     np.testing.assert_allclose(batch.cpu().numpy(), ref_rows.mean(dim=(1, 2)).cpu().numpy(), rtol=1e-3)
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,S,d,causal,qscale", [
+    (1, 2, 1, 1, 64, True, 1.5), (2, 2, 2, 7, 128, True, 1.5), (1, 4, 2, 130, 128, True, 1.5),
+    (1, 2, 2, 383, 64, True, 1.5), (1, 2, 1, 300, 64, False, 1.5), (1, 2, 2, 300, 128, False, 1.5),
+    (1, 2, 2, 1024, 64, True, 6.0), (1, 2, 1, 1024, 128, True, 6.0), (1, 2, 2, 640, 64, False, 6.0)])
+def test_edge_sizes_and_peaked_scores(pkg, cuda, B, Hq, Hkv, S, d, causal, qscale):
+    """Sequences shorter than a tile or ending mid-tile (query and key tiles partly past
+    the end), non-causal calls, and peaked scores (q scaled up: the row max grows by more
+    than 2^8 from one key tile to the next, so the kernel's lazy rescale of O, l and t
+    runs) -- each against the eager reference math."""
+    g = torch.Generator(device=cuda).manual_seed(S * 7 + d + int(qscale))
+    q = (torch.randn(B, Hq, S, d, generator=g, device=cuda) * qscale).half()
+    k = (torch.randn(B, Hkv, S, d, generator=g, device=cuda) * 1.5).half()
+    v = torch.randn(B, Hkv, S, d, generator=g, device=cuda).half()
+    out, batch, rows = pkg.flash_attention_entropy(q, k, v, causal=causal, return_rows=True)
+    torch.cuda.synchronize()
+    assert pkg._lib.device_check() == 0
+    ref_out, ref_rows = _eager(q, k, v, causal, d ** -0.5)
+    assert torch.isfinite(out.float()).all()
+    assert _relf(out.float(), ref_out.float()) < 1e-2
+    np.testing.assert_allclose(rows.cpu().numpy(), ref_rows.cpu().numpy(), rtol=2e-3, atol=2e-3)
+
+
 def test_argument_checks(pkg, cuda):
     lib = pkg.load_library()
     p = 256
