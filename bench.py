@@ -547,7 +547,7 @@ def main(argv=None) -> int:
     # of the step's shape (268 MB together, above L2: every call reads its logits from
     # HBM), events around each replay -- the throughput of the router's two launches
     # (rows, then the bucket scan) without per-call event overhead
-    gate_stream_us = None
+    gate_stream_us = gate_rows_only_us = None
     if rank == 0:
         lg_rot = [logits] + [torch.randn_like(logits) * float(logits.float().std()) for _ in range(7)]
         for x in lg_rot:
@@ -570,6 +570,29 @@ def main(argv=None) -> int:
             b.synchronize()
             ts.append(a.elapsed_time(b) * 1e3 / (4 * len(lg_rot)))
         gate_stream_us = statistics.median(ts)
+        del graph
+        # the router kernel alone (entropy + route id per row, no bucket scan), same buffers
+        rows_only = lambda x: pkg.softmax_entropy_rows(x, want_probs=False, tau_low=TAU[0], tau_high=TAU[1])
+        for x in lg_rot:
+            rows_only(x)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(4):
+                for x in lg_rot:
+                    rows_only(x)
+        graph.replay()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(5):
+            flush()
+            a, b = E(), E()
+            a.record()
+            graph.replay()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b) * 1e3 / (4 * len(lg_rot)))
+        gate_rows_only_us = statistics.median(ts)
         del graph, lg_rot
         router.route(logits)  # the step's routing again
         torch.cuda.synchronize()
@@ -722,13 +745,17 @@ def main(argv=None) -> int:
             "softmax_entropy": {"gbs": gate_bytes / gate_stream_us / 1e3,
                                 "frac": gate_bytes / gate_stream_us / 1e3 / peaks["hbm_gbs"],
                                 "us_per_call": gate_stream_us, "bytes_per_call": gate_bytes,
+                                "router_kernel_only": {"us_per_call": gate_rows_only_us,
+                                                       "gbs": gate_bytes / gate_rows_only_us / 1e3,
+                                                       "frac": gate_bytes / gate_rows_only_us / 1e3 / peaks["hbm_gbs"]},
                                 "at_16384_rows": gate_rows_16k,
                                 "gbs_single_call_eager": gate_gbs,
                                 "us_single_call_eager": 1e3 * sum(gate_ms) / len(gate_ms),
                                 "note": "router (entropy + route per row) and its bucket scan; algorithmic bytes "
                                         "2Mn + 4M + M; gbs from back-to-back calls replayed from a CUDA graph over "
                                         "8 logits buffers (above L2), the eager single call (events around it, "
-                                        "after an L2 flush) beside it; at_16384_rows: the same at config 5's "
+                                        "after an L2 flush) beside it; router_kernel_only: the router launch without the bucket "
+                                        "scan; at_16384_rows: the same at config 5's "
                                         "rows per GPU, with the router kernel alone (no bucket scan) beside it"}
             if gate_stream_us else None,
             "per_projection_tflops": {
