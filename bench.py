@@ -33,6 +33,7 @@ import re
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -114,11 +115,10 @@ class ClockSampler:
     def __init__(self, gpu_indices):
         self.gpus = {str(i) for i in gpu_indices}
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        self.path = os.path.join(tempfile.gettempdir(), f"ee_bench_clocks_{os.getpid()}.csv")
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
@@ -254,6 +254,62 @@ def cpu_baseline(torch, logits, acts, w_host, budget_s: float) -> dict:
             "sample": f"{R} of the {logits.shape[0]} rows per step, all three projections, median of {len(times)} "
                       f"steps (oracle/ee_cpu_reference.py: the reference's torch ops on the CPU)",
             "ms_per_sample_step": t * 1e3}
+
+
+def oracle_check(torch, router, logits, acts, ys, w_host, per_bucket: int = 16, seed: int = 5) -> dict:
+    """Parity of the timed step itself, checked outside the timed region against the CPU
+    oracle (the checker, never the thing measured): every row's entropy and route id
+    (the step's own logits law), and for a seeded sample of rows of each bucket the
+    three projections' outputs.  Bars: entropy within 1e-4 relative (1e-6 absolute),
+    route ids exact outside |H - tau| < 1e-6 (such rows are excluded and counted), INT8
+    rows bit-exact, FP8 / FP16 rows within 1e-2 relative Frobenius error."""
+    import numpy as np
+    from oracle import ee_oracle as orc
+
+    _, H_ref = orc.softmax_entropy(logits.cpu().numpy())
+    r_ref = orc.route(H_ref, *TAU)
+    H = router.H.cpu().numpy().astype(np.float64)
+    r = router.route_ids.cpu().numpy()
+    band = (np.abs(H_ref - TAU[0]) < 1e-6) | (np.abs(H_ref - TAU[1]) < 1e-6)
+    h_err = np.abs(H - H_ref)
+    out = {"rows": int(H.size), "band_rows_excluded": int(band.sum()),
+           "route_mismatch_outside_band": int(((r != r_ref) & ~band).sum()),
+           "entropy_out_of_tolerance": int((h_err > 1e-6 + 1e-4 * np.abs(H_ref)).sum()),
+           "entropy_max_rel_err": float((h_err / np.maximum(np.abs(H_ref), 1e-6)).max()),
+           "counts_match": [int((r == b).sum()) for b in range(3)] == router.counts.cpu().tolist()}
+    rng = np.random.default_rng(seed)
+    rows = np.concatenate([rng.choice(np.where((r_ref == b) & ~band)[0],
+                                      min(per_bucket, int(((r_ref == b) & ~band).sum())), replace=False)
+                           for b in range(3)])
+    rows_t = torch.from_numpy(rows).to(logits.device)
+    proj = {}
+    ok = out["route_mismatch_outside_band"] == 0 and out["entropy_out_of_tolerance"] == 0 and out["counts_match"]
+    for p, (name, _, _) in enumerate(PROJECTIONS):
+        a = acts[p].index_select(0, rows_t).cpu().numpy()
+        y = ys[p].index_select(0, rows_t).cpu().numpy()
+        w_kn, w_s = (t.cpu().numpy() for t in w_host[p])
+        res = {}
+        for b, tier in enumerate(("int8", "fp8", "fp16")):
+            sel = np.where(r_ref[rows] == b)[0]
+            if sel.size == 0:
+                continue
+            want = orc.linear_by_tier(a[sel], w_kn, w_s, b)
+            got = y[sel]
+            if b == 0:
+                res[tier] = {"rows": int(sel.size), "bit_exact": bool(np.array_equal(got.view(np.int16),
+                                                                                      want.view(np.int16)))}
+                ok &= res[tier]["bit_exact"]
+            else:
+                d = got.astype(np.float64) - want.astype(np.float64)
+                rel = float(np.linalg.norm(d) / max(np.linalg.norm(want.astype(np.float64)), 1e-30))
+                res[tier] = {"rows": int(sel.size), "rel_frobenius": rel}
+                ok &= rel <= 1e-2
+        proj[name] = res
+    out["sampled_rows"] = int(rows.size)
+    out["projections"] = proj
+    out["ok"] = bool(ok)
+    out["oracle"] = "oracle/ee_oracle.py (numpy restatement pinned to the reference's own outputs)"
+    return out
 
 
 def run_reference(args) -> int:
@@ -542,6 +598,13 @@ def main(argv=None) -> int:
     pack_ms = [[ev[1 + 2 * p if p == 0 else 3 + 2 * (p - 1)].elapsed_time(ev[2 + 2 * p]) for p in range(n_proj)]
                for ev in evs]
     gemm_ms = [[ev[2 + 2 * p].elapsed_time(ev[3 + 2 * p]) for p in range(n_proj)] for ev in evs]
+    pkg._lib.device_check()
+
+    # parity of the timed configuration: the router and outputs of the last step above
+    # (the timed step's launches on the same inputs) against the CPU oracle
+    parity = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        parity = oracle_check(torch, router, logits, acts, ys, w_host)
 
     # the router alone, back to back: a CUDA graph of route() calls over 8 logits buffers
     # of the step's shape (268 MB together, above L2: every call reads its logits from
@@ -777,6 +840,7 @@ def main(argv=None) -> int:
                                        "measured in this run"},
             "peaks": peaks,
             "cpu_baseline": cpu,
+            "parity": parity,
             "e2e": e2e,
             "configs": configs,
             "gpu_launches": launches_per_step * args.steps,

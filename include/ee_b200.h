@@ -89,6 +89,17 @@ EE_API int ee_set_gemm_splits(int splits);
  * (nullable) receives the word. */
 EE_API int ee_device_check(int* value);
 
+/* Failure-detection test hook (no counterpart in the reference, whose kernels have no
+ * bounded waits).  Arms a one-shot fault for the next launch of the single-CTA gated
+ * GEMM kernel (ee_set_gemm_policy(1) forces that kernel): its CTA `cta` issues neither
+ * the TMA copies nor the barrier arrival of its first K stage, so the MMA warp's bounded
+ * wait on that stage gives up after 2 s, the CTA unwinds (drains its MMAs and copies,
+ * frees its tensor memory) and sets the error word ee_device_check reports.  Nothing
+ * faults or hangs; that call's output is incomplete, every later call runs normally.
+ * After the error, re-zero each gated workspace's header (ee_gate_rows does) before
+ * routing with it again. */
+EE_API int ee_debug_drop_next_gemm_load(int cta);
+
 /* ---------------------------------------------------------------- softmax + entropy
  * Per row r of the fp16 matrix x [rows, n] (row stride ld):
  *   p = softmax(x[r]), H[r] = -sum p log p   (fp32 math)
@@ -239,8 +250,9 @@ EE_API int ee_linear_fp8(const void* A, int64_t lda, const uint8_t* W_e4m3_nk, c
  * the allocator and gives the plug-in no way to borrow from it.
  * Limits: M <= 16384 rows and M * K <= 2^24; larger calls return EE_ERR_UNSUPPORTED
  * (use ee_linear_int8 then).  The first call on a device looks up the block's device
- * address (cudaGetSymbolAddress, once per device); make that first call before any
- * stream capture begins.  All calls share the one block and each call overwrites what
+ * address (cudaGetSymbolAddress, once per device context: again after a
+ * cudaDeviceReset, which unloads the block); make that first call before any stream
+ * capture begins.  All calls share the one block and each call overwrites what
  * the previous left there (nothing in it needs to start at zero): calls that can
  * overlap on the GPU -- on different streams, or from different threads -- race on it
  * and must be serialised by the caller. */

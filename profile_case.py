@@ -10,9 +10,9 @@ mix about 24 / 55 / 21 %); device footprint is about 4*N*K + 5*rows*K + 2*rows*N
 --case attention: each repetition runs flash_attention_entropy (causal, output and
 per-row entropy) on q [B, Hq, S, D], k / v [B, Hkv, S, D].
 
-    python triton-kernels-optimization_b200/profile_case.py --rows 2048 --K 4096 --N 14336 --reps 4
+    python profile_case.py --rows 2048 --K 4096 --N 14336 --reps 4
     ncu --set full --clock-control none -k regex:gated_gemm -s 3 -c 1 -o prof <same command>
-    python triton-kernels-optimization_b200/profile_case.py --case attention --B 1 --Hq 32 --Hkv 4 --S 2048 --D 64
+    python profile_case.py --case attention --B 1 --Hq 32 --Hkv 4 --S 2048 --D 64
 """
 from __future__ import annotations
 
@@ -21,7 +21,7 @@ import math
 import os
 import sys
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 

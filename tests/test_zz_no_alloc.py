@@ -40,8 +40,11 @@ def _no_alloc(pkg, a, pack, y):
 
 
 def test_no_alloc_matches_workspace_entry_point_two_calls(pkg, cuda):
-    # the second call is smaller than the first, so stale scratch rows would show up
-    for M, K, N, seed in [(1024, 4096, 4096, 11), (300, 1024, 776, 12)]:
+    # each call is smaller than the one before, so stale scratch rows would show up; the
+    # first fills the scratch exactly (M * K = 2^24), the last takes the weight-streaming
+    # kernel (at most 64 rows)
+    for M, K, N, seed in [(4096, 4096, 256, 10), (1024, 4096, 4096, 11), (300, 1024, 776, 12),
+                          (16, 4096, 4096, 13)]:
         a, w = _inputs(M, K, N, seed, cuda)
         w_kn, w_s = pkg.quantize_weights_int8(w)
         pack = pkg.WeightPack(w_kn, w_s)
@@ -58,6 +61,7 @@ def test_no_alloc_matches_workspace_entry_point_two_calls(pkg, cuda):
 def test_no_alloc_rejects_sizes_beyond_its_scratch(pkg, cuda):
     lib = pkg.load_library()
     null = ctypes.c_void_p(16)  # never dereferenced: the size check comes first
-    st = lib.ee_linear_int8_noalloc(null, 8192, null, null, null, 4096, 256, 8192, 256, None)
-    assert st == -3  # EE_ERR_UNSUPPORTED
-    assert "exceeds its fixed scratch" in pkg._lib.last_error()
+    for M, K in [(4096, 8192), (16385, 16), (1, (1 << 24) + 16), (4097, 4096)]:
+        st = lib.ee_linear_int8_noalloc(null, K, null, null, null, M, 256, K, 256, None)
+        assert st == -3, (M, K)  # EE_ERR_UNSUPPORTED
+        assert "exceeds its fixed scratch" in pkg._lib.last_error()

@@ -31,6 +31,7 @@ SIGNATURES = {
     "ee_set_gemm_policy": (c_int, [c_int]),
     "ee_set_gemm_splits": (c_int, [c_int]),
     "ee_device_check": (c_int, [POINTER(c_int)]),
+    "ee_debug_drop_next_gemm_load": (c_int, [c_int]),
     "ee_softmax_entropy": (c_int, [_P, c_int64, c_int64, c_int64, c_int, c_int64, _P, c_int64, _P, _P, c_double,
                                    c_double, _P]),
     "ee_fused_softmax_entropy_4d": (c_int, [_P, c_int64, c_int64, c_int64, c_int, _P, _P, _P, _P]),
@@ -118,8 +119,19 @@ def call(name: str, *args) -> None:
     check(getattr(load(), name)(*args), name)
 
 
+# Bumped whenever device_check finds the error word set: a kernel that gave up may have
+# left a gated workspace's header (bucket counters, tile scheduler words) dirty, so every
+# EntropyRouter re-zeroes its header on its next route when the count has moved.
+error_epoch = 0
+
+
 def device_check() -> int:
-    """Read and clear the current device's error word; raise if it was set."""
+    """Read and clear the current device's error word; raise if it was set (after
+    marking every router's workspace header for re-zeroing)."""
+    global error_epoch
     v = c_int(0)
-    check(load().ee_device_check(ctypes.byref(v)), "ee_device_check")
+    st = load().ee_device_check(ctypes.byref(v))
+    if v.value != 0:
+        error_epoch += 1
+    check(st, "ee_device_check")
     return v.value

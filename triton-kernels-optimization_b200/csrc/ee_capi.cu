@@ -112,6 +112,7 @@ int check_gemm_shape(int64_t M, int64_t N, int64_t K, int64_t ldy) {
 std::atomic<int> g_gemm_policy{0};  // 0 auto, 1 single-CTA 128x256, 2 CTA-pair 256x256, 3 single-CTA 128x64,
                                     // 4 weight-streaming (skinny) where the call has at most 128 rows
 std::atomic<int> g_gemm_splits{0};  // skinny kernel's K splits per tile: 0 = chosen per call
+std::atomic<int> g_drop_next_load{0};  // ee_debug_drop_next_gemm_load: armed CTA + 1, or 0
 
 // K splits of the skinny kernel: one per 2048 of K (about 0.5 MB of fp16 weight per
 // CTA), but no more than keep the three buckets' 128-channel tiles in one wave of
@@ -256,6 +257,7 @@ int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cud
   // a split call runs one CTA (pair) per slot: its units outnumber its tiles
   const int grid = static_cast<int>(split ? slots : (tiles < slots ? tiles : slots));
   args.split_slots = split ? grid : 0;
+  if (!pair) args.drop_load_cta = g_drop_next_load.exchange(0, std::memory_order_relaxed);
   int st2 = pair ? check_launch(ee::launch_gated_gemm_pair(maps, args, grid, s), "gated_gemm_pair_kernel")
                  : check_launch(ee::launch_gated_gemm(maps, args, grid, bn, s), "gated_gemm_kernel");
   if (st2 != EE_OK || !split) return st2;
@@ -419,6 +421,12 @@ int ee_set_gemm_policy(int policy) {
 int ee_set_gemm_splits(int splits) {
   if (splits < 0 || splits > ee::kSkinnyMaxSplits) return fail(EE_ERR_INVALID, "splits must be 0 (automatic) .. 8");
   g_gemm_splits.store(splits, std::memory_order_relaxed);
+  return EE_OK;
+}
+
+int ee_debug_drop_next_gemm_load(int cta) {
+  if (cta < 0 || cta >= num_sms()) return fail(EE_ERR_INVALID, "cta must be in [0, %d)", num_sms());
+  g_drop_next_load.store(cta + 1, std::memory_order_relaxed);
   return EE_OK;
 }
 
@@ -783,25 +791,65 @@ static constexpr size_t kNoAllocScaleBytes = size_t(kNoAllocMaxRows) * sizeof(fl
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScaleBytes + kNoAllocMaxQuantBytes];
 
 namespace {
-// Device address of g_noalloc_scratch, looked up once per device.  In host code the
-// symbol g_noalloc_scratch is only a host-side handle: its device address has to come
-// from cudaGetSymbolAddress with that device current.
+// Device address of g_noalloc_scratch, looked up once per device context.  In host code
+// the symbol g_noalloc_scratch is only a host-side handle: its device address has to
+// come from cudaGetSymbolAddress with that device current.  The lookup is keyed on the
+// current context's unique id, so after cudaDeviceReset (which unloads the module and
+// with it the array) the next call looks the new array up instead of writing through
+// the old address.
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+
 struct NoAllocSlot {
-  std::once_flag once;
-  cudaError_t err = cudaSuccess;
-  void* ptr = nullptr;
+  std::mutex mu;
+  std::atomic<unsigned long long> ctx_id{0};  // 0: not looked up yet (context ids start at 1)
+  std::atomic<void*> ptr{nullptr};
 };
 NoAllocSlot g_noalloc_slots[64];
+
+int current_context_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (get_current == nullptr || get_id == nullptr) return fail(EE_ERR_CUDA, "cuCtxGetCurrent / cuCtxGetId unavailable");
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, id) != CUDA_SUCCESS)
+    return fail(EE_ERR_CUDA, "no current CUDA context");
+  return EE_OK;
+}
 
 int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(EE_ERR_UNSUPPORTED, "device ordinal %d >= 64", dev);
+  e = cudaSetDevice(dev);  // initialises the device's primary context if nothing has yet
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  unsigned long long id = 0;
+  int st = current_context_id(&id);
+  if (st != EE_OK) return st;
   NoAllocSlot& slot = g_noalloc_slots[dev];
-  std::call_once(slot.once, [&slot] { slot.err = cudaGetSymbolAddress(&slot.ptr, g_noalloc_scratch); });
-  if (slot.err != cudaSuccess) return cuda_fail(slot.err, "cudaGetSymbolAddress(g_noalloc_scratch)");
-  *out = slot.ptr;
+  if (slot.ctx_id.load(std::memory_order_acquire) != id) {
+    std::lock_guard<std::mutex> lock(slot.mu);
+    if (slot.ctx_id.load(std::memory_order_relaxed) != id) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+      slot.ptr.store(p, std::memory_order_relaxed);
+      slot.ctx_id.store(id, std::memory_order_release);
+    }
+  }
+  *out = slot.ptr.load(std::memory_order_relaxed);
   return EE_OK;
 }
 }  // namespace
@@ -915,7 +963,7 @@ int ee_gate_entropies(const float* H, int64_t M, double tau_low, double tau_high
   if (reinterpret_cast<uintptr_t>(H) & 3u) return fail(EE_ERR_MISALIGNED, "H must be 4-byte aligned");
   cudaStream_t s = as_stream(stream);
   GatedWs w = gated_ws(workspace, M, 0);
-  cudaError_t e = cudaMemsetAsync(workspace, 0, 128, s);  // ticket, counts, GEMM tile scheduler
+  cudaError_t e = cudaMemsetAsync(workspace, 0, kWsHeadBytes, s);  // ticket, counts, GEMM tile scheduler
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
   if (M > 0 && (st = check_launch(ee::launch_route_entropies(H, M, tau_low, tau_high, w.H, w.route, w.chunk_tab,
                                                               w.counts, w.ticket, s),

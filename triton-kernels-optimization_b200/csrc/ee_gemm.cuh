@@ -593,6 +593,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t stage = 0, phase = 0;
     uint32_t issued_mask = 0, issued_parity = 0;  // per stage: load in flight, its phase parity
     bool failed = false;
+    bool drop = args.drop_load_cta == static_cast<int>(blockIdx.x) + 1;  // test hook (GemmArgs)
     for (;;) {
       const int t = feed_produce(feed, dyn, ring, ring_full, ring_empty, args.sched, lane, abort_flag);
       if (t < 0) {
@@ -610,13 +611,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           failed = true;
           break;
         }
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&full[stage], kStageBytes);
-          tma_load_2d(sA + stage * kAStageBytes, ta, &full[stage], kb * kstep, pos0);
-          tma_load_2d(sB + stage * kBStageBytes, tw, &full[stage], kb * kstep, n0);
+        if (!drop) {
+          if (lane == 0) {
+            mbar_arrive_expect_tx(&full[stage], kStageBytes);
+            tma_load_2d(sA + stage * kAStageBytes, ta, &full[stage], kb * kstep, pos0);
+            tma_load_2d(sB + stage * kBStageBytes, tw, &full[stage], kb * kstep, n0);
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
         }
-        issued_mask |= 1u << stage;
-        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        drop = false;
         __syncwarp();
         if (++stage == kStages) {
           stage = 0;

@@ -112,6 +112,9 @@ struct GemmArgs {
   int split_slots;         // CTAs (single-CTA kernel) or CTA pairs of the launch
   int32_t* split_plan;     // [3] ranges per tile of each bucket, written by the GEMM's first
                            // CTA for the reduction kernel (with part)
+  int drop_load_cta;       // failure-detection test hook of the single-CTA kernel: 0 none, else
+                           // c + 1 -- CTA c issues neither the copies nor the arrival of its
+                           // first K stage, so its MMA warp's bounded wait on that stage gives up
 };
 constexpr int kPartBlockBytes = 128 * 256 * 4;  // one CTA's 128 x 256 accumulator
 constexpr int kMaxKSplits = 16;

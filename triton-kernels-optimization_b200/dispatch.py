@@ -141,6 +141,7 @@ class EntropyRouter:
         self.tau_high = float(tau_high)
         self.k_split = bool(k_split)
         self.M = 0
+        self._epoch = _lib.error_epoch
         self._ws: Optional[torch.Tensor] = None
         self._ws_k = 16
         self.H: Optional[torch.Tensor] = None
@@ -162,10 +163,16 @@ class EntropyRouter:
     def reset_workspace(self) -> None:
         """Zero the workspace head (bucket and tile counters, the router's scan state).
         Done at allocation; every kernel of the path leaves the head consistent after a
-        clean run, so ``route`` skips the memset.  Call it again after a device error
-        (``device_check`` != 0) before the next ``route``."""
+        clean run, so ``route`` skips the memset.  After ``_lib.device_check`` has found
+        a kernel's error word set, the next ``route`` / ``route_entropy`` of every router
+        zeroes it again by itself."""
         if self._ws is not None:
             self._ws[: _lib.load().ee_gated_workspace_head_bytes()].zero_()
+        self._epoch = _lib.error_epoch
+
+    def _recover(self) -> None:
+        if self._epoch != _lib.error_epoch:  # a kernel gave up since this router last routed
+            self.reset_workspace()
 
     def _views(self, M: int) -> None:
         off = (ctypes.c_int64 * 8)()
@@ -186,6 +193,7 @@ class EntropyRouter:
         if M != self.M or self.H is None:
             self._views(M)
         self.M = M
+        self._recover()
         with torch.cuda.device(logits.device):
             call("ee_gate_rows_keep", logits.data_ptr(), M, n, logits.stride(0), self.tau_low, self.tau_high, None,
                  None, None, self._ws.data_ptr(), self._ws.numel(), _stream())
@@ -201,6 +209,7 @@ class EntropyRouter:
         if M != self.M or self.H is None:
             self._views(M)
         self.M = M
+        self._recover()
         with torch.cuda.device(H.device):
             call("ee_gate_entropies", H.data_ptr(), M, self.tau_low, self.tau_high, None, None, self._ws.data_ptr(),
                  self._ws.numel(), _stream())
