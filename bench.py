@@ -78,6 +78,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs", action="store_true", help="skip the configs 1-3 measurements")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    ap.add_argument("--no-forward", action="store_true", help="skip the config-5 decoder-stack forward")
+    ap.add_argument("--forward-reps", type=int, default=5)
     return ap.parse_args(argv)
 
 
@@ -497,6 +499,119 @@ def measure_configs(torch, pkg, dev, peaks, flush) -> dict:
     return out
 
 
+# config 5 of the path's scope: 4 Llama-3-8B-shaped decoder layers over 16384 tokens
+C5 = {"layers": 4, "hidden": 4096, "heads": 32, "kv_heads": 8, "inter": 14336, "vocab": 128256, "seqs": 8,
+      "seq": 2048, "rope_theta": 5e5}
+
+
+def c5_flops_per_token(c=C5) -> float:
+    """2 x parameters per token of the decoder layers + 4 x layers x hidden x S_eff for
+    causal attention (S_eff = (S + 1) / 2); no lm_head."""
+    d, hq, hkv, hd, inter = c["hidden"], c["heads"], c["kv_heads"], c["hidden"] // c["heads"], c["inter"]
+    params = c["layers"] * (d * hq * hd * 2 + 2 * d * hkv * hd + 3 * d * inter)
+    return 2.0 * params + 4.0 * c["layers"] * d * (c["seq"] + 1) / 2
+
+
+def measure_forward(torch, pkg, dev, rank: int, world: int, reps: int, peaks, routing: str = "token") -> dict:
+    """Config 5: the decoder stack of 4 Llama-3-8B-shaped layers (random-init weights, the
+    same seed on every rank) over 8 sequences x 2048 tokens, the sequences split across
+    the ranks (mode R: strong scaling, no collective inside the forward).  One forward =
+    one replay of the decoder engine's CUDA graph (norms, q / k / v and o fp16 GEMMs,
+    rotary flash attention with row entropies, per-token routing at (0.41, 1.68), fused
+    SwiGLU and down gated GEMMs).  Time = max over ranks of the mean replay time (CUDA
+    events); e2e = token ids from pinned host memory, embedding gather, the forward and
+    the final hidden rows back to pinned host memory."""
+    import torch.distributed as dist
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaModel
+
+    c = C5
+    s0, s1 = pkg.sharding.row_shard(c["seqs"], world, rank)
+    B, S = s1 - s0, c["seq"]
+    torch.manual_seed(4242)
+    cfg = LlamaConfig(hidden_size=c["hidden"], num_hidden_layers=c["layers"], num_attention_heads=c["heads"],
+                      num_key_value_heads=c["kv_heads"], intermediate_size=c["inter"], vocab_size=c["vocab"],
+                      rms_norm_eps=1e-5, rope_theta=c["rope_theta"], max_position_embeddings=8192,
+                      attn_implementation="eager", initializer_range=0.02)
+    with torch.device(dev):
+        model = LlamaModel(cfg)
+    model = model.half().eval().requires_grad_(False)
+    eng = pkg.DecoderEngine.from_model(model, B, S, *TAU, routing=routing)
+    g = torch.Generator().manual_seed(7)
+    ids_all = torch.randint(0, c["vocab"], (c["seqs"], S), generator=g)
+    ids_host = ids_all[s0:s1].contiguous().pin_memory()
+    ids = ids_host.to(dev)
+    emb = model.embed_tokens.weight.detach()
+
+    def embed(x):
+        torch.index_select(emb, 0, x.reshape(-1), out=eng.input)
+
+    E = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    embed(ids)
+    eng.capture()
+    for _ in range(3):
+        eng.launch()
+    torch.cuda.synchronize()
+    pkg._lib.device_check()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    barrier()
+    torch.cuda.synchronize()
+    evs = [(E(), E()) for _ in range(reps)]
+    for a, b in evs:
+        a.record()
+        eng.launch()
+        b.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in evs) / reps)
+    counts = eng.layer_counts.sum(dim=0).cpu().tolist()
+    # end to end: ids in, final hidden rows out, through pinned host memory
+    out_host = torch.empty(eng.output.shape, dtype=torch.float16, pin_memory=True)
+    d_ids = torch.empty_like(ids)
+    barrier()
+    torch.cuda.synchronize()
+    a, b = E(), E()
+    a.record()
+    for _ in range(reps):
+        d_ids.copy_(ids_host, non_blocking=True)
+        embed(d_ids)
+        eng.launch()
+        out_host.copy_(eng.output, non_blocking=True)
+    b.record()
+    torch.cuda.synchronize()
+    ms_e2e = max_over_ranks(a.elapsed_time(b) / reps)
+    pkg._lib.device_check()
+    tokens = c["seqs"] * S
+    fpt = c5_flops_per_token()
+    res = {"workload": "config5_forward_llama3_8b_4_layers", "tokens": tokens, "sequences_per_gpu": B,
+           "ms_per_forward": ms, "tokens_per_s": tokens / ms * 1e3, "tflops": fpt * tokens / ms / 1e9,
+           "flops_per_token": fpt, "frac_of_bf16_peak": fpt * tokens / ms / 1e9 / peaks["bf16_tflops"]
+           if peaks else None,
+           "mlp_route_mix_INT8_FP8_FP16": counts, "routing": routing, "tau": list(TAU),
+           "e2e": {"tokens_per_s": tokens / ms_e2e * 1e3, "ms_per_forward": ms_e2e,
+                   "h2d_bytes_per_forward": int(ids_host.numel() * 8 * world),
+                   "d2h_bytes_per_forward": int(out_host.numel() * 2 * world),
+                   "path": "ids pinned -> device, embedding gather, DecoderEngine graph replay, final hidden -> "
+                           "pinned host"},
+           "scaling": "strong (16384 tokens split by sequence)", "graph_launches_per_forward": 1,
+           "timing": f"CUDA events around each of {reps} graph replays, mean, max over ranks",
+           "data": "random-init weights N(0, 0.02) (seed 4242), token ids uniform (seed 7)"}
+    eng.close()
+    del eng, model
+    torch.cuda.empty_cache()
+    return res
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
     if args.impl == "reference":
@@ -774,6 +889,10 @@ def main(argv=None) -> int:
                "path": "EntropyRouter.route + EntropyRouter.gated_linear per projection; pinned host in/out; "
                        "copy-in / compute / copy-out pipelined over 3 streams, 2 buffer sets"}
 
+    forward = None
+    if not args.no_forward:
+        forward = measure_forward(torch, pkg, dev, rank, world, args.forward_reps, peaks)
+
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -841,6 +960,7 @@ def main(argv=None) -> int:
             "peaks": peaks,
             "cpu_baseline": cpu,
             "parity": parity,
+            "forward": forward,
             "e2e": e2e,
             "configs": configs,
             "gpu_launches": launches_per_step * args.steps,

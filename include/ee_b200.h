@@ -162,6 +162,14 @@ EE_API int ee_flash_attention_rope_entropy(const void* q, int64_t ldq, const voi
                                            float scale, void* O, float* H, void* workspace, size_t workspace_bytes,
                                            void* stream);
 
+/* The block's router inputs from the attention's row entropies H fp32 [B, Hq, S]:
+ * token_entropy[b * S + s] = (sum over heads of H[b, h, s]) / Hq, heads added in
+ * ascending order (per-token routing), and batch_entropy[b] (nullable) = the mean of
+ * H[b] over heads and positions -- the reference's entropy_batch
+ * (EE/python/dispatch.py:244-245), the input of its batch-max dispatcher. */
+EE_API int ee_head_mean_entropy(const float* H, int64_t B, int64_t Hq, int64_t S, float* token_entropy,
+                                float* batch_entropy, void* stream);
+
 /* The Llama block's RMSNorm with the residual add before it folded in (transformers'
  * LlamaRMSNorm.forward and the block's `residual + x`, EE/python/dispatch.py:166-210):
  * with residual: s = fp16(residual + x), stored to sum_out when given; without: s = x;
@@ -375,6 +383,80 @@ EE_API int ee_engine_capture(ee_engine* engine, void* stream);
 /* Replays the recorded graph (records it first if needed). */
 EE_API int ee_engine_launch(ee_engine* engine, void* stream);
 EE_API int ee_engine_destroy(ee_engine* engine);
+
+/* ---------------------------------------------------------------- decoder-stack engine
+ * The whole decoder stack of a Llama-architecture model for one fixed batch shape
+ * [batch, seq] as one native object: the reference's Python layer loop
+ * (EE/python/quality_eval.py:133-141 over EntropyDispatchedLlamaBlock.forward,
+ * EE/python/dispatch.py:166-210; the C++ port its README lists as the next step) with
+ * every step on the device and no host round trip, eagerly (ee_decoder_run) or as one
+ * CUDA graph recorded once and replayed (ee_decoder_capture / ee_decoder_launch).
+ * Per layer, on M = batch * seq rows of width hidden:
+ *   x  = RMSNorm(h) (h = s_prev + mlp_prev folded into the norm pass, ee_add_rmsnorm)
+ *   qkv = x W_qkv^T                  fp16 GEMM of the fp16 weights (route_all = 0) or
+ *                                    gated GEMM routed by the previous layer's entropies
+ *                                    (route_all = 1; the first layer's rows take FP16)
+ *   o, H = flash attention with rotary embedding and row entropies
+ *                                    (ee_flash_attention_rope_entropy, causal)
+ *   Ht = mean over heads of H (per token), Hb = mean over heads and positions (per batch)
+ *   a  = o W_o^T                     as qkv, routed by this layer's entropies
+ *   s  = h + a, x2 = RMSNorm(s)      (one pass)
+ *   routes: per token by Ht (routing 0), or every row in the tier of max_b Hb
+ *           (routing 1, the reference dispatcher's batch-max rule, decided on the device)
+ *   m  = gated SwiGLU GEMM (gate / up interleaved) of x2, then gated GEMM down
+ *   h' = s + m                       (folded into the next layer's norm pass)
+ * then hidden_out = RMSNorm_final(h_last) and residual_out (nullable) = h_last.  The
+ * result equals running EntropyDispatchedLlamaBlock(attention="flash", routing=...,
+ * route_all=...) layer by layer through the same kernels, bit for bit. */
+typedef struct ee_decoder ee_decoder;
+
+typedef struct ee_weight_pack {
+  const int8_t* w_i8;      /* int8 [N, K] */
+  const uint8_t* w_e4m3;   /* e4m3 codes [N, K] */
+  const void* w_f16;       /* fp16 [N, K] */
+  const float* scale;      /* fp32 [N] */
+} ee_weight_pack;
+
+typedef struct ee_decoder_layer {
+  const void* input_norm;  /* fp16 [hidden] */
+  const void* post_norm;   /* fp16 [hidden] */
+  const void* qkv_f16;     /* route_all = 0: fp16 [(heads + 2 kv_heads) head_dim, hidden] (q, k, v rows) */
+  const void* o_f16;       /* route_all = 0: fp16 [hidden, heads head_dim] */
+  ee_weight_pack qkv;      /* route_all = 1: packs of the concatenated q / k / v weight */
+  ee_weight_pack o;        /* route_all = 1 */
+  ee_weight_pack gate_up;  /* gate and up interleaved in 128-row groups: N = 2 intermediate, K = hidden */
+  ee_weight_pack down;     /* N = hidden, K = intermediate */
+} ee_decoder_layer;
+
+#define EE_ROUTE_TOKEN 0
+#define EE_ROUTE_BATCH 1
+
+typedef struct ee_decoder_config {
+  int64_t batch, seq, hidden, heads, kv_heads, head_dim, intermediate;
+  float rms_eps;           /* every RMSNorm of the stack */
+  float attn_scale;        /* softmax scale (head_dim^-0.5 for Llama) */
+  double tau_low, tau_high;
+  int32_t routing;         /* EE_ROUTE_TOKEN or EE_ROUTE_BATCH */
+  int32_t route_all;       /* 0: MLP only (the reference's mode), 1: q / k / v and o too */
+} ee_decoder_config;
+
+EE_API size_t ee_decoder_workspace_bytes(const ee_decoder_config* cfg);
+/* Copies the descriptions; the weights, final_norm (fp16 [hidden]), the rotary tables
+ * cos / sin (fp16 [batch * seq, head_dim]) and layer_counts (nullable: device int32
+ * [n_layers, 3], the MLP's INT8 / FP8 / FP16 row counts of every layer, written by each
+ * forward) must outlive the engine.  workspace: 256-byte aligned, ee_decoder_workspace_bytes. */
+EE_API int ee_decoder_create(const ee_decoder_config* cfg, int32_t n_layers, const ee_decoder_layer* layers,
+                             const void* final_norm, const void* cos, const void* sin, int32_t* layer_counts,
+                             void* workspace, size_t workspace_bytes, ee_decoder** out);
+/* One forward: hidden_in fp16 [batch * seq, hidden] (read only) -> hidden_out fp16
+ * [batch * seq, hidden] and residual_out (nullable, fp16, same shape), on `stream`. */
+EE_API int ee_decoder_run(ee_decoder* dec, const void* hidden_in, void* hidden_out, void* residual_out, void* stream);
+/* Records one forward over these buffers into a CUDA graph (stream: a created stream). */
+EE_API int ee_decoder_capture(ee_decoder* dec, const void* hidden_in, void* hidden_out, void* residual_out,
+                              void* stream);
+/* Replays the recorded forward. */
+EE_API int ee_decoder_launch(ee_decoder* dec, void* stream);
+EE_API int ee_decoder_destroy(ee_decoder* dec);
 
 #ifdef __cplusplus
 }

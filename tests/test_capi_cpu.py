@@ -147,3 +147,27 @@ def test_calls_without_a_device_fail_cleanly(pkg, lib):
     p = ctypes.c_void_p(256)
     st = lib.ee_gemm_fp16(p, p, p, 128, 256, 128, 256, None)
     assert st == -4
+
+
+def test_decoder_engine_argument_checks(pkg, lib):
+    from importlib import import_module
+
+    eng = import_module("tko_b200.engine")
+    cfg = eng._DecoderConfigC(2, 256, 256, 4, 2, 64, 512, 1e-5, 0.125, 2.0, 4.0, 0, 0)
+    assert lib.ee_decoder_workspace_bytes(ctypes.byref(cfg)) > 0
+    for field, bad in (("head_dim", 96), ("intermediate", 500), ("kv_heads", 3), ("routing", 2), ("route_all", 5)):
+        c = eng._DecoderConfigC.from_buffer_copy(cfg)
+        setattr(c, field, bad)
+        assert lib.ee_decoder_workspace_bytes(ctypes.byref(c)) == 0, field
+    out = ctypes.c_void_p()
+    layers = (eng._DecoderLayerC * 1)()
+    p = ctypes.c_void_p(4096)
+    assert lib.ee_decoder_create(ctypes.byref(cfg), 1, layers, p, p, p, None, p, 1 << 30, None) == EE_ERR_INVALID
+    # a layer without its weights is rejected before anything touches the device
+    st = lib.ee_decoder_create(ctypes.byref(cfg), 1, layers, p, p, p, None, p, 1 << 30, ctypes.byref(out))
+    assert st == EE_ERR_INVALID and "missing a weight" in _msg(pkg) and not out.value
+    assert lib.ee_decoder_run(None, p, p, None, None) == EE_ERR_INVALID
+    assert lib.ee_decoder_launch(None, None) == EE_ERR_INVALID
+    assert lib.ee_decoder_destroy(None) == 0
+    assert lib.ee_head_mean_entropy(None, 2, 4, 8, p, None, None) == EE_ERR_INVALID
+    assert lib.ee_head_mean_entropy(ctypes.c_void_p(4098), 2, 4, 8, p, None, None) == EE_ERR_MISALIGNED

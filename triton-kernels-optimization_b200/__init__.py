@@ -19,7 +19,7 @@ from .dispatch import (
     gated_linear,
     tier_of,
 )
-from .engine import CubinEngine, GatedLayerEngine
+from .engine import CubinEngine, DecoderEngine, GatedLayerEngine
 from .llama import EntropyDispatchedLlamaBlock, build_dispatched_llama, dispatched_forward, eval_dispatched
 from .kernels import (
     SwiGLUPack,
@@ -31,6 +31,8 @@ from .kernels import (
     fused_softmax_entropy,
     gemm_accumulators,
     gemm_int8_prequant,
+    head_mean_entropy,
+    linear_f16,
     pack_for,
     quant_rows_e4m3,
     quant_rows_int8,

@@ -43,6 +43,7 @@ SIGNATURES = {
     "ee_flash_attention_rope_entropy": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, _P, c_int64, c_int64,
                                                 c_int64, c_int64, c_int64, c_int64, c_int, c_float, _P, _P, _P,
                                                 c_size_t, _P]),
+    "ee_head_mean_entropy": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, _P]),
     "ee_add_rmsnorm": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, c_float, _P, c_int64, c_int64, c_int64,
                                _P]),
     "ee_route": (c_int, [_P, c_int64, c_double, c_double, _P, _P]),
@@ -79,6 +80,12 @@ SIGNATURES = {
     "ee_engine_capture": (c_int, [_P, _P]),
     "ee_engine_launch": (c_int, [_P, _P]),
     "ee_engine_destroy": (c_int, [_P]),
+    "ee_decoder_workspace_bytes": (c_size_t, [_P]),
+    "ee_decoder_create": (c_int, [_P, c_int32, _P, _P, _P, _P, _P, _P, c_size_t, _P]),
+    "ee_decoder_run": (c_int, [_P, _P, _P, _P, _P]),
+    "ee_decoder_capture": (c_int, [_P, _P, _P, _P, _P]),
+    "ee_decoder_launch": (c_int, [_P, _P]),
+    "ee_decoder_destroy": (c_int, [_P]),
     "ee_gated_linear": (c_int, [_P, c_int64, c_int64, _P, c_int64, c_int64, c_int64, _P, _P, _P, _P, c_int64,
                                 c_double, c_double, _P, _P, _P, _P, c_int64, _P, c_size_t, _P]),
 }

@@ -192,4 +192,45 @@ __global__ void __launch_bounds__(256) transpose_v_kernel(const __half* __restri
   }
 }
 
+// ----------------------------------------------------------------------------------
+// Router inputs of the decoder block from the attention's row entropies H [B, Hq, S]:
+//   * head_mean_kernel: per query position the mean over the heads,
+//     out[b * S + s] = (sum_h H[b, h, s]) / Hq, heads added in ascending order -- the
+//     per-token entropy that routes that token's rows;
+//   * batch_max_fill_kernel: every one of M positions gets max_b Hb[b] (the per-batch
+//     means, B of them), so routing those values puts all rows in the tier the
+//     reference's dispatcher picks from the batch max (EE/python/dispatch.py:63-79).
+// ----------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) head_mean_kernel(const float* __restrict__ H, int64_t B, int64_t Hq,
+                                                        int64_t S, float* __restrict__ out) {
+  griddep_wait();  // the row entropies come from the previous kernel in the stream
+  griddep_launch_dependents();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;  // b * S + s
+  if (i >= B * S) return;
+  const int64_t b = i / S, s = i - b * S;
+  const float* h = H + b * Hq * S + s;
+  float acc = 0.f;
+  for (int64_t k = 0; k < Hq; ++k) acc += h[k * S];
+  out[i] = __fdiv_rn(acc, static_cast<float>(Hq));
+}
+
+__global__ void __launch_bounds__(256) batch_max_fill_kernel(const float* __restrict__ Hb, int64_t B,
+                                                             float* __restrict__ out, int64_t M) {
+  griddep_wait();
+  griddep_launch_dependents();
+  float m = Hb[0];
+  for (int64_t b = 1; b < B; ++b) m = fmaxf(m, Hb[b]);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < M; i += static_cast<int64_t>(gridDim.x) * 256)
+    out[i] = m;
+}
+
+// out[i] = v for i < M (the router input of rows that must all take one tier, e.g. +inf:
+// FP16 for the first layer's projections, which have no earlier entropy)
+__global__ void __launch_bounds__(256) fill_value_kernel(float* __restrict__ out, int64_t M, float v) {
+  griddep_wait();
+  griddep_launch_dependents();
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < M; i += static_cast<int64_t>(gridDim.x) * 256)
+    out[i] = v;
+}
+
 }  // namespace ee

@@ -617,6 +617,20 @@ int ee_flash_attention_rope_entropy(const void* q, int64_t ldq, const void* k, i
   return check_launch(ee::launch_flash_attention(a, s), "flash_attention_entropy");
 }
 
+int ee_head_mean_entropy(const float* H, int64_t B, int64_t Hq, int64_t S, float* token_entropy,
+                         float* batch_entropy, void* stream) {
+  if (B < 0 || Hq <= 0 || S < 0 || B * Hq * S >= (int64_t(1) << 40)) return fail(EE_ERR_INVALID, "bad shape");
+  if (B == 0 || S == 0) return EE_OK;
+  if (H == nullptr || token_entropy == nullptr) return fail(EE_ERR_INVALID, "H and token_entropy are required");
+  if ((reinterpret_cast<uintptr_t>(H) | reinterpret_cast<uintptr_t>(token_entropy) |
+       reinterpret_cast<uintptr_t>(batch_entropy)) & 3u)
+    return fail(EE_ERR_MISALIGNED, "H and the outputs must be 4-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  int st = check_launch(ee::launch_head_mean(H, B, Hq, S, token_entropy, s), "head_mean");
+  if (st != EE_OK || batch_entropy == nullptr) return st;
+  return check_launch(ee::launch_batch_mean(H, B, Hq * S, batch_entropy, s), "batch_mean");
+}
+
 // ------------------------------------------------------------------ the block's norms
 int ee_add_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, void* sum_out, int64_t lds,
                    const void* weight, float eps, void* y, int64_t ldy, int64_t M, int64_t d, void* stream) {

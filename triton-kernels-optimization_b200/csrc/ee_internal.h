@@ -73,6 +73,12 @@ int launch_quantize_weights(const void* W, int64_t ldw, int64_t N, int64_t K, in
 int launch_pack_weights(const int8_t* w_kn, const float* scale, int64_t K, int64_t N, int8_t* w_i8,
                         uint8_t* w_e4m3, void* w_f16, cudaStream_t s);
 int launch_batch_mean(const float* H, int64_t B, int64_t per_batch, float* out, cudaStream_t s);
+// per query position the mean over the heads of H [B, Hq, S] -> out [B * S]
+int launch_head_mean(const float* H, int64_t B, int64_t Hq, int64_t S, float* out, cudaStream_t s);
+// out[0 .. M) = max of Hb[0 .. B)
+int launch_batch_max_fill(const float* Hb, int64_t B, float* out, int64_t M, cudaStream_t s);
+// out[0 .. M) = v
+int launch_fill_value(float* out, int64_t M, float v, cudaStream_t s);
 // per-row attention entropy of probabilities fp16 (f32 = false) or fp32 [rows, n], row stride ld
 int launch_attention_entropy(const void* P, bool f32, int64_t rows, int64_t n, int64_t ld, float* H, cudaStream_t s);
 int launch_batch_max_route(const float* H, int64_t n, double tl, double th, float* max_out, int8_t* tier_out,

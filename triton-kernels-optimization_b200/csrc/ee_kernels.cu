@@ -199,6 +199,24 @@ int launch_batch_mean(const float* H, int64_t B, int64_t per_batch, float* out, 
   return status_of(cudaGetLastError());
 }
 
+int launch_head_mean(const float* H, int64_t B, int64_t Hq, int64_t S, float* out, cudaStream_t s) {
+  if (B * S <= 0) return 0;
+  return launch_pdl(head_mean_kernel, dim3(static_cast<unsigned>((B * S + 255) / 256)), dim3(256), 0, s, H, B, Hq, S,
+                    out);
+}
+
+int launch_batch_max_fill(const float* Hb, int64_t B, float* out, int64_t M, cudaStream_t s) {
+  if (B <= 0 || M <= 0) return 0;
+  const int64_t blocks = std::min<int64_t>((M + 255) / 256, 1024);
+  return launch_pdl(batch_max_fill_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, Hb, B, out, M);
+}
+
+int launch_fill_value(float* out, int64_t M, float v, cudaStream_t s) {
+  if (M <= 0) return 0;
+  const int64_t blocks = std::min<int64_t>((M + 255) / 256, 1024);
+  return launch_pdl(fill_value_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, out, M, v);
+}
+
 int launch_batch_max_route(const float* H, int64_t n, double tl, double th, float* max_out, int8_t* tier_out,
                            cudaStream_t s) {
   batch_max_route_kernel<<<1, 256, 0, s>>>(H, n, tl, th, max_out, tier_out);

@@ -8,6 +8,10 @@
 * ``GatedLayerEngine`` drives the C++ engine of include/ee_b200.h: a fixed list of gated
   layers (routing logits + projections at fixed device addresses) enqueued with no
   host round trip, eagerly or as one CUDA graph recorded once and replayed.
+* ``DecoderEngine`` drives the C++ decoder-stack engine (``ee_decoder_*``): the whole
+  Llama decoder stack of ``EntropyDispatchedLlamaBlock`` layers -- norms, projections,
+  rotary flash attention with row entropies, per-token or batch-max routing, fused
+  SwiGLU MLP -- for one batch shape, as one CUDA graph per forward.
 """
 from __future__ import annotations
 
@@ -154,6 +158,185 @@ class GatedLayerEngine:
     def close(self) -> None:
         if getattr(self, "_handle", None) and self._handle.value:
             _lib.load().ee_engine_destroy(self._handle)
+            self._handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class _WeightPackC(ctypes.Structure):
+    _fields_ = [("w_i8", ctypes.c_void_p), ("w_e4m3", ctypes.c_void_p), ("w_f16", ctypes.c_void_p),
+                ("scale", ctypes.c_void_p)]
+
+
+class _DecoderLayerC(ctypes.Structure):
+    _fields_ = [("input_norm", ctypes.c_void_p), ("post_norm", ctypes.c_void_p), ("qkv_f16", ctypes.c_void_p),
+                ("o_f16", ctypes.c_void_p), ("qkv", _WeightPackC), ("o", _WeightPackC), ("gate_up", _WeightPackC),
+                ("down", _WeightPackC)]
+
+
+class _DecoderConfigC(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int64), ("seq", ctypes.c_int64), ("hidden", ctypes.c_int64),
+                ("heads", ctypes.c_int64), ("kv_heads", ctypes.c_int64), ("head_dim", ctypes.c_int64),
+                ("intermediate", ctypes.c_int64), ("rms_eps", ctypes.c_float), ("attn_scale", ctypes.c_float),
+                ("tau_low", ctypes.c_double), ("tau_high", ctypes.c_double), ("routing", ctypes.c_int32),
+                ("route_all", ctypes.c_int32)]
+
+
+def _pack_c(p) -> _WeightPackC:
+    return _WeightPackC(p.w_i8.data_ptr(), p.w_e4m3.data_ptr(), p.w_f16.data_ptr(), p.scale.data_ptr())
+
+
+class DecoderEngine:
+    """The decoder stack of a Llama-architecture model as one native object (the
+    reference's per-layer Python loop, EE/python/quality_eval.py:133-141, with every step
+    on the device).
+
+    ``blocks`` are ``EntropyDispatchedLlamaBlock`` layers built with ``attention="flash"``
+    (their weight packs, norms and attention weights are used in place); ``final_norm``
+    the model's last RMSNorm weight; ``position_embeddings`` the (cos, sin) tables of the
+    rotary embedding for [batch, seq] positions (fp16 [batch, seq, head_dim], what
+    transformers' rotary module returns).  ``routing`` / ``route_all`` as the blocks'.
+    ``forward(hidden)`` copies fp16 [batch, seq, hidden] into the engine's input buffer
+    and replays the recorded graph; the result (after the final norm) is ``self.output``
+    and the last block's output (before it) ``self.residual``.  ``layer_counts`` [layers,
+    3] holds each layer's MLP INT8 / FP8 / FP16 row counts of the latest forward.
+    """
+
+    def __init__(self, blocks: Sequence, final_norm: torch.Tensor, position_embeddings, batch: int, seq: int,
+                 tau_low: float = 0.41, tau_high: float = 1.68, routing: str = "token", route_all: bool = False):
+        _require(len(blocks) > 0, "need at least one block")
+        _require(routing in ("token", "batch"), "routing must be 'token' or 'batch'")
+        b0 = blocks[0]
+        attn = b0.self_attn
+        dev = final_norm.device
+        hidden = b0.input_layernorm.weight.numel()
+        d = attn.head_dim
+        heads = b0._qkv_split[0] // d
+        kv = b0._qkv_split[1] // d
+        inter = b0.down_proj.in_features
+        eps = float(b0.input_layernorm.variance_epsilon)
+        self.batch, self.seq, self.hidden = int(batch), int(seq), int(hidden)
+        M = self.batch * self.seq
+        cfg = _DecoderConfigC(self.batch, self.seq, hidden, heads, kv, d, inter, eps, float(attn.scaling),
+                              float(tau_low), float(tau_high), 0 if routing == "token" else 1, int(bool(route_all)))
+        self._keep = []
+        layers = (_DecoderLayerC * len(blocks))()
+        for i, blk in enumerate(blocks):
+            _require(blk.attention == "flash", "DecoderEngine needs blocks built with attention='flash'")
+            _require(float(blk.input_layernorm.variance_epsilon) == eps and
+                     float(blk.post_attention_layernorm.variance_epsilon) == eps, "every RMSNorm must share eps")
+            gu = blk.swiglu_pack()
+            _require(gu is not None, "the intermediate size must be a multiple of 128")
+            w_in = blk.input_layernorm.weight.detach().to(torch.float16).contiguous()
+            w_post = blk.post_attention_layernorm.weight.detach().to(torch.float16).contiguous()
+            down = blk.down_proj._pack()
+            L = _DecoderLayerC()
+            L.input_norm, L.post_norm = w_in.data_ptr(), w_post.data_ptr()
+            L.gate_up, L.down = _pack_c(gu), _pack_c(down)
+            keep = [w_in, w_post, gu, down]
+            if route_all:
+                qp, op = blk.qkv_proj._pack(), blk.o_proj._pack()
+                L.qkv, L.o = _pack_c(qp), _pack_c(op)
+                keep += [qp, op]
+            else:
+                wq = blk.qkv_weight()
+                wo = blk.self_attn.o_proj.weight.detach().to(torch.float16).contiguous()
+                L.qkv_f16, L.o_f16 = wq.data_ptr(), wo.data_ptr()
+                keep += [wq, wo]
+            layers[i] = L
+            self._keep += keep
+        cos, sin = position_embeddings
+        self.cos = cos.to(torch.float16).reshape(M, d).contiguous()
+        self.sin = sin.to(torch.float16).reshape(M, d).contiguous()
+        self.final_norm = final_norm.detach().to(torch.float16).contiguous()
+        self.layer_counts = torch.zeros(len(blocks), 3, dtype=torch.int32, device=dev)
+        lib = _lib.load()
+        nbytes = lib.ee_decoder_workspace_bytes(ctypes.byref(cfg))
+        _require(nbytes > 0, "unsupported decoder shape")
+        self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.input = torch.empty(M, hidden, dtype=torch.float16, device=dev)
+        self.output = torch.empty(M, hidden, dtype=torch.float16, device=dev)
+        self.residual = torch.empty(M, hidden, dtype=torch.float16, device=dev)
+        self.device = dev
+        self.stream = torch.cuda.Stream(device=dev)  # graphs are recorded on a created stream
+        self._cfg, self._layers = cfg, layers
+        self._handle = ctypes.c_void_p()
+        with torch.cuda.device(dev):
+            call("ee_decoder_create", ctypes.byref(cfg), len(blocks), layers, self.final_norm.data_ptr(),
+                 self.cos.data_ptr(), self.sin.data_ptr(), self.layer_counts.data_ptr(), self.workspace.data_ptr(),
+                 self.workspace.numel(), ctypes.byref(self._handle))
+        self._captured = False
+
+    @classmethod
+    def from_model(cls, model, batch: int, seq: int, tau_low: float = 0.41, tau_high: float = 1.68,
+                   routing: str = "token", route_all: bool = False) -> "DecoderEngine":
+        """Engine over every decoder layer of a transformers Llama model (LlamaForCausalLM
+        or LlamaModel, fp16 on the device): the layers are wrapped as the reference's
+        build_dispatched_llama does (EE/python/dispatch.py:250-259), with flash attention;
+        positions 0 .. seq - 1 in every sequence.  ``self.blocks`` keeps the wrapped layers."""
+        from .llama import build_dispatched_llama
+
+        base = model.model if hasattr(model, "model") else model
+        wrap = model
+        if not hasattr(model, "model"):
+            wrap = torch.nn.Module()
+            wrap.model = base
+        blocks, _ = build_dispatched_llama(wrap, tau_low, tau_high, routing=routing, attention="flash",
+                                           route_all=route_all)
+        dev = base.norm.weight.device
+        pos = torch.arange(seq, device=dev).unsqueeze(0).expand(batch, seq)
+        probe = torch.empty(batch, seq, base.norm.weight.numel(), dtype=torch.float16, device=dev)
+        with torch.no_grad():
+            pe = base.rotary_emb(probe, pos)
+        eng = cls(blocks, base.norm.weight, pe, batch, seq, tau_low, tau_high, routing=routing, route_all=route_all)
+        eng.blocks = blocks
+        return eng
+
+    def run(self, hidden: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One eager forward on the current stream (reads ``hidden`` in place when given,
+        else the input buffer); returns the output buffer."""
+        x = self.input if hidden is None else hidden
+        _require(x.dtype == torch.float16 and x.is_contiguous() and x.numel() == self.input.numel(),
+                 "hidden must be contiguous fp16 [batch, seq, hidden]")
+        with torch.cuda.device(self.device):
+            call("ee_decoder_run", self._handle, x.data_ptr(), self.output.data_ptr(), self.residual.data_ptr(),
+                 torch.cuda.current_stream(self.device).cuda_stream)
+        return self.output
+
+    def capture(self) -> None:
+        """Record one forward over the engine's buffers into a CUDA graph (on the engine's
+        own stream, ordered after the caller's current stream)."""
+        cur = torch.cuda.current_stream(self.device)
+        self.stream.wait_stream(cur)
+        with torch.cuda.device(self.device):
+            call("ee_decoder_capture", self._handle, self.input.data_ptr(), self.output.data_ptr(),
+                 self.residual.data_ptr(), self.stream.cuda_stream)
+        cur.wait_stream(self.stream)
+        self._captured = True
+
+    def launch(self) -> None:
+        """Replay the recorded forward on the current stream (records it on first use)."""
+        if not self._captured:
+            self.capture()
+        with torch.cuda.device(self.device):
+            call("ee_decoder_launch", self._handle, torch.cuda.current_stream(self.device).cuda_stream)
+
+    def forward(self, hidden: torch.Tensor) -> torch.Tensor:
+        """hidden fp16 [batch, seq, hidden] -> the final-norm output (a view of the
+        engine's output buffer, valid until the next forward)."""
+        self.input.view_as(hidden).copy_(hidden)
+        self.launch()
+        return self.output.view(hidden.shape)
+
+    __call__ = forward
+
+    def close(self) -> None:
+        if getattr(self, "_handle", None) and self._handle.value:
+            _lib.load().ee_decoder_destroy(self._handle)
             self._handle = ctypes.c_void_p()
 
     def __del__(self):

@@ -237,6 +237,41 @@ def triton_fp16_gemm(a: torch.Tensor, b_int8, b_scale: torch.Tensor | None = Non
     return y
 
 
+def linear_f16(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp16 x [M, K] @ weight[N, K]^T -> fp16 [M, N] (nn.Linear without bias) on the
+    tcgen05 kind::f16 GEMM with an fp32 accumulator: the Llama block's unrouted
+    projections (q / k / v / o of the reference's MLP-only mode)."""
+    x = _check_act(x)
+    if x.stride(0) != x.shape[1]:
+        x = x.contiguous()
+    _check_cuda(weight, "weight")
+    _require(weight.dtype == torch.float16 and weight.dim() == 2 and weight.shape[1] == x.shape[1],
+             "weight must be fp16 [N, K] with K = x.shape[1]")
+    w = weight.contiguous()
+    M, K = x.shape
+    N = w.shape[0]
+    y = out if out is not None else torch.empty(M, N, dtype=torch.float16, device=x.device)
+    _require(y.shape == (M, N) and y.stride(1) == 1, "out must be fp16 [M, N] rows")
+    with torch.cuda.device(x.device):
+        call("ee_gemm_fp16", x.data_ptr(), w.data_ptr(), y.data_ptr(), M, N, K, y.stride(0), _stream())
+    return y
+
+
+def head_mean_entropy(rows: torch.Tensor):
+    """Router inputs from the attention's row entropies [B, Hq, S] (fp32): per token the
+    mean over the heads [B, S], and per batch the mean over heads and positions [B]
+    (the reference's entropy_batch, EE/python/dispatch.py:244-245), in one fixed order."""
+    _check_cuda(rows, "rows")
+    _require(rows.dim() == 3 and rows.dtype == torch.float32, "rows must be fp32 [B, Hq, S]")
+    rows = rows.contiguous()
+    B, Hq, S = rows.shape
+    token = torch.empty(B, S, dtype=torch.float32, device=rows.device)
+    batch = torch.empty(B, dtype=torch.float32, device=rows.device)
+    with torch.cuda.device(rows.device):
+        call("ee_head_mean_entropy", rows.data_ptr(), B, Hq, S, token.data_ptr(), batch.data_ptr(), _stream())
+    return token, batch
+
+
 def gemm_int8_prequant(a_int8: torch.Tensor, b, a_scale: torch.Tensor, b_scale: torch.Tensor | None = None):
     """Pre-quantised INT8 GEMM (the CubinEngine.forward contract, EE/csrc/engine.cpp:106-166)."""
     _check_cuda(a_int8, "a")
@@ -340,13 +375,15 @@ def attention_entropy(attn_weights: torch.Tensor, return_rows: bool = False):
 
 
 def flash_attention_entropy(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
-                            scale: float | None = None, return_rows: bool = False):
+                            scale: float | None = None, return_rows: bool = False, return_token: bool = False):
     """Attention with the entropy of every query row in one pass (no [B, H, S, S]
     probabilities): q fp16 [B, Hq, S, d], k / v fp16 [B, Hkv, S, d] (grouped heads),
     d = 64 or 128.  Returns (attn_output fp16 [B, S, Hq, d] -- the layout o_proj reads --,
     per-batch mean entropy fp32 [B]) and, with ``return_rows``, the per-row entropies
-    [B, Hq, S].  The entropy is -sum p ln p of the softmax of the reference's fp16 scores
-    (EE/python/dispatch.py:243-245 computes it from the materialised probabilities)."""
+    [B, Hq, S], and with ``return_token`` also the per-token mean over heads [B, S]
+    (``head_mean_entropy``).  The entropy is -sum p ln p of the softmax of the reference's
+    fp16 scores (EE/python/dispatch.py:243-245 computes it from the materialised
+    probabilities)."""
     for t, n in ((q, "q"), (k, "k"), (v, "v")):
         _check_cuda(t, n)
         _require(t.dim() == 4 and t.dtype == torch.float16, f"{n} must be fp16 [B, H, S, d]")
@@ -361,13 +398,15 @@ def flash_attention_entropy(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, c
     with torch.cuda.device(q.device):
         call("ee_flash_attention_entropy", q.data_ptr(), k.data_ptr(), v.data_ptr(), B, Hq, Hkv, S, d,
              int(bool(causal)), scale, out.data_ptr(), rows.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
-    batch = rows.mean(dim=(1, 2))
+    token, batch = head_mean_entropy(rows)
+    if return_token:
+        return out, batch, rows, token
     return (out, batch, rows) if return_rows else (out, batch)
 
 
 def flash_attention_rope_entropy(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor,
                                  sin: torch.Tensor, num_heads: int, num_kv_heads: int, causal: bool = True,
-                                 scale: float | None = None, return_rows: bool = False):
+                                 scale: float | None = None, return_rows: bool = False, return_token: bool = False):
     """flash_attention_entropy on the projections' outputs: q fp16 [B, S, Hq*d], k / v fp16
     [B, S, Hkv*d] (any row stride, unit column stride), cos / sin fp16 [B, S, d] (what
     transformers' LlamaRotaryEmbedding returns).  The rotary embedding is applied in the
@@ -392,7 +431,9 @@ def flash_attention_rope_entropy(q: torch.Tensor, k: torch.Tensor, v: torch.Tens
         call("ee_flash_attention_rope_entropy", q.data_ptr(), q.stride(1), k.data_ptr(), k.stride(1), v.data_ptr(),
              v.stride(1), cos.data_ptr(), sin.data_ptr(), cos.stride(1), B, Hq, Hkv, S, d, int(bool(causal)), scale,
              out.data_ptr(), rows.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
-    batch = rows.mean(dim=(1, 2))
+    token, batch = head_mean_entropy(rows)
+    if return_token:
+        return out, batch, rows, token
     return (out, batch, rows) if return_rows else (out, batch)
 
 

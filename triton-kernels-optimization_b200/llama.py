@@ -23,7 +23,7 @@ import torch.nn as nn
 
 from .dispatch import EntropyDispatchedLinear, EntropyRouter, PipelinedEntropyDispatcher, PrecisionTier
 from .kernels import (SwiGLUPack, _require, add_rmsnorm, attention_entropy, flash_attention_entropy,
-                      flash_attention_rope_entropy)
+                      flash_attention_rope_entropy, head_mean_entropy, linear_f16)
 
 
 class EntropyDispatchedLlamaBlock(nn.Module):
@@ -52,7 +52,8 @@ class EntropyDispatchedLlamaBlock(nn.Module):
             a = llama_block.self_attn
             self.qkv_proj = EntropyDispatchedLinear.from_linear(_concat_linears(a.q_proj, a.k_proj, a.v_proj))
             self.o_proj = EntropyDispatchedLinear.from_linear(a.o_proj)
-            self._qkv_split = (a.q_proj.out_features, a.k_proj.out_features, a.v_proj.out_features)
+        a = llama_block.self_attn
+        self._qkv_split = (a.q_proj.out_features, a.k_proj.out_features, a.v_proj.out_features)
         self.layer_entropy: Optional[torch.Tensor] = None
         self.token_entropy: Optional[torch.Tensor] = None
         self._router: Optional[EntropyRouter] = None
@@ -98,6 +99,28 @@ class EntropyDispatchedLlamaBlock(nn.Module):
             outputs += (present_kv,)
         return outputs
 
+    def swiglu_pack(self) -> Optional[SwiGLUPack]:
+        """Gate and up packs interleaved for the fused SwiGLU GEMM (None when the
+        intermediate size is not a multiple of 128)."""
+        gp, up = self.gate_proj._pack(), self.up_proj._pack()
+        if gp.N % 128 != 0:
+            return None
+        key = (id(gp), id(up))
+        if getattr(self, "_gu_key", None) != key:
+            self._gu, self._gu_key = SwiGLUPack(gp, up), key
+        return self._gu
+
+    def qkv_weight(self) -> torch.Tensor:
+        """The attention's q / k / v weights concatenated by rows (fp16 [(Hq + 2 Hkv) d,
+        hidden]): one GEMM for the three projections."""
+        a = self.self_attn
+        ws = (a.q_proj.weight, a.k_proj.weight, a.v_proj.weight)
+        key = tuple((w.data_ptr(), w._version) for w in ws)
+        if getattr(self, "_qkv_key", None) != key:
+            self._qkv_w = torch.cat([w.detach().to(torch.float16) for w in ws], dim=0).contiguous()
+            self._qkv_key = key
+        return self._qkv_w
+
     def _mlp_per_token(self, x: torch.Tensor, dispatcher: PipelinedEntropyDispatcher) -> torch.Tensor:
         shape = x.shape
         x2 = x.reshape(-1, shape[-1]).to(torch.float16).contiguous()
@@ -105,14 +128,11 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         r = self._router_for(dispatcher, M, max(self.gate_proj.in_features, self.down_proj.in_features), x2.device)
         r.route_entropy(self.token_entropy.reshape(-1))
         r.pack_rows(x2)  # one packing of the post-norm rows serves gate and up
-        gp, up = self.gate_proj._pack(), self.up_proj._pack()
-        if gp.N % 128 == 0:
-            key = (id(gp), id(up))
-            if getattr(self, "_gu_key", None) != key:
-                self._gu, self._gu_key = SwiGLUPack(gp, up), key
-            h = r.swiglu_packed(self._gu)  # gate, up, SiLU and the product in one GEMM
+        gu = self.swiglu_pack()
+        if gu is not None:
+            h = r.swiglu_packed(gu)  # gate, up, SiLU and the product in one GEMM
         else:
-            h = self.act_fn(r.gemm_packed(gp)) * r.gemm_packed(up)
+            h = self.act_fn(r.gemm_packed(self.gate_proj._pack())) * r.gemm_packed(self.up_proj._pack())
         out = r.gated_linear(h, self.down_proj._pack())
         return out.reshape(shape[:-1] + (self.down_proj.out_features,))
 
@@ -126,8 +146,14 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         attn = self.self_attn
         B, S, _ = hidden_states.shape
         d = attn.head_dim
+        # the unrouted projections run on the library's fp16 GEMM (bias-free Llama linears)
+        own_gemm = hidden_states.dtype == torch.float16 and all(
+            getattr(attn, n).bias is None for n in ("q_proj", "k_proj", "v_proj", "o_proj"))
         if self.route_all:
             qkv = self._routed(hidden_states, self.qkv_proj, dispatcher, prev=True)
+            q, k, v = qkv.split(self._qkv_split, dim=-1)
+        elif own_gemm:  # q / k / v as one GEMM of the concatenated weights
+            qkv = linear_f16(hidden_states.reshape(B * S, -1), self.qkv_weight()).reshape(B, S, -1)
             q, k, v = qkv.split(self._qkv_split, dim=-1)
         else:
             q, k, v = attn.q_proj(hidden_states), attn.k_proj(hidden_states), attn.v_proj(hidden_states)
@@ -135,21 +161,23 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         if q.dtype == torch.float16 and cos.dtype == torch.float16:
             # rotary embedding, head layout and V transpose in the attention's own launches
             Hkv = k.shape[-1] // d
-            out, batch, rows = flash_attention_rope_entropy(q, k, v, cos, sin, q.shape[-1] // d, Hkv, causal=True,
-                                                            scale=attn.scaling, return_rows=True)
+            out, batch, rows, token = flash_attention_rope_entropy(q, k, v, cos, sin, q.shape[-1] // d, Hkv,
+                                                                   causal=True, scale=attn.scaling, return_token=True)
         else:
             q = q.reshape(B, S, -1, d).transpose(1, 2)
             k = k.reshape(B, S, -1, d).transpose(1, 2)
             v = v.reshape(B, S, -1, d).transpose(1, 2)
             q, k = apply_rotary_pos_emb(q, k, cos, sin)
-            out, batch, rows = flash_attention_entropy(q.half(), k.half(), v.half(), causal=True,
-                                                       scale=attn.scaling, return_rows=True)
+            out, batch, rows, token = flash_attention_entropy(q.half(), k.half(), v.half(), causal=True,
+                                                              scale=attn.scaling, return_token=True)
         out = out.reshape(B, S, -1).to(hidden_states.dtype)
-        self.token_entropy = rows.mean(dim=1)
+        self.token_entropy = token  # [B, S]: per query position, mean over heads
         if self.route_all:
             if self.routing == "batch" and dispatcher is not None:
                 dispatcher.submit_entropy(batch)
             return self._routed(out, self.o_proj, dispatcher, prev=False), batch, rows
+        if own_gemm:
+            return linear_f16(out.reshape(B * S, -1), attn.o_proj.weight).reshape(B, S, -1), batch, rows
         return attn.o_proj(out), batch, rows
 
     def _routed(self, x: torch.Tensor, proj: "EntropyDispatchedLinear", dispatcher, prev: bool) -> torch.Tensor:
@@ -157,7 +185,8 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         (``routing="token"``) from the previous layer's token entropies (prev) or this
         layer's; per batch from the dispatcher's current tier.  No entropy yet: FP16."""
         if self.routing == "batch" or dispatcher is None:
-            tier = dispatcher.get_tier() if dispatcher is not None else PrecisionTier.FP16
+            first = prev and self.layer_idx == 0  # no earlier layer's entropy yet: FP16
+            tier = dispatcher.get_tier() if dispatcher is not None and not first else PrecisionTier.FP16
             return proj(x, tier=tier)
         shape = x.shape
         x2 = x.reshape(-1, shape[-1]).to(torch.float16).contiguous()
@@ -200,7 +229,10 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         _require(attn_weights is not None, "the attention module returned no probabilities (use eager attention)")
         present_kv = attn_outputs[2] if use_cache and len(attn_outputs) > 2 else None
         entropy_batch, rows = attention_entropy(attn_weights, return_rows=True)
-        self.token_entropy = rows.mean(dim=1)  # [B, S]: per query position, mean over heads
+        if rows.dim() == 3:  # [B, S]: per query position, mean over heads
+            self.token_entropy, _ = head_mean_entropy(rows)
+        else:
+            self.token_entropy = rows.mean(dim=1)
         return attn_output, entropy_batch, present_kv
 
 
