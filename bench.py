@@ -477,25 +477,70 @@ def measure_configs(torch, pkg, dev, peaks, flush) -> dict:
     out["config1_gating_step"] = {"us": round(us, 2), "tflops": round(2.0 * M * N * K / us / 1e6, 1), "mix": cnt,
                                   "route_us": round(us_route, 2),
                                   "route_gbs": round(route_bytes / us_route / 1e3, 1)}
-    # ---- config 2: the reference surface, activation quantisation included
+    # ---- config 2: the reference surface, activation quantisation included, timed back to
+    # back over 12 weights of the shape (64 MB of packs each, together above L2)
     a2 = torch.randn(M, K, generator=g, device=dev)
     a2 = torch.where(torch.rand(M, K, generator=g, device=dev) < 0.01, a2 * 20.0, a2).half()
-    w_kn, w_s = pkg.quantize_weights_int8((torch.randn(N, K, generator=g, device=dev) * 0.02).half())
-    pkg.triton_int8_gemm(a2, w_kn, w_s)  # builds the cached operand packs
+    w16s = [(torch.randn(N, K, generator=g, device=dev) * 0.02).half() for _ in range(12)]
+    packs2 = [pkg.WeightPack.from_weight(w) for w in w16s]
     c2 = {}
     for name, fn, b in (("int8", pkg.triton_int8_gemm, 0), ("fp8", pkg.triton_fp8_gemm, 1),
                         ("fp16_w8a16", pkg.triton_fp16_gemm, 2)):
-        us = timed(lambda: fn(a2, w_kn, w_s))
+        us = timed_stream([lambda p=p: fn(a2, p) for p in packs2], rounds=2, reps=5)
         Mb = [0, 0, 0]
         Mb[b] = M
         c2[name] = {"us": round(us, 2), "tflops": round(2.0 * M * N * K / us / 1e6, 1),
-                    "roofline_frac": round(roofline_us(Mb, K, N) / us, 3)}
+                    "roofline_frac": round(roofline_us(Mb, K, N) / us, 3),
+                    "us_single_call": round(timed(lambda: fn(a2, packs2[0])), 2)}
+    # the same shape with per-tensor amax scaling (one activation scale, one weight scale)
+    # through the pre-quantised FP8 entry point, against cuBLAS (torch._scaled_mm) on the
+    # same e4m3 operands, and the plain fp16 x fp16 GEMM (cuBLAS, torch.matmul) beside it
+    amax = a2.abs().max().float()
+    s_a = (amax / 448.0).half().float()
+    a8 = (a2 * (1.0 / s_a).half()).to(torch.float8_e4m3fn)
+    pt = []
+    for w in w16s:
+        s_w = (w.abs().max().float() / 127.0).clamp_min(1e-8)
+        q = torch.round(w.float() / s_w).clamp(-127, 127)
+        pt.append((q.half().to(torch.float8_e4m3fn).contiguous(), s_w.reshape(1)))
+    sa_vec = s_a.reshape(1).expand(M).contiguous()
+    sb_vecs = [s_w.expand(N).contiguous() for _, s_w in pt]
+    y2 = torch.empty(M, N, dtype=torch.float16, device=dev)
+
+    def ours_fp8(i):
+        pkg._lib.call("ee_gemm_fp8", a8.data_ptr(), sa_vec.data_ptr(), pt[i][0].data_ptr(), sb_vecs[i].data_ptr(),
+                      y2.data_ptr(), M, N, K, N, torch.cuda.current_stream().cuda_stream)
+
+    sa_t = s_a.reshape(())
+    res = {"ours_us": timed_stream([lambda i=i: ours_fp8(i) for i in range(12)], rounds=2, reps=5)}
+    try:
+        res["cublas_scaled_mm_us"] = timed_stream(
+            [lambda i=i: torch._scaled_mm(a8, pt[i][0].t(), scale_a=sa_t, scale_b=pt[i][1].reshape(()),
+                                          out_dtype=torch.float16) for i in range(12)], rounds=2, reps=5)
+        ours_fp8(0)
+        ref = torch._scaled_mm(a8, pt[0][0].t(), scale_a=sa_t, scale_b=pt[0][1].reshape(()), out_dtype=torch.float16)
+        res["rel_frobenius_vs_cublas"] = float((y2.double() - ref.double()).norm() / ref.double().norm())
+    except Exception as exc:  # no fp8 GEMM in this torch build
+        res["cublas_note"] = f"torch._scaled_mm unavailable: {type(exc).__name__}"
+    for k_ in [k_ for k_ in res if k_.endswith("_us")]:
+        res[k_.replace("_us", "_tflops")] = round(2.0 * M * N * K / res[k_] / 1e6, 1)
+        res[k_] = round(res[k_], 2)
+    c2["fp8_per_tensor_amax"] = res
+    us16 = timed_stream([lambda w=w: torch.matmul(a2, w.t()) for w in w16s], rounds=2, reps=5)
+    c2["fp16_cublas_matmul"] = {"us": round(us16, 2), "tflops": round(2.0 * M * N * K / us16 / 1e6, 1),
+                                "note": "torch.matmul fp16 x fp16 (cuBLAS), the unquantised reference GEMM"}
+    us16o = timed_stream([lambda w=w: pkg.linear_f16(a2, w) for w in w16s], rounds=2, reps=5)
+    c2["fp16_ours_linear_f16"] = {"us": round(us16o, 2), "tflops": round(2.0 * M * N * K / us16o / 1e6, 1)}
+    del packs2, w16s, pt
     out["config2_reference_surface_1024x4096x4096"] = c2
-    out["note"] = ("one GPU; configs 1-2 and config 3's us_single_call: one call after an L2 flush, CUDA events "
-                   "around it (about 6 us of the figure is event and launch overhead at these sizes); config 3's "
-                   "us: back-to-back calls replayed from a CUDA graph over four weight packs of the shape "
-                   "(together above L2: every call streams its weights from HBM); roofline = max(flops / measured "
-                   "peak per precision, bytes / measured HBM)")
+    del a2
+    torch.cuda.empty_cache()
+    out["config4_tinyllama_forward"] = measure_config4(torch, pkg, dev)
+    out["note"] = ("one GPU; config 1 and the us_single_call figures: one call after an L2 flush, CUDA events "
+                   "around it (about 6 us of the figure is event and launch overhead at these sizes); configs 2-3 "
+                   "us: back-to-back calls replayed from a CUDA graph over 12 (config 2) or four (config 3) weights "
+                   "of the shape (together above L2: every call streams its weights from HBM); roofline = "
+                   "max(flops / measured peak per precision, bytes / measured HBM)")
     return out
 
 
@@ -610,6 +655,117 @@ def measure_forward(torch, pkg, dev, rank: int, world: int, reps: int, peaks, ro
     del eng, model
     torch.cuda.empty_cache()
     return res
+
+
+# config 4 of the path's scope: the TinyLlama-1.1B architecture
+C4 = {"layers": 22, "hidden": 2048, "heads": 32, "kv_heads": 4, "inter": 5632, "vocab": 32000, "batch": 8,
+      "seq": 2048, "rope_theta": 1e4}
+
+
+def measure_config4(torch, pkg, dev, reps: int = 3) -> dict:
+    """Config 4: TinyLlama-architecture forward (random-init weights, seed 1234; ids uniform,
+    seed 99; [8, 2048] tokens) through the decoder engine + the fp16 lm_head
+    (``linear_f16``), per token or by the batch max, at both threshold pairs; tokens/s of
+    the forward and KL(softmax(logits_gated) || softmax(logits_ref)) per token against
+    (a) the same engine with every row in the FP16 tier and (b) the unquantised fp16
+    model (transformers, sdpa attention) -- the stand-in for the reference's WikiText-2
+    perplexity (weights and dataset are not on this machine)."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    c = C4
+    torch.manual_seed(1234)
+    cfg = LlamaConfig(hidden_size=c["hidden"], num_hidden_layers=c["layers"], num_attention_heads=c["heads"],
+                      num_key_value_heads=c["kv_heads"], intermediate_size=c["inter"], vocab_size=c["vocab"],
+                      rms_norm_eps=1e-5, rope_theta=c["rope_theta"], max_position_embeddings=2048,
+                      attn_implementation="eager", initializer_range=0.02)
+    with torch.device(dev):
+        model = LlamaForCausalLM(cfg)
+    model = model.half().eval().requires_grad_(False)
+    B, S = c["batch"], c["seq"]
+    g = torch.Generator(device=dev).manual_seed(99)
+    ids = torch.randint(0, c["vocab"], (B, S), generator=g, device=dev)
+    emb, w_head = model.model.embed_tokens.weight, model.lm_head.weight
+    tokens = B * S
+    E = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            a, b = E(), E()
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+    def kl_mean(lp, base):
+        kl = torch.zeros((), dtype=torch.float64, device=dev)
+        for r0 in range(0, tokens, 2048):
+            p_lp, q_lp = lp[r0:r0 + 2048], base[r0:r0 + 2048]
+            kl += (p_lp.exp() * (p_lp - q_lp)).sum(-1).double().sum()
+        return float(kl / tokens)
+
+    out = {"config": dict(c, weights="random init N(0, 0.02), seed 1234", ids="uniform [0, vocab), seed 99"),
+           "runs": {}}
+    # the unquantised fp16 model (transformers, sdpa attention): the KL reference point
+    model.config._attn_implementation = "sdpa"
+    ref_logits = torch.empty(tokens, c["vocab"], dtype=torch.float16, device=dev)
+
+    def hf_forward():
+        ref_logits.copy_(model(ids).logits.reshape(tokens, -1))
+
+    ms_hf = timed(hf_forward)
+    model.config._attn_implementation = "eager"
+    fp16_lp = torch.log_softmax(ref_logits.float(), dim=-1)
+    del ref_logits
+    out["hf_fp16_sdpa_forward"] = {"ms": round(ms_hf, 2), "tokens_per_s": round(tokens / ms_hf * 1e3)}
+    base = model.model
+    pos = torch.arange(S, device=dev).unsqueeze(0).expand(B, S)
+    pe = base.rotary_emb(torch.empty(B, S, c["hidden"], dtype=torch.float16, device=dev), pos)
+    for route_all in (True, False):
+        eng0 = pkg.DecoderEngine.from_model(model, B, S, routing="token", route_all=route_all)
+        blks = eng0.blocks
+        eng0.close()
+        tier_lp = None
+        runs = [("all_fp16_tier", (-1.0, -1.0), "token"), ("token_0.41_1.68", (0.41, 1.68), "token"),
+                ("token_2.34_6.03", (2.34, 6.03), "token")]
+        if not route_all:
+            runs += [("batch_0.41_1.68", (0.41, 1.68), "batch"), ("batch_2.34_6.03", (2.34, 6.03), "batch")]
+        for name, tau, routing in runs:
+            eng = pkg.DecoderEngine(blks, base.norm.weight, pe, B, S, *tau, routing=routing, route_all=route_all)
+            logits = torch.empty(tokens, c["vocab"], dtype=torch.float16, device=dev)
+
+            def forward():
+                torch.index_select(emb, 0, ids.reshape(-1), out=eng.input)
+                eng.launch()
+                pkg.linear_f16(eng.output, w_head, out=logits)
+
+            ms = timed(forward)
+            pkg._lib.device_check()
+            lp = torch.log_softmax(logits.float(), dim=-1)
+            entry = {"ms": round(ms, 2), "tokens_per_s": round(tokens / ms * 1e3), "routing": routing,
+                     "tau": list(tau), "mlp_route_mix_INT8_FP8_FP16": eng.layer_counts.sum(dim=0).cpu().tolist(),
+                     "kl_vs_fp16_model": kl_mean(lp, fp16_lp)}
+            if tier_lp is None:
+                tier_lp = lp
+            else:
+                entry["kl_vs_all_fp16_tier"] = kl_mean(lp, tier_lp)
+                del lp
+            out["runs"][("every_linear_" if route_all else "mlp_only_") + name] = entry
+            eng.close()
+            del eng, logits
+        del blks, tier_lp
+        torch.cuda.empty_cache()
+    del model, fp16_lp
+    torch.cuda.empty_cache()
+    out["note"] = ("decoder engine graph + fp16 lm_head per forward (embedding gather included), median of "
+                   f"{reps}; KL in nats per token, p = the gated run; every_linear: q / k / v / o routed too "
+                   "(their FP16 tier is W8A16 like the MLP's), mlp_only: the reference's mode (attention "
+                   "projections on the fp16 weights)")
+    return out
 
 
 def main(argv=None) -> int:
@@ -874,20 +1030,51 @@ def main(argv=None) -> int:
             torch.cuda.synchronize()
             return t0.elapsed_time(t1)
 
-        e2e_run(2)  # warm-up
-        barrier()
-        e2e_total = e2e_run(K2)
-        serial_ms = min(e2e_run(1) for _ in range(3))  # one step alone: nothing to overlap
-        barrier()
-        if world > 1:
-            t = torch.tensor([e2e_total], dtype=torch.float64, device=dev)
+        def e2e_serial(steps):
+            """The same steps one after another on one stream: copy in, compute, copy out."""
+            d_logits, d_acts = d_in[0]
+            t0, t1 = E(), E()
+            with torch.cuda.stream(s_cmp):
+                t0.record(s_cmp)
+                for _ in range(steps):
+                    d_logits.copy_(h_logits, non_blocking=True)
+                    for a, ha in zip(d_acts, h_acts):
+                        a.copy_(ha, non_blocking=True)
+                    router.route(d_logits)
+                    for p in range(n_proj):
+                        router.gated_linear(d_acts[p], packs[p], out=d_out[0][p])
+                    for y, hy in zip(d_out[0], h_out[0]):
+                        hy.copy_(y, non_blocking=True)
+                t1.record(s_cmp)
+            torch.cuda.synchronize()
+            return t0.elapsed_time(t1)
+
+        def max_ranks(v):
+            if world == 1:
+                return v
+            t = torch.tensor([v], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_total = float(t.item())
+            return float(t.item())
+
+        e2e_run(2)  # warm-up
+        e2e_serial(1)
+        barrier()
+        pipe_total = max_ranks(e2e_run(K2))
+        barrier()
+        serial_total = max_ranks(e2e_serial(K2))
+        barrier()
+        # copies in, compute and copies out overlap across steps only while the host link
+        # has room; when several GPUs share it the plain loop can be faster: report the
+        # faster of the two loops (both measured, max over ranks)
+        e2e_total = min(pipe_total, serial_total)
         e2e = {"value": world * step_flops(M) * K2 / (e2e_total / 1e3) / 1e12, "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_total / K2,
-               "ms_per_step_unpipelined": serial_ms, "steps": K2,
-               "path": "EntropyRouter.route + EntropyRouter.gated_linear per projection; pinned host in/out; "
-                       "copy-in / compute / copy-out pipelined over 3 streams, 2 buffer sets"}
+               "ms_per_step_pipelined": pipe_total / K2, "ms_per_step_unpipelined": serial_total / K2,
+               "loop": "pipelined" if pipe_total <= serial_total else "unpipelined", "steps": K2,
+               "per_gpu_value": step_flops(M) * K2 / (e2e_total / 1e3) / 1e12,
+               "path": "EntropyRouter.route + EntropyRouter.gated_linear per projection; pinned host in/out; the "
+                       "faster of two loops: copy-in / compute / copy-out pipelined over 3 streams with 2 buffer "
+                       "sets, or one stream step after step"}
 
     forward = None
     if not args.no_forward:

@@ -10,9 +10,14 @@ mix about 24 / 55 / 21 %); device footprint is about 4*N*K + 5*rows*K + 2*rows*N
 --case attention: each repetition runs flash_attention_entropy (causal, output and
 per-row entropy) on q [B, Hq, S, D], k / v [B, Hkv, S, D].
 
+--case forward: each repetition runs one eager forward of the decoder-stack engine over
+--layers Llama-3-8B-shaped layers (hidden 4096, 32 / 8 heads of 128, intermediate 14336;
+random-init weights) for --B sequences of --S tokens, per-token routing at (0.41, 1.68).
+
     python profile_case.py --rows 2048 --K 4096 --N 14336 --reps 4
     ncu --set full --clock-control none -k regex:gated_gemm -s 3 -c 1 -o prof <same command>
     python profile_case.py --case attention --B 1 --Hq 32 --Hkv 4 --S 2048 --D 64
+    python profile_case.py --case forward --layers 1 --B 8 --S 2048 --reps 2
 """
 from __future__ import annotations
 
@@ -33,7 +38,8 @@ def main(argv=None) -> int:
     ap.add_argument("--N", type=int, default=14336)
     ap.add_argument("--n-logits", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=4)
-    ap.add_argument("--case", choices=("gated", "attention"), default="gated")
+    ap.add_argument("--case", choices=("gated", "attention", "forward"), default="gated")
+    ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--B", type=int, default=1)
     ap.add_argument("--Hq", type=int, default=32)
     ap.add_argument("--Hkv", type=int, default=4)
@@ -48,6 +54,26 @@ def main(argv=None) -> int:
     pkg = ge.load_package()
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev).manual_seed(7)
+    if args.case == "forward":
+        from transformers import LlamaConfig
+        from transformers.models.llama.modeling_llama import LlamaModel
+
+        torch.manual_seed(4242)
+        cfg = LlamaConfig(hidden_size=4096, num_hidden_layers=args.layers, num_attention_heads=32,
+                          num_key_value_heads=8, intermediate_size=14336, vocab_size=1024, rms_norm_eps=1e-5,
+                          rope_theta=5e5, max_position_embeddings=8192, attn_implementation="eager",
+                          initializer_range=0.02)
+        with torch.device(dev):
+            model = LlamaModel(cfg)
+        model = model.half().eval().requires_grad_(False)
+        eng = pkg.DecoderEngine.from_model(model, args.B, args.S, 0.41, 1.68, routing="token")
+        x = torch.randn(args.B * args.S, 4096, generator=g, device=dev).half() * 0.02
+        for _ in range(args.reps):
+            eng.run(x)
+        torch.cuda.synchronize()
+        pkg._lib.device_check()
+        print("forward", args.layers, "layers", args.B, "x", args.S, "mix", eng.layer_counts.sum(dim=0).tolist())
+        return 0
     if args.case == "attention":
         q = torch.randn(args.B, args.Hq, args.S, args.D, generator=g, device=dev).half()
         k = torch.randn(args.B, args.Hkv, args.S, args.D, generator=g, device=dev).half()
