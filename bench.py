@@ -651,6 +651,39 @@ def measure_forward(torch, pkg, dev, rank: int, world: int, reps: int, peaks, ro
            "scaling": "strong (16384 tokens split by sequence)", "graph_launches_per_forward": 1,
            "timing": f"CUDA events around each of {reps} graph replays, mean, max over ranks",
            "data": "random-init weights N(0, 0.02) (seed 4242), token ids uniform (seed 7)"}
+    if world > 1:
+        # mode T beside it: the MLP's gate / up split by column across the ranks, rows
+        # all-gathered at the layer boundary and the SwiGLU output exchanged back (NCCL,
+        # two pipelined row chunks), on the same blocks; its output must equal mode R's
+        pos = torch.arange(S, device=dev).unsqueeze(0).expand(B, S)
+        pe = model.rotary_emb(eng.input.view(B, S, -1), pos)
+        mt = pkg.sharding.ColumnParallelDecoder(eng.blocks, model.norm.weight, pe, world, rank, chunks=2)
+        eng.launch()  # mode R's output for these ids
+        want = eng.residual.clone()
+        x0 = eng.input.view(B, S, -1).clone()
+        for _ in range(2):
+            _, h_t = mt.forward(x0)
+        torch.cuda.synchronize()
+        same = torch.tensor([1.0 if torch.equal(h_t.reshape(want.shape), want) else 0.0], device=dev)
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        barrier()
+        torch.cuda.synchronize()
+        a, b = E(), E()
+        a.record()
+        for _ in range(reps):
+            mt.forward(x0)
+        b.record()
+        torch.cuda.synchronize()
+        ms_t = max_over_ranks(a.elapsed_time(b) / reps)
+        pkg._lib.device_check()
+        res["mode_t"] = {"ms_per_forward": ms_t, "tokens_per_s": tokens / ms_t * 1e3,
+                         "tflops": fpt * tokens / ms_t / 1e9, "equals_mode_r_bitwise_on_every_rank": bool(same.item()),
+                         "path": "ColumnParallelDecoder: per layer norms, q / k / v / o and attention on the rank's "
+                                 "sequences; MLP gate / up column-sharded (I / world columns per rank), NCCL "
+                                 "all-gather of the rows and their entropies, fused SwiGLU GEMM, NCCL row-block "
+                                 "exchange, down GEMM; two row chunks pipelined; eager launches",
+                         "timing": f"CUDA events around {reps} forwards, mean, max over ranks"}
+        del mt, want, x0
     eng.close()
     del eng, model
     torch.cuda.empty_cache()

@@ -122,8 +122,13 @@ class _OracleOps:
                 out[idx] = orc.linear_by_tier(xn[idx], w[0], w[1], t)
         return torch.from_numpy(out)
 
-    def gate_up(self, x, H, gate, up):
-        return self._lin(x, H, gate), self._lin(x, H, up)
+    @staticmethod
+    def pack_swiglu(w_gate, w_up):
+        return _OracleOps.pack(w_gate), _OracleOps.pack(w_up)
+
+    def swiglu(self, x, H, gate_up):
+        g, u = self._lin(x, H, gate_up[0]), self._lin(x, H, gate_up[1])
+        return torch.nn.functional.silu(g.float()).half() * u
 
     def down(self, h, H, down):
         return self._lin(h, H, down)
@@ -138,13 +143,14 @@ def _mlp_inputs(m_total=24, d=64, inter=256, seed=11):
             "wd": (rng.standard_normal((d, inter)) * 0.05).astype(np.float16)}
 
 
-def _worker_mode_t(rank, world, port, inp, out_path):
+def _worker_mode_t(rank, world, port, inp, out_path, chunks):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     sh = _sharding()
     m = inp["x"].shape[0] // world
     mlp = sh.ColumnParallelGatedMLP(torch.from_numpy(inp["wg"]), torch.from_numpy(inp["wu"]),
-                                    torch.from_numpy(inp["wd"]), world, rank, ops=_OracleOps(0.41, 1.68))
+                                    torch.from_numpy(inp["wd"]), world, rank, ops=_OracleOps(0.41, 1.68),
+                                    chunks=chunks)
     assert mlp.cols[rank][1] - mlp.cols[rank][0] == inp["wg"].shape[0] // world
     rows = slice(rank * m, (rank + 1) * m)
     y = mlp.forward(torch.from_numpy(inp["x"][rows]), torch.from_numpy(inp["H"][rows]))
@@ -155,12 +161,13 @@ def _worker_mode_t(rank, world, port, inp, out_path):
     dist.destroy_process_group()
 
 
-def test_column_parallel_mlp_equals_single_rank(tmp_path):
+@pytest.mark.parametrize("chunks", [1, 2])
+def test_column_parallel_mlp_equals_single_rank(tmp_path, chunks):
     """Mode T (gate / up split by column, rows exchanged with an all-gather and an
-    all-to-all) gives the single-rank MLP bit for bit."""
+    all-to-all, in one or two pipelined row chunks) gives the single-rank MLP bit for bit."""
     inp = _mlp_inputs()
     out = str(tmp_path / "mode_t.npy")
-    mp.start_processes(_worker_mode_t, args=(2, _free_port(), inp, out), nprocs=2, start_method="spawn")
+    mp.start_processes(_worker_mode_t, args=(2, _free_port(), inp, out, chunks), nprocs=2, start_method="spawn")
     sh = _sharding()
     single = sh.ColumnParallelGatedMLP(torch.from_numpy(inp["wg"]), torch.from_numpy(inp["wu"]),
                                        torch.from_numpy(inp["wd"]), 1, 0, ops=_OracleOps(0.41, 1.68))
