@@ -170,6 +170,23 @@ EE_API int ee_flash_attention_rope_entropy(const void* q, int64_t ldq, const voi
 EE_API int ee_head_mean_entropy(const float* H, int64_t B, int64_t Hq, int64_t S, float* token_entropy,
                                 float* batch_entropy, void* stream);
 
+/* ee_flash_attention_rope_entropy with the reference's entropy exactly: H receives
+ * -sum_j p_j ln(p_j + 1e-10) (fp32) of the fp16-ROUNDED probabilities
+ * p_j = fp16(softmax_fp32(scores)_j) that transformers' eager attention returns and the
+ * reference's block reduces (EE/python/dispatch.py:236-245), instead of the entropy of
+ * the unrounded softmax.  Rounding a probability needs its row's normaliser, known only
+ * after the last key, so a second tcgen05 pass over the keys recomputes the scores and
+ * reduces the rounded probabilities (about half the first pass's tensor work plus an
+ * exponential and a logarithm per score).  O is the same as without it.  Workspace:
+ * ee_attention_exact_workspace_bytes (each row's exponent reference and sum after the
+ * rotary / attention workspace).  No counterpart in the reference's kernels. */
+EE_API size_t ee_attention_exact_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t S, int64_t head_dim);
+EE_API int ee_flash_attention_rope_entropy_exact(const void* q, int64_t ldq, const void* k, int64_t ldk,
+                                                 const void* v, int64_t ldv, const void* cos, const void* sin,
+                                                 int64_t ld_cs, int64_t B, int64_t Hq, int64_t Hkv, int64_t S,
+                                                 int64_t head_dim, int causal, float scale, void* O, float* H,
+                                                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* The Llama block's RMSNorm with the residual add before it folded in (transformers'
  * LlamaRMSNorm.forward and the block's `residual + x`, EE/python/dispatch.py:166-210):
  * with residual: s = fp16(residual + x), stored to sum_out when given; without: s = x;
@@ -438,6 +455,8 @@ typedef struct ee_decoder_config {
   double tau_low, tau_high;
   int32_t routing;         /* EE_ROUTE_TOKEN or EE_ROUTE_BATCH */
   int32_t route_all;       /* 0: MLP only (the reference's mode), 1: q / k / v and o too */
+  int32_t exact_entropy;   /* 1: route by the reference's entropy of fp16-rounded probabilities
+                              (ee_flash_attention_rope_entropy_exact), 0: by the online entropy */
 } ee_decoder_config;
 
 EE_API size_t ee_decoder_workspace_bytes(const ee_decoder_config* cfg);

@@ -153,9 +153,10 @@ def test_decoder_engine_argument_checks(pkg, lib):
     from importlib import import_module
 
     eng = import_module("tko_b200.engine")
-    cfg = eng._DecoderConfigC(2, 256, 256, 4, 2, 64, 512, 1e-5, 0.125, 2.0, 4.0, 0, 0)
+    cfg = eng._DecoderConfigC(2, 256, 256, 4, 2, 64, 512, 1e-5, 0.125, 2.0, 4.0, 0, 0, 0)
     assert lib.ee_decoder_workspace_bytes(ctypes.byref(cfg)) > 0
-    for field, bad in (("head_dim", 96), ("intermediate", 500), ("kv_heads", 3), ("routing", 2), ("route_all", 5)):
+    for field, bad in (("head_dim", 96), ("intermediate", 500), ("kv_heads", 3), ("routing", 2), ("route_all", 5),
+                       ("exact_entropy", 2)):
         c = eng._DecoderConfigC.from_buffer_copy(cfg)
         setattr(c, field, bad)
         assert lib.ee_decoder_workspace_bytes(ctypes.byref(c)) == 0, field

@@ -76,6 +76,8 @@ struct AttnArgs {
   int causal;
   __half* O;                     // [B, S, Hq, D]
   float* H;                      // [B, Hq, S] entropy of each query row (nats)
+  float2* ml;                    // nullable [B, Hq, S]: each row's exponent reference m (base 2) and
+                                 // l = sum 2^(x log2 e - m), for attention_entropy_exact_kernel
 };
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -520,6 +522,284 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
       if (store) args.H[bh * args.S + q] = 0.69314718055994531f * (__log2f(l) - t2 / l);
+      if (store && args.ml != nullptr) args.ml[bh * args.S + q] = make_float2(m2, l);
+    }
+    tc_fence_before();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+// ---------------------------------------------------------------------------------
+// The reference's rounding of the probabilities, as a second pass over the keys.
+//
+// The reference takes the entropy of transformers' fp16 probabilities,
+// -sum_j p_j ln(p_j + 1e-10) with p_j = fp16(softmax_fp32(s)_j) (EE/python/dispatch.py:
+// 243-245).  Rounding p_j to fp16 needs the row's normaliser, which the flash kernel
+// has only after its last key tile, so exact agreement takes a second pass: with each
+// row's exponent reference m and sum l from the first pass (AttnArgs::ml), this kernel
+// recomputes the fp16 scores S = Q K^T on the tensor core (the same tcgen05 MMAs and
+// roundings as the first pass, no P V), forms q_j = 2^(x_j log2 e - m) / l -- the fp32
+// softmax --, rounds it to fp16 and adds p ln(p + 1e-10) in fp32 as the reference does.
+// One CTA per (batch, query head, two 128-row query tiles), 384 threads:
+//   warp 0     TMA producer: both Q tiles once, K tiles of 128 keys into a 3-deep ring;
+//   warp 1     TMEM owner + single-thread UMMA issuer: S_w,j into one of two TMEM buffers
+//              of query tile w (S of tile j + 1 is issued while tile j is reduced);
+//   warps 4-11 warpgroup w = query tile w, one row per thread.
+// Every wait is bounded; on expiry the CTA records the error word, drains and exits.
+// ---------------------------------------------------------------------------------
+template <int D>
+struct ExactCfg {
+  static constexpr int KT = 128;
+  static constexpr int kKBlocks = D / 64;
+  static constexpr int kQTileBytes = kKBlocks * kAttnTileBytes;
+  static constexpr int kKBytes = kKBlocks * KT * 128;
+  static constexpr int kKStages = 3;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr size_t kSmem = 1024 + 2 * size_t(kQTileBytes) + kKStages * size_t(kKBytes) + kBarrierBytes;
+  static_assert(kSmem <= 227 * 1024, "exact-entropy shared memory above the 227 KB per-CTA limit");
+  static constexpr uint32_t kTmemCols = 512;  // 2 query tiles x 2 buffers x 128 key columns
+};
+
+__device__ __forceinline__ float lg2_approx_f(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attention_entropy_exact_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                                   const AttnArgs args) {
+  using Cfg = ExactCfg<D>;
+  constexpr int KT = Cfg::KT;
+  constexpr int NS = Cfg::kKStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + 2 * Cfg::kQTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sK + NS * Cfg::kKBytes);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;        // [NS]
+  uint64_t* k_empty = bars + 1 + NS;  // [NS]
+  uint64_t* s_full = bars + 1 + 2 * NS;  // [2 tiles][2 buffers] S ready (MMA commit)
+  uint64_t* s_free = s_full + 4;         // [2][2] S read into registers (4 warps)
+  uint64_t* drain = s_full + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 9);
+  static_assert((1 + 2 * NS + 9) * 8 + 8 <= Cfg::kBarrierBytes, "exact-entropy barrier region overflows");
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t nqc = (args.S + 2 * kAttnTile - 1) / (2 * kAttnTile);
+  const int qc = static_cast<int>(nqc - 1 - static_cast<int64_t>(blockIdx.x) % nqc);
+  const int64_t bh = static_cast<int64_t>(blockIdx.x) / nqc;
+  const int64_t b = bh / args.Hq, h = bh % args.Hq;
+  const int64_t hk = h / (args.Hq / args.Hkv);
+  const int64_t q0 = static_cast<int64_t>(qc) * 2 * kAttnTile;
+  const int nkv_all = static_cast<int>((args.S + KT - 1) / KT);
+  const int reach0 = static_cast<int>((q0 + kAttnTile + KT - 1) / KT);
+  const int reach1 = static_cast<int>((q0 + 2 * kAttnTile + KT - 1) / KT);
+  const int nkv0 = args.causal ? (reach0 < nkv_all ? reach0 : nkv_all) : nkv_all;
+  const int nkv1 = args.causal ? (reach1 < nkv_all ? reach1 : nkv_all) : nkv_all;
+  const int nkv_max = nkv1;
+  const int q_row0 = static_cast<int>(bh * args.S + q0);
+  const int k_row0 = static_cast<int>((b * args.Hkv + hk) * args.S);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+  }
+  griddep_wait();  // Q, K and the first pass's row statistics come from earlier kernels
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // -------------------------------------------------------------- TMA producer
+    bool failed = false;
+    uint32_t k_issued = 0, k_par = 0;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * Cfg::kQTileBytes);
+      for (int t = 0; t < 2; ++t)
+        for (int kb = 0; kb < Cfg::kKBlocks; ++kb)
+          tma_load_2d(sQ + t * Cfg::kQTileBytes + kb * kAttnTileBytes, &tm_q, q_full, kb * 64, q_row0 + t * kAttnTile);
+    }
+    for (int j = 0; j < nkv_max; ++j) {
+      const int s = j % NS;
+      const uint32_t ph = static_cast<uint32_t>(j / NS) & 1u;
+      if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag)) {
+        failed = true;
+        break;
+      }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&k_full[s], Cfg::kKBytes);
+        for (int kb = 0; kb < Cfg::kKBlocks; ++kb)
+          tma_load_2d(sK + s * Cfg::kKBytes + kb * (KT * 128), &tm_k, &k_full[s], kb * 64, k_row0 + j * KT);
+      }
+      k_issued |= 1u << s;
+      k_par = (k_par & ~(1u << s)) | (ph << s);
+      __syncwarp();
+    }
+    if (failed) {
+      if (lane == 0) {
+        atomicOr(&g_device_error, kErrWaitTimeout);
+        *abort_flag = 1;
+      }
+      (void)mbar_wait(q_full, 0u, nullptr);
+      for (int s = 0; s < NS; ++s)
+        if (k_issued & (1u << s)) (void)mbar_wait(&k_full[s], (k_par >> s) & 1u, nullptr);
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------------- UMMA issuer
+    constexpr uint32_t idesc_s = make_idesc(1u, 0u, kAttnTile, KT);  // f32 <- f16 x f16, 128 x 128
+    bool failed = !mbar_wait(q_full, 0u, abort_flag);
+    tc_fence_after();
+    for (int j = 0; j < nkv_max && !failed; ++j) {
+      const int s = j % NS;
+      if (!mbar_wait(&k_full[s], static_cast<uint32_t>(j / NS) & 1u, abort_flag)) {
+        failed = true;
+        break;
+      }
+      const int buf = j & 1;
+      const uint32_t use = static_cast<uint32_t>(j >> 1);
+      for (int w = 0; w < 2 && !failed; ++w) {
+        if (j >= (w == 0 ? nkv0 : nkv1)) continue;
+        if (!mbar_wait(&s_free[2 * w + buf], (use & 1u) ^ 1u, abort_flag)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t dst = tmem_base + static_cast<uint32_t>((2 * w + buf) * KT);
+          for (int kb = 0; kb < Cfg::kKBlocks; ++kb) {
+            const uint64_t da = sdesc_k_sw128(smem_u32(sQ + w * Cfg::kQTileBytes + kb * kAttnTileBytes));
+            const uint64_t db = sdesc_k_sw128(smem_u32(sK + s * Cfg::kKBytes + kb * (KT * 128)));
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              tc_mma<kKindF16>(dst, da + 2u * k, db + 2u * k, idesc_s, (kb == 0 && k == 0) ? 0u : 1u);
+          }
+          tc_commit(&s_full[2 * w + buf]);
+        }
+        __syncwarp();
+      }
+      if (!failed && lane == 0) tc_commit(&k_empty[s]);  // the stage is free once these MMAs are done
+      __syncwarp();
+    }
+    if (failed) {
+      if (lane == 0) {
+        atomicOr(&g_device_error, kErrWaitTimeout);
+        *abort_flag = 1;
+        tc_commit(drain);
+      }
+      __syncwarp();
+      (void)mbar_wait(drain, 0u, nullptr);
+    }
+  } else if (warp >= 4) {
+    // -------------------------------------------------------------- rows: the reference's entropy
+    const int w = (warp - 4) >> 2;
+    const int nkv_w = w == 0 ? nkv0 : nkv1;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int64_t q = q0 + w * kAttnTile + row;
+    const bool live = q < args.S;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    constexpr float kLog2eF = 1.4426950408889634f;
+    const float2 sc2 = make_float2(args.scale, args.scale);
+    const __half sch = __float2half_rn(args.scale);
+    const bool scale_is_f16 = __half2float(sch) == args.scale;
+    const uint32_t sch2 = static_cast<uint32_t>(__half_as_ushort(sch)) * 0x10001u;
+    const float2 ml = live ? args.ml[bh * args.S + q] : make_float2(0.f, 1.f);
+    const float inv_l = 1.f / ml.y;
+    const float2 lg2 = make_float2(kLog2eF, kLog2eF), negm = make_float2(-ml.x, -ml.x);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    bool failed = false;
+    for (int j = 0; j < nkv_w; ++j) {
+      const int buf = j & 1;
+      if (!mbar_wait_warp(&s_full[2 * w + buf], static_cast<uint32_t>(j >> 1) & 1u, abort_flag)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t t_s = tmem_base + static_cast<uint32_t>((2 * w + buf) * KT) + lane_off;
+      const int key0 = j * KT;
+      int lim = static_cast<int>(args.S - key0);
+      if (args.causal) {
+        const int64_t c = q - key0 + 1;
+        lim = c < lim ? static_cast<int>(c) : lim;
+      }
+      lim = lim < 0 ? 0 : (lim > KT ? KT : lim);
+      __half2 xs[KT / 2];
+#pragma unroll
+      for (int c0 = 0; c0 < KT; c0 += 64) {
+        uint32_t ra[32], rb[32];
+        __syncwarp();
+        tmem_ld32(t_s + c0, ra);
+        tmem_ld32(t_s + c0 + 32, rb);
+        tmem_ld_wait(ra);
+        regs_after_wait(rb);
+        if (scale_is_f16) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            xs[c0 / 2 + i] = scaled_scores_f16(ra[2 * i], ra[2 * i + 1], sch2);
+            xs[c0 / 2 + 16 + i] = scaled_scores_f16(rb[2 * i], rb[2 * i + 1], sch2);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            xs[c0 / 2 + i] = scaled_scores(ra[2 * i], ra[2 * i + 1], sc2);
+            xs[c0 / 2 + 16 + i] = scaled_scores(rb[2 * i], rb[2 * i + 1], sc2);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[2 * w + buf]);  // the buffer may take S of tile j + 2
+      if (!__all_sync(0xffffffffu, lim >= KT)) {
+        const __half neg = __ushort_as_half(kHalfLowest);
+#pragma unroll
+        for (int i = 0; i < KT / 2; ++i)
+          xs[i] = __halves2half2(2 * i < lim ? __low2half(xs[i]) : neg, 2 * i + 1 < lim ? __high2half(xs[i]) : neg);
+      }
+      // p = fp16(2^(x log2 e - m) / l): the reference's fp16 probability; then
+      // p * log2(p + 1e-10) in fp32 (masked keys: p = 0 contributes 0)
+#pragma unroll
+      for (int i = 0; i < KT / 2; ++i) {
+        const float2 d2 = __ffma2_rn(__half22float2(xs[i]), lg2, negm);
+        const __half2 p16 = __floats2half2_rn(ex2f(d2.x) * inv_l, ex2f(d2.y) * inv_l);
+        const float2 pf = __half22float2(p16);
+        acc[(2 * i) & 3] = fmaf(pf.x, lg2_approx_f(pf.x + 1e-10f), acc[(2 * i) & 3]);
+        acc[(2 * i + 1) & 3] = fmaf(pf.y, lg2_approx_f(pf.y + 1e-10f), acc[(2 * i + 1) & 3]);
+      }
+    }
+    if (failed) {
+      if (lane == 0) {
+        atomicOr(&g_device_error, kErrWaitTimeout);
+        *abort_flag = 1;
+      }
+    } else if (live) {
+      args.H[bh * args.S + q] = -0.69314718055994531f * ((acc[0] + acc[1]) + (acc[2] + acc[3]));
     }
     tc_fence_before();
   }

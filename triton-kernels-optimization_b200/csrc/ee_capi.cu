@@ -552,10 +552,16 @@ size_t ee_attention_rope_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int
          align256(sizeof(uint16_t) * size_t(B) * Hkv * S * head_dim) + ee_attention_workspace_bytes(B, Hkv, S, head_dim);
 }
 
-int ee_flash_attention_rope_entropy(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
-                                    const void* cos, const void* sin, int64_t ld_cs, int64_t B, int64_t Hq, int64_t Hkv,
-                                    int64_t S, int64_t head_dim, int causal, float scale, void* O, float* H,
-                                    void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+// the rotary flash attention of ee_flash_attention_rope_entropy; exact: the row
+// entropies come from a second pass over the keys with the reference's fp16 rounding of
+// each probability (the workspace then also holds each row's (m, l) of the first pass)
+int rope_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                   const void* cos, const void* sin, int64_t ld_cs, int64_t B, int64_t Hq, int64_t Hkv, int64_t S,
+                   int64_t head_dim, int causal, float scale, void* O, float* H, void* workspace,
+                   size_t workspace_bytes, void* stream, bool exact) {
   if (B < 0 || Hq <= 0 || Hkv <= 0 || S < 0) return fail(EE_ERR_INVALID, "bad shape");
   if (Hq % Hkv != 0) return fail(EE_ERR_INVALID, "Hq=%lld is not a multiple of Hkv=%lld", (long long)Hq, (long long)Hkv);
   if (head_dim != 64 && head_dim != 128) return fail(EE_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
@@ -569,10 +575,13 @@ int ee_flash_attention_rope_entropy(const void* q, int64_t ldq, const void* k, i
   if (!al16(q) || !al16(k) || !al16(v) || !al16(cos) || !al16(sin) || !al16(O) || (reinterpret_cast<uintptr_t>(H) & 3u) ||
       ldq % 8 || ldk % 8 || ldv % 8 || ld_cs % 8)
     return fail(EE_ERR_MISALIGNED, "q, k, v, cos, sin and O must be 16-byte aligned with row strides of 8 elements");
-  int st = check_ws(workspace, workspace_bytes, ee_attention_rope_workspace_bytes(B, Hq, Hkv, S, head_dim));
+  const size_t rope_bytes = ee_attention_rope_workspace_bytes(B, Hq, Hkv, S, head_dim);
+  int st = check_ws(workspace, workspace_bytes,
+                    exact ? ee_attention_exact_workspace_bytes(B, Hq, Hkv, S, head_dim) : rope_bytes);
   if (st != EE_OK) return st;
   cudaStream_t s = as_stream(stream);
   uint8_t* p = static_cast<uint8_t*>(workspace);
+  void* ml = exact ? p + rope_bytes : nullptr;
   __half* qr = reinterpret_cast<__half*>(p);
   p += align256(sizeof(uint16_t) * size_t(B) * Hq * S * head_dim);
   __half* kr = reinterpret_cast<__half*>(p);
@@ -614,7 +623,34 @@ int ee_flash_attention_rope_entropy(const void* q, int64_t ldq, const void* k, i
   a.causal = causal;
   a.O = O;
   a.H = H;
-  return check_launch(ee::launch_flash_attention(a, s), "flash_attention_entropy");
+  a.ml = ml;
+  if ((st = check_launch(ee::launch_flash_attention(a, s), "flash_attention_entropy")) != EE_OK || !exact) return st;
+  return check_launch(ee::launch_attention_entropy_exact(a, s), "attention_entropy_exact");
+}
+}  // namespace
+
+extern "C" {
+
+int ee_flash_attention_rope_entropy(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                                    const void* cos, const void* sin, int64_t ld_cs, int64_t B, int64_t Hq, int64_t Hkv,
+                                    int64_t S, int64_t head_dim, int causal, float scale, void* O, float* H,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  return rope_attention(q, ldq, k, ldk, v, ldv, cos, sin, ld_cs, B, Hq, Hkv, S, head_dim, causal, scale, O, H,
+                        workspace, workspace_bytes, stream, false);
+}
+
+size_t ee_attention_exact_workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t S, int64_t head_dim) {
+  if (B < 0 || Hq < 0 || Hkv < 0 || S < 0 || head_dim < 0) return 0;
+  return ee_attention_rope_workspace_bytes(B, Hq, Hkv, S, head_dim) + align256(sizeof(float) * 2 * size_t(B) * Hq * S);
+}
+
+int ee_flash_attention_rope_entropy_exact(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                                          int64_t ldv, const void* cos, const void* sin, int64_t ld_cs, int64_t B,
+                                          int64_t Hq, int64_t Hkv, int64_t S, int64_t head_dim, int causal,
+                                          float scale, void* O, float* H, void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+  return rope_attention(q, ldq, k, ldk, v, ldv, cos, sin, ld_cs, B, Hq, Hkv, S, head_dim, causal, scale, O, H,
+                        workspace, workspace_bytes, stream, true);
 }
 
 int ee_head_mean_entropy(const float* H, int64_t B, int64_t Hq, int64_t S, float* token_entropy,

@@ -222,7 +222,8 @@ bool dec_config_ok(const ee_decoder_config& c) {
   return c.batch > 0 && c.seq > 0 && c.hidden > 0 && c.heads > 0 && c.kv_heads > 0 && c.heads % c.kv_heads == 0 &&
          (c.head_dim == 64 || c.head_dim == 128) && c.intermediate > 0 && c.intermediate % 128 == 0 &&
          c.hidden % 16 == 0 && (c.routing == EE_ROUTE_TOKEN || c.routing == EE_ROUTE_BATCH) &&
-         (c.route_all == 0 || c.route_all == 1) && c.batch * c.seq < (int64_t(1) << 31);
+         (c.route_all == 0 || c.route_all == 1) && (c.exact_entropy == 0 || c.exact_entropy == 1) &&
+         c.batch * c.seq < (int64_t(1) << 31);
 }
 
 DecLayout dec_layout(const ee_decoder_config& c) {
@@ -250,7 +251,9 @@ DecLayout dec_layout(const ee_decoder_config& c) {
   L.o = take(2 * M * d);
   L.hmid = take(2 * M * I);
   L.mlp = take(2 * M * d);
-  L.att_ws_bytes = ee_attention_rope_workspace_bytes(c.batch, c.heads, c.kv_heads, c.seq, c.head_dim);
+  L.att_ws_bytes = c.exact_entropy
+                       ? ee_attention_exact_workspace_bytes(c.batch, c.heads, c.kv_heads, c.seq, c.head_dim)
+                       : ee_attention_rope_workspace_bytes(c.batch, c.heads, c.kv_heads, c.seq, c.head_dim);
   L.att_ws = take(L.att_ws_bytes);
   int64_t kmax = c.hidden > int64_t(nq) ? c.hidden : int64_t(nq);
   kmax = kmax > c.intermediate ? kmax : c.intermediate;
@@ -308,9 +311,9 @@ int run_decoder(ee_decoder& D, const void* hin, void* hout, void* rout, cudaStre
     }
     if ((st = dec_check(st, "qkv projection")) != EE_OK) return st;
     // rotary embedding + causal flash attention with the entropy of every query row
-    st = ee_flash_attention_rope_entropy(D.qkv, nqkv, D.qkv + nq, nqkv, D.qkv + nq + nkv, nqkv, D.cos, D.sin,
-                                         c.head_dim, c.batch, c.heads, c.kv_heads, c.seq, c.head_dim, 1, c.attn_scale,
-                                         D.att, D.rows, D.att_ws, D.att_ws_bytes, s);
+    st = (c.exact_entropy ? ee_flash_attention_rope_entropy_exact : ee_flash_attention_rope_entropy)(
+        D.qkv, nqkv, D.qkv + nq, nqkv, D.qkv + nq + nkv, nqkv, D.cos, D.sin, c.head_dim, c.batch, c.heads, c.kv_heads,
+        c.seq, c.head_dim, 1, c.attn_scale, D.att, D.rows, D.att_ws, D.att_ws_bytes, s);
     if ((st = dec_check(st, "attention")) != EE_OK) return st;
     st = ee_head_mean_entropy(D.rows, c.batch, c.heads, c.seq, D.ht[cur], batch ? D.hb : nullptr, s);
     if ((st = dec_check(st, "head mean")) != EE_OK) return st;
@@ -362,7 +365,7 @@ int ee_decoder_create(const ee_decoder_config* cfg, int32_t n_layers, const ee_d
   if (cfg == nullptr || !dec_config_ok(*cfg))
     return engine_fail(EE_ERR_INVALID,
                        "ee_decoder_create: bad config (head_dim 64 / 128, heads %% kv_heads == 0, intermediate %% 128 "
-                       "== 0, hidden %% 16 == 0, routing 0 / 1, route_all 0 / 1)");
+                       "== 0, hidden %% 16 == 0, routing 0 / 1, route_all 0 / 1, exact_entropy 0 / 1)");
   if (n_layers <= 0 || layers == nullptr || final_norm == nullptr || cos == nullptr || sin == nullptr)
     return engine_fail(EE_ERR_INVALID, "ee_decoder_create: layers, final_norm, cos and sin are required");
   for (int32_t l = 0; l < n_layers; ++l) {

@@ -160,8 +160,12 @@ struct AttnLaunch {
   int causal;
   void* O;
   float* H;
+  void* ml;  // nullable float2 [B, Hq, S]: each row's (m, l), for the exact-entropy pass
 };
 int launch_flash_attention(const AttnLaunch& a, cudaStream_t s);
+// second pass: H [B, Hq, S] from the fp16-rounded probabilities the reference's eager
+// path takes its entropy of (needs a.ml from launch_flash_attention; a.vt unused)
+int launch_attention_entropy_exact(const AttnLaunch& a, cudaStream_t s);
 // V element (b, h, s, c) at V + b * sb + h * sh + s * ss + c  ->  V^T [B*Hkv, D, S_pad]
 int launch_transpose_v(const void* V, int64_t B, int64_t Hkv, int64_t S, int64_t S_pad, int64_t D, int64_t sb,
                        int64_t sh, int64_t ss, void* VT, cudaStream_t s);

@@ -373,6 +373,7 @@ int launch_flash_attention(const AttnLaunch& a, cudaStream_t s) {
   args.causal = a.causal;
   args.O = static_cast<__half*>(a.O);
   args.H = a.H;
+  args.ml = static_cast<float2*>(a.ml);
   const int64_t nqc = (a.S + 2 * kAttnTile - 1) / (2 * kAttnTile);  // 256 query rows per CTA
   const dim3 grid(static_cast<unsigned>(a.B * a.Hq * nqc));
   if (a.D == 64)
@@ -380,6 +381,40 @@ int launch_flash_attention(const AttnLaunch& a, cudaStream_t s) {
                       a.vt, args);
   return launch_pdl(flash_attention_entropy_kernel<128>, grid, dim3(kAttnThreads), AttnCfg<128>::kSmem, s, a.q, a.k,
                     a.vt, args);
+}
+
+int launch_attention_entropy_exact(const AttnLaunch& a, cudaStream_t s) {
+  static std::once_flag once[64];
+  static cudaError_t err[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || a.ml == nullptr) return -4;
+  std::call_once(once[dev], [dev] {
+    err[dev] = cudaFuncSetAttribute(attention_entropy_exact_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(ExactCfg<64>::kSmem));
+    if (err[dev] == cudaSuccess)
+      err[dev] = cudaFuncSetAttribute(attention_entropy_exact_kernel<128>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(ExactCfg<128>::kSmem));
+  });
+  if (err[dev] != cudaSuccess) return -4;
+  AttnArgs args;
+  args.B = a.B;
+  args.Hq = a.Hq;
+  args.Hkv = a.Hkv;
+  args.S = a.S;
+  args.S_pad = a.S_pad;
+  args.scale = a.scale;
+  args.causal = a.causal;
+  args.O = nullptr;
+  args.H = a.H;
+  args.ml = static_cast<float2*>(a.ml);
+  const int64_t nqc = (a.S + 2 * kAttnTile - 1) / (2 * kAttnTile);
+  const dim3 grid(static_cast<unsigned>(a.B * a.Hq * nqc));
+  if (a.D == 64)
+    return launch_pdl(attention_entropy_exact_kernel<64>, grid, dim3(kAttnThreads), ExactCfg<64>::kSmem, s, a.q,
+                      a.k, args);
+  return launch_pdl(attention_entropy_exact_kernel<128>, grid, dim3(kAttnThreads), ExactCfg<128>::kSmem, s, a.q,
+                    a.k, args);
 }
 
 int read_and_clear_device_error(int* value) {

@@ -183,7 +183,7 @@ class _DecoderConfigC(ctypes.Structure):
                 ("heads", ctypes.c_int64), ("kv_heads", ctypes.c_int64), ("head_dim", ctypes.c_int64),
                 ("intermediate", ctypes.c_int64), ("rms_eps", ctypes.c_float), ("attn_scale", ctypes.c_float),
                 ("tau_low", ctypes.c_double), ("tau_high", ctypes.c_double), ("routing", ctypes.c_int32),
-                ("route_all", ctypes.c_int32)]
+                ("route_all", ctypes.c_int32), ("exact_entropy", ctypes.c_int32)]
 
 
 def _pack_c(p) -> _WeightPackC:
@@ -196,7 +196,7 @@ class DecoderEngine:
     on the device).
 
     ``blocks`` are ``EntropyDispatchedLlamaBlock`` layers built with ``attention="flash"``
-    (their weight packs, norms and attention weights are used in place); ``final_norm``
+    (their weight packs, norms, attention weights and entropy mode are used in place); ``final_norm``
     the model's last RMSNorm weight; ``position_embeddings`` the (cos, sin) tables of the
     rotary embedding for [batch, seq] positions (fp16 [batch, seq, head_dim], what
     transformers' rotary module returns).  ``routing`` / ``route_all`` as the blocks'.
@@ -222,11 +222,13 @@ class DecoderEngine:
         self.batch, self.seq, self.hidden = int(batch), int(seq), int(hidden)
         M = self.batch * self.seq
         cfg = _DecoderConfigC(self.batch, self.seq, hidden, heads, kv, d, inter, eps, float(attn.scaling),
-                              float(tau_low), float(tau_high), 0 if routing == "token" else 1, int(bool(route_all)))
+                              float(tau_low), float(tau_high), 0 if routing == "token" else 1, int(bool(route_all)),
+                              int(bool(b0.exact_entropy)))
         self._keep = []
         layers = (_DecoderLayerC * len(blocks))()
         for i, blk in enumerate(blocks):
             _require(blk.attention == "flash", "DecoderEngine needs blocks built with attention='flash'")
+            _require(blk.exact_entropy == b0.exact_entropy, "every block must use the same entropy mode")
             _require(float(blk.input_layernorm.variance_epsilon) == eps and
                      float(blk.post_attention_layernorm.variance_epsilon) == eps, "every RMSNorm must share eps")
             gu = blk.swiglu_pack()
@@ -273,7 +275,7 @@ class DecoderEngine:
 
     @classmethod
     def from_model(cls, model, batch: int, seq: int, tau_low: float = 0.41, tau_high: float = 1.68,
-                   routing: str = "token", route_all: bool = False) -> "DecoderEngine":
+                   routing: str = "token", route_all: bool = False, exact_entropy: bool = False) -> "DecoderEngine":
         """Engine over every decoder layer of a transformers Llama model (LlamaForCausalLM
         or LlamaModel, fp16 on the device): the layers are wrapped as the reference's
         build_dispatched_llama does (EE/python/dispatch.py:250-259), with flash attention;
@@ -286,7 +288,7 @@ class DecoderEngine:
             wrap = torch.nn.Module()
             wrap.model = base
         blocks, _ = build_dispatched_llama(wrap, tau_low, tau_high, routing=routing, attention="flash",
-                                           route_all=route_all)
+                                           route_all=route_all, exact_entropy=exact_entropy)
         dev = base.norm.weight.device
         pos = torch.arange(seq, device=dev).unsqueeze(0).expand(batch, seq)
         probe = torch.empty(batch, seq, base.norm.weight.numel(), dtype=torch.float16, device=dev)

@@ -406,13 +406,16 @@ def flash_attention_entropy(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, c
 
 def flash_attention_rope_entropy(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor,
                                  sin: torch.Tensor, num_heads: int, num_kv_heads: int, causal: bool = True,
-                                 scale: float | None = None, return_rows: bool = False, return_token: bool = False):
+                                 scale: float | None = None, return_rows: bool = False, return_token: bool = False,
+                                 exact_entropy: bool = False):
     """flash_attention_entropy on the projections' outputs: q fp16 [B, S, Hq*d], k / v fp16
     [B, S, Hkv*d] (any row stride, unit column stride), cos / sin fp16 [B, S, d] (what
     transformers' LlamaRotaryEmbedding returns).  The rotary embedding is applied in the
     same launch chain with the roundings of transformers' apply_rotary_pos_emb on fp16
     tensors, so the result equals flash_attention_entropy(apply_rotary_pos_emb(...)) bit
-    for bit.  Returns what flash_attention_entropy returns."""
+    for bit.  Returns what flash_attention_entropy returns.  With ``exact_entropy`` the
+    row entropies are the reference's: of the probabilities rounded to fp16 as the eager
+    attention returns them (a second tensor-core pass over the keys)."""
     for t, n in ((q, "q"), (k, "k"), (v, "v"), (cos, "cos"), (sin, "sin")):
         _check_cuda(t, n)
         _require(t.dim() == 3 and t.dtype == torch.float16 and t.stride(-1) == 1, f"{n} must be fp16 [B, S, n] rows")
@@ -426,9 +429,13 @@ def flash_attention_rope_entropy(q: torch.Tensor, k: torch.Tensor, v: torch.Tens
     scale = float(d ** -0.5 if scale is None else scale)
     out = torch.empty(B, S, Hq, d, dtype=torch.float16, device=q.device)
     rows = torch.empty(B, Hq, S, dtype=torch.float32, device=q.device)
-    ws = _workspace(_lib.load().ee_attention_rope_workspace_bytes(B, Hq, Hkv, S, d), q.device)
+    lib = _lib.load()
+    ws_bytes = (lib.ee_attention_exact_workspace_bytes if exact_entropy else lib.ee_attention_rope_workspace_bytes)(
+        B, Hq, Hkv, S, d)
+    ws = _workspace(ws_bytes, q.device)
+    name = "ee_flash_attention_rope_entropy_exact" if exact_entropy else "ee_flash_attention_rope_entropy"
     with torch.cuda.device(q.device):
-        call("ee_flash_attention_rope_entropy", q.data_ptr(), q.stride(1), k.data_ptr(), k.stride(1), v.data_ptr(),
+        call(name, q.data_ptr(), q.stride(1), k.data_ptr(), k.stride(1), v.data_ptr(),
              v.stride(1), cos.data_ptr(), sin.data_ptr(), cos.stride(1), B, Hq, Hkv, S, d, int(bool(causal)), scale,
              out.data_ptr(), rows.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
     token, batch = head_mean_entropy(rows)

@@ -30,7 +30,7 @@ class EntropyDispatchedLlamaBlock(nn.Module):
     """EE/python/dispatch.py:150-247 with the sm_100a kernels."""
 
     def __init__(self, llama_block, layer_idx: int = 0, routing: str = "batch", attention: str = "eager",
-                 route_all: bool = False):
+                 route_all: bool = False, exact_entropy: bool = False):
         super().__init__()
         _require(routing in ("batch", "token"), "routing must be 'batch' or 'token'")
         _require(attention in ("eager", "flash"), "attention must be 'eager' or 'flash'")
@@ -39,6 +39,9 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         self.routing = routing
         self.attention = attention
         self.route_all = route_all
+        # flash attention: route by the entropy of the fp16-rounded probabilities, as the
+        # reference's eager block computes it (a second pass over the keys), or online
+        self.exact_entropy = bool(exact_entropy)
         self.self_attn = llama_block.self_attn
         self.input_layernorm = llama_block.input_layernorm
         self.post_attention_layernorm = llama_block.post_attention_layernorm
@@ -162,7 +165,8 @@ class EntropyDispatchedLlamaBlock(nn.Module):
             # rotary embedding, head layout and V transpose in the attention's own launches
             Hkv = k.shape[-1] // d
             out, batch, rows, token = flash_attention_rope_entropy(q, k, v, cos, sin, q.shape[-1] // d, Hkv,
-                                                                   causal=True, scale=attn.scaling, return_token=True)
+                                                                   causal=True, scale=attn.scaling, return_token=True,
+                                                                   exact_entropy=self.exact_entropy)
         else:
             q = q.reshape(B, S, -1, d).transpose(1, 2)
             k = k.reshape(B, S, -1, d).transpose(1, 2)
@@ -245,7 +249,7 @@ def _concat_linears(*linears: nn.Linear) -> nn.Linear:
 
 
 def build_dispatched_llama(model, tau_low: float, tau_high: float, routing: str = "batch",
-                           attention: str = "eager", route_all: bool = False):
+                           attention: str = "eager", route_all: bool = False, exact_entropy: bool = False):
     """EE/python/dispatch.py:250-259: wraps every decoder layer of a transformers Llama
     model; returns (blocks, dispatcher).  ``route_all`` also dispatches q / k / v / o
     (with ``attention="flash"``)."""
@@ -253,7 +257,7 @@ def build_dispatched_llama(model, tau_low: float, tau_high: float, routing: str 
     blocks = []
     for i, layer in enumerate(model.model.layers):
         block = EntropyDispatchedLlamaBlock(layer, layer_idx=i, routing=routing, attention=attention,
-                                            route_all=route_all)
+                                            route_all=route_all, exact_entropy=exact_entropy)
         block = block.to(device).half()
         block.eval()
         blocks.append(block)
