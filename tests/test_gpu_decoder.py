@@ -91,3 +91,30 @@ def test_linear_f16_matches_torch(pkg, cuda):
     ref = (x.double() @ w.double().t())
     rel = ((y.double() - ref).norm() / ref.norm()).item()
     assert rel < 1e-3
+
+
+@torch.no_grad()
+def test_blocks_from_pack_file_equal_quantised_blocks(pkg, cuda, tmp_path):
+    """A model whose routed linears come from a weight-pack file (no quantisation at load)
+    computes the same forward as the one quantised from its weights, bit for bit."""
+    wrap = _model()
+    model = wrap.model
+    blocks, disp = pkg.build_dispatched_llama(wrap, *TAU, routing="token", attention="flash", route_all=True)
+    path = str(tmp_path / "model.eepack")
+    pkg.packfile.save_dispatched_llama(blocks, path)
+    packs = pkg.packfile.load_packs(path, device=cuda)
+    assert len(packs) == 5 * len(blocks)
+    blocks2, disp2 = pkg.build_dispatched_llama(wrap, *TAU, routing="token", attention="flash", route_all=True,
+                                                packs=packs)
+    B, S = 2, 256
+    ids = torch.randint(0, 512, (B, S), generator=torch.Generator().manual_seed(4)).to(cuda)
+    h0 = model.embed_tokens(ids).half()
+    pos = torch.arange(S, device=cuda).unsqueeze(0).expand(B, S)
+    pe = model.rotary_emb(h0, pos)
+    h, h2 = h0, h0
+    for b1, b2 in zip(blocks, blocks2):
+        assert b2.gate_proj._pack().w_i8.data_ptr() == packs[f"layers.{b1.layer_idx}.gate_proj"].w_i8.data_ptr()
+        h = b1(h, dispatcher=disp, position_ids=pos, position_embeddings=pe)[0]
+        h2 = b2(h2, dispatcher=disp2, position_ids=pos, position_embeddings=pe)[0]
+    torch.cuda.synchronize()
+    assert torch.equal(h, h2)

@@ -10,7 +10,7 @@ hand-written tcgen05 / TMA kernels behind the C ABI of
 so it is imported through ``__graft_entry__.load_package()`` (module name
 ``tko_b200``).
 """
-from . import _lib, sharding
+from . import _lib, packfile, sharding
 from .dispatch import (
     EntropyDispatchedLinear,
     EntropyRouter,

@@ -304,6 +304,23 @@ class EntropyDispatchedLinear(nn.Module):
             layer.bias = linear.bias.detach().to(torch.float16)
         return layer
 
+    @classmethod
+    def from_pack(cls, pack: WeightPack, bias: Optional[torch.Tensor] = None,
+                  scale_dtype: torch.dtype = torch.float32) -> "EntropyDispatchedLinear":
+        """A routed linear over a ready pack (a weight-pack file), with no quantisation at
+        load: ``weight_int8`` [K, N] is a view of the pack's int8 [N, K] and ``weight_scale``
+        the pack's scale (as ``scale_dtype``: fp16 for blocks that ``.half()`` converts, as
+        build_dispatched_llama does, so the conversion leaves the pack in place)."""
+        layer = cls(pack.K, pack.N, bias=bias is not None)
+        layer.weight_int8 = pack.w_i8.t()
+        layer.weight_scale = pack.scale.to(scale_dtype)
+        layer.pack = pack
+        w, s = layer.weight_int8, layer.weight_scale
+        layer._pack_key = (w.data_ptr(), w._version, w.device, s.data_ptr(), s._version, s.dtype)
+        if bias is not None:
+            layer.bias = bias.detach().to(torch.float16)
+        return layer
+
     def _pack(self) -> WeightPack:
         """The operand packs of the current buffers.  Rebuilt when a buffer moved or
         changed: ``module.half()`` (as the reference's build_dispatched_llama applies,

@@ -63,6 +63,21 @@ class WeightPack:
                  self.w_e4m3.data_ptr(), self.w_f16.data_ptr(), _stream())
 
     @classmethod
+    def from_arrays(cls, w_i8: torch.Tensor, w_e4m3: torch.Tensor, w_f16: torch.Tensor,
+                    scale: torch.Tensor) -> "WeightPack":
+        """A pack from its four arrays as stored (a weight-pack file): int8, e4m3 codes and
+        fp16 [N, K] and the fp32 scale [N], all on one device; nothing is recomputed."""
+        N, K = w_i8.shape
+        _require(w_i8.dtype == torch.int8 and w_e4m3.dtype == torch.uint8 and w_f16.dtype == torch.float16 and
+                 scale.dtype == torch.float32, "pack arrays must be int8 / uint8 / fp16 / fp32")
+        _require(w_e4m3.shape == (N, K) and w_f16.shape == (N, K) and scale.shape == (N,), "pack array shapes")
+        self = cls.__new__(cls)
+        self.K, self.N = int(K), int(N)
+        self.w_i8, self.w_e4m3, self.w_f16 = w_i8.contiguous(), w_e4m3.contiguous(), w_f16.contiguous()
+        self.scale = scale.contiguous()
+        return self
+
+    @classmethod
     def from_weight(cls, weight: torch.Tensor) -> "WeightPack":
         """Quantise an nn.Linear weight [N, K] on the device, then pack it."""
         w_int8, scale = quantize_weights_int8(weight)

@@ -30,7 +30,7 @@ class EntropyDispatchedLlamaBlock(nn.Module):
     """EE/python/dispatch.py:150-247 with the sm_100a kernels."""
 
     def __init__(self, llama_block, layer_idx: int = 0, routing: str = "batch", attention: str = "eager",
-                 route_all: bool = False, exact_entropy: bool = False):
+                 route_all: bool = False, exact_entropy: bool = False, packs: Optional[dict] = None):
         super().__init__()
         _require(routing in ("batch", "token"), "routing must be 'batch' or 'token'")
         _require(attention in ("eager", "flash"), "attention must be 'eager' or 'flash'")
@@ -45,16 +45,25 @@ class EntropyDispatchedLlamaBlock(nn.Module):
         self.self_attn = llama_block.self_attn
         self.input_layernorm = llama_block.input_layernorm
         self.post_attention_layernorm = llama_block.post_attention_layernorm
-        self.gate_proj = EntropyDispatchedLinear.from_linear(llama_block.mlp.gate_proj)
-        self.up_proj = EntropyDispatchedLinear.from_linear(llama_block.mlp.up_proj)
-        self.down_proj = EntropyDispatchedLinear.from_linear(llama_block.mlp.down_proj)
+        def routed(name, make_linear):
+            # from a weight-pack file when it holds this linear (no quantisation at load)
+            if packs is not None and name in packs:
+                p = packs[name]
+                p = p.to_weight_pack() if hasattr(p, "to_weight_pack") else p
+                return EntropyDispatchedLinear.from_pack(p, scale_dtype=torch.float16)
+            return EntropyDispatchedLinear.from_linear(make_linear())
+
+        mlp = llama_block.mlp
+        self.gate_proj = routed("gate_proj", lambda: mlp.gate_proj)
+        self.up_proj = routed("up_proj", lambda: mlp.up_proj)
+        self.down_proj = routed("down_proj", lambda: mlp.down_proj)
         self.act_fn = nn.SiLU()
         if route_all:
             # every linear of the block entropy-dispatched: q / k / v as one concatenated
             # projection (per-output-channel scales: concatenation changes nothing), o
             a = llama_block.self_attn
-            self.qkv_proj = EntropyDispatchedLinear.from_linear(_concat_linears(a.q_proj, a.k_proj, a.v_proj))
-            self.o_proj = EntropyDispatchedLinear.from_linear(a.o_proj)
+            self.qkv_proj = routed("qkv_proj", lambda: _concat_linears(a.q_proj, a.k_proj, a.v_proj))
+            self.o_proj = routed("o_proj", lambda: a.o_proj)
         a = llama_block.self_attn
         self._qkv_split = (a.q_proj.out_features, a.k_proj.out_features, a.v_proj.out_features)
         self.layer_entropy: Optional[torch.Tensor] = None
@@ -249,15 +258,22 @@ def _concat_linears(*linears: nn.Linear) -> nn.Linear:
 
 
 def build_dispatched_llama(model, tau_low: float, tau_high: float, routing: str = "batch",
-                           attention: str = "eager", route_all: bool = False, exact_entropy: bool = False):
+                           attention: str = "eager", route_all: bool = False, exact_entropy: bool = False,
+                           packs: Optional[dict] = None):
     """EE/python/dispatch.py:250-259: wraps every decoder layer of a transformers Llama
     model; returns (blocks, dispatcher).  ``route_all`` also dispatches q / k / v / o
-    (with ``attention="flash"``)."""
+    (with ``attention="flash"``).  ``packs`` (``packfile.load_packs`` of a file written by
+    ``packfile.save_dispatched_llama``) supplies the routed linears' packs instead of
+    quantising the model's weights."""
     device = next(model.parameters()).device
     blocks = []
     for i, layer in enumerate(model.model.layers):
+        mine = None
+        if packs is not None:
+            pre = f"layers.{i}."
+            mine = {k[len(pre):]: v for k, v in packs.items() if k.startswith(pre)}
         block = EntropyDispatchedLlamaBlock(layer, layer_idx=i, routing=routing, attention=attention,
-                                            route_all=route_all, exact_entropy=exact_entropy)
+                                            route_all=route_all, exact_entropy=exact_entropy, packs=mine)
         block = block.to(device).half()
         block.eval()
         blocks.append(block)
