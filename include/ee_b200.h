@@ -401,6 +401,55 @@ EE_API int ee_engine_capture(ee_engine* engine, void* stream);
 EE_API int ee_engine_launch(ee_engine* engine, void* stream);
 EE_API int ee_engine_destroy(ee_engine* engine);
 
+/* ---------------------------------------------------------------- entropy-tied KV cache
+ * The reference lists "dynamic KV-cache compression tied to the entropy metric" as its
+ * next step (README, Work In Progress) and has no code for it.  Here every cached token
+ * keeps its keys and values at the precision of its entropy tier -- the same dual-
+ * threshold route ids as the linears (0 INT8, 1 FP8-e4m3, 2 FP16): INT8 codes
+ * q = rn(x / s), s = amax / 127, or e4m3 codes of x / s, s = amax / 448, with one fp32
+ * scale per (token, KV head), or the fp16 values -- in two slot pools (8-bit: slots8
+ * token slots, fp16: slots16) shared by the batch's sequences and addressed through a
+ * per-sequence slot table, so the cache holds about 1 byte per value for 8-bit tokens
+ * and the decode attention reads that much less.  One device allocation of
+ * ee_kv_cache_bytes, carved by ee_kv_cache_init; the caller keeps the struct. */
+typedef struct ee_kv_cache {
+  int64_t batch, kv_heads, head_dim, max_tokens, slots8, slots16;
+  uint8_t* k8;         /* [slots8, kv_heads, head_dim] INT8 / e4m3 codes */
+  uint8_t* v8;
+  void* k16;           /* [slots16, kv_heads, head_dim] fp16 */
+  void* v16;
+  float* k_scale;      /* [slots8, kv_heads] */
+  float* v_scale;
+  int32_t* slot;       /* [batch, max_tokens]: (tier << 28) | slot in its pool */
+  int32_t* length;     /* [batch] tokens stored */
+  uint32_t* pool_used; /* [2] slots taken in the 8-bit and fp16 pools */
+} ee_kv_cache;
+
+EE_API size_t ee_kv_cache_bytes(int64_t batch, int64_t kv_heads, int64_t head_dim, int64_t max_tokens,
+                                int64_t slots8, int64_t slots16);
+/* Lays the cache out in `memory` (256-byte aligned, ee_kv_cache_bytes) and empties it
+ * (every length and pool counter zero) on `stream`.  head_dim 64 or 128. */
+EE_API int ee_kv_cache_init(ee_kv_cache* cache, void* memory, size_t bytes, int64_t batch, int64_t kv_heads,
+                            int64_t head_dim, int64_t max_tokens, int64_t slots8, int64_t slots16, void* stream);
+/* Appends t_new tokens to every sequence: row b * t_new + t of k_rows / v_rows (fp16
+ * [batch * t_new, kv_heads * head_dim], row strides ldk / ldv; K after the rotary
+ * embedding) at tier[b * t_new + t].  A token that finds its pool or its sequence full
+ * is not stored and sets the device error word (ee_device_check, bit 8). */
+EE_API int ee_kv_append(const ee_kv_cache* cache, const void* k_rows, int64_t ldk, const void* v_rows, int64_t ldv,
+                        const int8_t* tier, int64_t t_new, void* stream);
+/* One decode step's attention: query row b (fp16 q [batch, heads * head_dim], row stride
+ * ldq; heads a multiple of kv_heads: 1, 2, 4 or 8 query heads per KV head) against the
+ * sequence's cached tokens and its own new K / V rows (k_new / v_new fp16 [batch,
+ * kv_heads * head_dim], row stride ld_new, not yet appended), softmax(scale q k) v ->
+ * out fp16 [batch, heads * head_dim] (row stride ldo), and H (nullable, fp32 [batch,
+ * heads]) the entropy of each softmax row: the router input of the new token.  The
+ * tokens are split over CTAs (flash-decoding) whose partials merge in a second launch;
+ * workspace: ee_kv_decode_workspace_bytes. */
+EE_API size_t ee_kv_decode_workspace_bytes(int64_t batch, int64_t kv_heads, int64_t heads, int64_t head_dim);
+EE_API int ee_kv_decode_attention(const ee_kv_cache* cache, const void* q, int64_t ldq, int64_t heads,
+                                  const void* k_new, const void* v_new, int64_t ld_new, float scale, void* out,
+                                  int64_t ldo, float* H, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------- decoder-stack engine
  * The whole decoder stack of a Llama-architecture model for one fixed batch shape
  * [batch, seq] as one native object: the reference's Python layer loop

@@ -172,3 +172,20 @@ def test_decoder_engine_argument_checks(pkg, lib):
     assert lib.ee_decoder_destroy(None) == 0
     assert lib.ee_head_mean_entropy(None, 2, 4, 8, p, None, None) == EE_ERR_INVALID
     assert lib.ee_head_mean_entropy(ctypes.c_void_p(4098), 2, 4, 8, p, None, None) == EE_ERR_MISALIGNED
+
+
+def test_kv_cache_argument_checks(pkg, lib):
+    from importlib import import_module
+
+    kvc = import_module("tko_b200.kvcache")
+    assert lib.ee_kv_cache_bytes(2, 8, 128, 4096, 1000, 1000) > 0
+    assert lib.ee_kv_cache_bytes(2, 8, 96, 4096, 1000, 1000) == 0  # head_dim 64 or 128
+    assert lib.ee_kv_cache_bytes(2, 8, 128, 4096, 1 << 28, 1) == 0  # slot index above 28 bits
+    c = kvc._KvCacheC()
+    p = ctypes.c_void_p(4096)
+    assert lib.ee_kv_cache_init(None, p, 1 << 30, 2, 8, 128, 64, 8, 8, None) == EE_ERR_INVALID
+    assert lib.ee_kv_cache_init(ctypes.byref(c), p, 16, 2, 8, 128, 64, 8, 8, None) == EE_ERR_INVALID  # too small
+    assert lib.ee_kv_append(ctypes.byref(c), p, 1024, p, 1024, p, 1, None) == EE_ERR_INVALID  # not initialised
+    assert lib.ee_kv_decode_workspace_bytes(2, 8, 32, 128) > 0
+    assert lib.ee_kv_decode_attention(ctypes.byref(c), p, 4096, 32, p, p, 1024, 0.1, p, 4096, None, p, 1 << 20,
+                                      None) == EE_ERR_INVALID

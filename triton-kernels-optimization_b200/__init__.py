@@ -10,7 +10,8 @@ hand-written tcgen05 / TMA kernels behind the C ABI of
 so it is imported through ``__graft_entry__.load_package()`` (module name
 ``tko_b200``).
 """
-from . import _lib, packfile, sharding
+from . import _lib, kvcache, packfile, sharding
+from .kvcache import EntropyKVCache
 from .dispatch import (
     EntropyDispatchedLinear,
     EntropyRouter,

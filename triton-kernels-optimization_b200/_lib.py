@@ -48,6 +48,12 @@ SIGNATURES = {
     "ee_flash_attention_rope_entropy_exact": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, _P, c_int64,
                                                       c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_float,
                                                       _P, _P, _P, c_size_t, _P]),
+    "ee_kv_cache_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int64, c_int64]),
+    "ee_kv_cache_init": (c_int, [_P, _P, c_size_t, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, _P]),
+    "ee_kv_append": (c_int, [_P, _P, c_int64, _P, c_int64, _P, c_int64, _P]),
+    "ee_kv_decode_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64]),
+    "ee_kv_decode_attention": (c_int, [_P, _P, c_int64, c_int64, _P, _P, c_int64, c_float, _P, c_int64, _P, _P,
+                                       c_size_t, _P]),
     "ee_add_rmsnorm": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, c_float, _P, c_int64, c_int64, c_int64,
                                _P]),
     "ee_route": (c_int, [_P, c_int64, c_double, c_double, _P, _P]),

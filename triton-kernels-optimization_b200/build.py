@@ -18,7 +18,7 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_NAME = "libee_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 SOURCES = ["ee_kernels.cu", "ee_capi.cu", "ee_engine.cu"]
-DEPS = SOURCES + ["ee_internal.h", "ee_ptx.cuh", "ee_rows.cuh", "ee_gemm.cuh", "ee_gemm_skinny.cuh", "ee_attention.cuh", "ee_block.cuh"]
+DEPS = SOURCES + ["ee_internal.h", "ee_ptx.cuh", "ee_rows.cuh", "ee_gemm.cuh", "ee_gemm_skinny.cuh", "ee_attention.cuh", "ee_block.cuh", "ee_kvcache.cuh"]
 HEADER = os.path.join(os.path.dirname(PKG_DIR), "include", "ee_b200.h")
 
 NVCC_FLAGS = [

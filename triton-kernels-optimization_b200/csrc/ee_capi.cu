@@ -653,6 +653,142 @@ int ee_flash_attention_rope_entropy_exact(const void* q, int64_t ldq, const void
                         workspace, workspace_bytes, stream, true);
 }
 
+// ------------------------------------------------------------------ entropy-tied KV cache
+}  // extern "C"
+namespace {
+struct KvLayout {
+  size_t k8, v8, k16, v16, ks, vs, slot, length, pool, total;
+};
+KvLayout kv_layout(int64_t batch, int64_t kv_heads, int64_t head_dim, int64_t max_tokens, int64_t slots8,
+                   int64_t slots16) {
+  KvLayout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off += align256(bytes);
+    return at;
+  };
+  const size_t row = size_t(kv_heads) * head_dim;
+  L.k8 = take(size_t(slots8) * row);
+  L.v8 = take(size_t(slots8) * row);
+  L.k16 = take(2 * size_t(slots16) * row);
+  L.v16 = take(2 * size_t(slots16) * row);
+  L.ks = take(4 * size_t(slots8) * kv_heads);
+  L.vs = take(4 * size_t(slots8) * kv_heads);
+  L.slot = take(4 * size_t(batch) * max_tokens);
+  L.length = take(4 * size_t(batch));
+  L.pool = take(8);
+  L.total = off;
+  return L;
+}
+bool kv_shape_ok(int64_t batch, int64_t kv_heads, int64_t head_dim, int64_t max_tokens, int64_t slots8,
+                 int64_t slots16) {
+  return batch > 0 && kv_heads > 0 && (head_dim == 64 || head_dim == 128) && max_tokens > 0 && slots8 >= 0 &&
+         slots16 >= 0 && slots8 < (int64_t(1) << 28) && slots16 < (int64_t(1) << 28) &&
+         batch * max_tokens < (int64_t(1) << 31) && max_tokens < (int64_t(1) << 30);
+}
+ee::KvCacheArgs kv_args(const ee_kv_cache& c) {
+  ee::KvCacheArgs a;
+  a.batch = c.batch;
+  a.kv_heads = c.kv_heads;
+  a.head_dim = c.head_dim;
+  a.max_tokens = c.max_tokens;
+  a.slots8 = c.slots8;
+  a.slots16 = c.slots16;
+  a.k8 = c.k8;
+  a.v8 = c.v8;
+  a.k16 = c.k16;
+  a.v16 = c.v16;
+  a.k_scale = c.k_scale;
+  a.v_scale = c.v_scale;
+  a.slot = c.slot;
+  a.length = c.length;
+  a.pool_used = c.pool_used;
+  return a;
+}
+// token splits of the decode attention: about two CTAs per SM over the batch's KV heads
+int kv_splits(int64_t batch, int64_t kv_heads) {
+  const int64_t ctas = batch * kv_heads;
+  int64_t s = (2 * int64_t(num_sms()) + ctas - 1) / ctas;
+  return static_cast<int>(s < 1 ? 1 : (s > 64 ? 64 : s));
+}
+}  // namespace
+extern "C" {
+
+size_t ee_kv_cache_bytes(int64_t batch, int64_t kv_heads, int64_t head_dim, int64_t max_tokens, int64_t slots8,
+                         int64_t slots16) {
+  if (!kv_shape_ok(batch, kv_heads, head_dim, max_tokens, slots8, slots16)) return 0;
+  return kv_layout(batch, kv_heads, head_dim, max_tokens, slots8, slots16).total;
+}
+
+int ee_kv_cache_init(ee_kv_cache* cache, void* memory, size_t bytes, int64_t batch, int64_t kv_heads,
+                     int64_t head_dim, int64_t max_tokens, int64_t slots8, int64_t slots16, void* stream) {
+  if (cache == nullptr) return fail(EE_ERR_INVALID, "cache is NULL");
+  if (!kv_shape_ok(batch, kv_heads, head_dim, max_tokens, slots8, slots16))
+    return fail(EE_ERR_INVALID, "bad KV-cache shape (head_dim 64 / 128, positive sizes, pools < 2^28 slots)");
+  const KvLayout L = kv_layout(batch, kv_heads, head_dim, max_tokens, slots8, slots16);
+  int st = check_ws(memory, bytes, L.total);
+  if (st != EE_OK) return st;
+  uint8_t* p = static_cast<uint8_t*>(memory);
+  cache->batch = batch;
+  cache->kv_heads = kv_heads;
+  cache->head_dim = head_dim;
+  cache->max_tokens = max_tokens;
+  cache->slots8 = slots8;
+  cache->slots16 = slots16;
+  cache->k8 = p + L.k8;
+  cache->v8 = p + L.v8;
+  cache->k16 = p + L.k16;
+  cache->v16 = p + L.v16;
+  cache->k_scale = reinterpret_cast<float*>(p + L.ks);
+  cache->v_scale = reinterpret_cast<float*>(p + L.vs);
+  cache->slot = reinterpret_cast<int32_t*>(p + L.slot);
+  cache->length = reinterpret_cast<int32_t*>(p + L.length);
+  cache->pool_used = reinterpret_cast<uint32_t*>(p + L.pool);
+  cudaError_t e = cudaMemsetAsync(p + L.length, 0, L.total - L.length, as_stream(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+  return EE_OK;
+}
+
+int ee_kv_append(const ee_kv_cache* cache, const void* k_rows, int64_t ldk, const void* v_rows, int64_t ldv,
+                 const int8_t* tier, int64_t t_new, void* stream) {
+  if (cache == nullptr || cache->length == nullptr) return fail(EE_ERR_INVALID, "cache is not initialised");
+  if (t_new < 0) return fail(EE_ERR_INVALID, "t_new must be >= 0");
+  if (t_new == 0) return EE_OK;
+  if (!k_rows || !v_rows || !tier) return fail(EE_ERR_INVALID, "k_rows, v_rows and tier are required");
+  const int64_t row = cache->kv_heads * cache->head_dim;
+  if (ldk < row || ldv < row || ldk % 8 || ldv % 8 || !al16(k_rows) || !al16(v_rows))
+    return fail(EE_ERR_MISALIGNED, "K / V rows must be 16-byte aligned with strides >= kv_heads * head_dim, % 8");
+  if (cache->batch * t_new >= (int64_t(1) << 31)) return fail(EE_ERR_UNSUPPORTED, "too many tokens in one append");
+  return check_launch(ee::launch_kv_append(kv_args(*cache), k_rows, ldk, v_rows, ldv, tier, t_new, as_stream(stream)),
+                      "kv_append");
+}
+
+size_t ee_kv_decode_workspace_bytes(int64_t batch, int64_t kv_heads, int64_t heads, int64_t head_dim) {
+  if (batch <= 0 || kv_heads <= 0 || heads <= 0 || head_dim <= 0) return 0;
+  return align256(sizeof(float) * size_t(batch) * heads * kv_splits(batch, kv_heads) * (3 + head_dim));
+}
+
+int ee_kv_decode_attention(const ee_kv_cache* cache, const void* q, int64_t ldq, int64_t heads, const void* k_new,
+                           const void* v_new, int64_t ld_new, float scale, void* out, int64_t ldo, float* H,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  if (cache == nullptr || cache->length == nullptr) return fail(EE_ERR_INVALID, "cache is not initialised");
+  const int64_t G = heads / (cache->kv_heads > 0 ? cache->kv_heads : 1);
+  if (heads <= 0 || heads % cache->kv_heads || (G != 1 && G != 2 && G != 4 && G != 8))
+    return fail(EE_ERR_UNSUPPORTED, "heads must be 1, 2, 4 or 8 times kv_heads");
+  if (!q || !k_new || !v_new || !out) return fail(EE_ERR_INVALID, "q, k_new, v_new and out are required");
+  const int64_t d = cache->head_dim;
+  if (ldq < heads * d || ldo < heads * d || ld_new < cache->kv_heads * d || ldq % 8 || ldo % 8 || ld_new % 8 ||
+      !al16(q) || !al16(k_new) || !al16(v_new) || !al16(out) || (reinterpret_cast<uintptr_t>(H) & 3u))
+    return fail(EE_ERR_MISALIGNED, "q / k_new / v_new / out rows 16-byte aligned with strides % 8, H 4-byte aligned");
+  int st = check_ws(workspace, workspace_bytes, ee_kv_decode_workspace_bytes(cache->batch, cache->kv_heads, heads, d));
+  if (st != EE_OK) return st;
+  return check_launch(ee::launch_kv_decode_attention(kv_args(*cache), q, ldq, heads, k_new, v_new, ld_new, scale,
+                                                     kv_splits(cache->batch, cache->kv_heads),
+                                                     static_cast<float*>(workspace), out, ldo, H, as_stream(stream)),
+                      "kv_decode_attention");
+}
+
 int ee_head_mean_entropy(const float* H, int64_t B, int64_t Hq, int64_t S, float* token_entropy,
                          float* batch_entropy, void* stream) {
   if (B < 0 || Hq <= 0 || S < 0 || B * Hq * S >= (int64_t(1) << 40)) return fail(EE_ERR_INVALID, "bad shape");

@@ -17,6 +17,7 @@ enum DeviceError : int {
   kErrWaitTimeout = 1,  // an mbarrier wait in the GEMM gave up
   kErrTmem = 2,         // tensor-memory allocation returned an unusable address
   kErrShape = 4,        // a bucket holds more rows than the kernel's tile was launched for
+  kErrCapacity = 8,     // a KV-cache pool or sequence was full: the token was not stored
 };
 
 // ----------------------------------------------------------------- row kernels
@@ -150,6 +151,30 @@ constexpr int kSkinnyMaxSplits = 8;
 
 // device error word
 int read_and_clear_device_error(int* value);
+
+// entropy-tied KV cache (ee_kvcache.cuh); the fields of ee_kv_cache (include/ee_b200.h)
+struct KvCacheArgs {
+  int64_t batch, kv_heads, head_dim, max_tokens, slots8, slots16;
+  uint8_t* k8;
+  uint8_t* v8;
+  void* k16;
+  void* v16;
+  float* k_scale;
+  float* v_scale;
+  int32_t* slot;
+  int32_t* length;
+  uint32_t* pool_used;
+};
+// append t_new tokens to every sequence (rows b * t_new + t of k_rows / v_rows), each at
+// the tier tier[b * t_new + t]; then the lengths grow by t_new
+int launch_kv_append(const KvCacheArgs& c, const void* k_rows, int64_t ldk, const void* v_rows, int64_t ldv,
+                     const int8_t* tier, int64_t t_new, cudaStream_t s);
+// attention of one new query row per sequence (q rows [batch, Hq * D], row stride ldq)
+// over its cached tokens and its own new K / V rows (k_new / v_new [batch, kv_heads * D],
+// row stride ld_new); part: batch * Hq * splits * (3 + D) floats
+int launch_kv_decode_attention(const KvCacheArgs& c, const void* q, int64_t ldq, int64_t Hq, const void* k_new,
+                               const void* v_new, int64_t ld_new, float scale, int splits, float* part, void* out,
+                               int64_t ldo, float* H, cudaStream_t s);
 // flash attention with row entropy (ee_attention.cuh): Q [B*Hq*S, D], K [B*Hkv*S, D],
 // V^T [B*Hkv*D, S_pad] maps (box 64 x 128 / 64 x D), outputs O [B, S, Hq, D], H [B, Hq, S]
 constexpr int kAttnTile = 128;  // queries per attention CTA and keys per KV tile

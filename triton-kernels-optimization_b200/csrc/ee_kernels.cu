@@ -11,6 +11,7 @@
 #include "ee_gemm.cuh"
 #include "ee_gemm_skinny.cuh"
 #include "ee_internal.h"
+#include "ee_kvcache.cuh"
 #include "ee_rows.cuh"
 
 namespace ee {
@@ -415,6 +416,57 @@ int launch_attention_entropy_exact(const AttnLaunch& a, cudaStream_t s) {
                       a.k, args);
   return launch_pdl(attention_entropy_exact_kernel<128>, grid, dim3(kAttnThreads), ExactCfg<128>::kSmem, s, a.q,
                     a.k, args);
+}
+
+int launch_kv_append(const KvCacheArgs& c, const void* k_rows, int64_t ldk, const void* v_rows, int64_t ldv,
+                     const int8_t* tier, int64_t t_new, cudaStream_t s) {
+  if (c.batch <= 0 || t_new <= 0) return 0;
+  const dim3 grid(static_cast<unsigned>(c.batch * t_new));
+  const auto* kr = static_cast<const __half*>(k_rows);
+  const auto* vr = static_cast<const __half*>(v_rows);
+  int st = c.head_dim == 64
+               ? launch_pdl(kv_append_kernel<64>, grid, dim3(kKvThreads), 0, s, c, kr, ldk, vr, ldv, tier, t_new)
+               : launch_pdl(kv_append_kernel<128>, grid, dim3(kKvThreads), 0, s, c, kr, ldk, vr, ldv, tier, t_new);
+  if (st != 0) return st;
+  return launch_pdl(kv_commit_kernel, dim3(static_cast<unsigned>((c.batch + 127) / 128)), dim3(128), 0, s, c, t_new);
+}
+
+namespace {
+template <int D, int G>
+int run_kv_decode(const KvCacheArgs& c, const void* q, int64_t ldq, const void* k_new, const void* v_new,
+                  int64_t ld_new, float scale, int splits, float* part, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>(c.batch * c.kv_heads), static_cast<unsigned>(splits));
+  return launch_pdl(kv_decode_attention_kernel<D, G>, grid, dim3(kKvThreads), 0, s, c,
+                    static_cast<const __half*>(q), ldq, static_cast<const __half*>(k_new),
+                    static_cast<const __half*>(v_new), ld_new, scale, splits, part);
+}
+template <int D>
+int run_kv_decode_g(const KvCacheArgs& c, int64_t G, const void* q, int64_t ldq, const void* k_new,
+                    const void* v_new, int64_t ld_new, float scale, int splits, float* part, cudaStream_t s) {
+  switch (G) {
+    case 1: return run_kv_decode<D, 1>(c, q, ldq, k_new, v_new, ld_new, scale, splits, part, s);
+    case 2: return run_kv_decode<D, 2>(c, q, ldq, k_new, v_new, ld_new, scale, splits, part, s);
+    case 4: return run_kv_decode<D, 4>(c, q, ldq, k_new, v_new, ld_new, scale, splits, part, s);
+    case 8: return run_kv_decode<D, 8>(c, q, ldq, k_new, v_new, ld_new, scale, splits, part, s);
+    default: return -3;
+  }
+}
+}  // namespace
+
+int launch_kv_decode_attention(const KvCacheArgs& c, const void* q, int64_t ldq, int64_t Hq, const void* k_new,
+                               const void* v_new, int64_t ld_new, float scale, int splits, float* part, void* out,
+                               int64_t ldo, float* H, cudaStream_t s) {
+  if (c.batch <= 0) return 0;
+  const int64_t G = Hq / c.kv_heads;
+  int st = c.head_dim == 64 ? run_kv_decode_g<64>(c, G, q, ldq, k_new, v_new, ld_new, scale, splits, part, s)
+                            : run_kv_decode_g<128>(c, G, q, ldq, k_new, v_new, ld_new, scale, splits, part, s);
+  if (st != 0) return st;
+  const dim3 grid(static_cast<unsigned>(c.batch * Hq));
+  if (c.head_dim == 64)
+    return launch_pdl(kv_decode_combine_kernel<64>, grid, dim3(kKvThreads), 0, s, part, splits,
+                      static_cast<__half*>(out), ldo, H, static_cast<int>(Hq));
+  return launch_pdl(kv_decode_combine_kernel<128>, grid, dim3(kKvThreads), 0, s, part, splits,
+                    static_cast<__half*>(out), ldo, H, static_cast<int>(Hq));
 }
 
 int read_and_clear_device_error(int* value) {
