@@ -59,6 +59,7 @@ struct TileGeo {
   int cnt[3], off[3], mtiles[3], tiles[3];
   int halfmt[3];  // the bucket's half row tile (last m-tile with at most bm / 2 rows), or -1
   int spl[3];     // K ranges per tile
+  int gm[3];      // row tiles per raster group (tile_mn)
   int ntn, ntiles;
   int total;      // work units
 };
@@ -158,6 +159,32 @@ __device__ __forceinline__ void plan_splits_warp(TileGeo& g, const GemmArgs& a, 
 // when it holds at most 128 rows (instead of an M = 256 tile that is mostly padding).
 // K splits only for 256-column tiles (one partial block per CTA of a tile).  Called by
 // one whole warp (the split plan is spread over its lanes).
+//
+// Raster order of a bucket's tiles.  When the bucket's activation rows fit in L2 many
+// times over (at most kRasterWholeBytes), every row tile of an N column is visited before
+// the next column: CTAs running together share the weight tile and the rows stay in L2.
+// Above that (tens of thousands of rows at large K) sweeping all rows per column would
+// stream the activations from HBM once per wave, so the tiles go in groups of gm row
+// tiles (about kRasterGroupBytes of activations): every column of the group's rows before
+// the next group, the row tile fastest inside a group.
+constexpr long long kRasterWholeBytes = 64ll << 20;
+constexpr long long kRasterGroupBytes = 32ll << 20;
+__device__ __forceinline__ int raster_group(int mtiles, int bm, int K, int b) {
+  const long long per = static_cast<long long>(bm) * K * (b == kFP16 ? 2 : 1);  // bytes of one row tile
+  if (per * mtiles <= kRasterWholeBytes) return mtiles > 0 ? mtiles : 1;
+  const long long g = kRasterGroupBytes / per;
+  return g < 1 ? 1 : (g > mtiles ? mtiles : static_cast<int>(g));
+}
+// tile lt of a bucket -> (row tile, column tile) in that order
+__device__ __forceinline__ void tile_mn(int lt, int mtiles, int ntn, int gm, int& mt, int& nt) {
+  const int per_group = gm * ntn;
+  const int first = (lt / per_group) * gm;
+  const int in = lt - (lt / per_group) * per_group;
+  const int rows = mtiles - first < gm ? mtiles - first : gm;
+  mt = first + in % rows;
+  nt = in / rows;
+}
+
 __device__ __forceinline__ TileGeo make_geo_warp(const GemmArgs& a, int bm, int bn, bool half_tiles, int lane) {
   TileGeo g;
   if (a.dyn_counts != nullptr) {
@@ -179,6 +206,7 @@ __device__ __forceinline__ TileGeo make_geo_warp(const GemmArgs& a, int bm, int 
     g.ntiles += g.tiles[b];
     const int rem = g.cnt[b] % bm;
     g.halfmt[b] = (half_tiles && rem >= 1 && rem <= bm / 2) ? g.mtiles[b] - 1 : -1;
+    g.gm[b] = raster_group(g.mtiles[b], bm, a.K, b);
   }
   if (bn == kBN) {
     plan_splits_warp(g, a, bm == 2 * kBM ? 2 : 1, lane);
@@ -217,8 +245,8 @@ struct Unit {
 __device__ __forceinline__ Unit unit_in(const TileGeo& g, int b, int u, int bm, int bn, int K) {
   const int S = g.spl[b];
   const int t = u / S, r = u % S;
-  const int mt = t % g.mtiles[b];
-  const int nt = t / g.mtiles[b];
+  int mt, nt;
+  tile_mn(t, g.mtiles[b], g.ntn, g.gm[b], mt, nt);
   const int nkb = kblocks_of(b, K);
   Unit w;
   w.b = b;
@@ -1190,7 +1218,9 @@ __global__ void __launch_bounds__(kReduceThreads, 2) reduce_partials_kernel(cons
   const int mtiles = b == 2 ? geo.mtiles[2] : (b == 1 ? geo.mtiles[1] : geo.mtiles[0]);
   const int halfmt = b == 2 ? geo.halfmt[2] : (b == 1 ? geo.halfmt[1] : geo.halfmt[0]);
   const int off = b == 2 ? geo.off[2] : (b == 1 ? geo.off[1] : geo.off[0]);
-  const int mt = lt % mtiles, nt = lt / mtiles;
+  const int gm = b == 2 ? geo.gm[2] : (b == 1 ? geo.gm[1] : geo.gm[0]);
+  int mt, nt;
+  tile_mn(lt, mtiles, geo.ntn, gm, mt, nt);
   const bool half = mt == halfmt;
   const int pos0 = off + mt * bm, n0 = nt * kBN;
   const int ubase = b == 2 ? 0 : (b == 1 ? t2 * geo.spl[2] : t2 * geo.spl[2] + t1 * geo.spl[1]);
