@@ -79,3 +79,51 @@ def test_flash_token_routes_match_eager_reference_outside_band(pkg, cuda, d, Hkv
                                    "mix_ref": [int((want == t).sum()) for t in range(3)]}
         assert not (differ & ~in_band).any(), stats
     print("flash-route-parity " + json.dumps(stats))
+
+
+@pytest.mark.parametrize("d,Hkv,S", [(64, 4, 1024), (128, 8, 1024)])
+@torch.no_grad()
+def test_exact_entropy_mode_matches_eager_reference(pkg, cuda, d, Hkv, S):
+    """The exact-entropy mode (a second tensor-core pass that rounds every probability to
+    fp16 as the eager attention returns it) against the same reference: row entropies
+    within 1e-4 relative but for at most 1e-4 of the rows -- rows where one fp16 score of
+    torch's matmul rounds the other way than the tensor core's (both sum in fp32, in
+    different orders) -- and all within 1e-2; per-token routes identical outside
+    |H_ref - tau| < 1e-4 * max(1, H_ref), the count of tokens in that band reported."""
+    B, Hq = 2, 32
+    q, k, v = _inputs(B, Hq, Hkv, S, d, cuda, seed=11 + d)
+    scale = d ** -0.5
+    rows_ref = _reference_rows(q, k, scale)
+    # the rotary variant with cos = 1, sin = 0 is plain attention on [B, S, H * d] rows
+    qb, kb, vb = (t.transpose(1, 2).reshape(B, S, -1).contiguous() for t in (q, k, v))
+    cos = torch.ones(B, S, d, device=cuda, dtype=torch.float16)
+    sin = torch.zeros_like(cos)
+    out_on, _, rows_on, _ = pkg.flash_attention_rope_entropy(qb, kb, vb, cos, sin, Hq, Hkv, scale=scale,
+                                                             return_token=True)
+    out, _, rows, token = pkg.flash_attention_rope_entropy(qb, kb, vb, cos, sin, Hq, Hkv, scale=scale,
+                                                           return_token=True, exact_entropy=True)
+    torch.cuda.synchronize()
+    assert pkg._lib.device_check() == 0
+    assert torch.equal(out, out_on)  # the output is the first pass's either way
+    err = (rows - rows_ref).abs()
+    beyond = err > 1e-6 + 1e-4 * rows_ref.abs()
+    stats = {"d": d, "rows": rows.numel(), "rows_beyond_1e-4": int(beyond.sum()),
+             "rel_err_max": (err / rows_ref.clamp_min(1e-3)).max().item(),
+             "online_rows_beyond_1e-4": int(((rows_on - rows_ref).abs() > 1e-6 + 1e-4 * rows_ref.abs()).sum())}
+    assert int(beyond.sum()) <= max(1, rows.numel() // 10000), stats
+    assert torch.allclose(rows, rows_ref, rtol=1e-2, atol=1e-4), stats
+    tok_ref = rows_ref.mean(dim=1)
+    for tl, th in TAUS:
+        routes = []
+        for h in (tok_ref, token):
+            r = pkg.EntropyRouter(tl, th)
+            r.reserve(B * S, 16, cuda)
+            routes.append(r.route_entropy(h.reshape(-1)).clone())
+        h = tok_ref.reshape(-1)
+        band = 1e-4 * h.abs().clamp_min(1.0)
+        in_band = ((h - tl).abs() < band) | ((h - th).abs() < band)
+        differ = routes[0] != routes[1]
+        stats[f"tau_{tl}_{th}"] = {"route_mismatch": int(differ.sum()), "band_tokens": int(in_band.sum()),
+                                   "mismatch_outside_band": int((differ & ~in_band).sum())}
+        assert not (differ & ~in_band).any(), stats
+    print("exact-entropy-parity " + json.dumps(stats))

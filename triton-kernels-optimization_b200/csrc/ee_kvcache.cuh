@@ -222,11 +222,13 @@ __global__ void __launch_bounds__(kKvThreads) kv_decode_attention_kernel(const K
       for (int off = 16; off > 0; off >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, off);
       // sdot = score * log2 e; online update of m, l, t (base 2) and o
       if (sdot > m[g]) {
-        const float alpha = m[g] == -__builtin_huge_valf() ? 0.f : exp2f(m[g] - sdot);
-        tt[g] = alpha * (tt[g] + l[g] * (m[g] - sdot));
-        l[g] *= alpha;
+        if (m[g] != -__builtin_huge_valf()) {  // (the first token has nothing to rescale)
+          const float alpha = exp2f(m[g] - sdot);
+          tt[g] = alpha * (tt[g] + l[g] * (m[g] - sdot));
+          l[g] *= alpha;
 #pragma unroll
-        for (int e = 0; e < E; ++e) o[g][e] *= alpha;
+          for (int e = 0; e < E; ++e) o[g][e] *= alpha;
+        }
         m[g] = sdot;
       }
       const float p = exp2f(sdot - m[g]);
