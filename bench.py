@@ -536,6 +536,7 @@ def measure_configs(torch, pkg, dev, peaks, flush) -> dict:
     del a2
     torch.cuda.empty_cache()
     out["config4_tinyllama_forward"] = measure_config4(torch, pkg, dev)
+    out["kv_cache_decode_attention"] = measure_kv_cache(torch, pkg, dev, peaks)
     out["note"] = ("one GPU; config 1 and the us_single_call figures: one call after an L2 flush, CUDA events "
                    "around it (about 6 us of the figure is event and launch overhead at these sizes); configs 2-3 "
                    "us: back-to-back calls replayed from a CUDA graph over 12 (config 2) or four (config 3) weights "
@@ -640,8 +641,8 @@ def measure_forward(torch, pkg, dev, rank: int, world: int, reps: int, peaks, ro
     fpt = c5_flops_per_token()
     res = {"workload": "config5_forward_llama3_8b_4_layers", "tokens": tokens, "sequences_per_gpu": B,
            "ms_per_forward": ms, "tokens_per_s": tokens / ms * 1e3, "tflops": fpt * tokens / ms / 1e9,
-           "flops_per_token": fpt, "frac_of_bf16_peak": fpt * tokens / ms / 1e9 / peaks["bf16_tflops"]
-           if peaks else None,
+           "flops_per_token": fpt,
+           "frac_of_bf16_peak_per_gpu": fpt * tokens / ms / 1e9 / world / peaks["bf16_tflops"] if peaks else None,
            "mlp_route_mix_INT8_FP8_FP16": counts, "routing": routing, "tau": list(TAU),
            "e2e": {"tokens_per_s": tokens / ms_e2e * 1e3, "ms_per_forward": ms_e2e,
                    "h2d_bytes_per_forward": int(ids_host.numel() * 8 * world),
@@ -688,6 +689,60 @@ def measure_forward(torch, pkg, dev, rank: int, world: int, reps: int, peaks, ro
     del eng, model
     torch.cuda.empty_cache()
     return res
+
+
+def measure_kv_cache(torch, pkg, dev, peaks, reps: int = 20) -> dict:
+    """The entropy-tied KV cache at config 5's attention shape, long contexts: 16 sequences of
+    8192 cached tokens, 8 KV heads of 128 (32 query heads), tokens stored at the bench's route mix
+    (about 24 / 55 / 21 % INT8 / FP8 / FP16); one decode step's attention (32 query heads
+    per sequence against its cache + its own new K / V), timed back to back (CUDA graph of
+    `reps` steps).  Algorithmic bytes per step: the cache's K and V (+ scales and slot
+    table) and q / k_new / v_new / out; against the same cache kept in fp16."""
+    B, kv, d, Hq, T = 16, 8, 128, 32, 8192
+    g = torch.Generator(device=dev).manual_seed(21)
+    cache = pkg.EntropyKVCache(B, kv, d, T + 64, device=dev)
+    k = (torch.randn(B * T, kv * d, generator=g, device=dev)).half()
+    v = torch.randn(B * T, kv * d, generator=g, device=dev).half()
+    u = torch.rand(B * T, generator=g, device=dev)
+    tier = torch.where(u < 0.24, 0, torch.where(u < 0.79, 1, 2)).to(torch.int8)
+    cache.append(k, v, tier)
+    del k, v
+    q = torch.randn(B, Hq * d, generator=g, device=dev).half()
+    kn = torch.randn(B, kv * d, generator=g, device=dev).half()
+    vn = torch.randn(B, kv * d, generator=g, device=dev).half()
+    out = torch.empty_like(q)
+    cache.decode_attention(q, kn, vn, d ** -0.5, out=out)
+    torch.cuda.synchronize()
+    pkg._lib.device_check()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            cache.decode_attention(q, kn, vn, d ** -0.5, out=out)
+    graph.replay()
+    torch.cuda.synchronize()
+    E = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    ts = []
+    for _ in range(5):
+        a, b = E(), E()
+        a.record()
+        graph.replay()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b) * 1e3 / reps)
+    del graph
+    us = statistics.median(ts)
+    n8, n16 = int((tier != 2).sum()), int((tier == 2).sum())
+    cache_bytes = n8 * cache.bytes_per_token(0) + n16 * cache.bytes_per_token(2) + 4 * B * T
+    io = 2 * (2 * B * Hq * d + 2 * B * kv * d)
+    fp16_bytes = B * T * cache.bytes_per_token(2)
+    gbs = (cache_bytes + io) / us / 1e3
+    return {"shape": {"sequences": B, "cached_tokens": T, "kv_heads": kv, "head_dim": d, "query_heads": Hq},
+            "tier_mix_INT8_FP8_FP16": [int((tier == 0).sum()), int((tier == 1).sum()), n16],
+            "us_per_decode_step": round(us, 2), "bytes_per_step": cache_bytes + io, "gbs": round(gbs, 1),
+            "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 3), "cache_bytes": cache_bytes,
+            "cache_bytes_if_fp16": fp16_bytes, "cache_bytes_saved_frac": round(1 - cache_bytes / fp16_bytes, 3),
+            "note": "decode attention over the mixed-precision cache (split over tokens, partials merged), CUDA "
+                    f"graph of {reps} back-to-back steps; the cache ({cache_bytes >> 20} MiB) is well above L2"}
 
 
 # config 4 of the path's scope: the TinyLlama-1.1B architecture
