@@ -445,7 +445,7 @@ EE_API int ee_kv_append(const ee_kv_cache* cache, const void* k_rows, int64_t ld
  * heads]) the entropy of each softmax row: the router input of the new token.  The
  * tokens are split over CTAs (flash-decoding) whose partials merge in a second launch;
  * workspace: ee_kv_decode_workspace_bytes. */
-EE_API size_t ee_kv_decode_workspace_bytes(int64_t batch, int64_t kv_heads, int64_t heads, int64_t head_dim);
+EE_API size_t ee_kv_decode_workspace_bytes(const ee_kv_cache* cache, int64_t heads);
 EE_API int ee_kv_decode_attention(const ee_kv_cache* cache, const void* q, int64_t ldq, int64_t heads,
                                   const void* k_new, const void* v_new, int64_t ld_new, float scale, void* out,
                                   int64_t ldo, float* H, void* workspace, size_t workspace_bytes, void* stream);

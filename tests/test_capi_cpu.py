@@ -186,6 +186,8 @@ def test_kv_cache_argument_checks(pkg, lib):
     assert lib.ee_kv_cache_init(None, p, 1 << 30, 2, 8, 128, 64, 8, 8, None) == EE_ERR_INVALID
     assert lib.ee_kv_cache_init(ctypes.byref(c), p, 16, 2, 8, 128, 64, 8, 8, None) == EE_ERR_INVALID  # too small
     assert lib.ee_kv_append(ctypes.byref(c), p, 1024, p, 1024, p, 1, None) == EE_ERR_INVALID  # not initialised
-    assert lib.ee_kv_decode_workspace_bytes(2, 8, 32, 128) > 0
+    assert lib.ee_kv_decode_workspace_bytes(None, 32) == 0
+    c2 = kvc._KvCacheC(2, 8, 128, 4096, 8, 8)
+    assert lib.ee_kv_decode_workspace_bytes(ctypes.byref(c2), 32) > 0
     assert lib.ee_kv_decode_attention(ctypes.byref(c), p, 4096, 32, p, p, 1024, 0.1, p, 4096, None, p, 1 << 20,
                                       None) == EE_ERR_INVALID

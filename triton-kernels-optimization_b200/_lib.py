@@ -51,7 +51,7 @@ SIGNATURES = {
     "ee_kv_cache_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int64, c_int64]),
     "ee_kv_cache_init": (c_int, [_P, _P, c_size_t, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, _P]),
     "ee_kv_append": (c_int, [_P, _P, c_int64, _P, c_int64, _P, c_int64, _P]),
-    "ee_kv_decode_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64]),
+    "ee_kv_decode_workspace_bytes": (c_size_t, [_P, c_int64]),
     "ee_kv_decode_attention": (c_int, [_P, _P, c_int64, c_int64, _P, _P, c_int64, c_float, _P, c_int64, _P, _P,
                                        c_size_t, _P]),
     "ee_add_rmsnorm": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64, _P, c_float, _P, c_int64, c_int64, c_int64,

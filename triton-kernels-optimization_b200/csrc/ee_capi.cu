@@ -706,11 +706,15 @@ ee::KvCacheArgs kv_args(const ee_kv_cache& c) {
   a.pool_used = c.pool_used;
   return a;
 }
-// token splits of the decode attention: about two CTAs per SM over the batch's KV heads
-int kv_splits(int64_t batch, int64_t kv_heads) {
+// token splits of the decode attention: about 256 cached tokens per CTA (four warps of
+// 64), so that enough warps are in flight to hide the slot-table and row loads, and at
+// least two CTAs per SM over the batch's KV heads
+int kv_splits(int64_t batch, int64_t kv_heads, int64_t max_tokens) {
   const int64_t ctas = batch * kv_heads;
-  int64_t s = (2 * int64_t(num_sms()) + ctas - 1) / ctas;
-  return static_cast<int>(s < 1 ? 1 : (s > 64 ? 64 : s));
+  int64_t s = (max_tokens + 1 + 255) / 256;
+  const int64_t fill = (2 * int64_t(num_sms()) + ctas - 1) / ctas;
+  s = s > fill ? s : fill;
+  return static_cast<int>(s < 1 ? 1 : (s > 1024 ? 1024 : s));
 }
 }  // namespace
 extern "C" {
@@ -764,9 +768,10 @@ int ee_kv_append(const ee_kv_cache* cache, const void* k_rows, int64_t ldk, cons
                       "kv_append");
 }
 
-size_t ee_kv_decode_workspace_bytes(int64_t batch, int64_t kv_heads, int64_t heads, int64_t head_dim) {
-  if (batch <= 0 || kv_heads <= 0 || heads <= 0 || head_dim <= 0) return 0;
-  return align256(sizeof(float) * size_t(batch) * heads * kv_splits(batch, kv_heads) * (3 + head_dim));
+size_t ee_kv_decode_workspace_bytes(const ee_kv_cache* cache, int64_t heads) {
+  if (cache == nullptr || cache->batch <= 0 || cache->kv_heads <= 0 || heads <= 0 || cache->head_dim <= 0) return 0;
+  return align256(sizeof(float) * size_t(cache->batch) * heads *
+                  kv_splits(cache->batch, cache->kv_heads, cache->max_tokens) * (3 + cache->head_dim));
 }
 
 int ee_kv_decode_attention(const ee_kv_cache* cache, const void* q, int64_t ldq, int64_t heads, const void* k_new,
@@ -781,10 +786,10 @@ int ee_kv_decode_attention(const ee_kv_cache* cache, const void* q, int64_t ldq,
   if (ldq < heads * d || ldo < heads * d || ld_new < cache->kv_heads * d || ldq % 8 || ldo % 8 || ld_new % 8 ||
       !al16(q) || !al16(k_new) || !al16(v_new) || !al16(out) || (reinterpret_cast<uintptr_t>(H) & 3u))
     return fail(EE_ERR_MISALIGNED, "q / k_new / v_new / out rows 16-byte aligned with strides % 8, H 4-byte aligned");
-  int st = check_ws(workspace, workspace_bytes, ee_kv_decode_workspace_bytes(cache->batch, cache->kv_heads, heads, d));
+  int st = check_ws(workspace, workspace_bytes, ee_kv_decode_workspace_bytes(cache, heads));
   if (st != EE_OK) return st;
   return check_launch(ee::launch_kv_decode_attention(kv_args(*cache), q, ldq, heads, k_new, v_new, ld_new, scale,
-                                                     kv_splits(cache->batch, cache->kv_heads),
+                                                     kv_splits(cache->batch, cache->kv_heads, cache->max_tokens),
                                                      static_cast<float*>(workspace), out, ldo, H, as_stream(stream)),
                       "kv_decode_attention");
 }

@@ -193,8 +193,8 @@ __global__ void __launch_bounds__(kKvThreads) kv_decode_attention_kernel(const K
 #pragma unroll
     for (int e = 0; e < E; ++e) o[g][e] = 0.f;
   }
-  for (int64_t t = t0 + warp; t < t1; t += W) {
-    float kx[E], vx[E];
+  // one token's K and V slices (the new token's from k_new / v_new); false for a hole
+  auto load_token = [&](int64_t t, float* kx, float* vx) -> bool {
     if (t == len) {  // the new token, not in the cache yet
       const __half* kp = k_new + b * ld_new + h * D + lane * E;
       const __half* vp = v_new + b * ld_new + h * D + lane * E;
@@ -207,12 +207,15 @@ __global__ void __launch_bounds__(kKvThreads) kv_decode_attention_kernel(const K
         vx[e] = fv.x;
         vx[e + 1] = fv.y;
       }
-    } else {
-      const int code = c.slot[static_cast<int64_t>(b) * c.max_tokens + t];
-      if (code < 0) continue;  // a token its pool had no room for (warp-uniform)
-      kv_row<D, E>(c, code, h, false, lane * E, kx);
-      kv_row<D, E>(c, code, h, true, lane * E, vx);
+      return true;
     }
+    const int code = c.slot[static_cast<int64_t>(b) * c.max_tokens + t];
+    if (code < 0) return false;  // a token its pool had no room for (warp-uniform)
+    kv_row<D, E>(c, code, h, false, lane * E, kx);
+    kv_row<D, E>(c, code, h, true, lane * E, vx);
+    return true;
+  };
+  auto update = [&](const float* kx, const float* vx) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       float sdot = 0.f;
@@ -237,6 +240,14 @@ __global__ void __launch_bounds__(kKvThreads) kv_decode_attention_kernel(const K
 #pragma unroll
       for (int e = 0; e < E; ++e) o[g][e] = fmaf(p, vx[e], o[g][e]);
     }
+  };
+  // two tokens per step: both tokens' slot and row loads are in flight before either is used
+  for (int64_t t = t0 + warp; t < t1; t += 2 * W) {
+    float ka[E], va[E], kb[E], vb[E];
+    const bool oka = load_token(t, ka, va);
+    const bool okb = t + W < t1 && load_token(t + W, kb, vb);
+    if (oka) update(ka, va);
+    if (okb) update(kb, vb);
   }
   // the W warps' partials -> one per (split, query head), through shared memory
   __shared__ float s_mlt[W][G][3];

@@ -104,7 +104,7 @@ class EntropyKVCache:
         y = out if out is not None else torch.empty_like(q)
         H = torch.empty(B, heads, dtype=torch.float32, device=q.device)
         lib = _lib.load()
-        need = lib.ee_kv_decode_workspace_bytes(B, self.kv_heads, heads, self.head_dim)
+        need = lib.ee_kv_decode_workspace_bytes(ctypes.byref(self.c), heads)
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         with torch.cuda.device(self.device):

@@ -126,9 +126,10 @@ class ColumnParallelGatedMLP:
       2. route the gathered rows (every rank derives the same routes from the same H)
          and run this rank's gate / up columns over them in one fused SwiGLU GEMM
          -> h [world * m / chunks, I / world];
-      3. all-to-all: the row block of every other rank goes to it and this rank's rows
-         come back from every rank -> [m / chunks, I] (columns in rank order), issued
-         as soon as the chunk's h exists, so it overlaps the next chunk's GEMM;
+      3. all-to-all (NCCL's, or grouped point-to-point transfers on gloo): the row block
+         of every other rank goes to it and this rank's rows come back from every rank ->
+         [m / chunks, I] (columns in rank order), issued as soon as the chunk's h exists,
+         so it overlaps the next chunk's GEMM;
       4. the down projection (full weight) on the rank's own rows of the chunk.
     Per-row activation scales span the whole row (steps 2 and 4 see full rows), weight
     scales are per output column and no tile's K loop is split, so the result equals
@@ -148,6 +149,13 @@ class ColumnParallelGatedMLP:
         c0, c1 = self.cols[rank]
         self.gate_up = self.ops.pack_swiglu(w_gate[c0:c1], w_up[c0:c1])
         self.down_w = self.ops.pack(w_down)
+        self._set_exchange()
+
+    def _set_exchange(self) -> None:
+        # NCCL has a native all-to-all (equal column blocks); gloo exchanges by grouped
+        # point-to-point transfers
+        self._nccl = self.world > 1 and dist.is_initialized() and dist.get_backend(self.group) == "nccl"
+        self._equal_cols = len({c1 - c0 for c0, c1 in self.cols}) == 1
 
     @classmethod
     def from_blocks_mlp(cls, block, world: int, rank: int, group=None, tau_low: float = 0.41,
@@ -170,6 +178,7 @@ class ColumnParallelGatedMLP:
 
         self.gate_up = SwiGLUPack(sliced(block.gate_proj), sliced(block.up_proj))
         self.down_w = block.down_proj._pack()
+        self._set_exchange()
         return self
 
     def forward(self, x: torch.Tensor, H: torch.Tensor) -> torch.Tensor:
@@ -199,18 +208,26 @@ class ColumnParallelGatedMLP:
                 for w in gathers[c]:
                     w.wait()
             h_cols = self.ops.swiglu(xs[c], Hs[c], self.gate_up)  # [world * mc, I_r]
-            if world > 1:
+            if world > 1 and self._nccl and self._equal_cols:
+                # one NCCL all-to-all: row block r of h_cols goes to rank r
+                recv = torch.empty_like(h_cols)
+                work = dist.all_to_all_single(recv, h_cols, group=self.group, async_op=True)
+                exchanged.append(("a2a", recv, [work]))
+            elif world > 1:
                 recv = [h_cols.new_empty((mc, c1 - c0)) for c0, c1 in self.cols]
                 reqs = exchange_blocks([b.contiguous() for b in h_cols.split(mc, dim=0)], recv, self.rank,
                                        self.group, async_op=True)
-                exchanged.append((recv, reqs, h_cols))
+                exchanged.append(("p2p", recv, reqs))
             else:
-                exchanged.append(([h_cols], [], h_cols))
+                exchanged.append(("p2p", [h_cols], []))
         outs = []
-        for c, (recv, reqs, _) in enumerate(exchanged):
+        for c, (kind, recv, reqs) in enumerate(exchanged):
             for req in reqs:
                 req.wait()
-            h = torch.cat(recv, dim=1) if len(recv) > 1 else recv[0]
+            if kind == "a2a":  # [world, mc, I_r] -> [mc, world * I_r], columns in rank order
+                h = recv.view(world, mc, -1).permute(1, 0, 2).reshape(mc, -1)
+            else:
+                h = torch.cat(recv, dim=1) if len(recv) > 1 else recv[0]
             outs.append(self.ops.down(h.contiguous(), H[c * mc:(c + 1) * mc], self.down_w))
         return outs[0] if C == 1 else torch.cat(outs, dim=0)
 
