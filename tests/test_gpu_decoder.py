@@ -1,7 +1,7 @@
 """The decoder-stack engine (ee_decoder_*, DecoderEngine) against the Python layer loop
 of EntropyDispatchedLlamaBlock(attention="flash") through the same kernels: the last
 block's output bit for bit, eagerly and as a replayed CUDA graph, for per-token and
-batch-max routing, MLP-only and every-linear routing.  A small random-init Llama
+batch-max routing, MLP-only and every-linear routing, online and exact entropies.  A small random-init Llama
 (transformers) with thresholds that put rows in all three tiers."""
 import pytest
 import torch
@@ -26,12 +26,15 @@ def _model(layers=2, hidden=256, heads=4, kv=2, inter=512, vocab=512, seed=0):
     return wrap
 
 
-@pytest.mark.parametrize("routing,route_all", [("token", False), ("token", True), ("batch", False), ("batch", True)])
+@pytest.mark.parametrize("routing,route_all,exact", [("token", False, False), ("token", True, False),
+                                                     ("batch", False, False), ("batch", True, False),
+                                                     ("token", False, True), ("batch", True, True)])
 @torch.no_grad()
-def test_decoder_engine_equals_block_loop(pkg, cuda, routing, route_all):
+def test_decoder_engine_equals_block_loop(pkg, cuda, routing, route_all, exact):
     wrap = _model()
     model = wrap.model
-    blocks, disp = pkg.build_dispatched_llama(wrap, *TAU, routing=routing, attention="flash", route_all=route_all)
+    blocks, disp = pkg.build_dispatched_llama(wrap, *TAU, routing=routing, attention="flash", route_all=route_all,
+                                              exact_entropy=exact)
     B, S = 2, 256
     ids = torch.randint(0, 512, (B, S), generator=torch.Generator().manual_seed(3)).to(cuda)
     h0 = model.embed_tokens(ids).half()

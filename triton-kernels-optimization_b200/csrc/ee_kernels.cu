@@ -435,8 +435,9 @@ namespace {
 template <int D, int G>
 int run_kv_decode(const KvCacheArgs& c, const void* q, int64_t ldq, const void* k_new, const void* v_new,
                   int64_t ld_new, float scale, int splits, float* part, cudaStream_t s) {
-  const dim3 grid(static_cast<unsigned>(c.batch * c.kv_heads), static_cast<unsigned>(splits));
-  return launch_pdl(kv_decode_attention_kernel<D, G>, grid, dim3(kKvThreads), 0, s, c,
+  constexpr int GC = G < 4 ? G : 4;  // query heads per CTA (more heads: more CTAs over the same tokens)
+  const dim3 grid(static_cast<unsigned>(c.batch * c.kv_heads), static_cast<unsigned>(splits), G / GC);
+  return launch_pdl(kv_decode_attention_kernel<D, G, GC>, grid, dim3(kKvThreads), 0, s, c,
                     static_cast<const __half*>(q), ldq, static_cast<const __half*>(k_new),
                     static_cast<const __half*>(v_new), ld_new, scale, splits, part);
 }
