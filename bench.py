@@ -1199,6 +1199,7 @@ def main(argv=None) -> int:
             "scaling": "weak", "vs_baseline": None, "dtype": DTYPE, "data": "synthetic",
             "config": config_dict(M, world, mix),
             "tokens_per_s": world * M * args.steps / (total_ms / 1e3),
+            "forward_tokens_per_s": forward["tokens_per_s"] if forward else None,
             "softmax_entropy": {"gbs": gate_bytes / gate_stream_us / 1e3,
                                 "frac": gate_bytes / gate_stream_us / 1e3 / peaks["hbm_gbs"],
                                 "us_per_call": gate_stream_us, "bytes_per_call": gate_bytes,
