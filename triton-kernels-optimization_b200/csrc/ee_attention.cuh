@@ -6,12 +6,16 @@
 // One CTA per (batch, query head, 256 query rows = two 128-row query tiles), 384 threads:
 //   warp 0     TMA producer: both Q tiles once, then K and V^T tiles of 128 keys into
 //              rings (K 2 deep; V 2 deep at head_dim 64, 1 at 128);
-//   warp 1     TMEM owner + single-thread UMMA issuer: S_w = Q_w K_j^T (M 128, N KT) into
-//              the S buffer of query tile w, O_w += P_w V_j (M 128, N d) into the O
-//              accumulator of tile w, in the order S_0 S_1 | S_0' S_1' P_0V P_1V | ...: the
-//              next S of a warpgroup is issued as soon as its softmax holds the current
-//              one in registers, so it runs under that softmax's exponentials;
-//   warps 2-3  idle (they complete the producer warpgroup, which hands its registers to
+//   warps 1-2  UMMA issuers, one thread each, warp 1 + w for query tile w (warp 1 also owns
+//              TMEM): S_w = Q_w K_j^T (M 128, N KT) into the S buffer of tile w, O_w +=
+//              P_w V_j (M 128, N d) into its O accumulator, in the order S_w,0 |
+//              S_w,j+1 P_w V_j | ...: the next S is issued as soon as the softmax holds
+//              the current one in registers, so it runs under that softmax's
+//              exponentials, and neither tile's issue waits on the other's softmax.
+//              Each issuer commits its share of every K / V stage's release (the empty
+//              barriers count two), tile 0's issuer also for the key tiles past its
+//              causal reach;
+//   warp 3     idle (it completes the producer warpgroup, which hands its registers to
 //              the softmax warpgroups);
 //   warps 4-11 warpgroup w = query tile w, one whole row per thread: scores from TMEM into
 //              registers with the reference's fp16 roundings (fp16 Q K^T, times the scale,
@@ -149,9 +153,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* s_free = s_full + 2;          // [2] S_w read into registers (4 warps)
   uint64_t* p_full = s_full + 4;          // [2] P_w written, O_w corrected (4 warps)
   uint64_t* o_done = s_full + 6;          // [2] P_w V done: P_w free, O_w stable (MMA commit)
-  uint64_t* drain = s_full + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 9);
-  static_assert((1 + 2 * NS + 2 * NV + 9) * 8 + 8 <= Cfg::kBarrierBytes, "attention barrier region overflows");
+  uint64_t* drain = s_full + 8;          // [2] MMA drain on abort, one per issuing thread
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 10);
+  static_assert((1 + 2 * NS + 2 * NV + 10) * 8 + 8 <= Cfg::kBarrierBytes, "attention barrier region overflows");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -177,11 +181,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     mbar_init(q_full, 1);
     for (int i = 0; i < NS; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
+      mbar_init(&k_empty[i], 2);  // one commit per issuing thread
     }
     for (int i = 0; i < NV; ++i) {
       mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
+      mbar_init(&v_empty[i], 2);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -189,7 +193,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
     }
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -273,11 +278,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int s = 0; s < NV; ++s)
         if (v_issued & (1u << s)) (void)mbar_wait(&v_full[s], (v_par >> s) & 1u, nullptr);
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 2) {
     // -------------------------------------------------------------- UMMA issuer
-    // S_w,j = Q_w K_j^T into S_w; O_w (+)= P_w,j V_j.  Order: S_0,0  S_1,0, then per key
-    // tile j: P_0 V_j, S_0,j+1, P_1 V_j, S_1,j+1 -- the tensor core works for one
-    // warpgroup while the other one runs its softmax.
+    // S_w,j = Q_w K_j^T into S_w; O_w (+)= P_w,j V_j.  Order: S_w,0, then per key tile j:
+    // S_w,j+1, P_w V_j -- the tensor core works for one warpgroup while the other one
+    // runs its softmax.
     constexpr uint32_t idesc_s = make_idesc(1u, 0u, kAttnTile, KT);  // f32 <- f16 x f16, 128 x KT
     constexpr uint32_t idesc_o = make_idesc(1u, 0u, kAttnTile, D);   // f32 <- f16 x f16, 128 x D
     bool failed = !mbar_wait(q_full, 0u, abort_flag);
@@ -322,35 +327,43 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       return true;
     };
-    if (!failed) failed = !issue_s(0, 0);
-    if (!failed) failed = !issue_s(1, 0);
+    // this thread's query tile only; for the key tiles past its reach it still takes
+    // part in the K / V rings (waits for the stage, commits its share of the release)
+    const int w = warp - 1;
+    const int nkv_w = w == 0 ? nkv0 : nkv1;
+    if (!failed) failed = !issue_s(w, 0);
     if (!failed && lane == 0) tc_commit(&k_empty[0]);
     __syncwarp();
     for (int j = 0; j < nkv_max && !failed; ++j) {
-      // the next S of each warpgroup first: its TMEM columns are free as soon as the
-      // softmax holds S_j in registers (s_free), so it runs under this tile's
-      // exponentials instead of after them
-      if (j + 1 < nkv0 && !issue_s(0, j + 1)) failed = true;
-      if (!failed && j + 1 < nkv1) {
-        if (!issue_s(1, j + 1)) failed = true;
-        if (!failed && lane == 0) tc_commit(&k_empty[(j + 1) % NS]);  // both S of tile j + 1 issued
+      if (j + 1 < nkv_max) {
+        if (j + 1 < nkv_w) {
+          if (!issue_s(w, j + 1)) failed = true;
+        } else if (!mbar_wait(&k_full[(j + 1) % NS], static_cast<uint32_t>((j + 1) / NS) & 1u, abort_flag)) {
+          failed = true;
+        }
+        if (!failed && lane == 0) tc_commit(&k_empty[(j + 1) % NS]);
         __syncwarp();
       }
-      if (!failed && j < nkv0 && !issue_pv(0, j)) failed = true;
-      if (!failed && !issue_pv(1, j)) failed = true;
-      if (!failed && lane == 0) tc_commit(&v_empty[j % NV]);  // both P V of tile j issued
+      if (!failed) {
+        if (j < nkv_w) {
+          if (!issue_pv(w, j)) failed = true;
+        } else if (!mbar_wait(&v_full[j % NV], static_cast<uint32_t>(j / NV) & 1u, abort_flag)) {
+          failed = true;
+        }
+      }
+      if (!failed && lane == 0) tc_commit(&v_empty[j % NV]);
       __syncwarp();
     }
     if (failed) {
       if (lane == 0) {
         atomicOr(&g_device_error, kErrWaitTimeout);
         *abort_flag = 1;
-        tc_commit(drain);
+        tc_commit(&drain[w]);
       }
       __syncwarp();
-      (void)mbar_wait(drain, 0u, nullptr);
+      (void)mbar_wait(&drain[w], 0u, nullptr);
     }
-  }  // warps 2 and 3: nothing to do
+  }  // warp 3: nothing to do
   } else {
     warpgroup_reg_alloc<kAttnSoftmaxRegs>();
     // -------------------------------------------------------------- softmax / entropy / output
