@@ -33,7 +33,8 @@ __device__ int g_device_error;  // sticky error word, read back by read_and_clea
 constexpr int kAStageBytes = kBM * kBKBytes;  // 16 KB
 constexpr int kGemmThreads = 192;
 constexpr int kTmemCols = 2 * kBN;  // two accumulators
-constexpr int kBarrierBytes = 256;
+constexpr int kBarrierBytes = 384;
+constexpr int kScaleBytes = 1024;  // the tile's 256 column scales, staged by the epilogue warps
 // Single-CTA kernel, per tile width BN: B stage bytes, ring depth and shared memory.
 // BN = 256: 48 KB stages x 4; BN = 64 (weight-streaming calls): 24 KB stages x 8.
 template <int BN>
@@ -42,7 +43,8 @@ struct SingleCfg {
   static constexpr int kStageBytes = kAStageBytes + kBStageBytes;
   static constexpr int kStages = BN == kBN ? 4 : 8;
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;  // two accumulators (allocation >= 32 columns)
-  static constexpr size_t kSmem = 1024 /*alignment slack*/ + size_t(kStages) * kStageBytes + kBarrierBytes;
+  static constexpr size_t kSmem =
+      1024 /*alignment slack*/ + size_t(kStages) * kStageBytes + kBarrierBytes + kScaleBytes;
   static_assert(kSmem <= 227 * 1024, "single-CTA GEMM shared memory above the 227 KB per-CTA limit");
 };
 
@@ -303,15 +305,16 @@ __device__ __forceinline__ void mma_stage(uint32_t d_tmem, uint32_t a_addr, uint
 
 // Epilogue of one 32-lane quarter of a 128 x 256 accumulator, in two parts.
 // epilogue_prepare runs before the accumulator is ready: the thread's row (output row,
-// activation scale) and, for the 8-bit buckets, 8 of the tile's 256 column scales per
-// lane (columns n0 + 8*lane ..), so no global load is left on the drain's path.
-// epilogue_drain then reads TMEM 32 columns at a time, one chunk ahead of the math,
-// and builds each chunk's 32 column scales from the lanes that hold them by shuffles.
+// activation scale); stage_scales then puts the tile's column scales into shared memory
+// (each epilogue warp loads a quarter), so no global load is left on the drain's path.
+// epilogue_drain reads TMEM 32 columns at a time, one chunk ahead of the math; each
+// chunk's 32 column scales are read by every lane from the same shared-memory words
+// (broadcast), the dequantisation runs on f32x2 pairs and the fp16 row segment leaves in
+// 32-byte stores (full sectors) when the output rows allow it.
 struct EpiRow {
-  bool valid;
+  bool valid, v8;  // v8: 32-byte aligned output rows
   int64_t orow;
   float sa;
-  float sb[8];
 };
 
 __device__ __forceinline__ EpiRow epilogue_prepare(const GemmArgs& args, const TileGeo& geo, int b, int pos, int n0,
@@ -323,29 +326,74 @@ __device__ __forceinline__ EpiRow epilogue_prepare(const GemmArgs& args, const T
   e.valid = pos < end;
   e.orow = e.valid ? (args.perm ? static_cast<int64_t>(args.perm[pos]) : static_cast<int64_t>(pos)) : 0;
   e.sa = (e.valid && b != kFP16 && args.out_mode != 1) ? args.sa[pos] : 1.f;
-  const int c8 = n0 + 8 * lane;
-  if (b != kFP16 && args.out_mode != 1 && c8 < args.N) {  // N % 8 == 0: all 8 or none
-    const float4 q0 = __ldg(reinterpret_cast<const float4*>(args.sb + c8));
-    const float4 q1 = __ldg(reinterpret_cast<const float4*>(args.sb + c8 + 4));
-    e.sb[0] = q0.x; e.sb[1] = q0.y; e.sb[2] = q0.z; e.sb[3] = q0.w;
-    e.sb[4] = q1.x; e.sb[5] = q1.y; e.sb[6] = q1.z; e.sb[7] = q1.w;
-  } else {
-#pragma unroll
-    for (int k = 0; k < 8; ++k) e.sb[k] = 0.f;
-  }
+  e.v8 = (reinterpret_cast<uintptr_t>(args.Y) & 31u) == 0 && (args.ldy & 15) == 0;
   return e;
 }
 
-// one 32-column chunk c of the drain (r: its accumulator values); reached by the whole
-// warp (the shuffles), stores only for valid rows and columns
-__device__ __forceinline__ void epilogue_chunk(const GemmArgs& args, const EpiRow& e, int b, int n0, int c,
-                                               const uint32_t (&r)[32]) {
-  const int nc = n0 + c * 32;
-  float sbv[32];
-  if (b != kFP16) {
+// The tile's BN column scales into shared memory (zero past N), one quarter per epilogue
+// warp, between two barriers of the four epilogue warps: sc_free (every warp has drained
+// the previous tile, so its scales may be overwritten) and sc_full (all quarters
+// written).  k: tiles this warp has staged before.  False if a wait gave up.
+template <int BN>
+__device__ __forceinline__ bool stage_scales(const GemmArgs& args, int b, int n0, int quarter, int lane, float* s_sc,
+                                             uint64_t* sc_full, uint64_t* sc_free, uint32_t k,
+                                             const volatile int* abort) {
+  constexpr int kPer = BN / 4;
+  const bool need = b != kFP16 && args.out_mode != 1;
+  float v[(kPer + 31) / 32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) sbv[j] = __shfl_sync(0xffffffffu, e.sb[j & 7], 4 * c + (j >> 3));
+  for (int i = 0; i < (kPer + 31) / 32; ++i) {
+    const int j = quarter * kPer + i * 32 + lane;
+    v[i] = (need && i * 32 + lane < kPer && n0 + j < args.N) ? __ldg(args.sb + n0 + j) : 0.f;
   }
+  if (k > 0 && !mbar_wait(sc_free, (k - 1) & 1u, abort)) return false;
+#pragma unroll
+  for (int i = 0; i < (kPer + 31) / 32; ++i)
+    if (i * 32 + lane < kPer) s_sc[quarter * kPer + i * 32 + lane] = v[i];
+  __syncwarp();
+  if (lane == 0) mbar_arrive(sc_full);
+  return mbar_wait(sc_full, k & 1u, abort);
+}
+
+// the staged column scales c0 .. c0 + 31 of the tile, the same shared-memory words in
+// every lane
+__device__ __forceinline__ void tile_scales(const float* s_sc, int c0, float (&v)[32]) {
+  const uint32_t a = smem_u32(s_sc + c0);
+#pragma unroll
+  for (int g = 0; g < 8; ++g)
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v[4 * g]), "=f"(v[4 * g + 1]), "=f"(v[4 * g + 2]), "=f"(v[4 * g + 3])
+                 : "r"(a + 16u * g));
+}
+
+// the column scales of output columns nc .. nc + 31 from global memory (zero past N;
+// N % 8 == 0): the reduction kernel's path
+__device__ __forceinline__ void column_scales(const float* sb, int nc, int N, float (&v)[32]) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+    if (nc + 8 * g < N) {
+      lo = __ldg(reinterpret_cast<const float4*>(sb + nc + 8 * g));
+      hi = __ldg(reinterpret_cast<const float4*>(sb + nc + 8 * g + 4));
+    }
+    v[8 * g + 0] = lo.x; v[8 * g + 1] = lo.y; v[8 * g + 2] = lo.z; v[8 * g + 3] = lo.w;
+    v[8 * g + 4] = hi.x; v[8 * g + 5] = hi.y; v[8 * g + 6] = hi.z; v[8 * g + 7] = hi.w;
+  }
+}
+
+// 32 consecutive bytes (16 fp16) to global memory in one 256-bit store; p 32-byte aligned
+__device__ __forceinline__ void st_global_32B(void* p, const uint32_t (&w)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+               "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
+// one 32-column chunk c of the drain (r: its accumulator values); stores only for valid
+// rows and columns.  s_sc: the tile's staged column scales, or null to read them from
+// global memory
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& args, const EpiRow& e, int b, int n0, int c,
+                                               const uint32_t (&r)[32], const float* s_sc) {
+  const int nc = n0 + c * 32;
   if (!e.valid || nc >= args.N) return;
   if (args.out_mode == 1) {
     uint32_t* y = static_cast<uint32_t*>(args.Y) + e.orow * args.ldy + nc;
@@ -354,27 +402,49 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& args, const EpiRo
       if (nc + 4 * g < args.N) *reinterpret_cast<uint4*>(y + 4 * g) = make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
     return;
   }
-  float f[32];
+  // fp16 pairs of the row segment: (acc * sa) * sb per element, each product rounded
+  // (the f32x2 multiplies round each lane as the scalar ones do)
+  uint32_t h[16];
   if (b == kFP16) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
-  } else if (b == kINT8) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[j])), e.sa), sbv[j]);
+    for (int j = 0; j < 16; ++j) {
+      const __half2 v = __floats2half2_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+      h[j] = *reinterpret_cast<const uint32_t*>(&v);
+    }
   } else {
+    float sbv[32];
+    if (s_sc != nullptr)
+      tile_scales(s_sc, c * 32, sbv);
+    else
+      column_scales(args.sb, nc, args.N, sbv);
+    const float2 sa2 = make_float2(e.sa, e.sa);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__fmul_rn(__uint_as_float(r[j]), e.sa), sbv[j]);
+    for (int j = 0; j < 16; ++j) {
+      const float2 acc = (b == kINT8) ? make_float2(static_cast<float>(static_cast<int32_t>(r[2 * j])),
+                                                    static_cast<float>(static_cast<int32_t>(r[2 * j + 1])))
+                                      : make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+      const float2 f = __fmul2_rn(__fmul2_rn(acc, sa2), make_float2(sbv[2 * j], sbv[2 * j + 1]));
+      const __half2 v = __floats2half2_rn(f.x, f.y);
+      h[j] = *reinterpret_cast<const uint32_t*>(&v);
+    }
   }
   __half* y = static_cast<__half*>(args.Y) + e.orow * args.ldy + nc;
+  if (e.v8) {
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    if (nc + 8 * g < args.N) {
-      uint4 u;
-      __half2* h2 = reinterpret_cast<__half2*>(&u);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) h2[k] = __floats2half2_rn(f[8 * g + 2 * k], f[8 * g + 2 * k + 1]);
-      *reinterpret_cast<uint4*>(y + 8 * g) = u;
+    for (int q = 0; q < 2; ++q) {
+      if (nc + 16 * q + 16 <= args.N) {
+        const uint32_t w[8] = {h[8 * q], h[8 * q + 1], h[8 * q + 2], h[8 * q + 3],
+                               h[8 * q + 4], h[8 * q + 5], h[8 * q + 6], h[8 * q + 7]};
+        st_global_32B(y + 16 * q, w);
+      } else if (nc + 16 * q < args.N) {
+        *reinterpret_cast<uint4*>(y + 16 * q) = make_uint4(h[8 * q], h[8 * q + 1], h[8 * q + 2], h[8 * q + 3]);
+      }
     }
+  } else {
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+      if (nc + 8 * g < args.N)
+        *reinterpret_cast<uint4*>(y + 8 * g) = make_uint4(h[4 * g], h[4 * g + 1], h[4 * g + 2], h[4 * g + 3]);
   }
 }
 
@@ -392,18 +462,20 @@ __device__ __forceinline__ float swiglu_dequant(uint32_t r, int b, float sa, flo
 }
 
 __device__ __forceinline__ void swiglu_chunk(const GemmArgs& args, const EpiRow& e, int b, int n0, int c,
-                                             const uint32_t (&rg)[32], const uint32_t (&ru)[32]) {
-  float sg[32], su[32];
-  if (b != kFP16) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      sg[j] = __shfl_sync(0xffffffffu, e.sb[j & 7], 4 * c + (j >> 3));
-      su[j] = __shfl_sync(0xffffffffu, e.sb[j & 7], 16 + 4 * c + (j >> 3));
-    }
-  }
+                                             const uint32_t (&rg)[32], const uint32_t (&ru)[32], const float* s_sc) {
   const int inter = args.N / 2;
   const int oc = n0 / 2 + c * 32;  // first output column of the chunk
   if (!e.valid || oc >= inter) return;
+  float sg[32], su[32];
+  if (b != kFP16) {
+    if (s_sc != nullptr) {
+      tile_scales(s_sc, c * 32, sg);
+      tile_scales(s_sc, kBN / 2 + c * 32, su);
+    } else {
+      column_scales(args.sb, n0 + c * 32, args.N, sg);
+      column_scales(args.sb, n0 + kBN / 2 + c * 32, args.N, su);
+    }
+  }
   __half* y = static_cast<__half*>(args.Y) + e.orow * args.ldy + oc;
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
@@ -424,7 +496,7 @@ __device__ __forceinline__ void swiglu_chunk(const GemmArgs& args, const EpiRow&
 }
 
 __device__ __forceinline__ void epilogue_drain_swiglu(const GemmArgs& args, const EpiRow& e, int b, int n0,
-                                                      uint32_t taddr) {
+                                                      uint32_t taddr, const float* s_sc) {
   uint32_t rg[32], ru[32];
 #pragma unroll 1
   for (int c = 0; c < kBN / 64; ++c) {
@@ -433,7 +505,7 @@ __device__ __forceinline__ void epilogue_drain_swiglu(const GemmArgs& args, cons
     tmem_ld32(taddr + kBN / 2 + c * 32, ru);
     tmem_ld_wait(rg);
     tmem_ld_wait(ru);
-    swiglu_chunk(args, e, b, n0, c, rg, ru);
+    swiglu_chunk(args, e, b, n0, c, rg, ru, s_sc);
   }
   __syncwarp();
 }
@@ -445,10 +517,10 @@ __device__ __forceinline__ void epilogue_drain_swiglu(const GemmArgs& args, cons
 // of the tile (an even count: two per iteration).
 template <int BN = kBN>
 __device__ __forceinline__ void epilogue_drain(const GemmArgs& args, const EpiRow& e, int b, int n0, uint32_t taddr,
-                                               int chunk0 = 0, int nchunks = BN / 32) {
+                                               const float* s_sc, int chunk0 = 0, int nchunks = BN / 32) {
   if constexpr (BN == kBN) {
     if (args.out_mode == 2) {
-      epilogue_drain_swiglu(args, e, b, n0, taddr);
+      epilogue_drain_swiglu(args, e, b, n0, taddr, s_sc);
       return;
     }
   }
@@ -460,12 +532,12 @@ __device__ __forceinline__ void epilogue_drain(const GemmArgs& args, const EpiRo
   for (int c = 0; c < nchunks; c += 2) {
     __syncwarp();
     tmem_ld32(taddr + (c + 1) * 32, rb);
-    epilogue_chunk(args, e, b, n0, chunk0 + c, ra);
+    epilogue_chunk(args, e, b, n0, chunk0 + c, ra, s_sc);
     tmem_ld_wait(rb);
     const bool more = c + 2 < nchunks;
     __syncwarp();
     if (more) tmem_ld32(taddr + (c + 2) * 32, ra);
-    epilogue_chunk(args, e, b, n0, chunk0 + c + 1, rb);
+    epilogue_chunk(args, e, b, n0, chunk0 + c + 1, rb, s_sc);
     if (more) tmem_ld_wait(ra);
   }
   __syncwarp();
@@ -473,17 +545,19 @@ __device__ __forceinline__ void epilogue_drain(const GemmArgs& args, const EpiRo
 
 // ---------------------------------------------------------------------------------
 // tile feed.  Static mode: tiles blockIdx.x, blockIdx.x + gridDim.x, ...  Dynamic mode
-// (args.sched != nullptr): the producer warp claims the next tile from a global counter
-// and publishes it through a ring of kTileRing shared-memory slots; the MMA warp and the
-// four epilogue warps read the same sequence from the ring.  Claiming in tile order
-// (FP16 tiles first) gives longest-first list scheduling across the SMs.
+// (args.sched != nullptr): the producer warp takes tile blockIdx.x first (no claim: the
+// first wave needs no counter round trip), then claims gridDim.x + the next value of a
+// global counter, and publishes each tile through a ring of kTileRing shared-memory
+// slots; the MMA warp and the four epilogue warps read the same sequence from the ring.
+// Claiming in tile order (FP16 tiles first) gives longest-first list scheduling across
+// the SMs.
 // ---------------------------------------------------------------------------------
 constexpr int kTileRing = 4;
 constexpr uint32_t kRingConsumers = 5;  // MMA warp + 4 epilogue warps
 
 struct Feed {
   uint32_t slot, phase;
-  int next;  // static mode
+  int next;  // static mode: the next tile; dynamic mode: the first tile, then -1
 };
 
 // producer side; returns the tile (>= total: no more work) or -1 if a wait gave up
@@ -497,11 +571,12 @@ __device__ __forceinline__ int feed_produce(Feed& f, bool dyn, int* ring, uint64
   if (!mbar_wait(&ring_empty[f.slot], f.phase ^ 1u, abort)) return -1;
   int t = 0;
   if (lane == 0) {
-    t = static_cast<int>(atomicAdd(counter, 1u));
+    t = f.next >= 0 ? f.next : static_cast<int>(gridDim.x + atomicAdd(counter, 1u));
     ring[f.slot] = t;
     mbar_arrive(&ring_full[f.slot]);
   }
   t = __shfl_sync(0xffffffffu, t, 0);
+  f.next = -1;
   if (++f.slot == kTileRing) {
     f.slot = 0;
     f.phase ^= 1u;
@@ -549,7 +624,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr int kBStageBytes = Cfg::kBStageBytes;
   constexpr int kStageBytes = Cfg::kStageBytes;
   constexpr int kTmemCols = Cfg::kTmemCols;
-  static_assert((2 * kStages + 5 + 2 * kTileRing) * 8 + 8 + 4 * kTileRing <= kBarrierBytes,
+  static_assert((2 * kStages + 7 + 2 * kTileRing) * 8 + 8 + 4 * kTileRing <= kBarrierBytes,
                 "single-CTA GEMM barrier region overflows");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -563,24 +638,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain = acc_empty + 2;               // MMA drain on abort
   uint64_t* ring_full = drain + 1;               // [kTileRing] producer -> consumers
   uint64_t* ring_empty = ring_full + kTileRing;  // [kTileRing] consumers -> producer
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring_empty + kTileRing);
+  uint64_t* sc_full = ring_empty + kTileRing;     // the tile's column scales staged (4 epilogue warps)
+  uint64_t* sc_free = sc_full + 1;                // the previous tile's scales read (4 epilogue warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sc_free + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* ring = const_cast<int*>(abort_flag + 1);  // [kTileRing] tile indices
+  float* s_sc = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + kBarrierBytes);  // [BN]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  griddep_wait();  // bucket counts, packed rows and the tile counter come from earlier kernels
-  griddep_launch_dependents();
-  // the geometry lives in shared memory: the roles read the few fields they need per
-  // unit instead of holding all of it in registers for the whole kernel
-  __shared__ TileGeo s_geo;
-  make_geo_shared(&s_geo, args, kBM, BN, false);
-  const TileGeo& geo = s_geo;
-  if (static_cast<int>(blockIdx.x) >= geo.total) {  // uniform for the whole CTA
-    feed_retire(args);
-    return;
-  }
-  const bool dyn = args.sched != nullptr;
-
+  // barriers and descriptor prefetch first: they read nothing an earlier kernel writes
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -595,6 +661,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&ring_full[i], 1);
       mbar_init(&ring_empty[i], kRingConsumers);
     }
+    mbar_init(sc_full, 4);
+    mbar_init(sc_free, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -605,6 +673,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&tm_w1);
     tma_prefetch_desc(&tm_w2);
   }
+  griddep_wait();  // bucket counts, packed rows and the tile counter come from earlier kernels
+  griddep_launch_dependents();
+  // the geometry lives in shared memory: the roles read the few fields they need per
+  // unit instead of holding all of it in registers for the whole kernel
+  __shared__ TileGeo s_geo;
+  make_geo_shared(&s_geo, args, kBM, BN, false);
+  const TileGeo& geo = s_geo;
+  if (static_cast<int>(blockIdx.x) >= geo.total) {  // uniform for the whole CTA
+    feed_retire(args);
+    return;
+  }
+  const bool dyn = args.sched != nullptr;
+
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
@@ -726,7 +807,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5)
     const int quarter = warp & 3;  // TMEM lanes this warp may access: 32*quarter ..
-    uint32_t ab = 0, aphase = 0;
+    uint32_t ab = 0, aphase = 0, staged = 0;
     for (;;) {
       const int t = feed_consume(feed, dyn, ring, ring_full, ring_empty, lane, abort_flag);
       bool failed = t < 0;
@@ -741,6 +822,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       const int b = w.b, n0 = w.n0;
       const EpiRow er = epilogue_prepare(args, geo, b, w.pos0 + quarter * 32 + lane, n0, lane);
+      if (!failed && !stage_scales<BN>(args, b, n0, quarter, lane, s_sc, sc_full, sc_free, staged++, abort_flag))
+        failed = true;
       if (!failed && !mbar_wait(&acc_full[ab], aphase, abort_flag)) failed = true;
       if (failed) {
         if (lane == 0) {
@@ -754,10 +837,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (w.split)  // a K range of a split tile: raw partial, reduced by reduce_partials_kernel
         store_partial(args.part + static_cast<size_t>(t) * (kPartBlockBytes / 4), quarter, taddr, BN / 32, lane);
       else
-        epilogue_drain<BN>(args, er, b, n0, taddr);
+        epilogue_drain<BN>(args, er, b, n0, taddr, s_sc);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+      if (lane == 0) {
+        mbar_arrive(&acc_empty[ab]);
+        mbar_arrive(sc_free);
+      }
       ab ^= 1u;
       if (ab == 0) aphase ^= 1u;
     }
@@ -786,13 +872,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ---------------------------------------------------------------------------------
 
 // tile feed of a CTA pair: static (pair p: p, p + pairs, ...) or dynamic -- the leader's
-// producer claims a tile and publishes it into the tile ring of both CTAs (its own by a
+// producer takes tile p first, then claims pairs + the next counter value, and publishes
+// each tile into the tile ring of both CTAs (its own by a
 // local store, the peer's through distributed shared memory, each followed by an arrive
 // on that CTA's ring_full); the five consumers of each CTA (MMA issuer or the peer's
 // producer, four epilogue warps) release the slot on the leader's ring_empty.
 struct PairFeed {
   uint32_t slot, phase;
-  int next;
+  int next;  // static mode: the next tile; dynamic mode: the first tile, then -1
 };
 
 __device__ __forceinline__ int pair_feed_publish(PairFeed& f, bool dyn, int* ring, uint64_t* ring_full,
@@ -806,13 +893,14 @@ __device__ __forceinline__ int pair_feed_publish(PairFeed& f, bool dyn, int* rin
   if (!mbar_wait<true>(&ring_empty[f.slot], f.phase ^ 1u, abort)) return -1;
   int t = 0;
   if (lane == 0) {
-    t = static_cast<int>(atomicAdd(counter, 1u));
+    t = f.next >= 0 ? f.next : npairs + static_cast<int>(atomicAdd(counter, 1u));
     ring[f.slot] = t;
     mbar_arrive(&ring_full[f.slot]);
     st_shared_cluster_u32(map_to_cta(smem_u32(&ring[f.slot]), 1), static_cast<uint32_t>(t));
     mbar_arrive_cluster(map_to_cta(smem_u32(&ring_full[f.slot]), 1));
   }
   t = __shfl_sync(0xffffffffu, t, 0);
+  f.next = -1;
   if (++f.slot == kTileRing) {
     f.slot = 0;
     f.phase ^= 1u;
@@ -857,11 +945,11 @@ constexpr int kPairRows = 256;
 constexpr int kStagesPair = EE_PAIR_STAGES;
 constexpr int kHalfStageBytes = 128 * kBKBytes;  // 16 KB: one operand half of one CTA
 constexpr int kStageBytesPair = 2 * kHalfStageBytes;
-constexpr size_t kGemmSmemPair = 1024 + size_t(kStagesPair) * kStageBytesPair + kBarrierBytes;
+constexpr size_t kGemmSmemPair = 1024 + size_t(kStagesPair) * kStageBytesPair + kBarrierBytes + kScaleBytes;
 static_assert(kGemmSmemPair <= 227 * 1024, "pair GEMM shared memory above the 227 KB per-CTA limit");
 // barrier region: 2 per stage, 2 x 2 accumulator, drain, 2 per ring slot; then the TMEM
 // slot, the abort word and the ring itself
-static_assert((2 * kStagesPair + 5 + 2 * kTileRing) * 8 + 8 + 4 * kTileRing <= kBarrierBytes,
+static_assert((2 * kStagesPair + 7 + 2 * kTileRing) * 8 + 8 + 4 * kTileRing <= kBarrierBytes,
               "pair GEMM barrier region overflows");
 
 template <int KIND>
@@ -913,27 +1001,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain = acc_empty + 2;
   uint64_t* ring_full = drain + 1;               // [kTileRing] both CTAs: tile published
   uint64_t* ring_empty = ring_full + kTileRing;  // [kTileRing] leader: 10 consumers released the slot
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ring_empty + kTileRing);
+  uint64_t* sc_full = ring_empty + kTileRing;     // this CTA's column scales staged (4 epilogue warps)
+  uint64_t* sc_free = sc_full + 1;                // the previous tile's scales read (4 epilogue warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sc_free + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* ring = const_cast<int*>(abort_flag + 1);  // [kTileRing]
+  float* s_sc = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + kBarrierBytes);  // [kBN]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
-  griddep_wait();  // bucket counts, packed rows and the tile counter come from earlier kernels
-  griddep_launch_dependents();
-  // half tiles need each thread's gate and up columns in one lane: not with SwiGLU.  The
-  // geometry lives in shared memory (see gated_gemm_kernel).
-  __shared__ TileGeo s_geo;
-  make_geo_shared(&s_geo, args, kPairRows, kBN, args.out_mode != 2);
-  const TileGeo& geo = s_geo;
-  if (pair >= geo.total) {  // the same decision in both CTAs of the pair
-    if (leader) feed_retire_pair(args, npairs);
-    return;
-  }
-  const bool dyn = args.sched != nullptr;
-
+  // barriers and descriptor prefetch first: they read nothing an earlier kernel writes
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStagesPair; ++s) {
       mbar_init(&full[s], 1);
@@ -948,6 +1027,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       mbar_init(&ring_full[i], 1);
       mbar_init(&ring_empty[i], 2 * kRingConsumers);  // MMA / producer + 4 epilogue warps, x 2 CTAs
     }
+    mbar_init(sc_full, 4);
+    mbar_init(sc_free, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -958,6 +1039,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&tm_w1);
     tma_prefetch_desc(&tm_w2);
   }
+  griddep_wait();  // bucket counts, packed rows and the tile counter come from earlier kernels
+  griddep_launch_dependents();
+  // half tiles need each thread's gate and up columns in one lane: not with SwiGLU.  The
+  // geometry lives in shared memory (see gated_gemm_kernel).
+  __shared__ TileGeo s_geo;
+  make_geo_shared(&s_geo, args, kPairRows, kBN, args.out_mode != 2);
+  const TileGeo& geo = s_geo;
+  if (pair >= geo.total) {  // the same decision in both CTAs of the pair
+    if (leader) feed_retire_pair(args, npairs);
+    return;
+  }
+  const bool dyn = args.sched != nullptr;
+
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
     tmem_relinquish_pair();
@@ -1094,7 +1188,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;
-    uint32_t ab = 0, aphase = 0;
+    uint32_t ab = 0, aphase = 0, staged = 0;
     const uint32_t leader_acc_empty0 = map_to_cta(smem_u32(&acc_empty[0]), 0);
     PairFeed feed{0u, 0u, pair};
     for (;;) {
@@ -1113,7 +1207,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       const int row = half ? static_cast<int>(rank) * 64 + (quarter & 1) * 32 + lane
                            : static_cast<int>(rank) * 128 + quarter * 32 + lane;
       const EpiRow er = epilogue_prepare(args, geo, b, w.pos0 + row, n0, lane);
-      if (!mbar_wait(&acc_full[ab], aphase, abort_flag)) {
+      if (!stage_scales<kBN>(args, b, n0, quarter, lane, s_sc, sc_full, sc_free, staged++, abort_flag) ||
+          !mbar_wait(&acc_full[ab], aphase, abort_flag)) {
         if (lane == 0) {
           atomicOr(&g_device_error, kErrWaitTimeout);
           *abort_flag = 1;
@@ -1126,10 +1221,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         store_partial(args.part + (2 * static_cast<size_t>(t) + rank) * (kPartBlockBytes / 4), quarter, taddr,
                       half ? 4 : kBN / 32, lane);
       else
-        epilogue_drain(args, er, b, n0, taddr, half ? (quarter >> 1) * 4 : 0, half ? 4 : kBN / 32);
+        epilogue_drain(args, er, b, n0, taddr, s_sc, half ? (quarter >> 1) * 4 : 0, half ? 4 : kBN / 32);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(leader_acc_empty0 + ab * static_cast<uint32_t>(sizeof(uint64_t)));
+      if (lane == 0) {
+        mbar_arrive_cluster(leader_acc_empty0 + ab * static_cast<uint32_t>(sizeof(uint64_t)));
+        mbar_arrive(sc_free);
+      }
       ab ^= 1u;
       if (ab == 0) aphase ^= 1u;
     }
@@ -1235,7 +1333,7 @@ __global__ void __launch_bounds__(kReduceThreads, 2) reduce_partials_kernel(cons
     uint32_t rg[32], ru[32];
     sum_partial_chunk(args.part, blk0, ranks, S, q * 8 + warp, lane, as_int, rg);
     sum_partial_chunk(args.part, blk0, ranks, S, q * 8 + warp + 4, lane, as_int, ru);
-    swiglu_chunk(args, er, b, n0, warp, rg, ru);
+    swiglu_chunk(args, er, b, n0, warp, rg, ru, nullptr);
     return;
   }
   const int nchunks = half ? 4 : kBN / 32;
@@ -1243,7 +1341,7 @@ __global__ void __launch_bounds__(kReduceThreads, 2) reduce_partials_kernel(cons
   const EpiRow er = epilogue_prepare(args, geo, b, pos0 + row, n0, lane);
   uint32_t r[32];
   sum_partial_chunk(args.part, blk0, ranks, S, q * 8 + warp, lane, as_int, r);
-  epilogue_chunk(args, er, b, n0, (half ? (q >> 1) * 4 : 0) + warp, r);
+  epilogue_chunk(args, er, b, n0, (half ? (q >> 1) * 4 : 0) + warp, r, nullptr);
 }
 
 }  // namespace ee
