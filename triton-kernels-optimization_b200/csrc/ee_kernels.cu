@@ -435,9 +435,18 @@ namespace {
 template <int D, int G>
 int run_kv_decode(const KvCacheArgs& c, const void* q, int64_t ldq, const void* k_new, const void* v_new,
                   int64_t ld_new, float scale, int splits, float* part, cudaStream_t s) {
-  constexpr int GC = G < 4 ? G : 4;  // query heads per CTA (more heads: more CTAs over the same tokens)
+  constexpr int GC = G;  // every query head of the KV head in one CTA (rows of the M = 16 MMA)
+  static std::once_flag once[64];
+  static cudaError_t err[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -4;
+  std::call_once(once[dev], [dev] {
+    err[dev] = cudaFuncSetAttribute(kv_decode_attention_kernel<D, G, GC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(KvPipe<D>::kSmem));
+  });
+  if (err[dev] != cudaSuccess) return -4;
   const dim3 grid(static_cast<unsigned>(c.batch * c.kv_heads), static_cast<unsigned>(splits), G / GC);
-  return launch_pdl(kv_decode_attention_kernel<D, G, GC>, grid, dim3(kKvThreads), 0, s, c,
+  return launch_pdl(kv_decode_attention_kernel<D, G, GC>, grid, dim3(kKvPipeThreads), KvPipe<D>::kSmem, s, c,
                     static_cast<const __half*>(q), ldq, static_cast<const __half*>(k_new),
                     static_cast<const __half*>(v_new), ld_new, scale, splits, part);
 }

@@ -7,10 +7,11 @@
 //   * kv_append_kernel: one CTA per appended token: takes a slot in its tier's pool,
 //     quantises the token's K and V rows per KV head (INT8: s = amax / 127, q = rn(x / s);
 //     FP8: s = amax / 448, e4m3 = rn-satfinite(x / s)) or copies them (FP16);
-//   * kv_decode_attention_kernel: one CTA per (sequence, KV head, token split, group of up
-//     to four query heads): eight lanes per token, four tokens per warp step, the query
-//     heads against the split's cached tokens (+ the new token's own fp16 K / V),
-//     softmax with the row entropy as partials (m, l, t, o);
+//   * kv_decode_attention_kernel: one CTA per (sequence, KV head, token split): a producer
+//     warp gathers the split's K / V rows through the slot table into a ring of
+//     shared-memory stages with bulk copies, four consumer warps score the KV head's query
+//     heads against them (+ the new token's own fp16 K / V) on the tensor core with an
+//     online softmax and the row entropy, as partials (m, l, t, o);
 //   * kv_decode_combine_kernel: merges the splits of each (sequence, query head).
 // Included once, by ee_kernels.cu.
 #pragma once
@@ -123,260 +124,377 @@ __global__ void kv_commit_kernel(const KvCacheArgs c, int64_t t_new) {
   }
 }
 
-// Eight lanes per token: lane (grp, sl) = (lane / 8, lane % 8) holds elements
-// sl * E8 .. sl * E8 + E8 - 1 (E8 = D / 8) of token grp's K and V rows, so a warp has four
-// tokens' rows in flight per step (eight with the two-step unroll) and a dot product
-// needs three shuffles inside the lane group.
+// Decode attention as a copy pipeline.  One CTA per (sequence, KV head, token split, group
+// of up to eight query heads), 160 threads:
+//   warp 0     producer: per ring stage of kKvTT = 32 tokens, gathers the tokens' K and V
+//              rows (D bytes for an 8-bit token, 2 D for fp16, none for a hole) through
+//              the slot table with 16-byte asynchronous copies, four lanes per row, and
+//              their tiers and 8-bit scales into the stage's metadata; the copies complete
+//              on the stage's full barrier;
+//   warps 1-4  consumers: warp w takes tokens 8 (w - 1) .. + 7 of every stage and runs the
+//              query heads against them on the tensor core (mma.sync m16n8k16 / m16n8k8,
+//              fp16 operands, fp32 accumulation; the heads are the M = 16 rows, the 8-bit
+//              codes convert to fp16 exactly): S = Q K^T, then the online softmax per head
+//              (m base 2, l, t = sum p (x - m)) on S's fragment, then O += (p * s_v) V.
+//              The K scale and softmax scale multiply S in fp32.
+// The bytes in flight sit in the ring (kKvStages stages), not in registers.  Every wait is
+// bounded; on expiry the CTA records the error word, the producer waits (bounded) for its
+// copies in flight and the CTA exits.
+constexpr int kKvTT = 32;        // tokens per ring stage (eight per consumer warp)
+constexpr int kKvStages = 5;     // ring depth
+constexpr int kKvCWarps = 4;     // consumer warps
+constexpr int kKvPipeThreads = 32 * (1 + kKvCWarps);
+constexpr int kKvCodeNone = -2;  // past the split's tokens
+constexpr int kKvCodeNew = -3;   // the step's own token (its rows in k_new / v_new)
+
 template <int D>
-struct KvSlice {
-  static constexpr int E8 = D / 8;  // values per lane: 16 (D 128) or 8 (D 64)
+struct KvPipe {
+  static constexpr int kRow = 2 * D;                      // bytes per row slot (an fp16 row)
+  static constexpr int kRowsBytes = 2 * kKvTT * kRow;     // K rows, then V rows
+  static constexpr int kMetaBytes = kKvTT * 16;           // per token: K scale, V scale, tier
+  static constexpr int kStageBytes = kRowsBytes + kMetaBytes;
+  static constexpr size_t kSmem = 128 /*alignment slack*/ + size_t(kKvStages) * kStageBytes + 2 * kKvStages * 8 + 16;
 };
 
-// One token's K and V slices as loaded, before dequantisation: 16 (8-bit) or 32 (fp16)
-// bytes of each per lane, the tier and the two scales.  Loading a step's rows into these
-// registers one step ahead of its arithmetic keeps two steps of loads in flight per warp.
-// (A deeper ring of cp.async copies through shared memory measured slower: 471 against
-// 380 us at 16 x 8192 tokens; the kernel's 200+ registers per thread, two CTAs per SM,
-// limit it more than the depth of its prefetch.)
-struct KvRaw {
-  uint4 k[2], v[2];
-  float ks, vs;
-  int tier;  // 0 INT8, 1 FP8, 2 fp16 (the new token too), -1 nothing (hole / out of range)
-};
-
+// a stage's K row j / V row j / metadata
 template <int D>
-__device__ __forceinline__ void kv_load(const KvCacheArgs& c, int code, bool is_new, const __half* kn,
-                                        const __half* vn, int h, int e0, KvRaw& r) {
-  constexpr int E8 = KvSlice<D>::E8;
-  if (is_new) {
-    const __half* kp = kn + h * D + e0;
-    const __half* vp = vn + h * D + e0;
-    r.k[0] = *reinterpret_cast<const uint4*>(kp);
-    r.v[0] = *reinterpret_cast<const uint4*>(vp);
-    if constexpr (E8 == 16) {
-      r.k[1] = *reinterpret_cast<const uint4*>(kp + 8);
-      r.v[1] = *reinterpret_cast<const uint4*>(vp + 8);
+__device__ __forceinline__ uint8_t* kv_row(uint8_t* ring, int s, bool v, int j) {
+  return ring + s * KvPipe<D>::kStageBytes + (v ? kKvTT * KvPipe<D>::kRow : 0) + j * KvPipe<D>::kRow;
+}
+template <int D>
+__device__ __forceinline__ int4* kv_meta(uint8_t* ring, int s) {
+  return reinterpret_cast<int4*>(ring + s * KvPipe<D>::kStageBytes + KvPipe<D>::kRowsBytes);
+}
+
+// 16-byte asynchronous copy global -> shared (load/store path, no registers held), and the
+// arrival on `bar` once every copy this thread issued so far has landed (the barrier's
+// count includes it: noinc)
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_4(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// producer warp: the split's tokens [t0, t1) through the ring, nst stages; false if a wait
+// gave up (the copies already issued have then landed or timed out).  Lane l copies rows
+// 8 k + l / 4 (k = 0..3) of every stage, 16-byte chunks 4 q + l % 4: the four lanes of a
+// row move 64 contiguous bytes per instruction.  It reads those rows' slot codes itself
+// (one stage chunk ahead: four stages), and the row's first lane puts the tier into the
+// stage's metadata and copies the token's 8-bit scales there.
+constexpr int kKvChunk = 4;  // stages whose slot codes are read at once
+template <int D>
+__device__ __forceinline__ bool kv_produce(const KvCacheArgs& c, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                           const volatile int* abort, int64_t b, int h, int64_t len, int64_t t0,
+                                           int64_t t1, int nst, const __half* kn, const __half* vn, int lane) {
+  const int part = lane & 3;
+  auto codes_of = [&](int ch, int (&code)[kKvChunk][4]) {
+#pragma unroll
+    for (int ii = 0; ii < kKvChunk; ++ii)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int64_t t = t0 + static_cast<int64_t>(ch * kKvChunk + ii) * kKvTT + 8 * k + (lane >> 2);
+        code[ii][k] = t >= t1 ? kKvCodeNone : (t == len ? kKvCodeNew : c.slot[b * c.max_tokens + t]);  // -1: hole
+      }
+  };
+  int code[kKvChunk][4];
+  codes_of(0, code);
+  uint32_t issued = 0, parity = 0;  // per stage: copies issued, parity of the last issue
+  bool ok = true;
+  const int nch = (nst + kKvChunk - 1) / kKvChunk;
+  for (int ch = 0; ch < nch && ok; ++ch) {
+    int ncode[kKvChunk][4];
+    codes_of(ch + 1, ncode);  // the next chunk's codes, under this chunk's copies
+#pragma unroll
+    for (int ii = 0; ii < kKvChunk; ++ii) {
+      const int i = ch * kKvChunk + ii;
+      if (i >= nst) break;
+      const int s = i % kKvStages;
+      const uint32_t ph = static_cast<uint32_t>(i / kKvStages) & 1u;
+      if (!mbar_wait_warp(&empty[s], ph ^ 1u, abort)) {
+        ok = false;
+        break;
+      }
+      int4* meta = kv_meta<D>(ring, s);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int r = 8 * k + (lane >> 2);
+        const int cd = code[ii][k];
+        const int tier = cd == kKvCodeNew ? 2 : (cd >= 0 ? cd >> 28 : -1);
+        const size_t sl = static_cast<size_t>(cd & 0x0FFFFFFF);
+        const size_t roff = (sl * c.kv_heads + h) * D * (tier == 2 ? 2 : 1);
+        const uint8_t* kp = cd == kKvCodeNew ? reinterpret_cast<const uint8_t*>(kn + h * D)
+                                             : (tier == 2 ? static_cast<const uint8_t*>(c.k16) : c.k8) + roff;
+        const uint8_t* vp = cd == kKvCodeNew ? reinterpret_cast<const uint8_t*>(vn + h * D)
+                                             : (tier == 2 ? static_cast<const uint8_t*>(c.v16) : c.v8) + roff;
+        const int nchunk = tier < 0 ? 0 : (tier == 2 ? 2 * D / 16 : D / 16);
+        uint8_t* kd = kv_row<D>(ring, s, false, r);
+        uint8_t* vd = kv_row<D>(ring, s, true, r);
+#pragma unroll
+        for (int q = 0; q < 2 * D / 64; ++q) {
+          const int chunk = 4 * q + part;
+          if (chunk < nchunk) {
+            cp_async_16(kd + 16 * chunk, kp + 16 * chunk);
+            cp_async_16(vd + 16 * chunk, vp + 16 * chunk);
+          }
+        }
+        if (part == 0) {
+          int* mr = reinterpret_cast<int*>(&meta[r]);
+          mr[2] = tier;
+          if (tier == 0 || tier == 1) {
+            const size_t si = sl * c.kv_heads + h;
+            cp_async_4(mr, c.k_scale + si);
+            cp_async_4(mr + 1, c.v_scale + si);
+          } else {
+            mr[0] = __float_as_int(1.f);
+            mr[1] = __float_as_int(1.f);
+          }
+        }
+      }
+      cp_async_arrive_noinc(&full[s]);  // this lane's copies of the stage, when they land
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);  // publishes the tiers written above
+      issued |= 1u << s;
+      parity = (parity & ~(1u << s)) | (ph << s);
     }
-    r.tier = 2;
+#pragma unroll
+    for (int ii = 0; ii < kKvChunk; ++ii)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) code[ii][k] = ncode[ii][k];
+  }
+  if (!ok) {  // wait (bounded) for the copies in flight
+    for (int s = 0; s < kKvStages; ++s)
+      if (issued & (1u << s)) (void)mbar_wait(&full[s], (parity >> s) & 1u, nullptr);
+  }
+  return ok;
+}
+
+// fp16 pairs from 8-bit codes, exactly: four int8 (one word) -> (c0, c1), (c2, c3) by the
+// 1024-offset trick (fp16 1024 + u for the byte u = c + 128, minus 1152); two e4m3 (a half
+// word) -> one pair by cvt
+__device__ __forceinline__ void i8x4_to_h2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t x = w ^ 0x80808080u;
+  const uint32_t a = __byte_perm(x, 0x64646464u, 0x5140);  // bytes x0, 0x64, x1, 0x64
+  const uint32_t b = __byte_perm(x, 0x64646464u, 0x7362);  // bytes x2, 0x64, x3, 0x64
+  const __half2 off = __halves2half2(__ushort_as_half(0x6480u), __ushort_as_half(0x6480u));  // 1152
+  const __half2 ra = __hsub2(*reinterpret_cast<const __half2*>(&a), off);
+  const __half2 rb = __hsub2(*reinterpret_cast<const __half2*>(&b), off);
+  lo = *reinterpret_cast<const uint32_t*>(&ra);
+  hi = *reinterpret_cast<const uint32_t*>(&rb);
+}
+__device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t v16) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(static_cast<uint16_t>(v16)));
+  return h;
+}
+
+// n consecutive values of a ring row from byte offset `first` (in elements) as n / 2 fp16
+// pairs; zero for a row that holds nothing (tier < 0)
+template <int N>
+__device__ __forceinline__ void kv_pairs(const uint8_t* row, int tier, int first, uint32_t (&h)[N / 2]) {
+  if (tier < 0) {
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) h[i] = 0u;
     return;
   }
-  if (code < 0) {
-    r.tier = -1;
+  if (tier == 2) {  // fp16: the pairs as stored
+    const uint32_t a = smem_u32(row + 2 * first);
+#pragma unroll
+    for (int q = 0; q < N / 8; ++q)
+      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(h[4 * q]), "=r"(h[4 * q + 1]), "=r"(h[4 * q + 2]), "=r"(h[4 * q + 3])
+                   : "r"(a + 16u * q));
     return;
   }
-  const int tr = code >> 28, sl = code & 0x0FFFFFFF;
-  const size_t off = (static_cast<size_t>(sl) * c.kv_heads + h) * D + e0;
-  r.tier = tr;
-  if (tr == 2) {
-    const __half* kp = static_cast<const __half*>(c.k16) + off;
-    const __half* vp = static_cast<const __half*>(c.v16) + off;
-    r.k[0] = *reinterpret_cast<const uint4*>(kp);
-    r.v[0] = *reinterpret_cast<const uint4*>(vp);
-    if constexpr (E8 == 16) {
-      r.k[1] = *reinterpret_cast<const uint4*>(kp + 8);
-      r.v[1] = *reinterpret_cast<const uint4*>(vp + 8);
-    }
-    return;
-  }
-  const size_t si = static_cast<size_t>(sl) * c.kv_heads + h;
-  r.ks = c.k_scale[si];
-  r.vs = c.v_scale[si];
-  if constexpr (E8 == 16) {
-    r.k[0] = *reinterpret_cast<const uint4*>(c.k8 + off);
-    r.v[0] = *reinterpret_cast<const uint4*>(c.v8 + off);
+  uint32_t w[N / 4];
+  const uint32_t a = smem_u32(row + first);
+  if constexpr (N >= 16) {
+#pragma unroll
+    for (int q = 0; q < N / 16; ++q)
+      asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(w[4 * q]), "=r"(w[4 * q + 1]), "=r"(w[4 * q + 2]), "=r"(w[4 * q + 3])
+                   : "r"(a + 16u * q));
   } else {
-    const uint2 ku = *reinterpret_cast<const uint2*>(c.k8 + off);
-    const uint2 vu = *reinterpret_cast<const uint2*>(c.v8 + off);
-    r.k[0] = make_uint4(ku.x, ku.y, 0u, 0u);
-    r.v[0] = make_uint4(vu.x, vu.y, 0u, 0u);
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "r"(a));
+  }
+  if (tier == 0) {
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) i8x4_to_h2(w[i], h[2 * i], h[2 * i + 1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) {
+      h[2 * i] = e4m3x2_to_h2(w[i] & 0xFFFFu);
+      h[2 * i + 1] = e4m3x2_to_h2(w[i] >> 16);
+    }
   }
 }
 
-// the E8 floats of a loaded slice (is_v: the V slice)
-template <int D>
-__device__ __forceinline__ void kv_dequant(const KvRaw& r, bool is_v, float* x) {
-  constexpr int E8 = KvSlice<D>::E8;
-  const uint4* u = is_v ? r.v : r.k;
-  if (r.tier == 2) {
-#pragma unroll
-    for (int q = 0; q < E8 / 8; ++q) {
-      const __half2* hp = reinterpret_cast<const __half2*>(&u[q]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(hp[i]);
-        x[8 * q + 2 * i] = f.x;
-        x[8 * q + 2 * i + 1] = f.y;
-      }
-    }
-    return;
-  }
-  const float s = is_v ? r.vs : r.ks;
-  const uint32_t w[4] = {u[0].x, u[0].y, u[0].z, u[0].w};
-  if (r.tier == 0) {
-#pragma unroll
-    for (int i = 0; i < E8 / 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) x[4 * i + j] = static_cast<float>(static_cast<int8_t>(w[i] >> (8 * j))) * s;
-  } else {
-#pragma unroll
-    for (int i = 0; i < E8 / 4; ++i) {
-      const float2 lo = e4m3x2_to_f32x2(static_cast<uint16_t>(w[i] & 0xFFFFu));
-      const float2 hi = e4m3x2_to_f32x2(static_cast<uint16_t>(w[i] >> 16));
-      x[4 * i] = lo.x * s;
-      x[4 * i + 1] = lo.y * s;
-      x[4 * i + 2] = hi.x * s;
-      x[4 * i + 3] = hi.y * s;
-    }
-  }
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_1688(float (&d)[4], uint32_t a0, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(b0));
 }
 
 // Partial attention of query heads h * G + g0 .. + GC - 1 of KV head h over tokens [t0, t1)
-// of sequence b (t == len: the new token's own fp16 K / V).  Per lane group (one token at
-// a time) an online softmax per head: m (base 2), l, t = sum p (x - m) and the lane's
-// slice of o; the four groups of a warp merge by shuffles, the warps through shared memory.
+// of sequence b (t == len: the new token's own fp16 K / V), as (m, l, t, o) per head.
+// Fragment layout of a consumer lane (gq, q4) = (lane / 4, lane % 4): Q / S / P rows are
+// heads (row gq real when gq < GC; rows 8..15 zero); the K operand of token gq is its row
+// elements (D/4) q4 .. + D/4 - 1 in order (the MMA's k index is a fixed permutation of
+// the head dimension, the same for Q); S columns 2 q4, 2 q4 + 1 are tokens; the V operand
+// of P V block nb is dimension (D/8) gq + nb of tokens 2 q4, 2 q4 + 1, so O's columns
+// 2 q4, 2 q4 + 1 of block nb are dimensions (D/8) (2 q4) + nb and (D/8) (2 q4 + 1) + nb.
 template <int D, int G, int GC>
-__global__ void __launch_bounds__(kKvThreads) kv_decode_attention_kernel(const KvCacheArgs c,
-                                                                         const __half* __restrict__ q, int64_t ldq,
-                                                                         const __half* __restrict__ k_new,
-                                                                         const __half* __restrict__ v_new,
-                                                                         int64_t ld_new, float scale, int splits,
-                                                                         float* __restrict__ part) {
-  griddep_wait();
-  constexpr int E8 = KvSlice<D>::E8;
-  constexpr int W = kKvThreads / 32;
+__global__ void __launch_bounds__(kKvPipeThreads) kv_decode_attention_kernel(const KvCacheArgs c,
+                                                                             const __half* __restrict__ q, int64_t ldq,
+                                                                             const __half* __restrict__ k_new,
+                                                                             const __half* __restrict__ v_new,
+                                                                             int64_t ld_new, float scale, int splits,
+                                                                             float* __restrict__ part) {
+  static_assert(GC >= 1 && GC <= 8, "at most eight query heads per CTA (the M = 16 rows, 8..15 unused)");
+  constexpr int W = kKvCWarps;
+  constexpr int NB = D / 8;  // P V blocks of eight output dimensions
   constexpr float kNegInf = -__builtin_huge_valf();
+  extern __shared__ uint8_t kv_smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(kv_smem_raw) + 127) & ~uintptr_t(127));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kKvStages * KvPipe<D>::kStageBytes);
+  uint64_t* empty = full + kKvStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kKvStages);
   const int b = blockIdx.x / c.kv_heads, h = blockIdx.x % c.kv_heads;
   const int split = blockIdx.y;
   const int g0 = blockIdx.z * GC;  // first query head of the group this CTA handles
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int grp = lane >> 3, sl = lane & 7;
-  const int e0 = sl * E8;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kKvStages; ++s) {
+      mbar_init(&full[s], 33);  // the producer's 32 lanes' copies + its metadata arrival
+      mbar_init(&empty[s], W);  // one arrival per consumer warp
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  griddep_wait();
   const int64_t len = c.length[b];
   const int64_t total = len + 1;  // cached tokens and the new one
   const int64_t per = (total + splits - 1) / splits;
   const int64_t t0 = split * per, t1 = t0 + per < total ? t0 + per : total;
-  constexpr float kLog2e = 1.4426950408889634f;
-  float qv[GC][E8];
-#pragma unroll
-  for (int g = 0; g < GC; ++g) {
-    const __half* qp = q + b * ldq + (static_cast<int64_t>(h) * G + g0 + g) * D + e0;
-#pragma unroll
-    for (int e = 0; e < E8; e += 2) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(qp + e));
-      qv[g][e] = f.x * scale * kLog2e;
-      qv[g][e + 1] = f.y * scale * kLog2e;
-    }
-  }
-  float m[GC], l[GC], tt[GC], o[GC][E8];
-#pragma unroll
-  for (int g = 0; g < GC; ++g) {
-    m[g] = kNegInf;
-    l[g] = 0.f;
-    tt[g] = 0.f;
-#pragma unroll
-    for (int e = 0; e < E8; ++e) o[g][e] = 0.f;
-  }
-  const __half* kn = k_new + b * ld_new;
-  const __half* vn = v_new + b * ld_new;
-  // the warp's tokens: step i covers t = t0 + 4 * (warp + W * i) + grp; slot codes are read
-  // two steps ahead and rows one step ahead of the arithmetic
-  auto code_of = [&](int64_t t) -> int {
-    if (t >= t1) return -1;
-    if (t == len) return 0;  // the new token (its rows come from k_new / v_new)
-    return c.slot[static_cast<int64_t>(b) * c.max_tokens + t];
-  };
-  const int64_t stride = 4 * W;
-  int64_t tcur = t0 + 4 * warp + grp;
-  int code_next = code_of(tcur + stride);
-  KvRaw cur;
-  kv_load<D>(c, code_of(tcur), tcur < t1 && tcur == len, kn, vn, h, e0, cur);
-  if (tcur >= t1) cur.tier = -1;
-  for (int64_t base = t0 + 4 * warp; base < t1; base += stride) {
-    // next step's rows and the step after's codes, before this step's arithmetic
-    const int64_t tn = tcur + stride;
-    KvRaw nxt;
-    kv_load<D>(c, code_next, tn < t1 && tn == len, kn, vn, h, e0, nxt);
-    if (tn >= t1) nxt.tier = -1;
-    code_next = code_of(tn + stride);
-    const bool valid = cur.tier >= 0;
-    float kx[E8], vx[E8];
-    if (valid) {
-      kv_dequant<D>(cur, false, kx);
-      kv_dequant<D>(cur, true, vx);
-    } else {
-#pragma unroll
-      for (int e = 0; e < E8; ++e) kx[e] = vx[e] = 0.f;
-    }
-#pragma unroll
-    for (int g = 0; g < GC; ++g) {
-      float sdot = 0.f;
-#pragma unroll
-      for (int e = 0; e < E8; ++e) sdot = fmaf(qv[g][e], kx[e], sdot);
-      sdot += __shfl_xor_sync(0xffffffffu, sdot, 4);
-      sdot += __shfl_xor_sync(0xffffffffu, sdot, 2);
-      sdot += __shfl_xor_sync(0xffffffffu, sdot, 1);
-      if (!valid) continue;
-      if (sdot > m[g]) {
-        if (m[g] != kNegInf) {
-          const float alpha = exp2f(m[g] - sdot);
-          tt[g] = alpha * (tt[g] + l[g] * (m[g] - sdot));
-          l[g] *= alpha;
-#pragma unroll
-          for (int e = 0; e < E8; ++e) o[g][e] *= alpha;
-        }
-        m[g] = sdot;
-      }
-      const float p = exp2f(sdot - m[g]);
-      l[g] += p;
-      tt[g] = fmaf(p, sdot - m[g], tt[g]);
-#pragma unroll
-      for (int e = 0; e < E8; ++e) o[g][e] = fmaf(p, vx[e], o[g][e]);
-    }
-    cur = nxt;
-    tcur = tn;
-  }
-  // merge the warp's four token groups (lanes sl, sl + 8, sl + 16, sl + 24)
-#pragma unroll
-  for (int off = 8; off <= 16; off <<= 1) {
-#pragma unroll
-    for (int g = 0; g < GC; ++g) {
-      const float mo = __shfl_xor_sync(0xffffffffu, m[g], off);
-      const float lo = __shfl_xor_sync(0xffffffffu, l[g], off);
-      const float to = __shfl_xor_sync(0xffffffffu, tt[g], off);
-      const float M = fmaxf(m[g], mo);
-      const float a = m[g] == kNegInf ? 0.f : exp2f(m[g] - M);
-      const float bb = mo == kNegInf ? 0.f : exp2f(mo - M);
-      const float tn = (m[g] == kNegInf ? 0.f : a * (tt[g] + l[g] * (m[g] - M))) +
-                       (mo == kNegInf ? 0.f : bb * (to + lo * (mo - M)));
-      l[g] = l[g] * a + lo * bb;
-      tt[g] = tn;
-#pragma unroll
-      for (int e = 0; e < E8; ++e) {
-        const float oo = __shfl_xor_sync(0xffffffffu, o[g][e], off);
-        o[g][e] = o[g][e] * a + oo * bb;
-      }
-      m[g] = M;
-    }
-  }
-  // the W warps' partials -> one per (split, query head), through shared memory
+  const int nst = t1 > t0 ? static_cast<int>((t1 - t0 + kKvTT - 1) / kKvTT) : 0;
   __shared__ float s_mlt[W][GC][3];
   __shared__ float s_o[W][GC][D];
-#pragma unroll
-  for (int g = 0; g < GC; ++g) {
-    if (lane == 0) {
-      s_mlt[warp][g][0] = m[g];
-      s_mlt[warp][g][1] = l[g];
-      s_mlt[warp][g][2] = tt[g];
+  if (warp == 0) {
+    if (!kv_produce<D>(c, ring, full, empty, abort_flag, b, h, len, t0, t1, nst, k_new + b * ld_new,
+                       v_new + b * ld_new, lane)) {
+      if (lane == 0) {
+        atomicOr(&g_device_error, kErrWaitTimeout);
+        *abort_flag = 1;
+      }
     }
-    if (grp == 0) {
+  } else {
+    const int cw = warp - 1;
+    const int gq = lane >> 2, q4 = lane & 3;
+    const bool row_real = gq < GC;
+    constexpr float kLog2e = 1.4426950408889634f;
+    const float sl2e = scale * kLog2e;
+    // Q rows (fp16 as given), the MMA A operand: k-block kb is qa[2 kb], qa[2 kb + 1]
+    uint32_t qa[D / 8];
+    {
+      const uint32_t* qp = reinterpret_cast<const uint32_t*>(
+          q + b * ldq + (static_cast<int64_t>(h) * G + g0 + (row_real ? gq : 0)) * D + (D / 4) * q4);
 #pragma unroll
-      for (int e = 0; e < E8; ++e) s_o[warp][g][e0 + e] = o[g][e];
+      for (int i = 0; i < D / 8; ++i) qa[i] = row_real ? qp[i] : 0u;
+    }
+    float m = kNegInf, l = 0.f, tt = 0.f;  // row gq, over this lane's columns
+    float o[NB][4];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.f;
+    for (int i = 0; i < nst; ++i) {
+      const int s = i % kKvStages;
+      if (!mbar_wait_warp(&full[s], static_cast<uint32_t>(i / kKvStages) & 1u, abort_flag)) {
+        if (lane == 0) {
+          atomicOr(&g_device_error, kErrWaitTimeout);
+          *abort_flag = 1;
+        }
+        break;
+      }
+      const int j0 = 8 * cw;  // this warp's first token of the stage
+      const int4* meta = kv_meta<D>(ring, s);
+      const int4 mk = meta[j0 + gq], ma = meta[j0 + 2 * q4], mb = meta[j0 + 2 * q4 + 1];
+      uint32_t kf[D / 8];  // K of token gq, elements (D/4) q4 ..
+      kv_pairs<D / 4>(kv_row<D>(ring, s, false, j0 + gq), mk.z, (D / 4) * q4, kf);
+      uint32_t va[D / 16], vb[D / 16];  // V of tokens 2 q4, 2 q4 + 1, dimensions (D/8) gq ..
+      kv_pairs<D / 8>(kv_row<D>(ring, s, true, j0 + 2 * q4), ma.z, (D / 8) * gq, va);
+      kv_pairs<D / 8>(kv_row<D>(ring, s, true, j0 + 2 * q4 + 1), mb.z, (D / 8) * gq, vb);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);  // the stage's rows are in registers
+      float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kb = 0; kb < D / 16; ++kb) mma_16816(sc, qa[2 * kb], qa[2 * kb + 1], kf[2 * kb], kf[2 * kb + 1]);
+      // row gq, tokens 2 q4 and 2 q4 + 1: base-2 logits (K scale, softmax scale), holes -inf
+      const float x0 = ma.z >= 0 ? sc[0] * (sl2e * __int_as_float(ma.x)) : kNegInf;
+      const float x1 = mb.z >= 0 ? sc[1] * (sl2e * __int_as_float(mb.x)) : kNegInf;
+      float mt = fmaxf(x0, x1);
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+      if (mt > m) {
+        if (m != kNegInf) {
+          const float alpha = exp2f(m - mt);
+          tt = alpha * (tt + l * (m - mt));
+          l *= alpha;
+#pragma unroll
+          for (int nb = 0; nb < NB; ++nb) {
+            o[nb][0] *= alpha;
+            o[nb][1] *= alpha;
+          }
+        }
+        m = mt;
+      }
+      const float p0 = x0 == kNegInf ? 0.f : exp2f(x0 - m);
+      const float p1 = x1 == kNegInf ? 0.f : exp2f(x1 - m);
+      l += p0 + p1;
+      tt += (p0 > 0.f ? p0 * (x0 - m) : 0.f) + (p1 > 0.f ? p1 * (x1 - m) : 0.f);
+      // P (V scale folded in) as the A operand of row gq, k = tokens 2 q4, 2 q4 + 1
+      const __half2 ph = __floats2half2_rn(p0 * __int_as_float(ma.y), p1 * __int_as_float(mb.y));
+      const uint32_t pa = *reinterpret_cast<const uint32_t*>(&ph);
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        // tokens 2 q4, 2 q4 + 1 of dimension (D/8) gq + nb, interleaved
+        const uint32_t bv = __byte_perm(va[nb >> 1], vb[nb >> 1], (nb & 1) ? 0x7632 : 0x5410);
+        mma_1688(o[nb], pa, bv);
+      }
+    }
+    // the row's statistics over its four lanes (m is the same in all four)
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    tt += __shfl_xor_sync(0xffffffffu, tt, 1);
+    tt += __shfl_xor_sync(0xffffffffu, tt, 2);
+    if (row_real) {
+      if (q4 == 0) {
+        s_mlt[cw][gq][0] = m;
+        s_mlt[cw][gq][1] = l;
+        s_mlt[cw][gq][2] = tt;
+      }
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        s_o[cw][gq][(D / 8) * (2 * q4) + nb] = o[nb][0];
+        s_o[cw][gq][(D / 8) * (2 * q4 + 1) + nb] = o[nb][1];
+      }
     }
   }
   __syncthreads();
-  const size_t rec = 3 + D;  // m, l, t, o[D] per (sequence, query head, split)
+  // one record per (split, query head): m, l, t, o[D]
+  const size_t rec = 3 + D;
   const int Hq = static_cast<int>(c.kv_heads) * G;
-  for (int idx = threadIdx.x; idx < GC * (D + 1); idx += kKvThreads) {
+  for (int idx = threadIdx.x; idx < GC * (D + 1); idx += blockDim.x) {
     const int g = idx / (D + 1), col = idx % (D + 1);
     float M = kNegInf;
 #pragma unroll
