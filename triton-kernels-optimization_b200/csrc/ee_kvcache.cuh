@@ -125,13 +125,13 @@ __global__ void kv_commit_kernel(const KvCacheArgs c, int64_t t_new) {
 }
 
 // Decode attention as a copy pipeline.  One CTA per (sequence, KV head, token split, group
-// of up to eight query heads), 160 threads:
-//   warp 0     producer: per ring stage of kKvTT = 32 tokens, gathers the tokens' K and V
+// of up to eight query heads), 192 threads:
+//   warps 0-1  producers: per ring stage of kKvTT = 32 tokens, gather the tokens' K and V
 //              rows (D bytes for an 8-bit token, 2 D for fp16, none for a hole) through
 //              the slot table with 16-byte asynchronous copies, four lanes per row, and
 //              their tiers and 8-bit scales into the stage's metadata; the copies complete
 //              on the stage's full barrier;
-//   warps 1-4  consumers: warp w takes tokens 8 (w - 1) .. + 7 of every stage and runs the
+//   warps 2-5  consumers: warp w takes tokens 8 (w - 2) .. + 7 of every stage and runs the
 //              query heads against them on the tensor core (mma.sync m16n8k16 / m16n8k8,
 //              fp16 operands, fp32 accumulation; the heads are the M = 16 rows, the 8-bit
 //              codes convert to fp16 exactly): S = Q K^T, then the online softmax per head
@@ -143,7 +143,8 @@ __global__ void kv_commit_kernel(const KvCacheArgs c, int64_t t_new) {
 constexpr int kKvTT = 32;        // tokens per ring stage (eight per consumer warp)
 constexpr int kKvStages = 5;     // ring depth
 constexpr int kKvCWarps = 4;     // consumer warps
-constexpr int kKvPipeThreads = 32 * (1 + kKvCWarps);
+constexpr int kKvPWarps = 2;     // producer warps (16 rows of a stage each)
+constexpr int kKvPipeThreads = 32 * (kKvPWarps + kKvCWarps);
 constexpr int kKvCodeNone = -2;  // past the split's tokens
 constexpr int kKvCodeNew = -3;   // the step's own token (its rows in k_new / v_new)
 
@@ -180,33 +181,34 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
 }
 
 // producer warp: the split's tokens [t0, t1) through the ring, nst stages; false if a wait
-// gave up (the copies already issued have then landed or timed out).  Lane l copies rows
-// 8 k + l / 4 (k = 0..3) of every stage, 16-byte chunks 4 q + l % 4: the four lanes of a
-// row move 64 contiguous bytes per instruction.  It reads those rows' slot codes itself
-// (one stage chunk ahead: four stages), and the row's first lane puts the tier into the
-// stage's metadata and copies the token's 8-bit scales there.
+// gave up (the copies already issued have then landed or timed out).  Both producer warps
+// read the stage's 32 slot codes (lane l: token l, a chunk of four stages ahead) and rank
+// the tokens by tier; lane l of producer pw copies the rows of tokens 8 k + l / 4
+// (k = 2 pw, 2 pw + 1) into their ranked ring rows, 16-byte chunks 4 q + l % 4 (the four
+// lanes of a row move 64 contiguous bytes per instruction), and the row's first lane puts
+// the tier into the stage's metadata and copies the token's 8-bit scales there.
 constexpr int kKvChunk = 4;  // stages whose slot codes are read at once
 template <int D>
 __device__ __forceinline__ bool kv_produce(const KvCacheArgs& c, uint8_t* ring, uint64_t* full, uint64_t* empty,
                                            const volatile int* abort, int64_t b, int h, int64_t len, int64_t t0,
-                                           int64_t t1, int nst, const __half* kn, const __half* vn, int lane) {
+                                           int64_t t1, int nst, const __half* kn, const __half* vn, int pw, int lane) {
+  constexpr int K = 4 / kKvPWarps;  // row groups per producer warp
   const int part = lane & 3;
-  auto codes_of = [&](int ch, int (&code)[kKvChunk][4]) {
+  // lane l reads the code of token l of each stage
+  auto codes_of = [&](int ch, int (&code)[kKvChunk]) {
 #pragma unroll
-    for (int ii = 0; ii < kKvChunk; ++ii)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int64_t t = t0 + static_cast<int64_t>(ch * kKvChunk + ii) * kKvTT + 8 * k + (lane >> 2);
-        code[ii][k] = t >= t1 ? kKvCodeNone : (t == len ? kKvCodeNew : c.slot[b * c.max_tokens + t]);  // -1: hole
-      }
+    for (int ii = 0; ii < kKvChunk; ++ii) {
+      const int64_t t = t0 + static_cast<int64_t>(ch * kKvChunk + ii) * kKvTT + lane;
+      code[ii] = t >= t1 ? kKvCodeNone : (t == len ? kKvCodeNew : c.slot[b * c.max_tokens + t]);  // -1: hole
+    }
   };
-  int code[kKvChunk][4];
+  int code[kKvChunk];
   codes_of(0, code);
   uint32_t issued = 0, parity = 0;  // per stage: copies issued, parity of the last issue
   bool ok = true;
   const int nch = (nst + kKvChunk - 1) / kKvChunk;
   for (int ch = 0; ch < nch && ok; ++ch) {
-    int ncode[kKvChunk][4];
+    int ncode[kKvChunk];
     codes_of(ch + 1, ncode);  // the next chunk's codes, under this chunk's copies
 #pragma unroll
     for (int ii = 0; ii < kKvChunk; ++ii) {
@@ -219,10 +221,23 @@ __device__ __forceinline__ bool kv_produce(const KvCacheArgs& c, uint8_t* ring, 
         break;
       }
       int4* meta = kv_meta<D>(ring, s);
+      // the stage's ring row of token `lane`: tokens grouped by tier (INT8, FP8, fp16, then
+      // nothing), so that most consumer warps meet one tier (the attention does not
+      // depend on the tokens' order)
+      const int my_tier = code[ii] == kKvCodeNew ? 2 : (code[ii] >= 0 ? code[ii] >> 28 : 3);
+      const uint32_t below = (1u << lane) - 1u;
+      int dest = 0;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int r = 8 * k + (lane >> 2);
-        const int cd = code[ii][k];
+      for (int v = 0; v < 4; ++v) {
+        const uint32_t m = __ballot_sync(0xffffffffu, my_tier == v);
+        if (my_tier > v) dest += __popc(m);
+        if (my_tier == v) dest += __popc(m & below);
+      }
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int tok = 8 * (K * pw + k) + (lane >> 2);  // the token whose rows this lane copies
+        const int cd = __shfl_sync(0xffffffffu, code[ii], tok);
+        const int r = __shfl_sync(0xffffffffu, dest, tok);
         const int tier = cd == kKvCodeNew ? 2 : (cd >= 0 ? cd >> 28 : -1);
         const size_t sl = static_cast<size_t>(cd & 0x0FFFFFFF);
         const size_t roff = (sl * c.kv_heads + h) * D * (tier == 2 ? 2 : 1);
@@ -261,9 +276,7 @@ __device__ __forceinline__ bool kv_produce(const KvCacheArgs& c, uint8_t* ring, 
       parity = (parity & ~(1u << s)) | (ph << s);
     }
 #pragma unroll
-    for (int ii = 0; ii < kKvChunk; ++ii)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) code[ii][k] = ncode[ii][k];
+    for (int ii = 0; ii < kKvChunk; ++ii) code[ii] = ncode[ii];
   }
   if (!ok) {  // wait (bounded) for the copies in flight
     for (int s = 0; s < kKvStages; ++s)
@@ -376,7 +389,7 @@ __global__ void __launch_bounds__(kKvPipeThreads) kv_decode_attention_kernel(con
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kKvStages; ++s) {
-      mbar_init(&full[s], 33);  // the producer's 32 lanes' copies + its metadata arrival
+      mbar_init(&full[s], 33 * kKvPWarps);  // per producer warp: its 32 lanes' copies + its metadata arrival
       mbar_init(&empty[s], W);  // one arrival per consumer warp
     }
     *abort_flag = 0;
@@ -391,16 +404,16 @@ __global__ void __launch_bounds__(kKvPipeThreads) kv_decode_attention_kernel(con
   const int nst = t1 > t0 ? static_cast<int>((t1 - t0 + kKvTT - 1) / kKvTT) : 0;
   __shared__ float s_mlt[W][GC][3];
   __shared__ float s_o[W][GC][D];
-  if (warp == 0) {
+  if (warp < kKvPWarps) {
     if (!kv_produce<D>(c, ring, full, empty, abort_flag, b, h, len, t0, t1, nst, k_new + b * ld_new,
-                       v_new + b * ld_new, lane)) {
+                       v_new + b * ld_new, warp, lane)) {
       if (lane == 0) {
         atomicOr(&g_device_error, kErrWaitTimeout);
         *abort_flag = 1;
       }
     }
   } else {
-    const int cw = warp - 1;
+    const int cw = warp - kKvPWarps;
     const int gq = lane >> 2, q4 = lane & 3;
     const bool row_real = gq < GC;
     constexpr float kLog2e = 1.4426950408889634f;
@@ -436,9 +449,15 @@ __global__ void __launch_bounds__(kKvPipeThreads) kv_decode_attention_kernel(con
       kv_pairs<D / 8>(kv_row<D>(ring, s, true, j0 + 2 * q4 + 1), mb.z, (D / 8) * gq, vb);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);  // the stage's rows are in registers
-      float sc[4] = {0.f, 0.f, 0.f, 0.f};
+      // two independent accumulation chains over the k-blocks (even / odd), added after
+      float sc[4] = {0.f, 0.f, 0.f, 0.f}, sd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int kb = 0; kb < D / 16; ++kb) mma_16816(sc, qa[2 * kb], qa[2 * kb + 1], kf[2 * kb], kf[2 * kb + 1]);
+      for (int kb = 0; kb < D / 16; kb += 2) {
+        mma_16816(sc, qa[2 * kb], qa[2 * kb + 1], kf[2 * kb], kf[2 * kb + 1]);
+        mma_16816(sd, qa[2 * kb + 2], qa[2 * kb + 3], kf[2 * kb + 2], kf[2 * kb + 3]);
+      }
+      sc[0] += sd[0];
+      sc[1] += sd[1];
       // row gq, tokens 2 q4 and 2 q4 + 1: base-2 logits (K scale, softmax scale), holes -inf
       const float x0 = ma.z >= 0 ? sc[0] * (sl2e * __int_as_float(ma.x)) : kNegInf;
       const float x1 = mb.z >= 0 ? sc[1] * (sl2e * __int_as_float(mb.x)) : kNegInf;
