@@ -10,6 +10,10 @@ mix about 24 / 55 / 21 %); device footprint is about 4*N*K + 5*rows*K + 2*rows*N
 --case attention: each repetition runs flash_attention_entropy (causal, output and
 per-row entropy) on q [B, Hq, S, D], k / v [B, Hkv, S, D].
 
+--case kv: an entropy-tied KV cache of --B sequences x --S tokens (8 KV heads of 128, tokens
+stored at about 24 / 55 / 21 % INT8 / FP8 / FP16, the bench's seeds), then per repetition
+one decode step's attention of 32 query heads against it (+ its own new K / V).
+
 --case forward: each repetition runs one eager forward of the decoder-stack engine over
 --layers Llama-3-8B-shaped layers (hidden 4096, 32 / 8 heads of 128, intermediate 14336;
 random-init weights) for --B sequences of --S tokens, per-token routing at (0.41, 1.68).
@@ -18,6 +22,7 @@ random-init weights) for --B sequences of --S tokens, per-token routing at (0.41
     ncu --set full --clock-control none -k regex:gated_gemm -s 3 -c 1 -o prof <same command>
     python profile_case.py --case attention --B 1 --Hq 32 --Hkv 4 --S 2048 --D 64
     python profile_case.py --case forward --layers 1 --B 8 --S 2048 --reps 2
+    python profile_case.py --case kv --B 8 --S 8192 --reps 3
 """
 from __future__ import annotations
 
@@ -38,7 +43,7 @@ def main(argv=None) -> int:
     ap.add_argument("--N", type=int, default=14336)
     ap.add_argument("--n-logits", type=int, default=4096)
     ap.add_argument("--reps", type=int, default=4)
-    ap.add_argument("--case", choices=("gated", "attention", "forward"), default="gated")
+    ap.add_argument("--case", choices=("gated", "attention", "forward", "kv"), default="gated")
     ap.add_argument("--layers", type=int, default=1)
     ap.add_argument("--B", type=int, default=1)
     ap.add_argument("--Hq", type=int, default=32)
@@ -73,6 +78,26 @@ def main(argv=None) -> int:
         torch.cuda.synchronize()
         pkg._lib.device_check()
         print("forward", args.layers, "layers", args.B, "x", args.S, "mix", eng.layer_counts.sum(dim=0).tolist())
+        return 0
+    if args.case == "kv":
+        kv, d, hq = 8, 128, 32
+        gk = torch.Generator(device=dev).manual_seed(21)
+        cache = pkg.EntropyKVCache(args.B, kv, d, args.S + 64, device=dev)
+        k = torch.randn(args.B * args.S, kv * d, generator=gk, device=dev).half()
+        v = torch.randn(args.B * args.S, kv * d, generator=gk, device=dev).half()
+        u = torch.rand(args.B * args.S, generator=gk, device=dev)
+        tier = torch.where(u < 0.24, 0, torch.where(u < 0.79, 1, 2)).to(torch.int8)
+        cache.append(k, v, tier)
+        del k, v
+        q = torch.randn(args.B, hq * d, generator=gk, device=dev).half()
+        kn = torch.randn(args.B, kv * d, generator=gk, device=dev).half()
+        vn = torch.randn(args.B, kv * d, generator=gk, device=dev).half()
+        out = torch.empty_like(q)
+        for _ in range(args.reps):
+            cache.decode_attention(q, kn, vn, d ** -0.5, out=out)
+        torch.cuda.synchronize()
+        pkg._lib.device_check()
+        print("kv decode", args.B, "x", args.S, "tiers", [int((tier == t).sum()) for t in range(3)])
         return 0
     if args.case == "attention":
         q = torch.randn(args.B, args.Hq, args.S, args.D, generator=g, device=dev).half()
