@@ -50,7 +50,7 @@ def _codes_ref(x, t):
     return y.to(torch.float8_e4m3fn).view(torch.uint8), s.squeeze(-1)
 
 
-@pytest.mark.parametrize("d,kv,heads", [(128, 4, 32), (64, 4, 8)])
+@pytest.mark.parametrize("d,kv,heads", [(128, 4, 32), (64, 4, 8), (128, 8, 32), (64, 2, 2)])
 @torch.no_grad()
 def test_kv_cache_codes_and_decode_attention(pkg, cuda, d, kv, heads):
     B, T0, T_max = 3, 300, 512
