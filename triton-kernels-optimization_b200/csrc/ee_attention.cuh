@@ -130,6 +130,37 @@ __device__ __forceinline__ uint32_t p_offset(int row, int col) {
                                ((col & 7) << 1));
 }
 
+// The work unit t of a launch: (batch, query head, 256 query rows), longest causal units
+// first over the whole grid (all (batch, head) pairs of the last query chunk, then the
+// chunk before, ...); the CTAs take units t = blockIdx.x, + gridDim.x, ... (persistent).
+struct AttnUnit {
+  int64_t b, h, bh, q0;
+  int nkv0, nkv1;               // key tiles query tile 0 / 1 sees
+  int q_row0, k_row0, v_row0;   // rows in Q [B*Hq*S, D], K [B*Hkv*S, D], V^T [B*Hkv*D, S_pad]
+};
+template <int D>
+__device__ __forceinline__ AttnUnit attn_unit(const AttnArgs& args, int64_t t) {
+  constexpr int KT = AttnCfg<D>::KT;
+  const int64_t nqc = (args.S + 2 * kAttnTile - 1) / (2 * kAttnTile);
+  const int64_t nbh = args.B * args.Hq;
+  AttnUnit u;
+  const int64_t qc = nqc - 1 - t / nbh;
+  u.bh = t % nbh;
+  u.b = u.bh / args.Hq;
+  u.h = u.bh % args.Hq;
+  const int64_t hk = u.h / (args.Hq / args.Hkv);
+  u.q0 = qc * 2 * kAttnTile;
+  const int nkv_all = static_cast<int>((args.S + KT - 1) / KT);
+  const int reach0 = static_cast<int>((u.q0 + kAttnTile + KT - 1) / KT);
+  const int reach1 = static_cast<int>((u.q0 + 2 * kAttnTile + KT - 1) / KT);
+  u.nkv0 = args.causal ? (reach0 < nkv_all ? reach0 : nkv_all) : nkv_all;
+  u.nkv1 = args.causal ? (reach1 < nkv_all ? reach1 : nkv_all) : nkv_all;
+  u.q_row0 = static_cast<int>(u.bh * args.S + u.q0);
+  u.k_row0 = static_cast<int>((u.b * args.Hkv + hk) * args.S);
+  u.v_row0 = static_cast<int>((u.b * args.Hkv + hk) * D);
+  return u;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     flash_attention_entropy_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -153,32 +184,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* s_free = s_full + 2;          // [2] S_w read into registers (4 warps)
   uint64_t* p_full = s_full + 4;          // [2] P_w written, O_w corrected (4 warps)
   uint64_t* o_done = s_full + 6;          // [2] P_w V done: P_w free, O_w stable (MMA commit)
-  uint64_t* drain = s_full + 8;          // [2] MMA drain on abort, one per issuing thread
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 10);
-  static_assert((1 + 2 * NS + 2 * NV + 10) * 8 + 8 <= Cfg::kBarrierBytes, "attention barrier region overflows");
+  uint64_t* drain = s_full + 8;           // [2] MMA drain on abort, one per issuing thread
+  uint64_t* q_empty = s_full + 10;        // both issuers' S MMAs of a unit done: Q may reload
+  uint64_t* o_free = s_full + 11;         // [2] O_w of the finished unit read out (4 warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 13);
+  static_assert((1 + 2 * NS + 2 * NV + 13) * 8 + 8 <= Cfg::kBarrierBytes, "attention barrier region overflows");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // CTA = (batch, query head, 256 query rows); longest causal tiles first
-  const int64_t nqc = (args.S + 2 * kAttnTile - 1) / (2 * kAttnTile);
-  const int qc = static_cast<int>(nqc - 1 - static_cast<int64_t>(blockIdx.x) % nqc);
-  const int64_t bh = static_cast<int64_t>(blockIdx.x) / nqc;  // b * Hq + h
-  const int64_t b = bh / args.Hq, h = bh % args.Hq;
-  const int64_t hk = h / (args.Hq / args.Hkv);
-  const int64_t q0 = static_cast<int64_t>(qc) * 2 * kAttnTile;  // first query row of the CTA
-  const int nkv_all = static_cast<int>((args.S + KT - 1) / KT);
-  // key tiles the 128 rows of query tile 0 / 1 see (tile 1 never fewer than tile 0)
-  const int reach0 = static_cast<int>((q0 + kAttnTile + KT - 1) / KT);
-  const int reach1 = static_cast<int>((q0 + 2 * kAttnTile + KT - 1) / KT);
-  const int nkv0 = args.causal ? (reach0 < nkv_all ? reach0 : nkv_all) : nkv_all;
-  const int nkv1 = args.causal ? (reach1 < nkv_all ? reach1 : nkv_all) : nkv_all;
-  const int nkv_max = nkv1;
-  const int q_row0 = static_cast<int>(bh * args.S + q0);                     // row in Q [B*Hq*S, D]
-  const int k_row0 = static_cast<int>((b * args.Hkv + hk) * args.S);         // row in K [B*Hkv*S, D]
-  const int v_row0 = static_cast<int>((b * args.Hkv + hk) * D);              // row in V^T [B*Hkv*D, S_pad]
+  const int64_t nunits = args.B * args.Hq * ((args.S + 2 * kAttnTile - 1) / (2 * kAttnTile));
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 2);  // one commit per issuing thread
     for (int i = 0; i < NS; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 2);  // one commit per issuing thread
@@ -192,6 +210,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&s_free[i], 4);  // the four warps of the warpgroup
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
+      mbar_init(&o_free[i], 4);
     }
     mbar_init(&drain[0], 1);
     mbar_init(&drain[1], 1);
@@ -222,49 +241,70 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     bool failed = false;
     uint32_t k_issued = 0, v_issued = 0;  // bit s: stage s has received a load (for the abort drain)
     uint32_t k_par = 0, v_par = 0;        // bit s: phase parity of stage s's last load
-    if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, 2 * Cfg::kQTileBytes);
-      for (int t = 0; t < 2; ++t)
-        for (int kb = 0; kb < Cfg::kKBlocks; ++kb)
-          tma_load_2d(sQ + t * Cfg::kQTileBytes + kb * kAttnTileBytes, &tm_q, q_full, kb * 64, q_row0 + t * kAttnTile);
-    }
-    // K runs one tile ahead of V: S_{j+1} is issued (as soon as the softmax holds S_j)
-    // before P V_j (once P_j is written)
-    auto load_k = [&](int j) -> bool {
-      const int s = j % NS;
-      const uint32_t ph = static_cast<uint32_t>(j / NS) & 1u;
-      if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag)) return false;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&k_full[s], Cfg::kKBytes);
-        for (int kb = 0; kb < Cfg::kKBlocks; ++kb)
-          tma_load_2d(sK + s * Cfg::kKBytes + kb * (KT * 128), &tm_k, &k_full[s], kb * 64, k_row0 + j * KT);
-      }
-      k_issued |= 1u << s;
-      k_par = (k_par & ~(1u << s)) | (ph << s);
-      __syncwarp();
-      return true;
-    };
-    auto load_v = [&](int j) -> bool {
-      const int sv = j % NV;
-      const uint32_t phv = static_cast<uint32_t>(j / NV) & 1u;
-      if (!mbar_wait(&v_empty[sv], phv ^ 1u, abort_flag)) return false;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&v_full[sv], Cfg::kVBytes);
-        for (int vb = 0; vb < Cfg::kVBlocks; ++vb)
-          tma_load_2d(sV + sv * Cfg::kVBytes + vb * (D * 128), &tm_vt, &v_full[sv], j * KT + vb * 64, v_row0);
-      }
-      v_issued |= 1u << sv;
-      v_par = (v_par & ~(1u << sv)) | (phv << sv);
-      __syncwarp();
-      return true;
-    };
-    if (nkv_max > 0 && !load_k(0)) failed = true;
-    for (int j = 0; j < nkv_max && !failed; ++j) {
-      if (j + 1 < nkv_max && !load_k(j + 1)) {
+    uint32_t kt = 0, vt = 0;              // K / V tiles loaded so far (all units)
+    int q_loads = 0;                      // Q loads issued (one per unit)
+    for (int64_t t = blockIdx.x; t < nunits && !failed; t += gridDim.x) {
+      const AttnUnit un = attn_unit<D>(args, t);
+      const int nkv_max = un.nkv1;
+      // Q of this unit, once both issuers' S MMAs of the previous unit have read the old Q
+      if (q_loads > 0 && !mbar_wait_warp(q_empty, static_cast<uint32_t>(q_loads - 1) & 1u, abort_flag)) {
         failed = true;
         break;
       }
-      if (!load_v(j)) failed = true;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(q_full, 2 * Cfg::kQTileBytes);
+        for (int q = 0; q < 2; ++q)
+          for (int kb = 0; kb < Cfg::kKBlocks; ++kb)
+            tma_load_2d(sQ + q * Cfg::kQTileBytes + kb * kAttnTileBytes, &tm_q, q_full, kb * 64, un.q_row0 + q * kAttnTile);
+      }
+      ++q_loads;
+      __syncwarp();
+      // K runs one tile ahead of V: S_{j+1} is issued (as soon as the softmax holds S_j)
+      // before P V_j (once P_j is written)
+      auto load_k = [&](int j) -> bool {
+        const int s = kt % NS;
+        const uint32_t ph = (kt / NS) & 1u;
+        if (!mbar_wait_warp(&k_empty[s], ph ^ 1u, abort_flag)) return false;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&k_full[s], Cfg::kKBytes);
+          for (int kb = 0; kb < Cfg::kKBlocks; ++kb)
+            tma_load_2d(sK + s * Cfg::kKBytes + kb * (KT * 128), &tm_k, &k_full[s], kb * 64, un.k_row0 + j * KT);
+        }
+        k_issued |= 1u << s;
+        k_par = (k_par & ~(1u << s)) | (ph << s);
+        ++kt;
+        __syncwarp();
+        return true;
+      };
+      auto load_v = [&](int j) -> bool {
+        const int sv = vt % NV;
+        const uint32_t phv = (vt / NV) & 1u;
+        if (!mbar_wait_warp(&v_empty[sv], phv ^ 1u, abort_flag)) return false;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&v_full[sv], Cfg::kVBytes);
+          for (int vb = 0; vb < Cfg::kVBlocks; ++vb)
+            tma_load_2d(sV + sv * Cfg::kVBytes + vb * (D * 128), &tm_vt, &v_full[sv], j * KT + vb * 64, un.v_row0);
+        }
+        v_issued |= 1u << sv;
+        v_par = (v_par & ~(1u << sv)) | (phv << sv);
+        ++vt;
+        __syncwarp();
+        return true;
+      };
+      if (!load_k(0)) {
+        failed = true;
+        break;
+      }
+      for (int j = 0; j < nkv_max; ++j) {
+        if (j + 1 < nkv_max && !load_k(j + 1)) {
+          failed = true;
+          break;
+        }
+        if (!load_v(j)) {
+          failed = true;
+          break;
+        }
+      }
     }
     if (failed) {
       if (lane == 0) {
@@ -272,25 +312,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         *abort_flag = 1;
       }
       // let the loads already issued land before the CTA can exit (bounded, no abort)
-      (void)mbar_wait(q_full, 0u, nullptr);
+      if (q_loads > 0) (void)mbar_wait(q_full, static_cast<uint32_t>(q_loads - 1) & 1u, nullptr);
       for (int s = 0; s < NS; ++s)
         if (k_issued & (1u << s)) (void)mbar_wait(&k_full[s], (k_par >> s) & 1u, nullptr);
       for (int s = 0; s < NV; ++s)
         if (v_issued & (1u << s)) (void)mbar_wait(&v_full[s], (v_par >> s) & 1u, nullptr);
     }
   } else if (warp == 1 || warp == 2) {
-    // -------------------------------------------------------------- UMMA issuer
-    // S_w,j = Q_w K_j^T into S_w; O_w (+)= P_w,j V_j.  Order: S_w,0, then per key tile j:
-    // S_w,j+1, P_w V_j -- the tensor core works for one warpgroup while the other one
-    // runs its softmax.
+    // -------------------------------------------------------------- UMMA issuers
+    // One thread per query tile w = warp - 1.  Per unit: S_w,0, then per key tile j:
+    // S_w,j+1, P_w V_j -- the tensor core works for one warpgroup while the other one runs
+    // its softmax.  For the key tiles past its causal reach it still takes part in the K /
+    // V rings (waits for the stage, commits its share of the release).  Counters run over
+    // all units of the CTA: kt / vt the K / V tiles, g the tiles of query tile w.
     constexpr uint32_t idesc_s = make_idesc(1u, 0u, kAttnTile, KT);  // f32 <- f16 x f16, 128 x KT
     constexpr uint32_t idesc_o = make_idesc(1u, 0u, kAttnTile, D);   // f32 <- f16 x f16, 128 x D
-    bool failed = !mbar_wait(q_full, 0u, abort_flag);
-    tc_fence_after();
-    auto issue_s = [&](int w, int j) -> bool {
-      const int s = j % NS;
-      if (!mbar_wait(&k_full[s], static_cast<uint32_t>(j / NS) & 1u, abort_flag) ||
-          !mbar_wait(&s_free[w], (static_cast<uint32_t>(j) & 1u) ^ 1u, abort_flag))
+    const int w = warp - 1;
+    bool failed = false;
+    uint32_t kt = 0, vt = 0, g = 0;
+    int units = 0;
+    auto issue_s = [&](uint32_t kidx, uint32_t gidx) -> bool {
+      const int s = kidx % NS;
+      if (!mbar_wait(&k_full[s], (kidx / NS) & 1u, abort_flag) ||
+          !mbar_wait(&s_free[w], (gidx & 1u) ^ 1u, abort_flag))
         return false;
       tc_fence_after();
       if (lane == 0) {
@@ -307,10 +351,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       return true;
     };
-    auto issue_pv = [&](int w, int j) -> bool {
-      const int s = j % NV;
-      if (!mbar_wait(&v_full[s], static_cast<uint32_t>(j / NV) & 1u, abort_flag) ||
-          !mbar_wait(&p_full[w], static_cast<uint32_t>(j) & 1u, abort_flag))
+    auto issue_pv = [&](uint32_t vidx, uint32_t gidx, bool first) -> bool {
+      const int s = vidx % NV;
+      if (!mbar_wait(&v_full[s], (vidx / NV) & 1u, abort_flag) ||
+          !mbar_wait(&p_full[w], gidx & 1u, abort_flag))
         return false;
       tc_fence_after();
       if (lane == 0) {
@@ -320,39 +364,64 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const uint64_t db = sdesc_k_sw128(smem_u32(sV + s * Cfg::kVBytes + vb * (D * 128)));
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            tc_mma<kKindF16>(dst, da + 2u * k, db + 2u * k, idesc_o, (j == 0 && vb == 0 && k == 0) ? 0u : 1u);
+            tc_mma<kKindF16>(dst, da + 2u * k, db + 2u * k, idesc_o, (first && vb == 0 && k == 0) ? 0u : 1u);
         }
         tc_commit(&o_done[w]);
       }
       __syncwarp();
       return true;
     };
-    // this thread's query tile only; for the key tiles past its reach it still takes
-    // part in the K / V rings (waits for the stage, commits its share of the release)
-    const int w = warp - 1;
-    const int nkv_w = w == 0 ? nkv0 : nkv1;
-    if (!failed) failed = !issue_s(w, 0);
-    if (!failed && lane == 0) tc_commit(&k_empty[0]);
-    __syncwarp();
-    for (int j = 0; j < nkv_max && !failed; ++j) {
-      if (j + 1 < nkv_max) {
-        if (j + 1 < nkv_w) {
-          if (!issue_s(w, j + 1)) failed = true;
-        } else if (!mbar_wait(&k_full[(j + 1) % NS], static_cast<uint32_t>((j + 1) / NS) & 1u, abort_flag)) {
-          failed = true;
+    for (int64_t t = blockIdx.x; t < nunits && !failed; t += gridDim.x, ++units) {
+      const AttnUnit un = attn_unit<D>(args, t);
+      const int nkv_w = w == 0 ? un.nkv0 : un.nkv1;
+      const int nkv_max = un.nkv1;
+      if (!mbar_wait(q_full, static_cast<uint32_t>(units) & 1u, abort_flag)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      // after this thread's last S of the unit, the Q tiles may reload (when it completes)
+      auto q_release = [&](int j) {
+        if (j == nkv_w - 1) {
+          if (lane == 0) tc_commit(q_empty);
+          __syncwarp();
         }
-        if (!failed && lane == 0) tc_commit(&k_empty[(j + 1) % NS]);
+      };
+      if (!issue_s(kt, g)) {
+        failed = true;
+        break;
+      }
+      q_release(0);
+      if (lane == 0) tc_commit(&k_empty[kt % NS]);
+      __syncwarp();
+      for (int j = 0; j < nkv_max && !failed; ++j) {
+        if (j + 1 < nkv_max) {
+          const uint32_t kn = kt + j + 1;
+          if (j + 1 < nkv_w) {
+            if (!issue_s(kn, g + j + 1)) failed = true;
+            if (!failed) q_release(j + 1);
+          } else if (!mbar_wait(&k_full[kn % NS], (kn / NS) & 1u, abort_flag)) {
+            failed = true;
+          }
+          if (!failed && lane == 0) tc_commit(&k_empty[kn % NS]);
+          __syncwarp();
+        }
+        if (!failed) {
+          if (j < nkv_w) {
+            // the unit's first P V overwrites O_w: the previous unit's O_w must be read out
+            if (j == 0 && units > 0 && !mbar_wait(&o_free[w], static_cast<uint32_t>(units - 1) & 1u, abort_flag))
+              failed = true;
+            if (!failed && !issue_pv(vt + j, g + j, j == 0)) failed = true;
+          } else if (!mbar_wait(&v_full[(vt + j) % NV], ((vt + j) / NV) & 1u, abort_flag)) {
+            failed = true;
+          }
+        }
+        if (!failed && lane == 0) tc_commit(&v_empty[(vt + j) % NV]);
         __syncwarp();
       }
-      if (!failed) {
-        if (j < nkv_w) {
-          if (!issue_pv(w, j)) failed = true;
-        } else if (!mbar_wait(&v_full[j % NV], static_cast<uint32_t>(j / NV) & 1u, abort_flag)) {
-          failed = true;
-        }
-      }
-      if (!failed && lane == 0) tc_commit(&v_empty[j % NV]);
-      __syncwarp();
+      kt += nkv_max;
+      vt += nkv_max;
+      g += nkv_w;
     }
     if (failed) {
       if (lane == 0) {
@@ -374,10 +443,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // than 2^8 (then O_w in TMEM, l and t are rescaled once), so most tiles touch O not at
     // all; P = 2^(x log2 e - m) as fp16 into shared memory for the P V UMMA.
     const int w = (warp - 4) >> 2;
-    const int nkv_w = w == 0 ? nkv0 : nkv1;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const int64_t q = q0 + w * kAttnTile + row;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t t_s = tmem_base + Cfg::kTmemS + w * KT + lane_off;
     const uint32_t t_o = tmem_base + Cfg::kTmemO + w * D + lane_off;
@@ -388,10 +455,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const bool scale_is_f16 = __half2float(sch) == args.scale;  // uniform for the kernel
     const uint32_t sch2 = static_cast<uint32_t>(__half_as_ushort(sch)) * 0x10001u;
     uint8_t* pbuf = sP + w * Cfg::kPBytes;
-    float m2 = -__builtin_huge_valf(), l = 0.f, t2 = 0.f;
     bool failed = false;
+    uint32_t gbase = 0;  // this query tile's key tiles of the earlier units (all barrier phases count them)
+    for (int64_t tu = blockIdx.x; tu < nunits && !failed; tu += gridDim.x) {
+    const AttnUnit un = attn_unit<D>(args, tu);
+    const int nkv_w = w == 0 ? un.nkv0 : un.nkv1;
+    const int64_t q = un.q0 + w * kAttnTile + row;
+    const int64_t b = un.b, h = un.h, bh = un.bh;
+    float m2 = -__builtin_huge_valf(), l = 0.f, t2 = 0.f;
     for (int j = 0; j < nkv_w; ++j) {
-      if (!mbar_wait_warp(&s_full[w], static_cast<uint32_t>(j) & 1u, abort_flag)) {
+      const uint32_t gj = gbase + static_cast<uint32_t>(j);
+      if (!mbar_wait_warp(&s_full[w], gj & 1u, abort_flag)) {
         failed = true;
         break;
       }
@@ -457,7 +531,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const bool rescale = __any_sync(0xffffffffu, alpha != 1.f);
       if (j > 0) {
         // P_w V_{j-1} done: P_w may be rewritten and O_w is stable
-        if (!mbar_wait_warp(&o_done[w], static_cast<uint32_t>(j - 1) & 1u, abort_flag)) {
+        if (!mbar_wait_warp(&o_done[w], (gj - 1u) & 1u, abort_flag)) {
           failed = true;
           break;
         }
@@ -504,7 +578,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       l += (sp2[0].x + sp2[0].y) + (sp2[1].x + sp2[1].y);
       t2 += (spt2[0].x + spt2[0].y) + (spt2[1].x + spt2[1].y);
     }
-    if (!failed && nkv_w > 0 && !mbar_wait_warp(&o_done[w], static_cast<uint32_t>(nkv_w - 1) & 1u, abort_flag))
+    if (!failed && !mbar_wait_warp(&o_done[w], (gbase + static_cast<uint32_t>(nkv_w) - 1u) & 1u, abort_flag))
       failed = true;
     if (failed) {
       if (lane == 0) {
@@ -536,6 +610,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       if (store) args.H[bh * args.S + q] = 0.69314718055994531f * (__log2f(l) - t2 / l);
       if (store && args.ml != nullptr) args.ml[bh * args.S + q] = make_float2(m2, l);
+      // O_w is read out: the next unit's first P V may overwrite it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[w]);
+    }
+    gbase += static_cast<uint32_t>(nkv_w);
     }
     tc_fence_before();
   }

@@ -375,8 +375,11 @@ int launch_flash_attention(const AttnLaunch& a, cudaStream_t s) {
   args.O = static_cast<__half*>(a.O);
   args.H = a.H;
   args.ml = static_cast<float2*>(a.ml);
-  const int64_t nqc = (a.S + 2 * kAttnTile - 1) / (2 * kAttnTile);  // 256 query rows per CTA
-  const dim3 grid(static_cast<unsigned>(a.B * a.Hq * nqc));
+  // persistent: one CTA per SM (its shared memory), each taking units of 256 query rows
+  const int64_t nqc = (a.S + 2 * kAttnTile - 1) / (2 * kAttnTile);
+  const int64_t units = a.B * a.Hq * nqc;
+  const int64_t sms = sm_count();
+  const dim3 grid(static_cast<unsigned>(units < sms ? units : sms));
   if (a.D == 64)
     return launch_pdl(flash_attention_entropy_kernel<64>, grid, dim3(kAttnThreads), AttnCfg<64>::kSmem, s, a.q, a.k,
                       a.vt, args);
