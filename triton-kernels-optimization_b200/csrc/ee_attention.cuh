@@ -3,7 +3,12 @@
 // [B, H, S, S] probabilities (the reference's transformers attention returns them and
 // computes -sum p log(p + 1e-10) in torch, EE/python/dispatch.py:236-245).
 //
-// One CTA per (batch, query head, 256 query rows = two 128-row query tiles), 384 threads:
+// Persistent: one CTA per SM (its 165 / 231 KB of shared memory), 384 threads, taking work
+// units of (batch, query head, 256 query rows = two 128-row query tiles) longest causal
+// unit first; every barrier's phase runs on across the units, the next unit's Q loads as
+// soon as both issuers' last S MMAs of the current unit completed, and the first P V of a
+// unit (which overwrites O) waits until the previous unit's O is read out, so a unit's
+// loads and first scores overlap the previous unit's last tiles and output.  Roles:
 //   warp 0     TMA producer: both Q tiles once, then K and V^T tiles of 128 keys into
 //              rings (K 2 deep; V 2 deep at head_dim 64, 1 at 128);
 //   warps 1-2  UMMA issuers, one thread each, warp 1 + w for query tile w (warp 1 also owns
