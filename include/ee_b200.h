@@ -444,7 +444,8 @@ EE_API int ee_kv_append(const ee_kv_cache* cache, const void* k_rows, int64_t ld
  * out fp16 [batch, heads * head_dim] (row stride ldo), and H (nullable, fp32 [batch,
  * heads]) the entropy of each softmax row: the router input of the new token.  The
  * tokens are split over CTAs (flash-decoding) whose partials merge in a second launch;
- * workspace: ee_kv_decode_workspace_bytes. */
+ * workspace: ee_kv_decode_workspace_bytes.  The cache's K / V pools must be 16-byte
+ * aligned (the layout of ee_kv_cache_init is); EE_ERR_MISALIGNED otherwise. */
 EE_API size_t ee_kv_decode_workspace_bytes(const ee_kv_cache* cache, int64_t heads);
 EE_API int ee_kv_decode_attention(const ee_kv_cache* cache, const void* q, int64_t ldq, int64_t heads,
                                   const void* k_new, const void* v_new, int64_t ld_new, float scale, void* out,
