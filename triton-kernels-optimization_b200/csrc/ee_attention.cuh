@@ -653,8 +653,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 // recomputes the fp16 scores S = Q K^T on the tensor core (the same tcgen05 MMAs and
 // roundings as the first pass, no P V), forms q_j = 2^(x_j log2 e - m) / l -- the fp32
 // softmax --, rounds it to fp16 and adds p ln(p + 1e-10) in fp32 as the reference does.
-// One CTA per (batch, query head, two 128-row query tiles), 384 threads:
-//   warp 0     TMA producer: both Q tiles once, K tiles of 128 keys into a 3-deep ring;
+// Persistent like the flash kernel: one CTA per SM, 384 threads, taking the units
+// (batch, query head, two 128-row query tiles) longest first in snake order:
+//   warp 0     TMA producer: both Q tiles of a unit (once the unit before has issued its
+//              last S MMA), K tiles of 128 keys into a 3-deep ring running across units;
 //   warp 1     TMEM owner + single-thread UMMA issuer: S_w,j into one of two TMEM buffers
 //              of query tile w (S of tile j + 1 is issued while tile j is reduced);
 //   warps 4-11 warpgroup w = query tile w, one row per thread.
@@ -697,25 +699,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* s_full = bars + 1 + 2 * NS;  // [2 tiles][2 buffers] S ready (MMA commit)
   uint64_t* s_free = s_full + 4;         // [2][2] S read into registers (4 warps)
   uint64_t* drain = s_full + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 9);
-  static_assert((1 + 2 * NS + 9) * 8 + 8 <= Cfg::kBarrierBytes, "exact-entropy barrier region overflows");
+  uint64_t* q_empty = s_full + 9;  // the issuer's last S MMA of a unit done: Q may reload
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(s_full + 10);
+  static_assert((1 + 2 * NS + 10) * 8 + 8 <= Cfg::kBarrierBytes, "exact-entropy barrier region overflows");
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  static_assert(Cfg::KT == AttnCfg<D>::KT, "the units of the flash kernel");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t nqc = (args.S + 2 * kAttnTile - 1) / (2 * kAttnTile);
-  const int qc = static_cast<int>(nqc - 1 - static_cast<int64_t>(blockIdx.x) % nqc);
-  const int64_t bh = static_cast<int64_t>(blockIdx.x) / nqc;
-  const int64_t b = bh / args.Hq, h = bh % args.Hq;
-  const int64_t hk = h / (args.Hq / args.Hkv);
-  const int64_t q0 = static_cast<int64_t>(qc) * 2 * kAttnTile;
-  const int nkv_all = static_cast<int>((args.S + KT - 1) / KT);
-  const int reach0 = static_cast<int>((q0 + kAttnTile + KT - 1) / KT);
-  const int reach1 = static_cast<int>((q0 + 2 * kAttnTile + KT - 1) / KT);
-  const int nkv0 = args.causal ? (reach0 < nkv_all ? reach0 : nkv_all) : nkv_all;
-  const int nkv1 = args.causal ? (reach1 < nkv_all ? reach1 : nkv_all) : nkv_all;
-  const int nkv_max = nkv1;
-  const int q_row0 = static_cast<int>(bh * args.S + q0);
-  const int k_row0 = static_cast<int>((b * args.Hkv + hk) * args.S);
+  const int64_t nunits = args.B * args.Hq * ((args.S + 2 * kAttnTile - 1) / (2 * kAttnTile));
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -728,6 +719,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&s_free[i], 4);
     }
     mbar_init(drain, 1);
+    mbar_init(q_empty, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -748,53 +740,76 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (warp == 0) {
     // -------------------------------------------------------------- TMA producer
     bool failed = false;
-    uint32_t k_issued = 0, k_par = 0;
-    if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, 2 * Cfg::kQTileBytes);
-      for (int t = 0; t < 2; ++t)
-        for (int kb = 0; kb < Cfg::kKBlocks; ++kb)
-          tma_load_2d(sQ + t * Cfg::kQTileBytes + kb * kAttnTileBytes, &tm_q, q_full, kb * 64, q_row0 + t * kAttnTile);
-    }
-    for (int j = 0; j < nkv_max; ++j) {
-      const int s = j % NS;
-      const uint32_t ph = static_cast<uint32_t>(j / NS) & 1u;
-      if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag)) {
+    uint32_t k_issued = 0, k_par = 0, kt = 0;  // kt: K tiles loaded (all units)
+    int q_loads = 0;
+    int64_t t;
+    for (int64_t r = 0; !failed && (t = attn_unit_index(r, nunits)) >= 0; ++r) {
+      const AttnUnit un = attn_unit<D>(args, t);
+      if (q_loads > 0 && !mbar_wait_warp(q_empty, static_cast<uint32_t>(q_loads - 1) & 1u, abort_flag)) {
         failed = true;
         break;
       }
       if (lane == 0) {
-        mbar_arrive_expect_tx(&k_full[s], Cfg::kKBytes);
-        for (int kb = 0; kb < Cfg::kKBlocks; ++kb)
-          tma_load_2d(sK + s * Cfg::kKBytes + kb * (KT * 128), &tm_k, &k_full[s], kb * 64, k_row0 + j * KT);
+        mbar_arrive_expect_tx(q_full, 2 * Cfg::kQTileBytes);
+        for (int q = 0; q < 2; ++q)
+          for (int kb = 0; kb < Cfg::kKBlocks; ++kb)
+            tma_load_2d(sQ + q * Cfg::kQTileBytes + kb * kAttnTileBytes, &tm_q, q_full, kb * 64, un.q_row0 + q * kAttnTile);
       }
-      k_issued |= 1u << s;
-      k_par = (k_par & ~(1u << s)) | (ph << s);
+      ++q_loads;
       __syncwarp();
+      for (int j = 0; j < un.nkv1; ++j, ++kt) {
+        const int s = kt % NS;
+        const uint32_t ph = (kt / NS) & 1u;
+        if (!mbar_wait_warp(&k_empty[s], ph ^ 1u, abort_flag)) {
+          failed = true;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&k_full[s], Cfg::kKBytes);
+          for (int kb = 0; kb < Cfg::kKBlocks; ++kb)
+            tma_load_2d(sK + s * Cfg::kKBytes + kb * (KT * 128), &tm_k, &k_full[s], kb * 64, un.k_row0 + j * KT);
+        }
+        k_issued |= 1u << s;
+        k_par = (k_par & ~(1u << s)) | (ph << s);
+        __syncwarp();
+      }
     }
     if (failed) {
       if (lane == 0) {
         atomicOr(&g_device_error, kErrWaitTimeout);
         *abort_flag = 1;
       }
-      (void)mbar_wait(q_full, 0u, nullptr);
+      if (q_loads > 0) (void)mbar_wait(q_full, static_cast<uint32_t>(q_loads - 1) & 1u, nullptr);
       for (int s = 0; s < NS; ++s)
         if (k_issued & (1u << s)) (void)mbar_wait(&k_full[s], (k_par >> s) & 1u, nullptr);
     }
   } else if (warp == 1) {
     // -------------------------------------------------------------- UMMA issuer
+    // counters over all units of the CTA: kt the K tiles, g[w] the S tiles of query tile w
+    // (its buffer g & 1, that buffer's use g >> 1)
     constexpr uint32_t idesc_s = make_idesc(1u, 0u, kAttnTile, KT);  // f32 <- f16 x f16, 128 x 128
-    bool failed = !mbar_wait(q_full, 0u, abort_flag);
+    bool failed = false;
+    uint32_t kt = 0, g[2] = {0u, 0u};
+    int units = 0;
+    int64_t t;
+    for (int64_t r = 0; !failed && (t = attn_unit_index(r, nunits)) >= 0; ++r, ++units) {
+    const AttnUnit un = attn_unit<D>(args, t);
+    if (!mbar_wait(q_full, static_cast<uint32_t>(units) & 1u, abort_flag)) {
+      failed = true;
+      break;
+    }
     tc_fence_after();
-    for (int j = 0; j < nkv_max && !failed; ++j) {
-      const int s = j % NS;
-      if (!mbar_wait(&k_full[s], static_cast<uint32_t>(j / NS) & 1u, abort_flag)) {
+    for (int j = 0; j < un.nkv1 && !failed; ++j, ++kt) {
+      const int s = kt % NS;
+      if (!mbar_wait(&k_full[s], (kt / NS) & 1u, abort_flag)) {
         failed = true;
         break;
       }
-      const int buf = j & 1;
-      const uint32_t use = static_cast<uint32_t>(j >> 1);
       for (int w = 0; w < 2 && !failed; ++w) {
-        if (j >= (w == 0 ? nkv0 : nkv1)) continue;
+        if (j >= (w == 0 ? un.nkv0 : un.nkv1)) continue;
+        const int buf = static_cast<int>(g[w] & 1u);
+        const uint32_t use = g[w] >> 1;
+        ++g[w];
         if (!mbar_wait(&s_free[2 * w + buf], (use & 1u) ^ 1u, abort_flag)) {
           failed = true;
           break;
@@ -816,6 +831,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!failed && lane == 0) tc_commit(&k_empty[s]);  // the stage is free once these MMAs are done
       __syncwarp();
     }
+    // every S of the unit is issued: Q may reload once they complete
+    if (!failed && lane == 0) tc_commit(q_empty);
+    __syncwarp();
+    }
     if (failed) {
       if (lane == 0) {
         atomicOr(&g_device_error, kErrWaitTimeout);
@@ -828,25 +847,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp >= 4) {
     // -------------------------------------------------------------- rows: the reference's entropy
     const int w = (warp - 4) >> 2;
-    const int nkv_w = w == 0 ? nkv0 : nkv1;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const int64_t q = q0 + w * kAttnTile + row;
-    const bool live = q < args.S;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     constexpr float kLog2eF = 1.4426950408889634f;
     const float2 sc2 = make_float2(args.scale, args.scale);
     const __half sch = __float2half_rn(args.scale);
     const bool scale_is_f16 = __half2float(sch) == args.scale;
     const uint32_t sch2 = static_cast<uint32_t>(__half_as_ushort(sch)) * 0x10001u;
+    bool failed = false;
+    uint32_t gbase = 0;  // this query tile's S tiles of the earlier units
+    int64_t tu;
+    for (int64_t r = 0; !failed && (tu = attn_unit_index(r, nunits)) >= 0; ++r) {
+    const AttnUnit un = attn_unit<D>(args, tu);
+    const int nkv_w = w == 0 ? un.nkv0 : un.nkv1;
+    const int64_t q = un.q0 + w * kAttnTile + row;
+    const int64_t bh = un.bh;
+    const bool live = q < args.S;
     const float2 ml = live ? args.ml[bh * args.S + q] : make_float2(0.f, 1.f);
     const float inv_l = 1.f / ml.y;
     const float2 lg2 = make_float2(kLog2eF, kLog2eF), negm = make_float2(-ml.x, -ml.x);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    bool failed = false;
     for (int j = 0; j < nkv_w; ++j) {
-      const int buf = j & 1;
-      if (!mbar_wait_warp(&s_full[2 * w + buf], static_cast<uint32_t>(j >> 1) & 1u, abort_flag)) {
+      const uint32_t gj = gbase + static_cast<uint32_t>(j);
+      const int buf = static_cast<int>(gj & 1u);
+      if (!mbar_wait_warp(&s_full[2 * w + buf], (gj >> 1) & 1u, abort_flag)) {
         failed = true;
         break;
       }
@@ -909,6 +934,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     } else if (live) {
       args.H[bh * args.S + q] = -0.69314718055994531f * ((acc[0] + acc[1]) + (acc[2] + acc[3]));
+    }
+    gbase += static_cast<uint32_t>(nkv_w);
     }
     tc_fence_before();
   }

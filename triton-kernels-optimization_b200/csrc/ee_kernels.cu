@@ -412,8 +412,11 @@ int launch_attention_entropy_exact(const AttnLaunch& a, cudaStream_t s) {
   args.O = nullptr;
   args.H = a.H;
   args.ml = static_cast<float2*>(a.ml);
+  // persistent like the flash kernel: one CTA per SM taking the same units in the same order
   const int64_t nqc = (a.S + 2 * kAttnTile - 1) / (2 * kAttnTile);
-  const dim3 grid(static_cast<unsigned>(a.B * a.Hq * nqc));
+  const int64_t units = a.B * a.Hq * nqc;
+  const int64_t sms = sm_count();
+  const dim3 grid(static_cast<unsigned>(units < sms ? units : sms));
   if (a.D == 64)
     return launch_pdl(attention_entropy_exact_kernel<64>, grid, dim3(kAttnThreads), ExactCfg<64>::kSmem, s, a.q,
                       a.k, args);
