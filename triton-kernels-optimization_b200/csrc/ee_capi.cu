@@ -150,6 +150,17 @@ bool split_eligible(const ee::GemmArgs& args, int64_t tiles, int64_t slots) {
   return args.part != nullptr && args.K >= 8192 && 4 * tiles <= 3 * slots;
 }
 
+// The CTA-pair kernel between 513 and 768 rows may also split with up to two tiles per
+// pair: there the FP16 tiles (twice the 8-bit tiles' K loop) set the makespan while the
+// 8-bit tiles fit in one round, and the device's plan splits the FP16 tiles alone
+// (measured on B200, K 14336 x N 4096, the bench's routing law, back-to-back calls: 768
+// rows 95.5 -> 88.1 us).  At 1024 rows the 8-bit tiles alone fill the pairs (80 tiles on
+// 74), the plan keeps every tile whole, and the reduction launch alone cost 6.5 us
+// (100.6 -> 107.1 us), so the gate stops at 768.
+bool pair_split_eligible(const ee::GemmArgs& args, int64_t tiles, int64_t pairs) {
+  return args.part != nullptr && args.K >= 8192 && args.M_cap > 512 && args.M_cap <= 768 && tiles <= 2 * pairs;
+}
+
 // Automatic policy between 129 and 512 rows: single-CTA 128 x 256 tiles instead of CTA
 // pairs when they need fewer rounds of the persistent grid, or when only they qualify
 // for the K split (measured on B200 with 20/60/20 routing, back-to-back calls: 256 rows
@@ -212,7 +223,8 @@ int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cud
   const int64_t slots = pair ? num_sms() / 2 : num_sms();
   const int64_t split_tiles = pair ? row_tiles(args, dynamic_counts, ee::kPairTileRows) * ((args.N + ee::kBN - 1) / ee::kBN)
                                    : wide_tiles;
-  const bool split = policy != 3 && split_eligible(args, split_tiles, slots);
+  const bool split = policy != 3 && (split_eligible(args, split_tiles, slots) ||
+                                     (pair && pair_split_eligible(args, split_tiles, slots)));
   if (!split) {
     args.part = nullptr;
     args.part_blocks = 0;

@@ -66,50 +66,59 @@ struct TileGeo {
   int total;      // work units
 };
 
-// makespan estimate, in K stages per slot, of running every tile of bucket b as S[b]
-// ranges on `slots` CTAs (pairs) taking units longest first: the costliest group's
-// rounds, or the whole work levelled in units of the cheapest range, whichever is
-// longer.  A unit costs its stages + 1 (pipeline fill) + kSplitStoreCost when it stores
-// a partial block (128 KiB per CTA); a split plan adds kSplitOverhead for the reduction
-// pass's launch (plan_splits_warp adds its reads).  Costs measured on B200: one K stage
-// of a 128 x 256 (pair: 256 x 256) tile about 0.4 us.  32-bit arithmetic: plan_splits only plans for K loops of at most
+// Makespan, in K stages per slot, of the call's units on `slots` CTAs (pairs) in the
+// order the kernel hands them out: every FP16 unit (one cost, ca) first, then the 8-bit
+// units (INT8 and FP8 have the same K loop: one cost, cb, for S[0] == S[1]), each unit to
+// the slot that frees first.  A unit costs its stages + 1 (pipeline fill) +
+// kSplitStoreCost when it stores a partial block (128 KiB per CTA).  Closed form: the
+// FP16 units leave r = na mod slots slots one unit (ca) later than the other slots, at
+// lo; the 8-bit units start in the merged order of the two lattices lo + k cb (slots - r
+// slots) and lo + ca + k cb (r slots), so the last one starts where the nb-th of those
+// times lies -- first ceil(ca / cb) per early slot alone, then `slots` per period cb.
+// Costs measured on B200: one K stage of a 128 x 256 (pair: 256 x 256) tile about
+// 0.4 us.  32-bit arithmetic: plan_splits only plans for K loops of at most
 // kSplitMaxKBlocks stages and at most kSplitMaxTiles tiles.
 constexpr int kSplitOverhead = 8;
 constexpr int kSplitStoreCost = 2;
 constexpr int kSplitBlocksPerStage = 12;
 constexpr int kSplitMaxKBlocks = 1 << 12;
 constexpr int kSplitMaxTiles = 1024;
-__device__ __forceinline__ int split_estimate(const int (&tiles)[3], const int (&nkb)[3], const int (&S)[3],
+__device__ __forceinline__ int split_makespan(const int (&tiles)[3], const int (&nkb)[3], const int (&S)[3],
                                               int slots) {
-  int work = 0, cmax = 0, cmin = 1 << 30, nhi = 0;
-  bool split = false;
-#pragma unroll
-  for (int b = 0; b < 3; ++b) {
-    if (tiles[b] == 0) continue;
-    const int c = (nkb[b] + S[b] - 1) / S[b] + 1 + (S[b] > 1 ? kSplitStoreCost : 0);
-    const int u = tiles[b] * S[b];
-    work += u * c;
-    if (c > cmax) {
-      cmax = c;
-      nhi = u;
-    } else if (c == cmax) {
-      nhi += u;
+  const int na = tiles[2] * S[2], nb = (tiles[0] + tiles[1]) * S[0];
+  const int ca = (nkb[2] + S[2] - 1) / S[2] + 1 + (S[2] > 1 ? kSplitStoreCost : 0);
+  const int cb = (nkb[0] + S[0] - 1) / S[0] + 1 + (S[0] > 1 ? kSplitStoreCost : 0);
+  const int q = na / slots, r = na - q * slots;
+  const int lo = q * ca, hi = r > 0 ? lo + ca : lo;
+  if (nb == 0) return hi;
+  int start;  // of the last 8-bit unit, after lo
+  if (r == 0) {
+    start = ((nb - 1) / slots) * cb;
+  } else {
+    const int nlo = slots - r;
+    const int k1 = (ca + cb - 1) / cb;  // units each early slot starts before the late ones free
+    if (nb <= nlo * k1) {
+      start = ((nb - 1) / nlo) * cb;
+    } else {
+      const int n2 = nb - nlo * k1 - 1;
+      const int i = n2 / slots, rem = n2 - i * slots;
+      start = ca + i * cb + (rem < r ? 0 : k1 * cb - ca);
     }
-    cmin = c < cmin ? c : cmin;
-    split |= S[b] > 1;
   }
-  if (cmax == 0) return 0;
-  const int hi = cmax * ((nhi + slots - 1) / slots);
-  const int lvl = cmin * ((work + slots * cmin - 1) / (slots * cmin));
-  return (hi > lvl ? hi : lvl) + (split ? kSplitOverhead : 0);
+  const int end = lo + start + cb;
+  return end > hi ? end : hi;
 }
 
 // K-split plan, evaluated by one whole warp (the same result in every CTA and in the
-// reduction kernel): lane l scores the range length C = ceil(longest K loop / (l + 1)),
-// each bucket split into ceil(nkb / C) ranges (so ranges of all buckets are about
-// equally long), ranges of at least kSplitMinKBlocks stages, the partial blocks within
-// part_blocks; the smallest estimate wins, ties to fewer ranges.  Lanes >= kMaxKSplits
-// and invalid candidates score "never".
+// reduction kernel).  Lanes 0-15 score a common range length C = ceil(longest K loop /
+// (l + 1)), each bucket split into ceil(nkb / C) ranges (ranges of all buckets about
+// equally long); lanes 16-31 split only the FP16 tiles, into l - 14 ranges (the 8-bit
+// tiles whole: their K loops are half as long).  Ranges of at least kSplitMinKBlocks
+// stages, the partial blocks within part_blocks.  Score: split_makespan, plus for a plan
+// with any split kSplitOverhead (the reduction pass's launch) and the reduction's reads
+// of the split units' partial blocks (about one K stage of one slot per
+// kSplitBlocksPerStage blocks).  The smallest score wins, ties to the lower lane, and a
+// split must beat the whole tiles by a margin (1/8).
 __device__ __forceinline__ void plan_splits_warp(TileGeo& g, const GemmArgs& a, int ranks, int lane) {
   g.spl[0] = g.spl[1] = g.spl[2] = 1;
   if (a.part == nullptr || a.split_slots <= 0 || a.part_blocks <= 0 || g.ntiles > kSplitMaxTiles) return;
@@ -122,38 +131,48 @@ __device__ __forceinline__ void plan_splits_warp(TileGeo& g, const GemmArgs& a, 
     if (tiles[b] > 0 && nkb[b] > maxkb) maxkb = nkb[b];
   }
   if (maxkb < 2 * kSplitMinKBlocks || maxkb > kSplitMaxKBlocks) return;
-  const int j = lane + 1;
-  const int C = (maxkb + j - 1) / j;
   int S[3];
-  int units = 0;
+  bool ok;
+  if (lane < 16) {
+    const int C = (maxkb + lane) / (lane + 1);
+#pragma unroll
+    for (int b = 0; b < 3; ++b) {
+      const int sb = (nkb[b] + C - 1) / C;
+      S[b] = sb < 1 ? 1 : (sb > kMaxKSplits ? kMaxKSplits : sb);
+    }
+    ok = lane == 0 || C >= kSplitMinKBlocks;
+  } else {
+    const int s16 = lane - 14;
+    S[0] = S[1] = 1;
+    S[2] = s16;
+    ok = s16 <= kMaxKSplits && tiles[2] > 0 && tiles[0] + tiles[1] > 0 &&
+         (nkb[2] + s16 - 1) / s16 >= kSplitMinKBlocks;
+  }
+  int units = 0, split_units = 0;
 #pragma unroll
   for (int b = 0; b < 3; ++b) {
-    int sb = (nkb[b] + C - 1) / C;
-    sb = sb < 1 ? 1 : (sb > kMaxKSplits ? kMaxKSplits : sb);
-    S[b] = sb;
-    units += tiles[b] * sb;
+    units += tiles[b] * S[b];
+    split_units += S[b] > 1 ? tiles[b] * S[b] : 0;
   }
-  const bool ok = j <= kMaxKSplits && (j == 1 || (C >= kSplitMinKBlocks && units * ranks <= a.part_blocks));
-  // the reduction pass reads every partial block once: about one K stage of one slot per
-  // kSplitBlocksPerStage blocks
-  int e = ok ? split_estimate(tiles, nkb, S, a.split_slots) + (j > 1 ? units * ranks / kSplitBlocksPerStage : 0)
-             : (1 << 30);
-  // a split must beat the whole tiles by a margin (the estimate is coarse)
+  ok = ok && (lane == 0 || units * ranks <= a.part_blocks);
+  int e = 1 << 30;
+  if (ok)
+    e = split_makespan(tiles, nkb, S, a.split_slots) +
+        (split_units > 0 ? kSplitOverhead + split_units * ranks / kSplitBlocksPerStage : 0);
   const int e1 = __shfl_sync(0xffffffffu, e, 0);
-  if (j > 1 && 8ll * e >= 7ll * e1) e = 1 << 30;
-  // argmin over the warp of (estimate, j)
-  unsigned long long key = (static_cast<unsigned long long>(static_cast<unsigned>(e)) << 8) | static_cast<unsigned>(j);
+  if (lane > 0 && 8ll * e >= 7ll * e1) e = 1 << 30;
+  // argmin over the warp of (score, lane)
+  unsigned long long key = (static_cast<unsigned long long>(static_cast<unsigned>(e)) << 8) | static_cast<unsigned>(lane);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
     key = other < key ? other : key;
   }
-  const int jb = static_cast<int>(key & 0xffu);
-  const int Cb = (maxkb + jb - 1) / jb;
+  const int lb = static_cast<int>(key & 0xffu);
 #pragma unroll
   for (int b = 0; b < 3; ++b) {
-    int sb = (nkb[b] + Cb - 1) / Cb;
-    g.spl[b] = sb < 1 ? 1 : (sb > kMaxKSplits ? kMaxKSplits : sb);
+    const int sb = __shfl_sync(0xffffffffu, S[b], lb);
+    g.spl[b] = tiles[b] > 0 ? sb : 1;  // a bucket without tiles: nothing to reduce
   }
 }
 
