@@ -8,7 +8,9 @@ mix about 24 / 55 / 21 %); device footprint is about 4*N*K + 5*rows*K + 2*rows*N
 (+ 77 MB of split room above 64 rows).
 
 --case attention: each repetition runs flash_attention_entropy (causal, output and
-per-row entropy) on q [B, Hq, S, D], k / v [B, Hkv, S, D].
+per-row entropy) on q [B, Hq, S, D], k / v [B, Hkv, S, D]; with --exact the exact-entropy
+mode instead (flash_attention_rope_entropy with cos = 1, sin = 0 on [B, S, H * D] rows:
+the flash pass, then the second pass that rounds each probability to fp16).
 
 --case kv: an entropy-tied KV cache of --B sequences x --S tokens (8 KV heads of 128, tokens
 stored at about 24 / 55 / 21 % INT8 / FP8 / FP16, the bench's seeds), then per repetition
@@ -21,6 +23,7 @@ random-init weights) for --B sequences of --S tokens, per-token routing at (0.41
     python profile_case.py --rows 2048 --K 4096 --N 14336 --reps 4
     ncu --set full --clock-control none -k regex:gated_gemm -s 3 -c 1 -o prof <same command>
     python profile_case.py --case attention --B 1 --Hq 32 --Hkv 4 --S 2048 --D 64
+    python profile_case.py --case attention --exact --B 2 --Hq 32 --Hkv 8 --S 2048 --D 128
     python profile_case.py --case forward --layers 1 --B 8 --S 2048 --reps 2
     python profile_case.py --case kv --B 8 --S 8192 --reps 3
 """
@@ -50,6 +53,7 @@ def main(argv=None) -> int:
     ap.add_argument("--Hkv", type=int, default=4)
     ap.add_argument("--S", type=int, default=2048)
     ap.add_argument("--D", type=int, default=64)
+    ap.add_argument("--exact", action="store_true", help="attention: the exact-entropy mode")
     args = ap.parse_args(argv)
 
     import torch
@@ -98,6 +102,19 @@ def main(argv=None) -> int:
         torch.cuda.synchronize()
         pkg._lib.device_check()
         print("kv decode", args.B, "x", args.S, "tiers", [int((tier == t).sum()) for t in range(3)])
+        return 0
+    if args.case == "attention" and args.exact:
+        B, S, D = args.B, args.S, args.D
+        q = torch.randn(B, S, args.Hq * D, generator=g, device=dev).half()
+        k = torch.randn(B, S, args.Hkv * D, generator=g, device=dev).half()
+        v = torch.randn(B, S, args.Hkv * D, generator=g, device=dev).half()
+        cos = torch.ones(B, S, D, device=dev, dtype=torch.float16)
+        sin = torch.zeros_like(cos)
+        for _ in range(args.reps):
+            out, hb = pkg.flash_attention_rope_entropy(q, k, v, cos, sin, args.Hq, args.Hkv, exact_entropy=True)
+        torch.cuda.synchronize()
+        pkg._lib.device_check()
+        print("exact-entropy attention", tuple(q.shape), "kv", tuple(k.shape), "batch entropy", hb.cpu().tolist())
         return 0
     if args.case == "attention":
         q = torch.randn(args.B, args.Hq, args.S, args.D, generator=g, device=dev).half()
