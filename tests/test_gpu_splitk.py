@@ -121,8 +121,9 @@ def test_split_repeated_calls_one_workspace(pkg, cuda):
 
 @pytest.mark.parametrize("counts,whole_8bit", [((32, 704, 32), True), ((194, 447, 127), False)])
 def test_pair_split_between_512_and_768_rows(pkg, cuda, counts, whole_8bit):
-    """768 rows x K 14336 on the CTA-pair kernel, where the host lets the device plan a K
-    split with up to two tiles per pair.  With a small FP16 bucket the FP16 tiles (twice
+    """768 rows x K 14336 on the CTA-pair kernel (forced: the automatic policy takes
+    single-CTA tiles there), where the host lets the device plan a K split with up to two
+    tiles per pair.  With a small FP16 bucket the FP16 tiles (twice
     the 8-bit K loop) set the makespan and the plan splits them alone: INT8 and FP8 rows
     identical to the unsplit run (their tiles ran whole).  With the bench's routing mix
     the plan splits every bucket (one range length for all).  Either way the split
@@ -131,7 +132,46 @@ def test_pair_split_between_512_and_768_rows(pkg, cuda, counts, whole_8bit):
     K, N = 14336, 4096
     H, a, w = _inputs(counts, K, N, 768, cuda)
     p = pkg.WeightPack(*pkg.quantize_weights_int8(w))
-    y0 = _route(pkg, H, K, False, cuda).gated_linear(a, p)
+    lib = pkg.load_library()
+    assert lib.ee_set_gemm_policy(2) == 0
+    try:
+        y0 = _route(pkg, H, K, False, cuda).gated_linear(a, p)
+        r1 = _route(pkg, H, K, True, cuda)
+        y1 = r1.gated_linear(a, p)
+        torch.cuda.synchronize()
+    finally:
+        assert lib.ee_set_gemm_policy(0) == 0
+    assert pkg._lib.device_check() == 0
+    rows = [torch.nonzero(r1.route_ids == b).flatten() for b in range(3)]
+    same = [torch.equal(y1[r].view(torch.int16), y0[r].view(torch.int16)) for r in rows]
+    assert same[0]
+    assert same[1] == whole_8bit
+    assert not same[2]
+    for b, ref in ((1, _ref_fp8), (2, _ref_fp16)):
+        assert _relf(y1[rows[b]], y0[rows[b]]) < 1e-3
+        assert _relf(y1[rows[b]], ref(a[rows[b]], p)) < 1e-2
+    assert torch.equal(y1[rows[0]].view(torch.int16), _ref_int8(a[rows[0]], p).view(torch.int16))
+
+
+@pytest.mark.parametrize("counts,whole_8bit", [((194, 447, 127), True), ((120, 300, 200), True),
+                                               ((150, 400, 150), False)])
+def test_single_cta_split_between_512_and_768_rows(pkg, cuda, counts, whole_8bit):
+    """513..768 rows x K 14336 x N 4096: the automatic policy takes single-CTA 128 x 256
+    tiles with the K split.  With 128-row tiles the 8-bit tiles fit in one round, so for
+    the bench's routing mix at 768 rows (and a larger FP16 share at 620) the plan splits
+    the FP16 tiles alone; with a third FP16 tile row it splits every bucket.  Against the
+    single-CTA kernel without split room (forced): INT8 rows identical, FP8 rows identical
+    when their tiles ran whole on the same kernel, FP16 rows not identical (summed from
+    ranges) but within the unsplit run's last bits and the reference tolerance."""
+    K, N = 14336, 4096
+    H, a, w = _inputs(counts, K, N, sum(counts) + 1, cuda)
+    p = pkg.WeightPack(*pkg.quantize_weights_int8(w))
+    lib = pkg.load_library()
+    assert lib.ee_set_gemm_policy(1) == 0
+    try:
+        y0 = _route(pkg, H, K, False, cuda).gated_linear(a, p)
+    finally:
+        assert lib.ee_set_gemm_policy(0) == 0
     r1 = _route(pkg, H, K, True, cuda)
     y1 = r1.gated_linear(a, p)
     torch.cuda.synchronize()

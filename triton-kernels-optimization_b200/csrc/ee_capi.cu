@@ -150,8 +150,9 @@ bool split_eligible(const ee::GemmArgs& args, int64_t tiles, int64_t slots) {
   return args.part != nullptr && args.K >= 8192 && 4 * tiles <= 3 * slots;
 }
 
-// The CTA-pair kernel between 513 and 768 rows may also split with up to two tiles per
-// pair: there the FP16 tiles (twice the 8-bit tiles' K loop) set the makespan while the
+// The CTA-pair kernel (forced; the automatic policy takes single-CTA tiles there when they
+// may split) between 513 and 768 rows may also split with up to two tiles per pair: there
+// the FP16 tiles (twice the 8-bit tiles' K loop) set the makespan while the
 // 8-bit tiles fit in one round, and the device's plan splits the FP16 tiles alone
 // (measured on B200, K 14336 x N 4096, the bench's routing law, back-to-back calls: 768
 // rows 95.5 -> 88.1 us).  At 1024 rows the 8-bit tiles alone fill the pairs (80 tiles on
@@ -161,15 +162,28 @@ bool pair_split_eligible(const ee::GemmArgs& args, int64_t tiles, int64_t pairs)
   return args.part != nullptr && args.K >= 8192 && args.M_cap > 512 && args.M_cap <= 768 && tiles <= 2 * pairs;
 }
 
+// Between 513 and 768 rows with K >= 8192 the automatic policy takes single-CTA 128 x 256
+// tiles, which may split with up to two tiles per SM: with 128-row tiles the 8-bit
+// buckets' tiles fit in one round of the 148 CTAs, so the plan can level the makespan by
+// splitting the FP16 tiles (measured on B200, K 14336 x N 4096, the bench's routing law,
+// back-to-back calls: 768 rows 95.1 us with whole pair tiles, 87.9 with the pairs' split,
+// 79.7 here).  Above 768 rows the single-CTA tiles' larger operand traffic per flop costs
+// more than the levelling saves (1024 rows 106.9 us against 100.5 for whole pair tiles,
+// 1280 rows 113.5 against 104.6), so the pairs keep those.
+bool single_split_eligible(const ee::GemmArgs& args, int64_t tiles, int64_t sms) {
+  return args.part != nullptr && args.K >= 8192 && args.M_cap > 512 && args.M_cap <= 768 && tiles <= 2 * sms;
+}
+
 // Automatic policy between 129 and 512 rows: single-CTA 128 x 256 tiles instead of CTA
 // pairs when they need fewer rounds of the persistent grid, or when only they qualify
 // for the K split (measured on B200 with 20/60/20 routing, back-to-back calls: 256 rows
 // x N 14336 49 us against 58, 512 rows x K 14336 69 us against 82; pairs stay ahead or
 // equal on the other Llama-3-8B shapes and above 512 rows).
 bool single_beats_pairs(const ee::GemmArgs& args, bool dynamic_counts) {
-  if (args.M_cap > 512) return false;
+  if (args.M_cap > 768) return false;
   const int64_t ntn = (args.N + ee::kBN - 1) / ee::kBN;
   const int64_t st = row_tiles(args, dynamic_counts, ee::kBM) * ntn;
+  if (args.M_cap > 512) return single_split_eligible(args, st, num_sms());
   const int64_t pt = row_tiles(args, dynamic_counts, ee::kPairTileRows) * ntn;
   const int64_t sms = num_sms(), pairs = num_sms() / 2;
   const int64_t s_rounds = (st + sms - 1) / sms, p_rounds = (pt + pairs - 1) / pairs;
@@ -224,7 +238,8 @@ int run_gemm(const GemmOperands& op, ee::GemmArgs args, bool dynamic_counts, cud
   const int64_t split_tiles = pair ? row_tiles(args, dynamic_counts, ee::kPairTileRows) * ((args.N + ee::kBN - 1) / ee::kBN)
                                    : wide_tiles;
   const bool split = policy != 3 && (split_eligible(args, split_tiles, slots) ||
-                                     (pair && pair_split_eligible(args, split_tiles, slots)));
+                                     (pair ? pair_split_eligible(args, split_tiles, slots)
+                                           : single_split_eligible(args, split_tiles, slots)));
   if (!split) {
     args.part = nullptr;
     args.part_blocks = 0;
