@@ -178,7 +178,8 @@ bool single_split_eligible(const ee::GemmArgs& args, int64_t tiles, int64_t sms)
 // pairs when they need fewer rounds of the persistent grid, or when only they qualify
 // for the K split (measured on B200 with 20/60/20 routing, back-to-back calls: 256 rows
 // x N 14336 49 us against 58, 512 rows x K 14336 69 us against 82; pairs stay ahead or
-// equal on the other Llama-3-8B shapes and above 512 rows).
+// equal on the other Llama-3-8B shapes).  Between 513 and 768 rows: single-CTA tiles
+// when they may split (single_split_eligible); above 768 rows always pairs.
 bool single_beats_pairs(const ee::GemmArgs& args, bool dynamic_counts) {
   if (args.M_cap > 768) return false;
   const int64_t ntn = (args.N + ee::kBN - 1) / ee::kBN;
