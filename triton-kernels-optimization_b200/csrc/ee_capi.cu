@@ -152,12 +152,12 @@ bool split_eligible(const ee::GemmArgs& args, int64_t tiles, int64_t slots) {
 
 // The CTA-pair kernel (forced; the automatic policy takes single-CTA tiles there when they
 // may split) between 513 and 768 rows may also split with up to two tiles per pair: there
-// the FP16 tiles (twice the 8-bit tiles' K loop) set the makespan while the
-// 8-bit tiles fit in one round, and the device's plan splits the FP16 tiles alone
-// (measured on B200, K 14336 x N 4096, the bench's routing law, back-to-back calls: 768
-// rows 95.5 -> 88.1 us).  At 1024 rows the 8-bit tiles alone fill the pairs (80 tiles on
-// 74), the plan keeps every tile whole, and the reduction launch alone cost 6.5 us
-// (100.6 -> 107.1 us), so the gate stops at 768.
+// the FP16 tiles (twice the 8-bit tiles' K loop) set the makespan while the 8-bit tiles
+// fit in one round, and the device's plan splits the FP16 tiles, alone or with the 8-bit
+// ones (measured on B200, K 14336 x N 4096, the bench's routing law, back-to-back calls:
+// 768 rows 95.1 -> 87.9 us).  At 1024 rows the 8-bit tiles alone can fill the pairs (80
+// tiles on 74), the plan then keeps every tile whole, and the reduction launch alone cost
+// 6.5 us (100.6 -> 107.1 us), so the gate stops at 768.
 bool pair_split_eligible(const ee::GemmArgs& args, int64_t tiles, int64_t pairs) {
   return args.part != nullptr && args.K >= 8192 && args.M_cap > 512 && args.M_cap <= 768 && tiles <= 2 * pairs;
 }
